@@ -1,0 +1,418 @@
+#!/usr/bin/env python
+"""Headline benchmark of the GGUF K-quant linear path on B200.
+
+Workload (the largest single-GPU configuration of
+the Q4_K_M dequant-GEMM metric): the linear stack of a Z-Image-style 6B
+single-stream DiT -- hidden 3840, 30 layers, per layer qkv [11520, 3840],
+out [3840, 3840], w1 / w3 [10240, 3840] (SwiGLU), w2 [3840, 10240]; M = 8448
+tokens (1024x1024 image: 4096 image + 128 text tokens, CFG 2).  Q4_K_M mix:
+every tensor Q4_K except w2 (ffn_down), which is Q6_K in even layers.
+Weights ~ N(0, 0.02), activations ~ N(0, 1) bf16, all synthetic.
+
+A step is one pass of the hot path over the batch: 150 quantised linears.
+With --gpus N each weight is N-column sharded across the ranks (one process
+per GPU) and every linear's bf16 output is all-gathered over NVLink with NCCL,
+overlapped with the next linear's GEMM.  Prints one JSON line (rank 0).
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import tempfile
+import time
+from pathlib import Path
+
+import numpy as np
+
+ROOT = Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT))
+
+METRIC = "Q4_K_M dequant-GEMM TFLOPS (% bf16 TC peak); small-M GEMV GB/s (% HBM)"
+HIDDEN, FFN, LAYERS, M_TOKENS = 3840, 10240, 30, 8448
+Q4_K, Q6_K = 12, 14
+DISTINCT_LAYERS = 2     # weight contents cycle over 2 seeds; every layer has its own HBM buffers
+
+
+def layer_linears(layer: int):
+    """(name, N, K, ggml_type) of one layer's linears in the Q4_K_M mix."""
+    return [("qkv", 3 * HIDDEN, HIDDEN, Q4_K), ("out", HIDDEN, HIDDEN, Q4_K), ("w1", FFN, HIDDEN, Q4_K),
+            ("w3", FFN, HIDDEN, Q4_K), ("w2", HIDDEN, FFN, Q6_K if layer % 2 == 0 else Q4_K)]
+
+
+def step_flops(layers: int, m: int = M_TOKENS) -> float:
+    return float(sum(2.0 * m * n * k for l in range(layers) for _, n, k, _ in layer_linears(l)))
+
+
+def peaks():
+    p = ROOT / "MEASURED_PEAKS.json"
+    if p.exists():
+        d = json.loads(p.read_text())
+        return d["hbm_gbs"], d["bf16_tflops"], d["bf16_tflops_sustained"], "measured"
+    return 6650.0, 1590.0, 1400.0, "fallback"
+
+
+# ---------------------------------------------------------------- clocks
+class ClockSampler:
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, device: int):
+        self.device, self.proc, self.path = device, None, None
+
+    def start(self):
+        try:
+            fd, self.path = tempfile.mkstemp(suffix=".csv")
+            os.close(fd)
+            self.proc = subprocess.Popen(["nvidia-smi", "-i", str(self.device), f"--query-gpu={self.FIELDS}",
+                                          "--format=csv,noheader,nounits", "-lms", "200", "-f", self.path],
+                                         stdout=subprocess.DEVNULL, stderr=subprocess.DEVNULL)
+        except OSError:
+            self.proc = None
+
+    def stop(self):
+        if not self.proc:
+            return None
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except subprocess.TimeoutExpired:
+            self.proc.kill()
+        rows = []
+        for line in Path(self.path).read_text().splitlines():
+            parts = [p.strip() for p in line.split(",")]
+            if len(parts) >= 9:
+                rows.append(parts)
+        os.unlink(self.path)
+        if not rows:
+            return None
+        sm = [float(r[1]) for r in rows if r[1].replace(".", "").isdigit()]
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = sorted({names[i] for r in rows for i in range(4) if r[5 + i].lower().startswith("active")})
+        return {"sm_mhz": statistics.median(sm) if sm else None,
+                "sm_max_mhz": float(rows[0][2]) if rows[0][2].replace(".", "").isdigit() else None,
+                "reasons": reasons, "samples": len(rows)}
+
+
+# ---------------------------------------------------------------- CPU path
+def cpu_reference_sample(m_sample: int, linears, threads: int):
+    """The reference's CPU path on a bounded sample: decode_cpu_into -> f32
+    (row-split over `threads`, as RowDecodePool) then an fp32 matmul with
+    torch on `threads` host threads.  Returns (seconds, flops, kind)."""
+    import torch
+    sys.path.insert(0, str(ROOT / "tests"))
+    from oracle import oracle
+    kind = "reference" if oracle.ref() is not None else "port"
+    torch.set_num_threads(threads)
+    x = torch.randn(m_sample, FFN, generator=torch.Generator().manual_seed(5))
+    t0 = time.perf_counter()
+    flops = 0.0
+    for name, n, k, typ, raw in linears:
+        w = oracle.decode_parallel(raw, typ, n, k, 0, which="ref" if kind == "reference" else "port", threads=threads)
+        y = x[:, :k] @ torch.from_numpy(w).T
+        flops += 2.0 * m_sample * n * k
+        del y, w
+    return time.perf_counter() - t0, flops, kind
+
+
+def make_cpu_linears(layer: int = 0):
+    """Raw GGUF blocks of one layer's linears (same seeds as the GPU arm)."""
+    from turbocider_b200 import cuda as tcc
+    out = []
+    for i, (name, n, k, typ) in enumerate(layer_linears(layer)):
+        w = (np.random.default_rng(1000 * layer + i).standard_normal((n, k), dtype=np.float32) * np.float32(0.02))
+        out.append((name, n, k, typ, tcc.quantize(typ, w)))
+    return out
+
+
+def run_reference(args):
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return 0
+    threads = os.cpu_count() or 1
+    linears = make_cpu_linears(0)
+    m_sample = args.cpu_rows
+    for _ in range(args.warmup):
+        cpu_reference_sample(m_sample, linears, threads)
+    times, flops, kind = [], 0.0, "port"
+    for _ in range(args.steps):
+        t, flops, kind = cpu_reference_sample(m_sample, linears, threads)
+        times.append(t)
+    total = sum(times)
+    value = flops * args.steps / total / 1e12
+    sample = (f"layer 0 of the config-5 stack (qkv, out, w1, w3, w2 Q6_K): decode_cpu_into->f32 of the 5 weights "
+              f"+ fp32 matmul at {m_sample} of {M_TOKENS} rows, per step")
+    line = {"impl": "reference", "metric": METRIC, "value": round(value, 4), "unit": "TFLOPS",
+            "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
+            "ms_per_step": round(1e3 * total / args.steps, 3), "higher_is_better": True, "scaling": "strong",
+            "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+            "config": {"workload": "config5_zimage_6b_linear_stack", "layers": LAYERS, "m_tokens": M_TOKENS,
+                       "hidden": HIDDEN, "ffn": FFN, "mix": "Q4_K_M", "cpu_sample_rows": m_sample},
+            "cpu_baseline": {"value": round(value, 4), "unit": "TFLOPS", "cores": threads, "kind": kind,
+                             "sample": sample},
+            "e2e": {"value": round(value, 4), "unit": "TFLOPS", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    print(json.dumps(line), flush=True)
+    return 0
+
+
+# ---------------------------------------------------------------- GPU arm
+def build_weights(ctx, rank, world, layers, device):
+    """Upload every layer's weight shard (rows [r N/g, (r+1) N/g)) to HBM."""
+    import torch
+    from turbocider_b200 import cuda as tcc
+    threads = max(1, (os.cpu_count() or 8) // max(1, world))
+    raw_cache = {}
+    for d in range(min(DISTINCT_LAYERS, layers)):
+        for i, (name, n, k, typ) in enumerate(layer_linears(d)):
+            g = torch.Generator(device=device).manual_seed(1000 * d + i)
+            rows = n // world
+            w = torch.randn(n, k, generator=g, device=device)[rank * rows:(rank + 1) * rows].mul_(0.02)
+            raw_cache[(d, name)] = (tcc.quantize(typ, w.cpu().numpy(), threads=threads), rows, k, typ)
+            del w
+    weights = []
+    for layer in range(layers):
+        lw = {}
+        for name, n, k, typ in layer_linears(layer):
+            raw, rows, kk, t = raw_cache[(layer % DISTINCT_LAYERS, name)]
+            assert t == typ
+            lw[name] = tcc.Weight.upload(ctx, typ, rows, kk, raw)
+        weights.append(lw)
+    return weights
+
+
+def gemv_measure(ctx, device, hbm_peak):
+    """Config 2: Q6_K GEMV, K=12288, N=3072, M in {1, 4, 16}; 10 weight copies
+    (310 MB > L2) cycled inside a CUDA graph so every call streams HBM."""
+    import torch
+    from turbocider_b200 import cuda as tcc
+    n, k, copies, calls = 3072, 12288, 10, 40
+    w = (np.random.default_rng(2).standard_normal((n, k), dtype=np.float32) * np.float32(0.02))
+    raw = tcc.quantize(Q6_K, w)
+    ws = [tcc.Weight.upload(ctx, Q6_K, n, k, raw) for _ in range(copies)]
+    out = {}
+    stream = torch.cuda.Stream(device)
+    for m in (1, 4, 16):
+        x = torch.randn(m, k, device=device).to(torch.bfloat16)
+        y = torch.empty(m, n, device=device, dtype=torch.bfloat16)
+        with torch.cuda.stream(stream):
+            for i in range(copies):
+                tcc.qlinear(ctx, ws[i], x, out=y, stream=stream)
+            stream.synchronize()
+            graph = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(graph, stream=stream):
+                for i in range(calls):
+                    tcc.qlinear(ctx, ws[i % copies], x, out=y, stream=stream)
+            for _ in range(3):
+                graph.replay()
+            stream.synchronize()
+            ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            reps = 10
+            ev0.record(stream)
+            for _ in range(reps):
+                graph.replay()
+            ev1.record(stream)
+            ev1.synchronize()
+        sec = ev0.elapsed_time(ev1) / 1e3 / (reps * calls)
+        nbytes = len(raw) + m * k * 2 + m * n * 2
+        gbs = nbytes / sec / 1e9
+        out[str(m)] = {"us_per_call": round(sec * 1e6, 3), "gbs": round(gbs, 1), "frac": round(gbs / hbm_peak, 4),
+                       "bytes_per_call": nbytes}
+        del graph
+    assert ctx.status() == 0
+    for wt in ws:
+        wt.free()
+    return {"config": "configs[1]: Q6_K W[3072, 12288], X bf16 [M, 12288]; 10 weight copies cycled (> L2), "
+                      "40 calls per CUDA graph", "peak_gbs": hbm_peak, "m": out}
+
+
+def run_ours(args):
+    import torch
+    import torch.distributed as dist
+    from turbocider_b200 import cuda as tcc
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if world != args.gpus:
+        raise SystemExit(f"--gpus {args.gpus} but WORLD_SIZE={world}: launch N>1 with torchrun")
+    torch.cuda.set_device(local)
+    device = torch.device("cuda", local)
+    if world > 1:
+        import datetime
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=device)
+    hbm_peak, tc_burst, tc_sustained, peak_src = peaks()
+    layers = args.layers
+    ctx = tcc.Context(local)
+    weights = build_weights(ctx, rank, world, layers, device)
+
+    m = M_TOKENS
+    g = torch.Generator(device=device).manual_seed(7)
+    x_h = torch.randn(m, HIDDEN, generator=g, device=device).to(torch.bfloat16)
+    x_f = torch.randn(m, FFN, generator=g, device=device).to(torch.bfloat16)
+    compute = torch.cuda.Stream(device)
+    comm = torch.cuda.Stream(device)
+    names = [l[0] for l in layer_linears(0)]
+    nloc = {name: n // world for name, n, _, _ in layer_linears(0)}
+    # double-buffered local outputs and gathered outputs per linear
+    y_loc = {(name, b): torch.empty(m, nloc[name], device=device, dtype=torch.bfloat16) for name in names for b in (0, 1)}
+    y_all = ({(name, b): torch.empty(world, m, nloc[name], device=device, dtype=torch.bfloat16)
+              for name in names for b in (0, 1)} if world > 1 else {})
+    gathered = {(name, b): None for name in names for b in (0, 1)}
+
+    def one_step(timing=None):
+        for layer in range(layers):
+            b = layer & 1
+            for name in names:
+                x = x_f if name == "w2" else x_h
+                if world > 1 and gathered[(name, b)] is not None:
+                    compute.wait_event(gathered[(name, b)])     # buffer reuse after its gather
+                if timing is not None:
+                    e0 = torch.cuda.Event(enable_timing=True)
+                    e0.record(compute)
+                tcc.qlinear(ctx, weights[layer][name], x, out=y_loc[(name, b)], stream=compute)
+                if timing is not None:
+                    e1 = torch.cuda.Event(enable_timing=True)
+                    e1.record(compute)
+                    timing.append((e0, e1, 2.0 * m * nloc[name] * weights[layer][name].k))
+                if world > 1:
+                    done = torch.cuda.Event()
+                    done.record(compute)
+                    comm.wait_event(done)
+                    with torch.cuda.stream(comm):
+                        dist.all_gather_into_tensor(y_all[(name, b)], y_loc[(name, b)])
+                    ev = torch.cuda.Event()
+                    ev.record(comm)
+                    gathered[(name, b)] = ev
+        if world > 1:
+            compute.wait_stream(comm)
+
+    def barrier():
+        if world > 1:
+            dist.barrier()
+        torch.cuda.synchronize(device)
+
+    with torch.cuda.stream(compute):
+        for _ in range(args.warmup):
+            one_step()
+    barrier()
+    if ctx.status(clear=True):
+        raise SystemExit("device status word set during warm-up")
+
+    clocks = ClockSampler(local)
+    clocks.start()
+    timing = []
+    barrier()
+    t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    t0.record(compute)
+    for _ in range(args.steps):
+        one_step(timing)
+    t1.record(compute)
+    barrier()
+    clock_info = clocks.stop()
+    elapsed = t0.elapsed_time(t1) / 1e3
+    if world > 1:
+        tt = torch.tensor([elapsed], device=device, dtype=torch.float64)
+        dist.all_reduce(tt, op=dist.ReduceOp.MAX)
+        elapsed = float(tt.item())
+    flops = step_flops(layers) * args.steps
+    value = flops / elapsed / 1e12
+    gemm_time = sum(a.elapsed_time(b) for a, b, _ in timing) / 1e3
+    gemm_flops = sum(f for _, _, f in timing)
+    achieved = gemm_flops / gemm_time / 1e12
+    status = ctx.status(clear=True)
+
+    # end to end: pinned host inputs -> HBM, the stack, result -> pinned host
+    h_xh = x_h.cpu().pin_memory()
+    h_xf = x_f.cpu().pin_memory()
+    last = y_all[("w2", (layers - 1) & 1)] if world > 1 else y_loc[("w2", (layers - 1) & 1)]
+    h_y = torch.empty(last.shape, dtype=last.dtype, pin_memory=True)
+    e2e_steps = max(1, min(args.steps, 3))
+    barrier()
+    s0, s1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    s0.record(compute)
+    with torch.cuda.stream(compute):
+        for _ in range(e2e_steps):
+            x_h.copy_(h_xh, non_blocking=True)
+            x_f.copy_(h_xf, non_blocking=True)
+            one_step()
+            h_y.copy_(last, non_blocking=True)
+    s1.record(compute)
+    barrier()
+    e2e_sec = s0.elapsed_time(s1) / 1e3
+    if world > 1:
+        tt = torch.tensor([e2e_sec], device=device, dtype=torch.float64)
+        dist.all_reduce(tt, op=dist.ReduceOp.MAX)
+        e2e_sec = float(tt.item())
+    e2e_value = step_flops(layers) * e2e_steps / e2e_sec / 1e12
+
+    gemv = None
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_extras:
+        gemv = gemv_measure(ctx, device, hbm_peak)
+        t, f, kind = cpu_reference_sample(args.cpu_rows, make_cpu_linears(0), os.cpu_count() or 1)
+        cpu = {"value": round(f / t / 1e12, 4), "unit": "TFLOPS", "cores": os.cpu_count() or 1, "kind": kind,
+               "sample": f"layer 0 of the stack (5 linears): decode_cpu_into->f32 + fp32 torch matmul at "
+                         f"{args.cpu_rows} of {M_TOKENS} rows; {t:.1f} s"}
+
+    traffic = None
+    tfile = ROOT / "profiles" / "gemm_traffic.json"
+    if tfile.exists():
+        traffic = json.loads(tfile.read_text()).get("bytes_per_launch")
+    if rank == 0:
+        peak = tc_sustained
+        line = {"metric": METRIC, "value": round(value, 2), "unit": "TFLOPS", "n_gpus": world, "steps": args.steps,
+                "warmup": args.warmup, "ms_per_step": round(1e3 * elapsed / args.steps, 3),
+                "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
+                "dtype": "bf16", "data": "synthetic",
+                "config": {"workload": "config5_zimage_6b_linear_stack", "layers": layers, "m_tokens": m,
+                           "hidden": HIDDEN, "ffn": FFN, "mix": "Q4_K_M (w2 Q6_K in even layers)",
+                           "parallelism": f"N-shard x{world} + NCCL all-gather" if world > 1 else "single GPU",
+                           "l2": "inputs larger than L2 (3 GB of packed weights streamed per step)",
+                           "weights": f"{layers} distinct HBM buffers per tensor, contents cycle over "
+                                      f"{DISTINCT_LAYERS} seeds"},
+                "gpu_launches": len(timing),
+                "roofline": {"bound": "tensor", "achieved": round(achieved, 2), "peak": peak, "unit": "TFLOP/s",
+                             "frac": round(achieved / peak, 4), "traffic": traffic,
+                             "kernel": "gemm_kernel (tcgen05 Q4_K/Q6_K)", "peak_source": f"{peak_src} sustained"},
+                "e2e": {"value": round(e2e_value, 2), "unit": "TFLOPS",
+                        "h2d_bytes_per_step": int(h_xh.numel() * 2 + h_xf.numel() * 2),
+                        "d2h_bytes_per_step": int(h_y.numel() * 2), "steps": e2e_steps},
+                "clocks": clock_info, "status_word": status}
+        if cpu:
+            line["cpu_baseline"] = cpu
+        if gemv:
+            line["gemv"] = gemv
+        print(json.dumps(line), flush=True)
+    for lw in weights:
+        for wt in lw.values():
+            wt.free()
+    ctx.close()
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+    return 0
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=10)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--layers", type=int, default=LAYERS)
+    ap.add_argument("--cpu-rows", type=int, default=1024)
+    ap.add_argument("--no-extras", action="store_true", help="skip the GEMV and CPU-baseline legs")
+    args = ap.parse_args()
+    if args.warmup < 3 and args.impl == "ours":
+        args.warmup = 3
+    return run_reference(args) if args.impl == "reference" else run_ours(args)
+
+
+if __name__ == "__main__":
+    sys.exit(main())

@@ -1,0 +1,155 @@
+#ifndef TURBOCIDER_CUDA_H
+#define TURBOCIDER_CUDA_H
+/*
+ * TurboCider CUDA backend for B200 (sm_100a): GGUF K-quant (Q4_K / Q6_K)
+ * dequantise-and-matmul, exported as a plain C ABI.
+ *
+ * This backend sits beside the reference's native backends.  Its operator
+ * replaces the quantised branch of Weights::project
+ * (reference native/backends/mlx.cpp:626-690, reached from linear() at
+ * native/backends/mlx.cpp:1624), and its dequantiser is bit-exact to the
+ * reference CPU decoder decode_cpu_into (native/core/gguf_decode.cpp:433-445).
+ *
+ * Conventions (mirroring bindings/c/include/turbocider/turbocider.h:7-12 and
+ * the op-level probe ABI tests/native/gguf_core_probe.cpp:31-65):
+ *   - every int-returning call returns TC_CUDA_OK (0), TC_CUDA_FAIL (1) or
+ *     TC_CUDA_CANCELLED (2); the reason for a failure is available from
+ *     tc_cuda_last_error() on the calling thread;
+ *   - no C++ exception crosses this boundary and no kernel traps: device-side
+ *     faults (nonfinite scales, fp16 overflow, pipeline timeouts) set bits in
+ *     the context's status word, read with tc_cuda_status();
+ *   - device pointers are caller-owned unless returned by this API; `stream`
+ *     is a cudaStream_t passed as void* (NULL = the legacy default stream);
+ *     every launch is asynchronous on that stream;
+ *   - calls on one context are serialised by the caller.
+ *
+ * Ratios: Q4_K = 256 weights / 144 bytes, Q6_K = 256 weights / 210 bytes
+ * (reference native/core/gguf_directory.hpp:21-26).
+ */
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define TC_CUDA_ABI_VERSION 1u
+
+enum { TC_CUDA_OK = 0, TC_CUDA_FAIL = 1, TC_CUDA_CANCELLED = 2 };
+
+/* GGML on-disk type ids (reference native/core/gguf_directory.hpp:21-26). */
+enum { TC_GGML_Q4_K = 12, TC_GGML_Q5_K = 13, TC_GGML_Q6_K = 14 };
+
+/* Target / output dtypes; same numbering as tc::gguf::DecodeDType
+ * (reference native/core/gguf_decode.hpp:18). */
+enum { TC_DTYPE_F32 = 0, TC_DTYPE_F16 = 1, TC_DTYPE_BF16 = 2 };
+
+/* Staging precision of the dequantised weight inside the tensor-core GEMM. */
+enum { TC_STAGE_BF16 = 0, TC_STAGE_F16 = 1 };
+
+/* Status-word bits (tc_cuda_status). */
+enum {
+    TC_STATUS_NONFINITE_SCALE = 1u << 0, /* a d/dmin master scale is inf/nan   */
+    TC_STATUS_F16_OVERFLOW    = 1u << 1, /* a value does not fit fp16          */
+    TC_STATUS_TIMEOUT         = 1u << 2, /* a bounded pipeline wait gave up    */
+    TC_STATUS_GEOMETRY        = 1u << 3  /* a kernel saw an impossible tile    */
+};
+
+typedef struct tc_cuda_ctx tc_cuda_ctx;
+typedef struct tc_cuda_weight tc_cuda_weight;
+
+/* ABI version of this library (cf. tc_abi_version, turbocider.h:24). */
+uint32_t tc_cuda_abi_version(void);
+
+/* Reason for the last failure on this thread; "" after a success
+ * (cf. tc_gguf_test_error, gguf_core_probe.cpp:31). */
+const char *tc_cuda_last_error(void);
+
+/* Create a context on `device`.  The context owns the device status word and
+ * reusable split-K workspace; it does not own streams. */
+int tc_cuda_init(int device, tc_cuda_ctx **ctx);
+void tc_cuda_free(tc_cuda_ctx *ctx);
+
+/* Read (and, if clear != 0, reset) the device status word.  Synchronises the
+ * device.  Replaces the reference's DecodeError throw sites
+ * (gguf_decode.cpp:43, :393, :401-404) for work done on the GPU. */
+int tc_cuda_status(tc_cuda_ctx *ctx, uint32_t *bits, int clear);
+
+/* Upload a GGUF tensor [N rows, K columns] (ne[0] = K contiguous) of type
+ * Q4_K or Q6_K from host memory and keep it resident in HBM in the kernels'
+ * panel layout.  `raw_host` holds whole rows, row pitch K/256*block_bytes, as
+ * in the GGUF payload.  Rows [n_begin, n_begin + n_count) are uploaded (an
+ * N-column shard); n_count = 0 means all rows.  The blocks' bytes are moved,
+ * never re-encoded; every d/dmin is checked finite (the reference rejects
+ * such blocks at decode time, gguf_decode.cpp:78, :92).  Synchronous.
+ * Replaces the MLX-affine import of GgufPackedBank::load_candidate
+ * (reference native/runtime/streaming/gguf_packed_bank.cpp:374-517). */
+int tc_cuda_weight_upload(tc_cuda_ctx *ctx, uint32_t ggml_type, uint64_t n, uint64_t k,
+                          const void *raw_host, uint64_t raw_bytes, uint64_t n_begin,
+                          uint64_t n_count, tc_cuda_weight **weight);
+
+/* As tc_cuda_weight_upload, but the raw rows are already in device memory
+ * (e.g. a staging slot filled by tc_cuda_stage_copy) and the re-layout is
+ * enqueued on `stream` without synchronising.  `weight` must have been
+ * created by tc_cuda_weight_create with the same type and shape. */
+int tc_cuda_weight_create(tc_cuda_ctx *ctx, uint32_t ggml_type, uint64_t n, uint64_t k,
+                          tc_cuda_weight **weight);
+int tc_cuda_weight_fill_device(tc_cuda_ctx *ctx, tc_cuda_weight *weight, const void *raw_device,
+                               uint64_t raw_bytes, void *stream);
+void tc_cuda_weight_free(tc_cuda_weight *weight);
+
+/* Shape queries of an uploaded weight. */
+int tc_cuda_weight_info(const tc_cuda_weight *weight, uint32_t *ggml_type, uint64_t *n,
+                        uint64_t *k, uint64_t *device_bytes);
+
+/* Dequantise an uploaded weight to a dense row-major [n, k] matrix with leading
+ * dimension `ld` elements, dtype TC_DTYPE_*.  Bit-exact to decode_cpu_into
+ * with the same target dtype (gguf_decode.cpp:433-445, write_value :112-116). */
+int tc_cuda_dequant(tc_cuda_ctx *ctx, const tc_cuda_weight *weight, int dtype, void *dst,
+                    uint64_t ld, void *stream);
+
+/* Device mirror of decode_cpu_into (gguf_decode.cpp:433-445 and the probe ABI
+ * tc_gguf_test_decode, gguf_core_probe.cpp:32-50): decode the slice
+ * [row_begin, +rows) x [column_begin, +columns) of a raw GGUF K-quant matrix
+ * in device memory into a strided device target (byte strides).  Geometry is
+ * validated on the host with the reference's rules and messages; value
+ * errors (nonfinite scale, fp16 overflow) are reported in the status word. */
+int tc_cuda_decode(tc_cuda_ctx *ctx, uint32_t ggml_type, const void *source, uint64_t source_bytes,
+                   uint64_t source_rows, uint64_t source_columns, uint64_t row_begin,
+                   uint64_t rows, uint64_t column_begin, uint64_t columns, int dtype,
+                   void *target, uint64_t target_bytes, uint64_t row_stride,
+                   uint64_t column_stride, void *stream);
+
+/* Quantised linear Y[M, N] = X[M, K] * W^T (fp32 accumulate) -- the operator
+ * behind Weights::project (reference native/backends/mlx.cpp:668-679).
+ *   X        bf16 [M, K] row-major, device; M = seg_offsets[n_seg].
+ *   Y        [M, N] row-major, device, dtype out_dtype (TC_DTYPE_BF16 or
+ *            TC_DTYPE_F32); row stride ldy elements (0 = N).
+ *   weights  n_weights uploaded weights with identical N, K;
+ *   seg_offsets  int32 [n_seg + 1] host array, 0 = seg_offsets[0] <= ... :
+ *            rows of X that belong to request segment s (ragged packing of
+ *            several requests along M);
+ *   seg_weight   int32 [n_seg] host array: which weight segment s uses (e.g.
+ *            image vs text stream);  NULL = weight 0 for every segment.
+ * Dispatch: the warp GEMV for segments with at most 16 rows, the tcgen05
+ * tensor-core GEMM otherwise.  `stage` selects the GEMM's operand precision
+ * (TC_STAGE_BF16 uses X as given; TC_STAGE_F16 converts X to fp16 first). */
+int tc_cuda_qlinear(tc_cuda_ctx *ctx, const tc_cuda_weight *const *weights, uint32_t n_weights,
+                    const int32_t *seg_offsets, const int32_t *seg_weight, uint32_t n_seg,
+                    const void *x, void *y, uint64_t ldy, int out_dtype, int stage, void *stream);
+
+/* Force one kernel family for a call (testing and benchmarking):
+ *   0 automatic, 1 warp GEMV (any M), 2 tensor-core GEMM (any M). */
+int tc_cuda_set_path(tc_cuda_ctx *ctx, int path);
+
+/* Host-side GGUF K-quant quantiser (not in the reference, which ships no
+ * encoder): quantise a row-major fp32 [rows, cols] matrix (cols % 256 == 0) to
+ * raw GGUF blocks of `ggml_type` (Q4_K or Q6_K) using `threads` CPU threads.
+ * Used to build synthetic weights; decode(quantise(W)) approximates W. */
+int tc_quantize(uint32_t ggml_type, const float *w, uint64_t rows, uint64_t cols, void *blocks,
+                uint64_t blocks_bytes, int threads);
+
+#ifdef __cplusplus
+}
+#endif
+#endif

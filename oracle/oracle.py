@@ -1,0 +1,181 @@
+"""TEST INFRASTRUCTURE ONLY: CPU checkers of the K-quant linear path.
+
+Only tests/, __graft_entry__.smoke() and bench.py's cpu_baseline / reference
+legs may import this module, and only as the checker or the timed CPU
+baseline; the product (turbocider_b200) never imports it.
+
+Two decoders are available:
+  * "port" -- libkqoracle.so, our C restatement of the reference decoder
+    (oracle/kq_oracle.c; reference native/core/gguf_decode.cpp);
+  * "ref"  -- _ref/libtcref.so, the reference's own decoder compiled from its
+    sources by oracle/Makefile (present wherever it was built; the GPU box
+    receives the built file).
+The GEMM oracle restates the reference's projection probe
+(tools/native/qwen21_gguf_import_probe.cpp:57-74: decode_cpu_into(f32) then an
+fp32 matmul) with an fp64 matmul so that only the kernel's own rounding shows.
+"""
+from __future__ import annotations
+
+import ctypes as C
+import os
+import subprocess
+from concurrent.futures import ThreadPoolExecutor
+from pathlib import Path
+
+import numpy as np
+
+HERE = Path(__file__).resolve().parent
+PORT_SO = HERE / "libkqoracle.so"
+REF_SO = HERE / "_ref" / "libtcref.so"
+BLOCK_BYTES = {12: 144, 13: 176, 14: 210}
+F32, F16, BF16 = 0, 1, 2
+
+_port = None
+_ref = None
+
+
+def build() -> None:
+    """Build the port (always) and the reference decoder (when its sources exist)."""
+    subprocess.run(["make", "-s", "-C", str(HERE)], check=True, capture_output=True)
+
+
+def port() -> C.CDLL:
+    global _port
+    if _port is None:
+        if not PORT_SO.exists():
+            build()
+        lib = C.CDLL(str(PORT_SO))
+        lib.kq_last_error.restype = C.c_char_p
+        lib.kq_half_to_float.argtypes = [C.c_uint16]
+        lib.kq_half_to_float.restype = C.c_float
+        lib.kq_float_to_bf16.argtypes = [C.c_float, C.POINTER(C.c_uint16)]
+        lib.kq_float_to_half.argtypes = [C.c_float, C.POINTER(C.c_uint16)]
+        lib.kq_decode.argtypes = [C.c_uint32, C.c_void_p] + [C.c_uint64] * 7 + [C.c_uint32, C.c_void_p] + [C.c_uint64] * 3
+        _port = lib
+    return _port
+
+
+def ref() -> C.CDLL | None:
+    """The reference decoder, or None when it was not built here."""
+    global _ref
+    if _ref is None and REF_SO.exists():
+        lib = C.CDLL(str(REF_SO))
+        lib.tc_gguf_test_error.restype = C.c_char_p
+        lib.tc_gguf_test_half.argtypes = [C.c_uint16]
+        lib.tc_gguf_test_half.restype = C.c_float
+        lib.tc_gguf_test_round.argtypes = [C.c_uint32, C.c_float, C.POINTER(C.c_uint16)]
+        lib.tc_gguf_test_decode.argtypes = ([C.c_uint32, C.c_void_p] + [C.c_uint64] * 7 + [C.c_uint32, C.c_void_p]
+                                            + [C.c_uint64] * 3 + [C.POINTER(C.c_uint64), C.c_uint64, C.c_int,
+                                                                   C.POINTER(C.c_uint64)])
+        _ref = lib
+    return _ref
+
+
+def _as_u8(raw) -> np.ndarray:
+    if isinstance(raw, (bytes, bytearray)):
+        return np.frombuffer(raw, dtype=np.uint8)
+    return np.ascontiguousarray(raw).view(np.uint8).reshape(-1)
+
+
+def decode(raw, ggml_type: int, rows: int, cols: int, dtype: int = F32, which: str = "port",
+           row_begin: int = 0, nrows: int | None = None, col_begin: int = 0, ncols: int | None = None):
+    """Decode a slice of a raw K-quant matrix.  Returns (status, array, error):
+    array is float32 (dtype F32) or uint16 bit patterns (F16/BF16), shape
+    [nrows, ncols]; on failure array is None and error holds the message."""
+    src = _as_u8(raw)
+    nrows = rows - row_begin if nrows is None else nrows
+    ncols = cols - col_begin if ncols is None else ncols
+    item = 4 if dtype == F32 else 2
+    out = np.zeros((max(nrows, 1), max(ncols, 1)), dtype=np.float32 if dtype == F32 else np.uint16)
+    args = (ggml_type, src.ctypes.data, src.nbytes, rows, cols, row_begin, nrows, col_begin, ncols, dtype,
+            out.ctypes.data, out.nbytes, ncols * item, item)
+    if which == "port":
+        lib = port()
+        rc = lib.kq_decode(*args)
+        err = lib.kq_last_error().decode()
+    else:
+        lib = ref()
+        if lib is None:
+            raise RuntimeError("reference decoder not built (oracle/_ref)")
+        stats = (C.c_uint64 * 4)()
+        rc = lib.tc_gguf_test_decode(*args, None, 0, 0, stats)
+        err = lib.tc_gguf_test_error().decode()
+    return rc, (out if rc == 0 else None), err
+
+
+def decode_checked(raw, ggml_type: int, rows: int, cols: int, dtype: int = F32, which: str = "port") -> np.ndarray:
+    rc, out, err = decode(raw, ggml_type, rows, cols, dtype, which)
+    if rc:
+        raise ValueError(err)
+    return out
+
+
+def decode_parallel(raw, ggml_type: int, rows: int, cols: int, dtype: int = F32, which: str = "ref",
+                    threads: int | None = None) -> np.ndarray:
+    """Row-split decode over host threads (as the reference's RowDecodePool,
+    native/runtime/streaming/gguf_packed_bank.cpp:48-100).  ctypes releases the
+    GIL during each call, so the threads run in parallel."""
+    src = _as_u8(raw)
+    threads = threads or os.cpu_count() or 1
+    item = 4 if dtype == F32 else 2
+    out = np.empty((rows, cols), dtype=np.float32 if dtype == F32 else np.uint16)
+    row_bytes = cols // 256 * BLOCK_BYTES[ggml_type]
+    step = (rows + threads - 1) // threads
+
+    def work(r0):
+        r1 = min(rows, r0 + step)
+        if r0 >= r1:
+            return 0
+        sub = src[r0 * row_bytes:r1 * row_bytes]
+        dst = out[r0:r1]
+        if which == "port":
+            return port().kq_decode(ggml_type, sub.ctypes.data, sub.nbytes, r1 - r0, cols, 0, r1 - r0, 0, cols,
+                                    dtype, dst.ctypes.data, dst.nbytes, cols * item, item)
+        stats = (C.c_uint64 * 4)()
+        return ref().tc_gguf_test_decode(ggml_type, sub.ctypes.data, sub.nbytes, r1 - r0, cols, 0, r1 - r0, 0,
+                                         cols, dtype, dst.ctypes.data, dst.nbytes, cols * item, item, None, 0, 0,
+                                         stats)
+
+    with ThreadPoolExecutor(threads) as pool:
+        codes = list(pool.map(work, range(0, rows, step)))
+    if any(codes):
+        raise ValueError("decode failed")
+    return out
+
+
+def bf16_bits_to_f32(bits: np.ndarray) -> np.ndarray:
+    return (np.asarray(bits, dtype=np.uint16).astype(np.uint32) << 16).view(np.float32)
+
+
+def f32_to_bf16_bits(x: np.ndarray) -> np.ndarray:
+    """Round-to-nearest-even fp32 -> bf16 bit patterns (finite inputs)."""
+    b = np.ascontiguousarray(x, dtype=np.float32).view(np.uint32)
+    return ((b + 0x7FFF + ((b >> 16) & 1)) >> 16).astype(np.uint16)
+
+
+def staged_weight(raw, ggml_type: int, n: int, k: int, staging: str, which: str = "port") -> np.ndarray:
+    """The weight as the kernel sees it: decode to the staging dtype
+    (bf16 / f16 / f32) and widen exactly to float64."""
+    if staging == "f32":
+        return decode_checked(raw, ggml_type, n, k, F32, which).astype(np.float64)
+    if staging == "bf16":
+        return bf16_bits_to_f32(decode_checked(raw, ggml_type, n, k, BF16, which)).astype(np.float64)
+    bits = decode_checked(raw, ggml_type, n, k, F16, which)
+    return bits.view(np.float16).astype(np.float64)
+
+
+def qlinear_ref(x_bf16_bits: np.ndarray, raw, ggml_type: int, n: int, k: int, staging: str = "f32",
+                which: str = "port") -> np.ndarray:
+    """fp64 oracle of Y = X * W^T.  X is given as bf16 bit patterns [M, K]; with
+    staging "f16" it is first rounded to fp16 (as the kernel's fp16 mode)."""
+    x = bf16_bits_to_f32(x_bf16_bits)
+    if staging == "f16":
+        x = x.astype(np.float16)
+    w = staged_weight(raw, ggml_type, n, k, staging, which)
+    return x.astype(np.float64) @ w.T
+
+
+def rel_l2(a, b) -> float:
+    a = np.asarray(a, dtype=np.float64)
+    b = np.asarray(b, dtype=np.float64)
+    return float(np.linalg.norm(a - b) / max(np.linalg.norm(b), 1e-300))

@@ -1,0 +1,155 @@
+"""GPU parity of the quantised linear (tc_cuda_qlinear) against the fp64
+oracle (reference decoder semantics + fp64 matmul).
+
+Tolerances (relative L2 over the whole output):
+  * fp32 output vs the oracle that stages W in the SAME dtype as the kernel
+    (bf16 by default, fp16 with TC_STAGE_F16):            <= 1e-4  (TIGHT)
+    -- only the kernel's fp32 accumulation order differs;
+  * warp GEMV (exact fp32 dequant) vs the fp32-decode oracle: <= 1e-5;
+  * fp16 staging vs the fp32-decode oracle:                  <= 1e-3  (north-star bar);
+  * bf16 staging vs the fp32-decode oracle:                  <= 3e-3  (bf16 W rounding
+    alone costs ~1.6e-3; reported);
+  * bf16 output vs the staged oracle:                        <= 3e-3  (bf16 output rounding).
+At the full config-5 sizes a sampled-row check is used (every row of the
+sample against the oracle), since the full fp64 oracle would take minutes.
+"""
+from __future__ import annotations
+
+import numpy as np
+import pytest
+
+import kq_cases
+from oracle import oracle
+
+pytestmark = pytest.mark.gpu
+
+TIGHT = 1e-4
+
+
+def _setup(ctx, typ, n, k, m, wseed=0, xseed=1):
+    import torch
+    from turbocider_b200 import cuda as tcc
+    raw = tcc.quantize(typ, kq_cases.synthetic_weight(n, k, seed=wseed))
+    weight = tcc.Weight.upload(ctx, typ, n, k, raw)
+    xb = kq_cases.synthetic_x_bf16(m, k, seed=xseed)
+    x = torch.from_numpy(xb.view(np.int16)).view(torch.bfloat16).cuda()
+    return raw, weight, xb, x
+
+
+def _run(ctx, weight, x, out_dtype, stage=0, path=0, seg=None, seg_w=None, weights=None):
+    from turbocider_b200 import cuda as tcc
+    ctx.set_path(path)
+    try:
+        y = tcc.qlinear(ctx, weights or weight, x, seg_offsets=seg, seg_weight=seg_w, out_dtype=out_dtype, stage=stage)
+    finally:
+        ctx.set_path(0)
+    assert ctx.status() == 0
+    return y.float().cpu().numpy().astype(np.float64)
+
+
+@pytest.mark.parametrize("typ", [12, 14])
+def test_gemm_config1_shape(ctx, typ):
+    """Config 1 (M=256, N=3072, K=3072) through the tcgen05 GEMM."""
+    from turbocider_b200 import cuda as tcc
+    n = k = 3072
+    raw, w, xb, x = _setup(ctx, typ, n, k, 256)
+    y = _run(ctx, w, x, tcc.F32)
+    e_staged = oracle.rel_l2(y, oracle.qlinear_ref(xb, raw, typ, n, k, "bf16"))
+    e_f32 = oracle.rel_l2(y, oracle.qlinear_ref(xb, raw, typ, n, k, "f32"))
+    print(f"type {typ}: rel-L2 vs bf16-staged oracle {e_staged:.2e}, vs f32-decode oracle {e_f32:.2e}")
+    assert e_staged <= TIGHT
+    assert e_f32 <= 3e-3
+    yb = _run(ctx, w, x, tcc.BF16)
+    assert oracle.rel_l2(yb, oracle.qlinear_ref(xb, raw, typ, n, k, "bf16")) <= 3e-3
+
+
+@pytest.mark.parametrize("typ", [12, 14])
+def test_gemm_fp16_staging_meets_1e3_vs_f32_decode(ctx, typ):
+    from turbocider_b200 import cuda as tcc
+    n, k, m = 1024, 2048, 384
+    raw, w, xb, x = _setup(ctx, typ, n, k, m, wseed=11)
+    y = _run(ctx, w, x, tcc.F32, stage=tcc.STAGE_F16)
+    assert oracle.rel_l2(y, oracle.qlinear_ref(xb, raw, typ, n, k, "f16")) <= TIGHT
+    e = oracle.rel_l2(y, oracle.qlinear_ref(xb, raw, typ, n, k, "f32"))
+    print(f"type {typ} fp16 staging vs f32 decode: {e:.2e}")
+    assert e <= 1e-3
+
+
+@pytest.mark.parametrize("typ", [12, 14])
+@pytest.mark.parametrize("m,n,k", [(17, 200, 512), (129, 384, 1024), (300, 256, 768), (64, 130, 256),
+                                   (1000, 640, 2560)])
+def test_gemm_ragged_edges(ctx, typ, m, n, k):
+    """M and N not multiples of the tile, every BN variant (64/128/256)."""
+    from turbocider_b200 import cuda as tcc
+    raw, w, xb, x = _setup(ctx, typ, n, k, m, wseed=m + n)
+    y = _run(ctx, w, x, tcc.F32, path=2)
+    assert oracle.rel_l2(y, oracle.qlinear_ref(xb, raw, typ, n, k, "bf16")) <= TIGHT
+
+
+@pytest.mark.parametrize("typ", [12, 14])
+@pytest.mark.parametrize("m", [1, 2, 3, 4, 16])
+def test_gemv_config2_shape(ctx, typ, m):
+    """Config 2 (K=12288, N=3072, M in {1..16}) through the warp GEMV."""
+    from turbocider_b200 import cuda as tcc
+    n, k = 3072, 12288
+    raw, w, xb, x = _setup(ctx, typ, n, k, m, wseed=2)
+    y = _run(ctx, w, x, tcc.F32)
+    assert oracle.rel_l2(y, oracle.qlinear_ref(xb, raw, typ, n, k, "f32")) <= 1e-5
+    yb = _run(ctx, w, x, tcc.BF16)
+    assert oracle.rel_l2(yb, oracle.qlinear_ref(xb, raw, typ, n, k, "f32")) <= 3e-3
+
+
+def test_forced_paths_agree(ctx):
+    """M=40 through the GEMV (forced) and through the GEMM."""
+    from turbocider_b200 import cuda as tcc
+    n, k, m = 512, 1024, 40
+    raw, w, xb, x = _setup(ctx, 12, n, k, m, wseed=4)
+    yv = _run(ctx, w, x, tcc.F32, path=1)
+    yg = _run(ctx, w, x, tcc.F32, path=2)
+    assert oracle.rel_l2(yv, oracle.qlinear_ref(xb, raw, 12, n, k, "f32")) <= 1e-5
+    assert oracle.rel_l2(yg, oracle.qlinear_ref(xb, raw, 12, n, k, "bf16")) <= TIGHT
+
+
+def test_ragged_segments_two_weights(ctx):
+    """Three request segments packed along M (image / text streams): two use
+    weight A, one uses weight B; the 3-row segment goes to the GEMV."""
+    import torch
+    from turbocider_b200 import cuda as tcc
+    n, k = 384, 1024
+    segs = [0, 512, 515, 772]
+    ra = tcc.quantize(12, kq_cases.synthetic_weight(n, k, seed=21))
+    rb = tcc.quantize(12, kq_cases.synthetic_weight(n, k, seed=22))
+    wa, wb = tcc.Weight.upload(ctx, 12, n, k, ra), tcc.Weight.upload(ctx, 12, n, k, rb)
+    xb = kq_cases.synthetic_x_bf16(segs[-1], k, seed=23)
+    x = torch.from_numpy(xb.view(np.int16)).view(torch.bfloat16).cuda()
+    y = _run(ctx, None, x, tcc.F32, seg=segs, seg_w=[0, 1, 0], weights=[wa, wb])
+    ya = oracle.qlinear_ref(xb, ra, 12, n, k, "bf16")
+    yb = oracle.qlinear_ref(xb, rb, 12, n, k, "bf16")
+    yf = oracle.qlinear_ref(xb, ra, 12, n, k, "f32")
+    assert oracle.rel_l2(y[0:512], ya[0:512]) <= TIGHT
+    assert oracle.rel_l2(y[512:515], oracle.qlinear_ref(xb[512:515], rb, 12, n, k, "f32")) <= 1e-5
+    assert oracle.rel_l2(y[515:772], ya[515:772]) <= TIGHT
+    assert oracle.rel_l2(y[0:512], yf[0:512]) <= 3e-3
+    del yb
+
+
+def test_empty_and_zero_segments(ctx):
+    import torch
+    from turbocider_b200 import cuda as tcc
+    raw, w, xb, x = _setup(ctx, 14, 256, 512, 130, wseed=8)
+    y = _run(ctx, w, x, tcc.F32, seg=[0, 0, 130, 130])
+    assert oracle.rel_l2(y, oracle.qlinear_ref(xb, raw, 14, 256, 512, "bf16")) <= TIGHT
+    with pytest.raises(tcc.BackendError, match="non-decreasing"):
+        tcc.qlinear(ctx, w, x, seg_offsets=[0, 100, 50])
+
+
+@pytest.mark.parametrize("typ,n,k", [(12, 10240, 3840), (14, 3840, 10240)])
+def test_full_size_config5_sampled_rows(ctx, typ, n, k):
+    """Config 5 sizes (M = 8448): every output column of 64 sampled rows."""
+    from turbocider_b200 import cuda as tcc
+    m = 8448
+    raw, w, xb, x = _setup(ctx, typ, n, k, m, wseed=31)
+    y = _run(ctx, w, x, tcc.F32)
+    rows = np.random.default_rng(0).choice(m, 64, replace=False)
+    ref = oracle.qlinear_ref(xb[rows], raw, typ, n, k, "bf16")
+    assert oracle.rel_l2(y[rows], ref) <= TIGHT

@@ -1,0 +1,68 @@
+"""In-tree build of the TurboCider CUDA backend: libturbocider_cuda.so.
+
+Compiles every source under csrc/ for sm_100a only (``-gencode
+arch=compute_100a,code=sm_100a``) with nvcc, in parallel, and links one
+shared library next to this file so that it travels with the repository.
+No JIT cache is used.  Run ``python -m turbocider_b200.build``.
+"""
+from __future__ import annotations
+
+import concurrent.futures as cf
+import os
+import shutil
+import subprocess
+import sys
+from pathlib import Path
+
+HERE = Path(__file__).resolve().parent
+CSRC = HERE / "csrc"
+OUT = HERE / "libturbocider_cuda.so"
+OBJ = HERE / "_build"
+ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
+COMMON = ["-std=c++17", "-O3", "-lineinfo", "-Xcompiler", "-fPIC", "-Xcompiler", "-Wall",
+          "--expt-relaxed-constexpr", "-I", str(HERE.parent / "include")]
+
+
+def nvcc() -> str:
+    path = shutil.which("nvcc") or "/usr/local/cuda/bin/nvcc"
+    if not Path(path).exists():
+        raise RuntimeError("nvcc not found: the CUDA backend cannot be built")
+    return path
+
+
+def sources() -> list[Path]:
+    return sorted(p for p in CSRC.iterdir() if p.suffix in (".cu", ".cpp"))
+
+
+def _compile(src: Path, verbose: bool) -> Path:
+    obj = OBJ / (src.stem + ".o")
+    deps = [src] + list(CSRC.glob("*.cuh")) + list(CSRC.glob("*.h")) + list((HERE.parent / "include").glob("*.h"))
+    if obj.exists() and obj.stat().st_mtime >= max(d.stat().st_mtime for d in deps):
+        return obj
+    cmd = [nvcc(), *ARCH, *COMMON, "-c", str(src), "-o", str(obj)]
+    if src.suffix == ".cu" and verbose:
+        cmd += ["-Xptxas", "-v"]
+    res = subprocess.run(cmd, capture_output=True, text=True)
+    if res.returncode != 0:
+        raise RuntimeError(f"nvcc failed on {src.name}:\n{res.stderr}")
+    if verbose and res.stderr:
+        print(res.stderr, file=sys.stderr)
+    return obj
+
+
+def build(verbose: bool = False) -> Path:
+    OBJ.mkdir(exist_ok=True)
+    srcs = sources()
+    with cf.ThreadPoolExecutor(max_workers=min(8, os.cpu_count() or 1)) as pool:
+        objs = list(pool.map(lambda s: _compile(s, verbose), srcs))
+    if OUT.exists() and OUT.stat().st_mtime >= max(o.stat().st_mtime for o in objs):
+        return OUT
+    cmd = [nvcc(), *ARCH, "-shared", "-o", str(OUT), *map(str, objs), "-lpthread"]
+    res = subprocess.run(cmd, capture_output=True, text=True)
+    if res.returncode != 0:
+        raise RuntimeError(f"link failed:\n{res.stderr}")
+    return OUT
+
+
+if __name__ == "__main__":
+    print(build(verbose="-v" in sys.argv))

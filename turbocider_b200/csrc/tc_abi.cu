@@ -1,0 +1,336 @@
+// C-ABI layer of the TurboCider CUDA backend (declared in
+// include/turbocider_cuda.h).  Validates arguments with the reference's
+// rules and messages, owns device buffers, and dispatches the kernels.
+// No exception crosses the boundary; errors are returned as status codes
+// with a thread-local message (as tests/native/gguf_core_probe.cpp:10-50 of
+// the reference does for its op-level probe ABI).
+#include <algorithm>
+#include <cstdio>
+#include <cstring>
+#include <new>
+#include <string>
+#include <vector>
+
+#include "../../include/turbocider_cuda.h"
+#include "kq_format.cuh"
+#include "tc_internal.h"
+
+namespace {
+
+thread_local std::string g_error;
+
+int fail(const std::string &reason) {
+    g_error = reason;
+    return TC_CUDA_FAIL;
+}
+int ok() {
+    g_error.clear();
+    return TC_CUDA_OK;
+}
+int cuda_fail(const char *what, cudaError_t e) {
+    return fail(std::string(what) + ": " + cudaGetErrorString(e));
+}
+
+// Runs a body with the context's device current, restoring the caller's.
+struct DeviceGuard {
+    int previous = -1;
+    explicit DeviceGuard(int device) {
+        if (cudaGetDevice(&previous) != cudaSuccess) previous = -1;
+        if (previous != device) cudaSetDevice(device);
+    }
+    ~DeviceGuard() {
+        int now = -1;
+        if (previous >= 0 && cudaGetDevice(&now) == cudaSuccess && now != previous) cudaSetDevice(previous);
+    }
+};
+
+bool supported_type(uint32_t type) { return type == TC_GGML_Q4_K || type == TC_GGML_Q6_K; }
+
+tc::WeightView view_of(const tc_cuda_weight *w) {
+    return {w->chunks, w->type, w->kb, w->panels, (uint32_t)w->n};
+}
+
+// Grows the context workspace (never shrinks; freed with the context).
+int ensure_workspace(tc_cuda_ctx *ctx, size_t bytes) {
+    if (ctx->workspace_bytes >= bytes) return TC_CUDA_OK;
+    if (ctx->workspace) cudaFree(ctx->workspace);
+    ctx->workspace = nullptr;
+    ctx->workspace_bytes = 0;
+    cudaError_t e = cudaMalloc(&ctx->workspace, bytes);
+    if (e != cudaSuccess) return cuda_fail("workspace allocation", e);
+    ctx->workspace_bytes = bytes;
+    return TC_CUDA_OK;
+}
+
+}  // namespace
+
+extern "C" {
+
+uint32_t tc_cuda_abi_version(void) { return TC_CUDA_ABI_VERSION; }
+
+const char *tc_cuda_last_error(void) { return g_error.c_str(); }
+
+int tc_cuda_init(int device, tc_cuda_ctx **out) {
+    if (!out) return fail("null context out-parameter");
+    *out = nullptr;
+    int count = 0;
+    cudaError_t e = cudaGetDeviceCount(&count);
+    if (e != cudaSuccess || count == 0) return fail("no CUDA device available (the TurboCider CUDA backend has no CPU fallback)");
+    if (device < 0 || device >= count) return fail("invalid CUDA device ordinal");
+    cudaDeviceProp prop{};
+    if ((e = cudaGetDeviceProperties(&prop, device)) != cudaSuccess) return cuda_fail("device query", e);
+    if (prop.major != 10) return fail("the TurboCider CUDA backend targets sm_100a (B200); found sm_" +
+                                      std::to_string(prop.major) + std::to_string(prop.minor));
+    DeviceGuard guard(device);
+    auto *ctx = new (std::nothrow) tc_cuda_ctx;
+    if (!ctx) return fail("out of host memory");
+    ctx->device = device;
+    ctx->sm_count = prop.multiProcessorCount;
+    if ((e = cudaMalloc(&ctx->status, 4 * sizeof(uint32_t))) != cudaSuccess) {
+        delete ctx;
+        return cuda_fail("status word allocation", e);
+    }
+    if ((e = cudaMemset(ctx->status, 0, 4 * sizeof(uint32_t))) != cudaSuccess) {
+        cudaFree(ctx->status);
+        delete ctx;
+        return cuda_fail("status word init", e);
+    }
+    *out = ctx;
+    return ok();
+}
+
+void tc_cuda_free(tc_cuda_ctx *ctx) {
+    if (!ctx) return;
+    DeviceGuard guard(ctx->device);
+    if (ctx->workspace) cudaFree(ctx->workspace);
+    if (ctx->status) cudaFree(ctx->status);
+    delete ctx;
+}
+
+int tc_cuda_status(tc_cuda_ctx *ctx, uint32_t *bits, int clear) {
+    if (!ctx || !bits) return fail("null context or out-parameter");
+    DeviceGuard guard(ctx->device);
+    cudaError_t e = cudaDeviceSynchronize();
+    if (e != cudaSuccess) return cuda_fail("device synchronise", e);
+    if ((e = cudaMemcpy(bits, ctx->status, sizeof(uint32_t), cudaMemcpyDeviceToHost)) != cudaSuccess)
+        return cuda_fail("status read", e);
+    if (clear && (e = cudaMemset(ctx->status, 0, sizeof(uint32_t))) != cudaSuccess) return cuda_fail("status clear", e);
+    return ok();
+}
+
+int tc_cuda_weight_create(tc_cuda_ctx *ctx, uint32_t type, uint64_t n, uint64_t k, tc_cuda_weight **out) {
+    if (!ctx || !out) return fail("null context or out-parameter");
+    *out = nullptr;
+    if (!supported_type(type)) return fail("gguf_decode: unsupported tensor type");
+    if (!n || !k || k % tc::kBlockWeights) return fail("invalid source geometry");
+    if (n > (1ull << 31) || k > (1ull << 31)) return fail("weight shape exceeds the 2^31 limit");
+    DeviceGuard guard(ctx->device);
+    auto *w = new (std::nothrow) tc_cuda_weight;
+    if (!w) return fail("out of host memory");
+    w->device = ctx->device;
+    w->type = type;
+    w->n = n;
+    w->k = k;
+    w->kb = (uint32_t)(k / tc::kBlockWeights);
+    w->panels = (uint32_t)((n + tc::kPanelRows - 1) / tc::kPanelRows);
+    w->bytes = (uint64_t)w->panels * w->kb * tc::chunk_bytes(type);
+    cudaError_t e = cudaMalloc(&w->chunks, w->bytes);
+    if (e != cudaSuccess) {
+        delete w;
+        return cuda_fail("weight allocation", e);
+    }
+    *out = w;
+    return ok();
+}
+
+int tc_cuda_weight_fill_device(tc_cuda_ctx *ctx, tc_cuda_weight *w, const void *raw, uint64_t raw_bytes,
+                               void *stream) {
+    if (!ctx || !w || !raw) return fail("null context, weight or source");
+    const uint64_t need = w->n * w->kb * tc::block_bytes(w->type);
+    if (raw_bytes < need) return fail("packed source too short");
+    DeviceGuard guard(ctx->device);
+    cudaError_t e = tc::launch_relayout(w->type, static_cast<const uint8_t *>(raw), w->n, w->kb, w->chunks, w->panels,
+                                        ctx->status, static_cast<cudaStream_t>(stream));
+    if (e != cudaSuccess) return cuda_fail("re-layout launch", e);
+    return ok();
+}
+
+int tc_cuda_weight_upload(tc_cuda_ctx *ctx, uint32_t type, uint64_t n, uint64_t k, const void *raw_host,
+                          uint64_t raw_bytes, uint64_t n_begin, uint64_t n_count, tc_cuda_weight **out) {
+    if (!ctx || !out || !raw_host) return fail("null context, source or out-parameter");
+    *out = nullptr;
+    if (!supported_type(type)) return fail("gguf_decode: unsupported tensor type");
+    if (!n || !k || k % tc::kBlockWeights) return fail("invalid source geometry");
+    if (n_count == 0) n_count = n - std::min(n_begin, n);
+    if (n_begin >= n || n_count > n - n_begin) return fail("row slice out of bounds");
+    const uint64_t row_bytes = k / tc::kBlockWeights * tc::block_bytes(type);
+    if (raw_bytes / row_bytes < n) return fail("packed source too short");
+    tc_cuda_weight *w = nullptr;
+    int rc = tc_cuda_weight_create(ctx, type, n_count, k, &w);
+    if (rc) return rc;
+    DeviceGuard guard(ctx->device);
+    void *staging = nullptr;
+    const uint64_t shard_bytes = n_count * row_bytes;
+    cudaError_t e = cudaMalloc(&staging, shard_bytes);
+    if (e == cudaSuccess)
+        e = cudaMemcpy(staging, static_cast<const uint8_t *>(raw_host) + n_begin * row_bytes, shard_bytes,
+                       cudaMemcpyHostToDevice);
+    if (e == cudaSuccess) e = cudaMemset(ctx->status + 1, 0, sizeof(uint32_t));
+    if (e == cudaSuccess)
+        e = tc::launch_relayout(type, static_cast<const uint8_t *>(staging), n_count, w->kb, w->chunks, w->panels,
+                                ctx->status + 1, nullptr);
+    uint32_t bits = 0;
+    if (e == cudaSuccess) e = cudaMemcpy(&bits, ctx->status + 1, sizeof(uint32_t), cudaMemcpyDeviceToHost);
+    if (staging) cudaFree(staging);
+    if (e != cudaSuccess) {
+        tc_cuda_weight_free(w);
+        return cuda_fail("weight upload", e);
+    }
+    if (bits & TC_STATUS_NONFINITE_SCALE) {
+        tc_cuda_weight_free(w);
+        return fail("nonfinite weight/scale or conversion overflow");
+    }
+    *out = w;
+    return ok();
+}
+
+void tc_cuda_weight_free(tc_cuda_weight *w) {
+    if (!w) return;
+    DeviceGuard guard(w->device);
+    if (w->chunks) cudaFree(w->chunks);
+    delete w;
+}
+
+int tc_cuda_weight_info(const tc_cuda_weight *w, uint32_t *type, uint64_t *n, uint64_t *k, uint64_t *bytes) {
+    if (!w) return fail("null weight");
+    if (type) *type = w->type;
+    if (n) *n = w->n;
+    if (k) *k = w->k;
+    if (bytes) *bytes = w->bytes;
+    return ok();
+}
+
+int tc_cuda_dequant(tc_cuda_ctx *ctx, const tc_cuda_weight *w, int dtype, void *dst, uint64_t ld, void *stream) {
+    if (!ctx || !w || !dst) return fail("null context, weight or target");
+    if (dtype < 0 || dtype > 2) return fail("gguf_decode: invalid target dtype");
+    if (ld < w->k) return fail("invalid/overlapping row stride");
+    DeviceGuard guard(ctx->device);
+    cudaError_t e = tc::launch_dequant_panel(view_of(w), dtype, dst, ld, ctx->status, static_cast<cudaStream_t>(stream));
+    if (e != cudaSuccess) return cuda_fail("dequant launch", e);
+    return ok();
+}
+
+// Geometry rules and messages of the reference's validate() and
+// decode_cpu_into() (native/core/gguf_decode.cpp:160-183, :433-438).
+int tc_cuda_decode(tc_cuda_ctx *ctx, uint32_t type, const void *source, uint64_t source_bytes, uint64_t source_rows,
+                   uint64_t source_columns, uint64_t row_begin, uint64_t rows, uint64_t column_begin,
+                   uint64_t columns, int dtype, void *target, uint64_t target_bytes, uint64_t row_stride,
+                   uint64_t column_stride, void *stream) {
+    if (!ctx) return fail("null context");
+    if (row_begin > source_rows || rows > source_rows - row_begin) return fail("row slice out of bounds");
+    if (!supported_type(type)) return fail("gguf_decode: unsupported tensor type");
+    if (!source || !target) return fail("null source/target storage");
+    if (!source_rows || !source_columns || source_columns % tc::kBlockWeights) return fail("invalid source geometry");
+    if (!rows || !columns || column_begin > source_columns || columns > source_columns - column_begin)
+        return fail("invalid decode slice");
+    const uint64_t row_bytes = source_columns / tc::kBlockWeights * tc::block_bytes(type);
+    if (source_rows > UINT64_MAX / row_bytes) return fail("gguf_decode: multiplication overflow");
+    if (source_rows * row_bytes > source_bytes) return fail("packed source too short");
+    if (dtype < 0 || dtype > 2) return fail("gguf_decode: invalid target dtype");
+    const uint64_t item = dtype == TC_DTYPE_F32 ? 4 : 2;
+    if (column_stride < item) return fail("invalid/overlapping column stride");
+    if (columns - 1 > (UINT64_MAX - item) / column_stride) return fail("gguf_decode: multiplication overflow");
+    const uint64_t row_extent = (columns - 1) * column_stride + item;
+    if (row_stride < row_extent) return fail("invalid/overlapping row stride");
+    if (rows - 1 > (UINT64_MAX - row_extent) / row_stride) return fail("gguf_decode: multiplication overflow");
+    const uint64_t extent = (rows - 1) * row_stride + row_extent;
+    if (extent > target_bytes) return fail("decode target too short");
+    const uintptr_t s0 = reinterpret_cast<uintptr_t>(source), t0 = reinterpret_cast<uintptr_t>(target);
+    const uint64_t source_extent = source_rows * row_bytes;
+    if (!(s0 + source_extent <= t0 || t0 + extent <= s0)) return fail("packed source overlaps target");
+    DeviceGuard guard(ctx->device);
+    cudaError_t e = tc::launch_decode_raw(type, static_cast<const uint8_t *>(source), row_bytes, row_begin, rows,
+                                          column_begin, columns, dtype, static_cast<uint8_t *>(target), row_stride,
+                                          column_stride, ctx->status, static_cast<cudaStream_t>(stream));
+    if (e != cudaSuccess) return cuda_fail("decode launch", e);
+    return ok();
+}
+
+int tc_cuda_set_path(tc_cuda_ctx *ctx, int path) {
+    if (!ctx) return fail("null context");
+    if (path < 0 || path > 2) return fail("invalid path selector");
+    ctx->path = path;
+    return ok();
+}
+
+int tc_cuda_qlinear(tc_cuda_ctx *ctx, const tc_cuda_weight *const *weights, uint32_t n_weights,
+                    const int32_t *seg_offsets, const int32_t *seg_weight, uint32_t n_seg, const void *x, void *y,
+                    uint64_t ldy, int out_dtype, int stage, void *stream) {
+    if (!ctx || !weights || !n_weights || !x || !y || !seg_offsets) return fail("null argument");
+    if (!n_seg) return fail("no segments");
+    if (out_dtype != TC_DTYPE_F32 && out_dtype != TC_DTYPE_BF16) return fail("output dtype must be f32 or bf16");
+    if (stage != TC_STAGE_BF16 && stage != TC_STAGE_F16) return fail("invalid staging precision");
+    const tc_cuda_weight *w0 = weights[0];
+    if (!w0) return fail("null weight");
+    for (uint32_t i = 0; i < n_weights; ++i) {
+        if (!weights[i]) return fail("null weight");
+        if (weights[i]->n != w0->n || weights[i]->k != w0->k) return fail("weights of one call must share N and K");
+        if (weights[i]->device != ctx->device) return fail("weight lives on another device");
+    }
+    if (ldy == 0) ldy = w0->n;
+    if (ldy < w0->n) return fail("invalid/overlapping row stride");
+    if (seg_offsets[0] != 0) return fail("seg_offsets[0] must be 0");
+    for (uint32_t s = 0; s < n_seg; ++s) {
+        if (seg_offsets[s + 1] < seg_offsets[s]) return fail("seg_offsets must be non-decreasing");
+        if (seg_weight && (seg_weight[s] < 0 || (uint32_t)seg_weight[s] >= n_weights))
+            return fail("seg_weight out of range");
+    }
+    if (reinterpret_cast<uintptr_t>(x) % 16) return fail("X must be 16-byte aligned");
+    const uint64_t m_total = (uint64_t)seg_offsets[n_seg];
+    if (!m_total) return ok();
+    DeviceGuard guard(ctx->device);
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+    const uint64_t k = w0->k;
+
+    // Split segments: small ones to the GEMV, the rest to the tensor-core GEMM
+    // (one launch per weight type).
+    std::vector<tc::SegmentView> gemm[2];
+    std::vector<tc::SegmentView> gemv;
+    for (uint32_t i = 0; i < n_seg; ++i) {
+        const uint32_t b = (uint32_t)seg_offsets[i], e = (uint32_t)seg_offsets[i + 1];
+        if (b == e) continue;
+        const tc_cuda_weight *w = weights[seg_weight ? seg_weight[i] : 0];
+        const tc::SegmentView sv{b, e, view_of(w)};
+        const bool small = (e - b) <= 16;
+        if ((small && ctx->path != 2) || ctx->path == 1) {
+            // The GEMV handles at most 16 rows per launch; longer forced
+            // segments are cut into 16-row pieces.
+            for (uint32_t m = b; m < e; m += 16) gemv.push_back({m, std::min(e, m + 16), sv.w});
+        } else {
+            gemm[w->type == TC_GGML_Q4_K ? 0 : 1].push_back(sv);
+        }
+    }
+    const uint16_t *xg = static_cast<const uint16_t *>(x);
+    if (stage == TC_STAGE_F16 && (!gemm[0].empty() || !gemm[1].empty())) {
+        int rc = ensure_workspace(ctx, m_total * k * 2);
+        if (rc) return rc;
+        cudaError_t e = tc::launch_x_to_f16(xg, static_cast<uint16_t *>(ctx->workspace), m_total * k, ctx->status, s);
+        if (e != cudaSuccess) return cuda_fail("fp16 staging launch", e);
+        xg = static_cast<const uint16_t *>(ctx->workspace);
+    }
+    for (int t = 0; t < 2; ++t) {
+        for (size_t i = 0; i < gemm[t].size(); i += 32) {
+            const uint32_t cnt = (uint32_t)std::min<size_t>(32, gemm[t].size() - i);
+            cudaError_t e = tc::launch_gemm(gemm[t].data() + i, cnt, xg, m_total, k, y, ldy, out_dtype,
+                                            stage == TC_STAGE_F16, ctx->sm_count, ctx->status, s);
+            if (e != cudaSuccess) return cuda_fail("GEMM launch", e);
+        }
+    }
+    for (const auto &sv : gemv) {
+        cudaError_t e = tc::launch_gemv(sv, static_cast<const uint16_t *>(x), k, y, ldy, out_dtype, ctx->status, s);
+        if (e != cudaSuccess) return cuda_fail("GEMV launch", e);
+    }
+    return ok();
+}
+
+}  // extern "C"

@@ -1,0 +1,58 @@
+// Internal host-side declarations shared by the C-ABI layer and the kernel
+// launchers.  Nothing here crosses the public ABI.
+#pragma once
+#include <cstdint>
+#include <cuda_runtime.h>
+
+struct tc_cuda_ctx {
+    int device = 0;
+    int sm_count = 0;
+    uint32_t *status = nullptr;      // device status word (TC_STATUS_* bits)
+    void *workspace = nullptr;       // grows on demand: fp16 copy of X, split-K partials
+    size_t workspace_bytes = 0;
+    int path = 0;                    // 0 auto, 1 GEMV, 2 GEMM
+};
+
+struct tc_cuda_weight {
+    int device = 0;
+    uint32_t type = 0;               // 12 = Q4_K, 14 = Q6_K
+    uint64_t n = 0, k = 0;
+    uint32_t kb = 0;                 // super-blocks per row, K / 256
+    uint32_t panels = 0;             // ceil(N / 128)
+    uint8_t *chunks = nullptr;       // panel layout, panels * kb chunks
+    uint64_t bytes = 0;
+};
+
+namespace tc {
+
+// Geometry handed to the kernels for one weight.
+struct WeightView {
+    const uint8_t *chunks;
+    uint32_t type, kb, panels;
+    uint32_t n;
+};
+
+// One ragged request segment of a quantised linear.
+struct SegmentView {
+    uint32_t m_begin, m_end;         // rows of X / Y
+    WeightView w;
+};
+
+cudaError_t launch_relayout(uint32_t type, const uint8_t *raw, uint64_t n, uint32_t kb,
+                            uint8_t *chunks, uint32_t panels, uint32_t *status, cudaStream_t s);
+cudaError_t launch_dequant_panel(const WeightView &w, int dtype, void *dst, uint64_t ld,
+                                 uint32_t *status, cudaStream_t s);
+cudaError_t launch_decode_raw(uint32_t type, const uint8_t *src, uint64_t row_bytes,
+                              uint64_t row_begin, uint64_t rows, uint64_t column_begin,
+                              uint64_t columns, int dtype, uint8_t *dst, uint64_t row_stride,
+                              uint64_t column_stride, uint32_t *status, cudaStream_t s);
+cudaError_t launch_gemv(const SegmentView &seg, const uint16_t *x, uint64_t k, void *y,
+                        uint64_t ldy, int out_dtype, uint32_t *status, cudaStream_t s);
+cudaError_t launch_x_to_f16(const uint16_t *x, uint16_t *x16, uint64_t count, uint32_t *status,
+                            cudaStream_t s);
+// Tensor-core GEMM over a list of segments that share type, N and K.
+cudaError_t launch_gemm(const SegmentView *segs, uint32_t n_seg, const uint16_t *x,
+                        uint64_t m_total, uint64_t k, void *y, uint64_t ldy, int out_dtype,
+                        int stage_f16, int sm_count, uint32_t *status, cudaStream_t s);
+
+}  // namespace tc

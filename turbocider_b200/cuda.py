@@ -1,0 +1,228 @@
+"""ctypes binding of libturbocider_cuda.so (include/turbocider_cuda.h).
+
+This is the Python face of the C ABI, in the style of the reference's own
+ctypes-driven op tests (tests/native/test_gguf_execution.py:67-85).  Device
+buffers are torch tensors (PyTorch is used for device memory and streams
+only); every computation runs in the CUDA library.  There is no CPU
+fallback: loading fails loudly when the library is missing.
+"""
+from __future__ import annotations
+
+import ctypes as C
+import os
+from pathlib import Path
+
+import numpy as np
+
+LIB_PATH = Path(__file__).resolve().parent / "libturbocider_cuda.so"
+
+Q4_K, Q5_K, Q6_K = 12, 13, 14
+F32, F16, BF16 = 0, 1, 2
+STAGE_BF16, STAGE_F16 = 0, 1
+STATUS_NONFINITE_SCALE, STATUS_F16_OVERFLOW, STATUS_TIMEOUT, STATUS_GEOMETRY = 1, 2, 4, 8
+BLOCK_BYTES = {Q4_K: 144, Q6_K: 210}
+
+_lib = None
+
+
+class BackendError(RuntimeError):
+    """A failed C-ABI call (status 1); the message is tc_cuda_last_error()."""
+
+
+class DecodeError(BackendError):
+    """Mirror of tc::gguf::DecodeError (reference native/core/gguf_decode.hpp:10-16)."""
+
+
+_vp, _u32, _u64, _i32 = C.c_void_p, C.c_uint32, C.c_uint64, C.c_int32
+
+EXPORTS = {
+    # name: (restype, argtypes)
+    "tc_cuda_abi_version": (_u32, []),
+    "tc_cuda_last_error": (C.c_char_p, []),
+    "tc_cuda_init": (C.c_int, [C.c_int, C.POINTER(_vp)]),
+    "tc_cuda_free": (None, [_vp]),
+    "tc_cuda_status": (C.c_int, [_vp, C.POINTER(_u32), C.c_int]),
+    "tc_cuda_weight_upload": (C.c_int, [_vp, _u32, _u64, _u64, _vp, _u64, _u64, _u64, C.POINTER(_vp)]),
+    "tc_cuda_weight_create": (C.c_int, [_vp, _u32, _u64, _u64, C.POINTER(_vp)]),
+    "tc_cuda_weight_fill_device": (C.c_int, [_vp, _vp, _vp, _u64, _vp]),
+    "tc_cuda_weight_free": (None, [_vp]),
+    "tc_cuda_weight_info": (C.c_int, [_vp, C.POINTER(_u32), C.POINTER(_u64), C.POINTER(_u64), C.POINTER(_u64)]),
+    "tc_cuda_dequant": (C.c_int, [_vp, _vp, C.c_int, _vp, _u64, _vp]),
+    "tc_cuda_decode": (C.c_int, [_vp, _u32, _vp, _u64, _u64, _u64, _u64, _u64, _u64, _u64, C.c_int, _vp, _u64,
+                                 _u64, _u64, _vp]),
+    "tc_cuda_qlinear": (C.c_int, [_vp, C.POINTER(_vp), _u32, C.POINTER(_i32), C.POINTER(_i32), _u32, _vp, _vp,
+                                  _u64, C.c_int, C.c_int, _vp]),
+    "tc_cuda_set_path": (C.c_int, [_vp, C.c_int]),
+    "tc_quantize": (C.c_int, [_u32, _vp, _u64, _u64, _vp, _u64, C.c_int]),
+}
+
+
+def lib() -> C.CDLL:
+    """Load the backend library (built in-tree by turbocider_b200.build)."""
+    global _lib
+    if _lib is None:
+        if not LIB_PATH.exists():
+            raise ImportError(f"{LIB_PATH} is missing: run `python -m turbocider_b200.build` "
+                              "(the CUDA backend has no CPU fallback)")
+        handle = C.CDLL(str(LIB_PATH))
+        for name, (res, args) in EXPORTS.items():
+            fn = getattr(handle, name)
+            fn.restype = res
+            fn.argtypes = args
+        _lib = handle
+    return _lib
+
+
+def _check(rc: int, cls=BackendError):
+    if rc != 0:
+        raise cls(lib().tc_cuda_last_error().decode())
+
+
+def _stream_ptr(stream) -> int | None:
+    if stream is None:
+        import torch
+        return torch.cuda.current_stream().cuda_stream
+    return getattr(stream, "cuda_stream", stream)
+
+
+def quantize(ggml_type: int, w: np.ndarray, threads: int | None = None) -> np.ndarray:
+    """Quantise a fp32 [rows, cols] matrix to raw GGUF blocks (uint8 array)."""
+    w = np.ascontiguousarray(w, dtype=np.float32)
+    rows, cols = w.shape
+    out = np.empty(rows * (cols // 256) * BLOCK_BYTES[ggml_type], dtype=np.uint8)
+    rc = lib().tc_quantize(ggml_type, w.ctypes.data, rows, cols, out.ctypes.data, out.nbytes,
+                           threads or os.cpu_count() or 1)
+    if rc != 0:
+        raise BackendError("tc_quantize rejected the input (type, shape or nonfinite values)")
+    return out
+
+
+class Context:
+    """A device context: status word and workspace on one GPU."""
+
+    def __init__(self, device: int = 0):
+        self._h = _vp()
+        _check(lib().tc_cuda_init(device, C.byref(self._h)))
+        self.device = device
+
+    @property
+    def handle(self):
+        return self._h
+
+    def status(self, clear: bool = True) -> int:
+        bits = _u32()
+        _check(lib().tc_cuda_status(self._h, C.byref(bits), int(clear)))
+        return bits.value
+
+    def set_path(self, path: int):
+        _check(lib().tc_cuda_set_path(self._h, path))
+
+    def close(self):
+        if self._h:
+            lib().tc_cuda_free(self._h)
+            self._h = _vp()
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+
+class Weight:
+    """A K-quant weight resident in HBM (panel layout)."""
+
+    def __init__(self, ctx: Context, handle):
+        self.ctx, self._h = ctx, handle
+        t, n, k, b = _u32(), _u64(), _u64(), _u64()
+        _check(lib().tc_cuda_weight_info(handle, C.byref(t), C.byref(n), C.byref(k), C.byref(b)))
+        self.ggml_type, self.n, self.k, self.device_bytes = t.value, n.value, k.value, b.value
+
+    @classmethod
+    def upload(cls, ctx: Context, ggml_type: int, n: int, k: int, raw, n_begin: int = 0, n_count: int = 0):
+        raw = np.ascontiguousarray(np.frombuffer(raw, dtype=np.uint8) if isinstance(raw, (bytes, bytearray))
+                                   else raw).view(np.uint8).reshape(-1)
+        h = _vp()
+        _check(lib().tc_cuda_weight_upload(ctx.handle, ggml_type, n, k, raw.ctypes.data, raw.nbytes, n_begin,
+                                           n_count, C.byref(h)), DecodeError)
+        return cls(ctx, h)
+
+    @classmethod
+    def create(cls, ctx: Context, ggml_type: int, n: int, k: int):
+        h = _vp()
+        _check(lib().tc_cuda_weight_create(ctx.handle, ggml_type, n, k, C.byref(h)))
+        return cls(ctx, h)
+
+    def fill_device(self, raw_device, stream=None):
+        """Re-layout raw GGUF rows already in device memory (torch uint8 tensor)."""
+        _check(lib().tc_cuda_weight_fill_device(self.ctx.handle, self._h, raw_device.data_ptr(),
+                                                raw_device.numel(), _stream_ptr(stream)))
+
+    @property
+    def handle(self):
+        return self._h
+
+    def free(self):
+        if self._h:
+            lib().tc_cuda_weight_free(self._h)
+            self._h = _vp()
+
+    def __del__(self):
+        try:
+            self.free()
+        except Exception:
+            pass
+
+
+def dequant(ctx: Context, w: Weight, dtype: int = BF16, out=None, stream=None):
+    """Dequantise an uploaded weight into a dense torch tensor [n, k]."""
+    import torch
+    tdt = {F32: torch.float32, F16: torch.float16, BF16: torch.bfloat16}[dtype]
+    if out is None:
+        out = torch.empty((w.n, w.k), dtype=tdt, device=f"cuda:{ctx.device}")
+    _check(lib().tc_cuda_dequant(ctx.handle, w.handle, dtype, out.data_ptr(), out.stride(0), _stream_ptr(stream)))
+    return out
+
+
+def decode(ctx: Context, ggml_type: int, source, source_rows: int, source_columns: int, row_begin: int, rows: int,
+           column_begin: int, columns: int, dtype: int, target, row_stride: int, column_stride: int,
+           stream=None, check: bool = True):
+    """Device mirror of decode_cpu_into on raw GGUF bytes (torch uint8 tensors).
+
+    Raises DecodeError with the reference's message for geometry errors, and
+    (when check=True, which synchronises) for nonfinite scales / fp16
+    overflow detected by the kernel.
+    """
+    _check(lib().tc_cuda_decode(ctx.handle, ggml_type, source.data_ptr(), source.numel() * source.element_size(),
+                                source_rows, source_columns, row_begin, rows, column_begin, columns, dtype,
+                                target.data_ptr(), target.numel() * target.element_size(), row_stride,
+                                column_stride, _stream_ptr(stream)), DecodeError)
+    if check:
+        bits = ctx.status(clear=True)
+        if bits & STATUS_NONFINITE_SCALE:
+            raise DecodeError("nonfinite weight/scale or conversion overflow")
+        if bits & STATUS_F16_OVERFLOW:
+            raise DecodeError("FP16 conversion overflow")
+
+
+def qlinear(ctx: Context, weights, x, seg_offsets=None, seg_weight=None, out_dtype: int = BF16,
+            stage: int = STAGE_BF16, out=None, stream=None):
+    """Y = X * W^T through tc_cuda_qlinear.  `weights` is a Weight or a list of
+    them; seg_offsets / seg_weight describe ragged request segments along M."""
+    import torch
+    ws = weights if isinstance(weights, (list, tuple)) else [weights]
+    m = x.shape[0]
+    if seg_offsets is None:
+        seg_offsets = [0, m]
+    seg_offsets = list(seg_offsets)
+    n_seg = len(seg_offsets) - 1
+    offs = (_i32 * len(seg_offsets))(*seg_offsets)
+    sw = (_i32 * n_seg)(*seg_weight) if seg_weight is not None else None
+    handles = (_vp * len(ws))(*[w.handle for w in ws])
+    n = ws[0].n
+    if out is None:
+        out = torch.empty((m, n), dtype=torch.float32 if out_dtype == F32 else torch.bfloat16,
+                          device=x.device)
+    _check(lib().tc_cuda_qlinear(ctx.handle, handles, len(ws), offs, sw, n_seg, x.data_ptr(), out.data_ptr(),
+                                 out.stride(0), out_dtype, stage, _stream_ptr(stream)))
+    return out
