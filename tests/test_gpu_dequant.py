@@ -72,7 +72,7 @@ def test_decode_slices_and_strides_bit_exact(ctx, golden):
 
 def test_decode_pattern_extreme_nonfinite(ctx, golden):
     c = golden["cases"]
-    for typ in (12, 14):
+    for typ in kq_cases.K_TYPES:
         for rows in (1, 3, 17):
             for cols in (256, 512, 1024):
                 raw = kq_cases.pattern_case(typ, rows, cols)
@@ -85,8 +85,6 @@ def test_decode_pattern_extreme_nonfinite(ctx, golden):
     for key, expect in c["nonfinite"].items():
         typ, where, bits = key.split("/")
         typ, bits = int(typ), int(bits, 16)
-        if typ == 13:
-            continue
         raw = bytearray(kq_cases.extreme_case(typ, 1.0))
         off = 208 if typ == 14 else (0 if where == "d" else 2)
         raw[off:off + 2] = bits.to_bytes(2, "little")

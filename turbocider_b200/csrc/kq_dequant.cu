@@ -78,7 +78,7 @@ __device__ __forceinline__ void store_value(uint8_t *p, float v, bool &ovf) {
 // Decode the 32 weights of group G (0..7) of one super-block whose fields are
 // reached through the accessor.  Q4_K group G = sub-block G; Q6_K group
 // G = 4h + g covers weights 128h + 32g + j.
-struct Q4Fields { const uint8_t *qs32; const uint8_t *sc12; uint16_t d, dmin; };
+struct Q4Fields { const uint8_t *qs32; const uint8_t *sc12; uint16_t d, dmin; const uint8_t *qh32 = nullptr; };
 struct Q6Fields { const uint8_t *ql32; const uint8_t *qh32; const uint8_t *sc16; uint16_t d; };
 
 __device__ __forceinline__ void q4k_group(const Q4Fields &f, uint32_t g, float out[32], bool &bad) {
@@ -88,6 +88,12 @@ __device__ __forceinline__ void q4k_group(const Q4Fields &f, uint32_t g, float o
     q4k_scale_min(g, f.sc12, sc, mn);
     const float dg = d * (float)sc, mg = dmin * (float)mn;
     const uint32_t shift = (g & 1) * 4;
+    if (f.qh32) {  // Q5_K: fifth bit of weight j of sub-block g is bit g of qh[j] (gguf_decode.cpp:87)
+#pragma unroll
+        for (int j = 0; j < 32; ++j)
+            out[j] = q4k_value(dg, mg, ((f.qs32[j] >> shift) & 15u) | (((f.qh32[j] >> g) & 1u) << 4));
+        return;
+    }
 #pragma unroll
     for (int j = 0; j < 32; ++j) out[j] = q4k_value(dg, mg, (f.qs32[j] >> shift) & 15u);
 }
@@ -160,6 +166,9 @@ __global__ void decode_raw_kernel(uint32_t type, const uint8_t *__restrict__ src
     bool bad = false, ovf = false;
     if (type == 12) {
         Q4Fields f{p + 16 + (G / 2) * 32, p + 4, ld16(p), ld16(p + 2)};
+        q4k_group(f, G, v, bad);
+    } else if (type == 13) {
+        Q4Fields f{p + 48 + (G / 2) * 32, p + 4, ld16(p), ld16(p + 2), p + 16};
         q4k_group(f, G, v, bad);
     } else {
         const uint32_t h = G / 4, g = G % 4;

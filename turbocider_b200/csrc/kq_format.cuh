@@ -53,7 +53,7 @@ constexpr uint32_t kQ4Qs = 0, kQ4Sc = 16384, kQ4Dm = 17920;
 constexpr uint32_t kQ6Ql = 0, kQ6Qh = 16384, kQ6Sc = 24576, kQ6D = 26624;
 
 __host__ __device__ constexpr uint32_t block_bytes(uint32_t type) {
-    return type == 12 ? kQ4KBytes : type == 14 ? kQ6KBytes : 0u;
+    return type == 12 ? kQ4KBytes : type == 14 ? kQ6KBytes : type == 13 ? 176u : 0u;
 }
 __host__ __device__ constexpr uint32_t chunk_bytes(uint32_t type) {
     return type == 12 ? kQ4KChunk : type == 14 ? kQ6KChunk : 0u;

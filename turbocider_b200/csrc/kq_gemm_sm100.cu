@@ -339,6 +339,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             for (int i = 0; i < kWStages; ++i)
                 if (w_used[i]) bar_wait(w_full(i), w_last[i], abort_flag, p.status, false);
         }
+        __syncwarp();
     } else if (warp == 1) {
         // ---------------------------------------------------- MMA issuer
         if (lane == 0) {

@@ -228,7 +228,7 @@ int tc_cuda_decode(tc_cuda_ctx *ctx, uint32_t type, const void *source, uint64_t
                    uint64_t column_stride, void *stream) {
     if (!ctx) return fail("null context");
     if (row_begin > source_rows || rows > source_rows - row_begin) return fail("row slice out of bounds");
-    if (!supported_type(type)) return fail("gguf_decode: unsupported tensor type");
+    if (!supported_type(type) && type != TC_GGML_Q5_K) return fail("gguf_decode: unsupported tensor type");
     if (!source || !target) return fail("null source/target storage");
     if (!source_rows || !source_columns || source_columns % tc::kBlockWeights) return fail("invalid source geometry");
     if (!rows || !columns || column_begin > source_columns || columns > source_columns - column_begin)
