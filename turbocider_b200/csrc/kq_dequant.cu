@@ -35,7 +35,7 @@ __global__ void relayout_kernel(uint32_t type, const uint8_t *__restrict__ raw, 
     if (type == 12) {
         // qs quarters: 4 x 32 bytes
         for (uint32_t s = 0; s < 4; ++s) {
-            uint8_t *dst = chunk + kQ4Qs + s * 4096 + r * 32;
+            uint8_t *dst = chunk + kQ4Qs + s * 4096 + row_slot(r) * 32;
             for (uint32_t i = 0; i < 32; i += 4) {
                 uint32_t v = 0;
                 if (blk) v = blk[16 + 32 * s + i] | (blk[17 + 32 * s + i] << 8) |
@@ -52,11 +52,11 @@ __global__ void relayout_kernel(uint32_t type, const uint8_t *__restrict__ raw, 
         // ql: [h][part][row][32]
         for (uint32_t h = 0; h < 2; ++h)
             for (uint32_t part = 0; part < 2; ++part) {
-                uint8_t *dst = chunk + kQ6Ql + ((h * 2 + part) * kPanelRows + r) * 32;
+                uint8_t *dst = chunk + kQ6Ql + ((h * 2 + part) * kPanelRows + row_slot(r)) * 32;
                 for (uint32_t i = 0; i < 32; ++i) dst[i] = blk ? blk[64 * h + 32 * part + i] : 0;
             }
         for (uint32_t h = 0; h < 2; ++h) {
-            uint8_t *dst = chunk + kQ6Qh + (h * kPanelRows + r) * 32;
+            uint8_t *dst = chunk + kQ6Qh + (h * kPanelRows + row_slot(r)) * 32;
             for (uint32_t i = 0; i < 32; ++i) dst[i] = blk ? blk[128 + 32 * h + i] : 0;
         }
         uint8_t *sc = chunk + kQ6Sc + r * 16;
@@ -128,13 +128,13 @@ __global__ void dequant_panel_kernel(WeightView w, uint8_t *__restrict__ dst, ui
     bool bad = false, ovf = false;
     if (w.type == 12) {
         const uint32_t dm = *reinterpret_cast<const uint32_t *>(chunk + kQ4Dm + r * 4);
-        Q4Fields f{chunk + kQ4Qs + (G / 2) * 4096 + r * 32, chunk + kQ4Sc + r * 12,
+        Q4Fields f{chunk + kQ4Qs + (G / 2) * 4096 + row_slot(r) * 32, chunk + kQ4Sc + r * 12,
                    (uint16_t)(dm & 0xffffu), (uint16_t)(dm >> 16)};
         q4k_group(f, G, v, bad);
     } else {
         const uint32_t h = G / 4, g = G % 4;
-        Q6Fields f{chunk + kQ6Ql + ((h * 2 + (g & 1)) * kPanelRows + r) * 32,
-                   chunk + kQ6Qh + (h * kPanelRows + r) * 32, chunk + kQ6Sc + r * 16,
+        Q6Fields f{chunk + kQ6Ql + ((h * 2 + (g & 1)) * kPanelRows + row_slot(r)) * 32,
+                   chunk + kQ6Qh + (h * kPanelRows + row_slot(r)) * 32, chunk + kQ6Sc + r * 16,
                    *reinterpret_cast<const uint16_t *>(chunk + kQ6D + r * 2)};
         q6k_group(f, h, g, v, bad);
     }

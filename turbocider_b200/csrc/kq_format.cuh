@@ -34,6 +34,10 @@
 //     sc  [128 rows][16 B]                    @24576
 //     d   [128 rows] fp16                     @26624
 // Rows past N in the last panel are zero blocks (d = 0: every weight is 0).
+// The per-row 32-byte pieces of qs / ql / qh are stored at row_slot(r), a
+// permutation inside each aligned group of four rows chosen so that the four
+// rows read by a half-warp of dequantisers fall in four different 32-byte
+// shared-memory bank windows; sc / dm / d stay in natural row order.
 #pragma once
 #include <cstdint>
 #include <cuda_bf16.h>
@@ -51,6 +55,10 @@ constexpr uint32_t kQ6KChunk = kPanelRows * kQ6KBytes;  // 26880
 constexpr uint32_t kQ4Qs = 0, kQ4Sc = 16384, kQ4Dm = 17920;
 // Q6_K chunk field offsets
 constexpr uint32_t kQ6Ql = 0, kQ6Qh = 16384, kQ6Sc = 24576, kQ6D = 26624;
+
+__host__ __device__ constexpr uint32_t row_slot(uint32_t r) {
+    return (r & ~3u) | ((r + 2u * ((r >> 2) & 1u)) & 3u);
+}
 
 __host__ __device__ constexpr uint32_t block_bytes(uint32_t type) {
     return type == 12 ? kQ4KBytes : type == 14 ? kQ6KBytes : type == 13 ? 176u : 0u;

@@ -7,16 +7,16 @@
 // TMEM as [128 lanes = n] x [BN columns = tokens] fp32.  Each weight element
 // is dequantised once per BN tokens.
 //
-// One persistent CTA per SM, 14 warps, warp-specialised:
+// One persistent CTA per SM, 22 warps, warp-specialised:
 //   warp 0     TMA producer: one bulk copy per packed weight chunk (128 rows x
 //              256 K, 18/26 KB) and one 2-D tensor copy per activation stage
 //              (BN x 64 bf16, SWIZZLE_128B);
 //   warp 1     TMEM allocator and the single MMA-issuing thread
 //              (tcgen05.mma kind::f16, 4 x K16 per stage, commit to mbarriers);
-//   warps 2-9  dequantisers: unpack the packed chunk in shared memory into the
+//   warps 2-5  epilogue: tcgen05.ld 32 columns at a time and store Y;
+//   warps 6-21 dequantisers: unpack the packed chunk in shared memory into the
 //              swizzled bf16 (or fp16) A tile, bit-exact to the reference
-//              decoder, then fence.proxy.async and arrive;
-//   warps 10-13 epilogue: tcgen05.ld 32 columns at a time and store Y.
+//              decoder, then fence.proxy.async and arrive.
 // TMEM holds two BN-column accumulators so the epilogue of tile i overlaps
 // the main loop of tile i+1.  Every mbarrier wait is bounded (globaltimer);
 // on timeout the kernel sets TC_STATUS_TIMEOUT, drains its own copies and
@@ -31,8 +31,8 @@
 namespace tc {
 namespace {
 
-constexpr int kThreads = 448;
-constexpr int kDequantWarp0 = 2, kDequantThreads = 256, kEpiWarp0 = 10, kEpiThreads = 128;
+constexpr int kThreads = 704;   // 22 warps
+constexpr int kEpiWarp0 = 2, kEpiThreads = 128, kDequantWarp0 = 6, kDequantThreads = 512;
 constexpr int kStages = 3;      // activation / A-tile pipeline depth (64 K each)
 constexpr int kWStages = 2;     // packed chunk pipeline depth (256 K each)
 constexpr int kMaxSeg = 32;
@@ -60,7 +60,7 @@ struct Layout {
     static constexpr uint32_t a_off = x_off + kStages * x_stage;
     static constexpr uint32_t w_off = a_off + kStages * a_stage;
     static constexpr uint32_t t_off = (w_off + kWStages * w_stage + 127) / 128 * 128;
-    static constexpr uint32_t table_bytes = 8192;
+    static constexpr uint32_t table_bytes = 128 * 80;  // 80-byte row stride (conflict-free)
     static constexpr uint32_t bar_off = t_off + 2 * table_bytes;
     // x_full[S] a_full[S] st_empty[S] w_full[W] w_empty[W] t_ready[2] acc_full[2] acc_empty[2] fin
     static constexpr uint32_t n_bars = 3 * kStages + 2 * kWStages + 7;
@@ -170,34 +170,70 @@ __device__ __forceinline__ Tile tile_of(const GemmParams &p, uint32_t t) {
 }
 
 // ------------------------------------------------------------ dequant
-// Scale table of one chunk (shared memory, 8 KB):
-//   Q4_K: float2 (d*sc_g, dmin*m_g) for [128 rows][8 sub-blocks]
-//   Q6_K: float  d*sc_i            for [128 rows][16 sub-blocks]
+// Packed fp32x2 arithmetic (sm_100a): two lanes of fp32 per 64-bit register.
+__device__ __forceinline__ uint64_t f2pack(uint32_t lo, uint32_t hi) {
+    uint64_t r;
+    asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "r"(lo), "r"(hi));
+    return r;
+}
+__device__ __forceinline__ void f2unpack(uint64_t v, float &lo, float &hi) {
+    asm("mov.b64 {%0, %1}, %2;" : "=f"(lo), "=f"(hi) : "l"(v));
+}
+__device__ __forceinline__ uint64_t f2add(uint64_t a, uint64_t b) {
+    uint64_t r;
+    asm("add.rn.f32x2 %0, %1, %2;" : "=l"(r) : "l"(a), "l"(b));
+    return r;
+}
+__device__ __forceinline__ uint64_t f2mul(uint64_t a, uint64_t b) {
+    uint64_t r;
+    asm("mul.rn.f32x2 %0, %1, %2;" : "=l"(r) : "l"(a), "l"(b));
+    return r;
+}
+__device__ __forceinline__ uint64_t f2fma(uint64_t a, uint64_t b, uint64_t c) {
+    uint64_t r;
+    asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(r) : "l"(a), "l"(b), "l"(c));
+    return r;
+}
+__device__ __forceinline__ uint64_t f2splat(float v) { return f2pack(__float_as_uint(v), __float_as_uint(v)); }
+// Byte i of w as the float 2^23 + byte (exact): the byte goes into the low
+// mantissa bits under the exponent of 2^23.
+__device__ __forceinline__ uint32_t magic_byte(uint32_t w, uint32_t i) {
+    uint32_t r;
+    asm("prmt.b32 %0, %1, %2, %3;" : "=r"(r) : "r"(w), "r"(0x4B000000u), "r"(0x7440u | i));
+    return r;
+}
+
+// Scale table of one chunk (shared memory, 128 rows x 80 bytes):
+//   Q4_K row r: {d*sc_g, dmin*m_g} for g = 0..7, with d*sc_g pre-divided by 16
+//               for odd g (their codes are read in place from the high nibble,
+//               i.e. multiplied by 16; the power of two keeps every product exact);
+//   Q6_K row r: d*sc_i for the 16 sub-blocks.
+// Thread dt writes 16 bytes of row dt % 128 (conflict-free with the odd
+// 80-byte stride, as are the reads of the dequant tasks).
 template <int TYPE>
 __device__ __forceinline__ void build_table(const uint8_t *wc, float *tab, uint32_t dt) {
-    const uint32_t r = dt >> 1, half = dt & 1;
+    const uint32_t r = dt & 127, j = dt >> 7;
+    float4 v;
     if (TYPE == 12) {
         const uint32_t dm = *reinterpret_cast<const uint32_t *>(wc + kQ4Dm + r * 4);
         const float d = half_bits_to_float((uint16_t)(dm & 0xffffu)), dmin = half_bits_to_float((uint16_t)(dm >> 16));
         const uint8_t *sc = wc + kQ4Sc + r * 12;
-        float2 *out = reinterpret_cast<float2 *>(tab) + r * 8 + half * 4;
-#pragma unroll
-        for (uint32_t i = 0; i < 4; ++i) {
-            uint32_t s, m;
-            q4k_scale_min(half * 4 + i, sc, s, m);
-            out[i] = make_float2(d * (float)s, dmin * (float)m);
-        }
+        uint32_t s0, m0, s1, m1;
+        q4k_scale_min(2 * j, sc, s0, m0);
+        q4k_scale_min(2 * j + 1, sc, s1, m1);
+        v = make_float4(d * (float)s0, dmin * (float)m0, d * (float)s1 * 0.0625f, dmin * (float)m1);
     } else {
         const float d = half_bits_to_float(*reinterpret_cast<const uint16_t *>(wc + kQ6D + r * 2));
-        const int8_t *sc = reinterpret_cast<const int8_t *>(wc + kQ6Sc + r * 16 + half * 8);
-        float *out = tab + r * 16 + half * 8;
-#pragma unroll
-        for (uint32_t i = 0; i < 8; ++i) out[i] = d * (float)sc[i];
+        const int8_t *sc = reinterpret_cast<const int8_t *>(wc + kQ6Sc + r * 16 + 4 * j);
+        v = make_float4(d * (float)sc[0], d * (float)sc[1], d * (float)sc[2], d * (float)sc[3]);
     }
+    *reinterpret_cast<float4 *>(reinterpret_cast<uint8_t *>(tab) + r * 80 + 16 * j) = v;
 }
 
 template <bool F16>
-__device__ __forceinline__ uint32_t pack2(float lo, float hi, bool &ovf) {
+__device__ __forceinline__ uint32_t pack_pair(uint64_t v, bool &ovf) {
+    float lo, hi;
+    f2unpack(v, lo, hi);
     if (F16) {
         const __half2 h = __floats2half2_rn(lo, hi);
         const uint32_t u = *reinterpret_cast<const uint32_t *>(&h);
@@ -209,50 +245,61 @@ __device__ __forceinline__ uint32_t pack2(float lo, float hi, bool &ovf) {
     }
 }
 
-// Dequantise one task: weight row r, 8 bytes (t) of the 64-weight slice q.
-// Writes two 16-byte chunks (K 8t..8t+7 and 32+8t..32+8t+7 of the slice) of
-// the swizzled A tile.
+// Four weights from the four bytes of `codes` (each 2^23 + byte exactly),
+// as v = scale * (byte - bias) [Q6_K, bias = 2^23 + 32] or
+// v = scale * (byte - 2^23) - min [Q4_K]: one magic subtract and one
+// multiply / FMA per pair, both exact except the Q4_K FMA's single rounding,
+// which is the reference's own rounding of d*q - m.
+template <int TYPE, bool F16>
+__device__ __forceinline__ uint2 four_values(uint32_t codes, uint64_t scale2, uint64_t off2, uint64_t min2, bool &ovf) {
+    const uint64_t p0 = f2add(f2pack(magic_byte(codes, 0), magic_byte(codes, 1)), off2);
+    const uint64_t p1 = f2add(f2pack(magic_byte(codes, 2), magic_byte(codes, 3)), off2);
+    uint64_t v0, v1;
+    if (TYPE == 12) { v0 = f2fma(scale2, p0, min2); v1 = f2fma(scale2, p1, min2); }
+    else { v0 = f2mul(scale2, p0); v1 = f2mul(scale2, p1); }
+    return make_uint2(pack_pair<F16>(v0, ovf), pack_pair<F16>(v1, ovf));
+}
+
+// One task: weight row r, bytes 8t..8t+7 of the 64-weight slice q.  Writes
+// two 16-byte chunks (slice K 8t..8t+7 and 32+8t..32+8t+7) of the swizzled
+// A tile.  Q4_K: low nibbles = sub-block 2q, high nibbles = sub-block 2q+1.
+// Q6_K: half h = q/2, groups g0 = 2(q&1) (ql part 0) and g0+1 (part 1).
 template <int TYPE, bool F16>
 __device__ __forceinline__ void dequant_task(const uint8_t *wc, const float *tab, uint32_t q, uint32_t r,
                                              uint32_t t, uint8_t *a, bool &ovf) {
-    float lo[8], hi[8];
+    const uint32_t slot = row_slot(r);
+    const uint8_t *trow = reinterpret_cast<const uint8_t *>(tab) + r * 80;
+    uint2 lo0, lo1, hi0, hi1;
     if (TYPE == 12) {
-        const uint2 b = *reinterpret_cast<const uint2 *>(wc + kQ4Qs + q * 4096 + r * 32 + t * 8);
-        const float4 s = *reinterpret_cast<const float4 *>(tab + (r * 8 + 2 * q) * 2);
-        const uint32_t w[2] = {b.x, b.y};
-#pragma unroll
-        for (int i = 0; i < 8; ++i) {
-            const uint32_t byte = (w[i >> 2] >> (8 * (i & 3))) & 0xffu;
-            lo[i] = q4k_value(s.x, s.y, byte & 15u);
-            hi[i] = q4k_value(s.z, s.w, byte >> 4);
-        }
+        const uint2 b = *reinterpret_cast<const uint2 *>(wc + kQ4Qs + q * 4096 + slot * 32 + t * 8);
+        const float4 s = *reinterpret_cast<const float4 *>(trow + 16 * q);
+        const uint64_t off2 = f2splat(-8388608.0f);
+        const uint64_t dl = f2splat(s.x), ml = f2splat(-s.y), dh = f2splat(s.z), mh = f2splat(-s.w);
+        lo0 = four_values<12, F16>(b.x & 0x0F0F0F0Fu, dl, off2, ml, ovf);
+        lo1 = four_values<12, F16>(b.y & 0x0F0F0F0Fu, dl, off2, ml, ovf);
+        hi0 = four_values<12, F16>(b.x & 0xF0F0F0F0u, dh, off2, mh, ovf);
+        hi1 = four_values<12, F16>(b.y & 0xF0F0F0F0u, dh, off2, mh, ovf);
     } else {
         const uint32_t h = q >> 1, shift = (q & 1) * 4, g0 = 2 * (q & 1);
-        const uint2 la = *reinterpret_cast<const uint2 *>(wc + kQ6Ql + ((h * 2 + 0) * kPanelRows + r) * 32 + t * 8);
-        const uint2 lb = *reinterpret_cast<const uint2 *>(wc + kQ6Ql + ((h * 2 + 1) * kPanelRows + r) * 32 + t * 8);
-        const uint2 qh = *reinterpret_cast<const uint2 *>(wc + kQ6Qh + (h * kPanelRows + r) * 32 + t * 8);
-        const float da = tab[r * 16 + 8 * h + (t >> 1) + 2 * g0];
-        const float db = tab[r * 16 + 8 * h + (t >> 1) + 2 * (g0 + 1)];
-        const uint32_t wa[2] = {la.x, la.y}, wb[2] = {lb.x, lb.y}, wh[2] = {qh.x, qh.y};
-#pragma unroll
-        for (int i = 0; i < 8; ++i) {
-            const uint32_t sh = 8 * (i & 3);
-            const uint32_t ba = (wa[i >> 2] >> sh) & 0xffu, bb = (wb[i >> 2] >> sh) & 0xffu;
-            const uint32_t bh = (wh[i >> 2] >> sh) & 0xffu;
-            const int ca = (int)(((ba >> shift) & 15u) | (((bh >> (2 * g0)) & 3u) << 4)) - 32;
-            const int cb = (int)(((bb >> shift) & 15u) | (((bh >> (2 * g0 + 2)) & 3u) << 4)) - 32;
-            lo[i] = da * (float)ca;
-            hi[i] = db * (float)cb;
-        }
+        const uint2 la = *reinterpret_cast<const uint2 *>(wc + kQ6Ql + ((h * 2 + 0) * kPanelRows + slot) * 32 + t * 8);
+        const uint2 lb = *reinterpret_cast<const uint2 *>(wc + kQ6Ql + ((h * 2 + 1) * kPanelRows + slot) * 32 + t * 8);
+        const uint2 qh = *reinterpret_cast<const uint2 *>(wc + kQ6Qh + (h * kPanelRows + slot) * 32 + t * 8);
+        const float *tf = reinterpret_cast<const float *>(trow);
+        const uint64_t da = f2splat(tf[8 * h + (t >> 1) + 2 * g0]);
+        const uint64_t db = f2splat(tf[8 * h + (t >> 1) + 2 * g0 + 2]);
+        const uint64_t off2 = f2splat(-8388640.0f);  // -(2^23 + 32)
+        const uint32_t ca0 = ((la.x >> shift) & 0x0F0F0F0Fu) | (((qh.x >> (2 * g0)) & 0x03030303u) << 4);
+        const uint32_t ca1 = ((la.y >> shift) & 0x0F0F0F0Fu) | (((qh.y >> (2 * g0)) & 0x03030303u) << 4);
+        const uint32_t cb0 = ((lb.x >> shift) & 0x0F0F0F0Fu) | (((qh.x >> (2 * g0 + 2)) & 0x03030303u) << 4);
+        const uint32_t cb1 = ((lb.y >> shift) & 0x0F0F0F0Fu) | (((qh.y >> (2 * g0 + 2)) & 0x03030303u) << 4);
+        lo0 = four_values<14, F16>(ca0, da, off2, 0, ovf);
+        lo1 = four_values<14, F16>(ca1, da, off2, 0, ovf);
+        hi0 = four_values<14, F16>(cb0, db, off2, 0, ovf);
+        hi1 = four_values<14, F16>(cb1, db, off2, 0, ovf);
     }
-    uint4 plo, phi;
-    plo.x = pack2<F16>(lo[0], lo[1], ovf); plo.y = pack2<F16>(lo[2], lo[3], ovf);
-    plo.z = pack2<F16>(lo[4], lo[5], ovf); plo.w = pack2<F16>(lo[6], lo[7], ovf);
-    phi.x = pack2<F16>(hi[0], hi[1], ovf); phi.y = pack2<F16>(hi[2], hi[3], ovf);
-    phi.z = pack2<F16>(hi[4], hi[5], ovf); phi.w = pack2<F16>(hi[6], hi[7], ovf);
     uint8_t *row = a + (r >> 3) * 1024 + (r & 7) * 128;
-    *reinterpret_cast<uint4 *>(row + ((t ^ (r & 7)) << 4)) = plo;
-    *reinterpret_cast<uint4 *>(row + (((4 + t) ^ (r & 7)) << 4)) = phi;
+    *reinterpret_cast<uint4 *>(row + ((t ^ (r & 7)) << 4)) = make_uint4(lo0.x, lo0.y, lo1.x, lo1.y);
+    *reinterpret_cast<uint4 *>(row + (((4 + t) ^ (r & 7)) << 4)) = make_uint4(hi0.x, hi0.y, hi1.x, hi1.y);
 }
 
 // ------------------------------------------------------------ the kernel
@@ -375,7 +422,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             bar_wait(fin, 0, abort_flag, p.status, false);
         }
         __syncwarp();
-    } else if (warp < (uint32_t)kEpiWarp0) {
+    } else if (warp >= (uint32_t)kDequantWarp0) {
         // ---------------------------------------------------- dequantisers
         const uint32_t dt = threadIdx.x - kDequantWarp0 * 32, dw = dt / 32;
         uint32_t st = 0, ph = 0, ws = 0, wph = 0, tb = 0, tph = 0;
@@ -391,9 +438,8 @@ __global__ void __launch_bounds__(kThreads, 1)
                 for (uint32_t q = 0; q < 4; ++q) {
                     if (!(ok = bar_wait(st_empty(st), ph ^ 1, abort_flag, p.status))) break;
                     uint8_t *a = smem + L::a_off + st * L::a_stage;
-#pragma unroll
-                    for (uint32_t i = 0; i < 2; ++i) {
-                        const uint32_t r = 8 * dw + 64 * i + (lane >> 3) + 4 * ((lane >> 2) & 1);
+                    {
+                        const uint32_t r = 8 * dw + (lane >> 3) + 4 * ((lane >> 2) & 1);
                         dequant_task<TYPE, F16>(wc, tab, q, r, lane & 3, a, ovf);
                     }
                     fence_proxy_async();

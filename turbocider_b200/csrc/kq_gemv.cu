@@ -32,7 +32,7 @@ __global__ void __launch_bounds__(256) gemv_kernel(WeightView w, const uint16_t 
     const uint32_t warps = gridDim.x * (blockDim.x / 32);
     constexpr uint32_t chunk = TYPE == 12 ? kQ4KChunk : kQ6KChunk;
     for (uint32_t row = blockIdx.x * (blockDim.x / 32) + threadIdx.x / 32; row < w.n; row += warps) {
-        const uint32_t r = row % kPanelRows;
+        const uint32_t r = row % kPanelRows, slot = row_slot(r);
         const uint8_t *panel = w.chunks + (uint64_t)(row / kPanelRows) * w.kb * chunk;
         float acc[MT];
 #pragma unroll
@@ -41,7 +41,7 @@ __global__ void __launch_bounds__(256) gemv_kernel(WeightView w, const uint16_t 
             const uint8_t *c = panel + (uint64_t)kb * chunk;
             if (TYPE == 12) {
                 const uint32_t s = lane / 8, t = lane % 8;
-                const uint32_t q = __ldg(reinterpret_cast<const uint32_t *>(c + kQ4Qs + s * 4096 + r * 32 + t * 4));
+                const uint32_t q = __ldg(reinterpret_cast<const uint32_t *>(c + kQ4Qs + s * 4096 + slot * 32 + t * 4));
                 const uint32_t *scw = reinterpret_cast<const uint32_t *>(c + kQ4Sc + r * 12);
                 uint32_t sw[3] = {__ldg(scw), __ldg(scw + 1), __ldg(scw + 2)};
                 const uint8_t *sc = reinterpret_cast<const uint8_t *>(sw);
@@ -71,9 +71,9 @@ __global__ void __launch_bounds__(256) gemv_kernel(WeightView w, const uint16_t 
             } else {
                 const uint32_t h = lane / 16, part = (lane / 8) % 2, t = lane % 8;
                 const uint32_t ql = __ldg(reinterpret_cast<const uint32_t *>(
-                    c + kQ6Ql + ((h * 2 + part) * kPanelRows + r) * 32 + t * 4));
+                    c + kQ6Ql + ((h * 2 + part) * kPanelRows + slot) * 32 + t * 4));
                 const uint32_t qh = __ldg(reinterpret_cast<const uint32_t *>(
-                    c + kQ6Qh + (h * kPanelRows + r) * 32 + t * 4));
+                    c + kQ6Qh + (h * kPanelRows + slot) * 32 + t * 4));
                 const float d = half_bits_to_float(__ldg(reinterpret_cast<const uint16_t *>(c + kQ6D + r * 2)));
                 const int8_t *sc = reinterpret_cast<const int8_t *>(c + kQ6Sc + r * 16);
                 const uint32_t ga = part, gb = 2 + part;     // low / high nibble groups
