@@ -92,23 +92,35 @@ __device__ __forceinline__ bool bar_try(uint32_t b, uint32_t parity) {
         : "=r"(ok) : "r"(b), "r"(parity) : "memory");
     return ok != 0;
 }
+// Waits up to `hint_ns` with the thread suspended (it resumes as soon as the
+// phase completes), so waiting warps do not take issue slots from the
+// dequantisers.
+__device__ __forceinline__ bool bar_try_sleep(uint32_t b, uint32_t parity, uint32_t hint_ns) {
+    uint32_t ok;
+    asm volatile(
+        "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n selp.u32 %0, 1, 0, p;\n}\n"
+        : "=r"(ok) : "r"(b), "r"(parity), "r"(hint_ns) : "memory");
+    return ok != 0;
+}
 // Bounded wait.  Returns false if the CTA is aborting or the wait timed out
 // (which starts the abort).  `honor_abort` = false is used by the drains.
-__device__ __noinline__ bool bar_wait(uint32_t b, uint32_t parity, volatile uint32_t *abort_flag,
-                                      uint32_t *status, bool honor_abort = true) {
-    if (bar_try(b, parity)) return true;
+__device__ __noinline__ bool bar_wait_slow(uint32_t b, uint32_t parity, volatile uint32_t *abort_flag,
+                                           uint32_t *status, bool honor_abort) {
     const uint64_t t0 = gtimer();
-    for (uint32_t it = 1;; ++it) {
-        if (bar_try(b, parity)) return true;
-        if ((it & 31u) == 0) {
-            if (honor_abort && *abort_flag) return false;
-            if (gtimer() - t0 > kTimeoutNs) {
-                atomicOr(status, kStatusTimeout);
-                *abort_flag = 1u;
-                return false;
-            }
+    for (;;) {
+        if (bar_try_sleep(b, parity, 20000u)) return true;
+        if (honor_abort && *abort_flag) return false;
+        if (gtimer() - t0 > kTimeoutNs) {
+            atomicOr(status, kStatusTimeout);
+            *abort_flag = 1u;
+            return false;
         }
     }
+}
+__device__ __forceinline__ bool bar_wait(uint32_t b, uint32_t parity, volatile uint32_t *abort_flag,
+                                         uint32_t *status, bool honor_abort = true) {
+    if (bar_try(b, parity)) return true;
+    return bar_wait_slow(b, parity, abort_flag, status, honor_abort);
 }
 __device__ __forceinline__ void tma_load_2d(uint32_t dst, const CUtensorMap *map, uint32_t b, int x, int y) {
     asm volatile(

@@ -62,6 +62,29 @@ int ensure_workspace(tc_cuda_ctx *ctx, size_t bytes) {
     return TC_CUDA_OK;
 }
 
+// Grows the GEMV split-K workspace: partials and per-tile counters.  The
+// counters are zeroed once here; every complete kernel leaves them at zero.
+int ensure_gemv_workspace(tc_cuda_ctx *ctx, size_t floats, size_t counters) {
+    if (floats > ctx->gemv_partials_floats) {
+        if (ctx->gemv_partials) cudaFree(ctx->gemv_partials);
+        ctx->gemv_partials = nullptr;
+        ctx->gemv_partials_floats = 0;
+        cudaError_t e = cudaMalloc(&ctx->gemv_partials, floats * sizeof(float));
+        if (e != cudaSuccess) return cuda_fail("GEMV workspace allocation", e);
+        ctx->gemv_partials_floats = floats;
+    }
+    if (counters > ctx->gemv_counters_n) {
+        if (ctx->gemv_counters) cudaFree(ctx->gemv_counters);
+        ctx->gemv_counters = nullptr;
+        ctx->gemv_counters_n = 0;
+        cudaError_t e = cudaMalloc(&ctx->gemv_counters, counters * sizeof(uint32_t));
+        if (e == cudaSuccess) e = cudaMemset(ctx->gemv_counters, 0, counters * sizeof(uint32_t));
+        if (e != cudaSuccess) return cuda_fail("GEMV counter allocation", e);
+        ctx->gemv_counters_n = counters;
+    }
+    return TC_CUDA_OK;
+}
+
 }  // namespace
 
 extern "C" {
@@ -103,6 +126,8 @@ void tc_cuda_free(tc_cuda_ctx *ctx) {
     if (!ctx) return;
     DeviceGuard guard(ctx->device);
     if (ctx->workspace) cudaFree(ctx->workspace);
+    if (ctx->gemv_partials) cudaFree(ctx->gemv_partials);
+    if (ctx->gemv_counters) cudaFree(ctx->gemv_counters);
     if (ctx->status) cudaFree(ctx->status);
     delete ctx;
 }
@@ -327,7 +352,14 @@ int tc_cuda_qlinear(tc_cuda_ctx *ctx, const tc_cuda_weight *const *weights, uint
         }
     }
     for (const auto &sv : gemv) {
-        cudaError_t e = tc::launch_gemv(sv, static_cast<const uint16_t *>(x), k, y, ldy, out_dtype, ctx->status, s);
+        tc::GemvSplit sp = tc::gemv_split(sv.w);
+        if (sp.n_slices > 1) {
+            int rc = ensure_gemv_workspace(ctx, tc::gemv_workspace_floats(sv.w), (sv.w.n + 15) / 16);
+            if (rc) return rc;
+            sp.partials = ctx->gemv_partials;
+            sp.counters = ctx->gemv_counters;
+        }
+        cudaError_t e = tc::launch_gemv(sv, static_cast<const uint16_t *>(x), k, y, ldy, out_dtype, sp, s);
         if (e != cudaSuccess) return cuda_fail("GEMV launch", e);
     }
     return ok();

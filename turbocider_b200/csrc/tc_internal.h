@@ -8,8 +8,12 @@ struct tc_cuda_ctx {
     int device = 0;
     int sm_count = 0;
     uint32_t *status = nullptr;      // device status word (TC_STATUS_* bits)
-    void *workspace = nullptr;       // grows on demand: fp16 copy of X, split-K partials
+    void *workspace = nullptr;       // grows on demand: fp16 copy of X
     size_t workspace_bytes = 0;
+    float *gemv_partials = nullptr;  // GEMV K-slice partials (grows on demand)
+    size_t gemv_partials_floats = 0;
+    uint32_t *gemv_counters = nullptr;  // per-16-row-tile arrival counters, kept at 0
+    size_t gemv_counters_n = 0;
     int path = 0;                    // 0 auto, 1 GEMV, 2 GEMM
 };
 
@@ -46,8 +50,18 @@ cudaError_t launch_decode_raw(uint32_t type, const uint8_t *src, uint64_t row_by
                               uint64_t row_begin, uint64_t rows, uint64_t column_begin,
                               uint64_t columns, int dtype, uint8_t *dst, uint64_t row_stride,
                               uint64_t column_stride, uint32_t *status, cudaStream_t s);
+// Small-M GEMV K split: n_slices CTAs per 16-row tile.  With n_slices > 1
+// the kernel needs `partials` (gemv_workspace_floats floats) and one zeroed
+// uint32 counter per 16-row tile; both are left as found (counters back to 0).
+struct GemvSplit {
+    uint32_t kb_per_slice = 0, n_slices = 1;
+    float *partials = nullptr;
+    uint32_t *counters = nullptr;
+};
+GemvSplit gemv_split(const WeightView &w);
+size_t gemv_workspace_floats(const WeightView &w);
 cudaError_t launch_gemv(const SegmentView &seg, const uint16_t *x, uint64_t k, void *y,
-                        uint64_t ldy, int out_dtype, uint32_t *status, cudaStream_t s);
+                        uint64_t ldy, int out_dtype, const GemvSplit &split, cudaStream_t s);
 cudaError_t launch_x_to_f16(const uint16_t *x, uint16_t *x16, uint64_t count, uint32_t *status,
                             cudaStream_t s);
 // Tensor-core GEMM over a list of segments that share type, N and K.
