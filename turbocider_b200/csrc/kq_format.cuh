@@ -83,6 +83,21 @@ __device__ __forceinline__ void q4k_scale_min(uint32_t g, const uint8_t *s, uint
     }
 }
 
+// Same, from the 12 scale bytes held in three little-endian 32-bit words
+// (register-resident: no byte-addressed local array).
+__device__ __forceinline__ void q4k_scale_min_w(uint32_t g, uint32_t w0, uint32_t w1, uint32_t w2,
+                                                uint32_t &sc, uint32_t &mn) {
+    auto byte = [&](uint32_t i) -> uint32_t {
+        const uint32_t w = i < 4 ? w0 : i < 8 ? w1 : w2;
+        return (w >> (8 * (i & 3))) & 0xffu;
+    };
+    if (g < 4) { sc = byte(g) & 63u; mn = byte(g + 4) & 63u; }
+    else {
+        sc = (byte(g + 4) & 15u) | ((byte(g - 4) >> 6) << 4);
+        mn = (byte(g + 4) >> 4) | ((byte(g) >> 6) << 4);
+    }
+}
+
 // Q4_K weight value: exactly the reference's (d*sc)*q - dmin*m (see header).
 __device__ __forceinline__ float q4k_value(float dg, float mg, uint32_t q) {
     return fmaf(dg, (float)q, -mg);

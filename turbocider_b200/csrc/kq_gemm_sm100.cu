@@ -22,6 +22,9 @@
 // on timeout the kernel sets TC_STATUS_TIMEOUT, drains its own copies and
 // MMAs, frees TMEM and returns -- it never traps.
 // No TMA multicast is used anywhere (every CTA loads its own tiles).
+// Launched with programmatic dependent launch: the prologue (barriers, TMEM)
+// of this GEMM overlaps the tail of the previous kernel; the producer waits
+// (griddepcontrol.wait) before its first activation load.
 #include <cuda.h>
 #include <cudaTypedefs.h>
 
@@ -366,9 +369,13 @@ __global__ void __launch_bounds__(kThreads, 1)
     tc_fence_after();
     const uint32_t tmem = *tmem_slot;
 
+    if (threadIdx.x == 0) asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
     if (warp == 0) {
         // ---------------------------------------------------- producer
         if (lane == 0) {
+            // X (and the Y the epilogue writes) may belong to the previous
+            // kernel in the stream: wait for it before the first activation load.
+            asm volatile("griddepcontrol.wait;" ::: "memory");
             uint32_t st = 0, ph = 0, ws = 0, wph = 0;
             uint32_t x_last[kStages], w_last[kWStages];
             bool x_used[kStages] = {}, w_used[kWStages] = {};
@@ -530,8 +537,17 @@ cudaError_t launch_inst(const CUtensorMap &map, const GemmParams &p, int sm_coun
         configured = true;
     }
     const unsigned grid = p.n_tiles < (uint32_t)sm_count ? p.n_tiles : (unsigned)sm_count;
-    kernel<<<grid, kThreads, L::bytes, s>>>(map, p);
-    return cudaGetLastError();
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(grid);
+    cfg.blockDim = dim3(kThreads);
+    cfg.dynamicSmemBytes = L::bytes;
+    cfg.stream = s;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    return cudaLaunchKernelEx(&cfg, kernel, map, p);
 }
 
 template <int TYPE, int BN>

@@ -20,15 +20,20 @@
 // Result: fp32 accumulation of exactly-represented products; equal to the
 // fp32-decode + fp32 matmul oracle up to summation order.
 //
-// Work split: CTA (x, y) = (16 weight rows, one K slice of 4*u super-blocks),
-// 4 warps each taking u super-blocks, so that thousands of short CTAs keep
+// Work split: CTA (x, y) = (16 weight rows, one K slice of 4 super-blocks),
+// 4 warps each taking one super-block, so that thousands of short CTAs keep
 // every SM's loads in flight (the CTA count is independent of the SM count).
-// Each warp issues all loads of its super-block before computing.  A CTA
+// Each warp issues all loads of its super-block first; the CTA stages its X
+// slice in shared memory meanwhile (rows padded so token rows use distinct
+// banks).  A CTA
 // sums its warps through shared memory; with several K slices it stores the
 // 16 x M partial in the context workspace, and the last CTA of the row tile to
 // finish (per-tile arrival counter) adds the slices in slice order -- a fixed
 // order, so results are deterministic -- writes Y and resets the counter.
 // The N8 side of the MMA carries the tokens: NT = 1 or 2 tiles of 8.
+// Launches use programmatic dependent launch: weight prefetch overlaps the
+// tail of the previous kernel in the stream; X, the workspace and Y are
+// touched only after griddepcontrol.wait.
 #include "kq_format.cuh"
 #include "tc_internal.h"
 
@@ -37,18 +42,11 @@ namespace {
 
 constexpr int kWarps = 4;
 
-__device__ __forceinline__ uint32_t ldg32(const uint8_t *p) { return __ldg(reinterpret_cast<const uint32_t *>(p)); }
-
 // Two code bytes (selector 0x4140: bytes 0,1; 0x4342: bytes 2,3) as the bf16
-// pair (128 + c0, 128 + c1).
+// pair (128 + c0, 128 + c1): each byte lands under the exponent of 128.
 __device__ __forceinline__ uint32_t code_pair(uint32_t codes, uint32_t sel) {
     uint32_t r;
     asm("prmt.b32 %0, %1, %2, %3;" : "=r"(r) : "r"(codes), "r"(0x43434343u), "r"(sel));
-    return r;
-}
-__device__ __forceinline__ uint32_t bf16x2_sub(uint32_t a, uint32_t b) {
-    uint32_t r;
-    asm("sub.rn.bf16x2 %0, %1, %2;" : "=r"(r) : "r"(a), "r"(b));
     return r;
 }
 __device__ __forceinline__ void mma16816(float (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3,
@@ -60,196 +58,373 @@ __device__ __forceinline__ void mma16816(float (&d)[4], uint32_t a0, uint32_t a1
         : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1), "f"(c[0]), "f"(c[1]), "f"(c[2]), "f"(c[3]));
 }
 
-// A fragment from the code words of rows g (cg) and g+8 (cg8), minus `bias`
-// (a bf16x2 constant: 128 for Q4_K, 160 for Q6_K).
-struct AFrag { uint32_t r0, r1, r2, r3; };
-__device__ __forceinline__ AFrag a_frag(uint32_t cg, uint32_t cg8, uint32_t bias) {
-    return {bf16x2_sub(code_pair(cg, 0x4140u), bias), bf16x2_sub(code_pair(cg8, 0x4140u), bias),
-            bf16x2_sub(code_pair(cg, 0x4342u), bias), bf16x2_sub(code_pair(cg8, 0x4342u), bias)};
-}
+// ---------------------------------------------------------------- staging
+// Per-warp stage in shared memory: the packed fields of 16 weight rows for one
+// super-block (contiguous pieces of the panel chunk, one bulk copy each) and
+// the matching 256 columns of X for each token.
+//   Q4_K: qs [4][16 rows][32] | sc [16][12] | dm [16][4]              = 2304 B
+//   Q6_K: ql [4 = h*2+part][16][32] | qh [2][16][32] | sc [16][16] | d [16][2] = 3360 B
+// followed by X [m][256] bf16.  Row r of a piece is at row_slot(r0 + r) - r0.
+template <int TYPE> struct StageGeo;
+template <> struct StageGeo<12> {
+    static constexpr uint32_t w_bytes = 2304, qs = 0, sc = 2048, dm = 2240;
+};
+template <> struct StageGeo<14> {
+    static constexpr uint32_t w_bytes = 3360, ql = 0, qh = 2048, sc = 3072, d = 3328;
+};
 
-template <int NT>
-__device__ __forceinline__ void x_frag(const uint16_t *const (&xr)[NT], uint64_t kpos, uint32_t (&b)[NT][2]) {
-#pragma unroll
-    for (int nt = 0; nt < NT; ++nt) {
-        if (xr[nt]) {
-            const uint2 v = __ldg(reinterpret_cast<const uint2 *>(xr[nt] + kpos));
-            b[nt][0] = v.x;
-            b[nt][1] = v.y;
-        } else {
-            b[nt][0] = b[nt][1] = 0u;
+__device__ __forceinline__ uint32_t s_u32(const void *p) { return (uint32_t)__cvta_generic_to_shared(p); }
+__device__ __forceinline__ void mbar_init(uint32_t b, uint32_t n) {
+    asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(b), "r"(n));
+}
+__device__ __forceinline__ void mbar_expect(uint32_t b, uint32_t bytes) {
+    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(b), "r"(bytes) : "memory");
+}
+__device__ __forceinline__ void bulk_g2s(uint32_t dst, const void *src, uint32_t bytes, uint32_t b) {
+    asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];"
+                 ::"r"(dst), "l"(src), "r"(bytes), "r"(b) : "memory");
+}
+__device__ __forceinline__ bool mbar_try(uint32_t b, uint32_t parity) {
+    uint32_t ok;
+    asm volatile("{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n"
+                 " selp.u32 %0, 1, 0, p;\n}\n"
+                 : "=r"(ok) : "r"(b), "r"(parity), "r"(20000u) : "memory");
+    return ok != 0;
+}
+// Bounded wait (about one second); false on timeout, after setting the
+// timeout bit of the status word.
+__device__ __noinline__ bool mbar_wait(uint32_t b, uint32_t parity, uint32_t *status) {
+    uint64_t t0, t1;
+    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t0));
+    for (;;) {
+        if (mbar_try(b, parity)) return true;
+        asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t1));
+        if (t1 - t0 > 1000000000ull) {
+            atomicOr(status, 1u << 2);
+            return false;
         }
     }
 }
 
-template <int TYPE, int NT, int DT>
+// Lane 0 of a warp: enqueue the weight copies of one super-block into stage
+// buffer st (the stage's barrier expects the X bytes too; issue_x adds them).
+template <int TYPE>
+__device__ __forceinline__ void issue_w(uint8_t *st, uint32_t bar, const uint8_t *chunk, uint32_t r0,
+                                        uint32_t m_count) {
+    using SG = StageGeo<TYPE>;
+    mbar_expect(bar, SG::w_bytes + m_count * 512);
+    const uint32_t d = s_u32(st);
+    if constexpr (TYPE == 12) {
+#pragma unroll
+        for (uint32_t q = 0; q < 4; ++q) bulk_g2s(d + SG::qs + q * 512, chunk + kQ4Qs + q * 4096 + r0 * 32, 512, bar);
+        bulk_g2s(d + SG::sc, chunk + kQ4Sc + r0 * 12, 192, bar);
+        bulk_g2s(d + SG::dm, chunk + kQ4Dm + r0 * 4, 64, bar);
+    } else {
+#pragma unroll
+        for (uint32_t hp = 0; hp < 4; ++hp)
+            bulk_g2s(d + SG::ql + hp * 512, chunk + kQ6Ql + (hp * kPanelRows + r0) * 32, 512, bar);
+#pragma unroll
+        for (uint32_t h = 0; h < 2; ++h)
+            bulk_g2s(d + SG::qh + h * 512, chunk + kQ6Qh + (h * kPanelRows + r0) * 32, 512, bar);
+        bulk_g2s(d + SG::sc, chunk + kQ6Sc + r0 * 16, 256, bar);
+        bulk_g2s(d + SG::d, chunk + kQ6D + r0 * 2, 32, bar);
+    }
+}
+template <int TYPE>
+__device__ __forceinline__ void issue_x(uint8_t *st, uint32_t bar, const uint16_t *x, uint64_t k, uint32_t m_begin,
+                                        uint32_t m_count, uint32_t kb) {
+    const uint32_t d = s_u32(st) + StageGeo<TYPE>::w_bytes;
+    for (uint32_t tok = 0; tok < m_count; ++tok)
+        bulk_g2s(d + tok * 512, x + (uint64_t)(m_begin + tok) * k + (uint64_t)kb * 256, 512, bar);
+}
+// Programmatic dependent launch: let the next kernel in the stream start its
+// prologue, and wait for the previous one before touching its outputs.
+__device__ __forceinline__ void pdl_launch_dependents() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+
+__device__ __forceinline__ uint32_t lds32(const uint8_t *p) { return *reinterpret_cast<const uint32_t *>(p); }
+
+// Four bytes of a word as exact small-integer floats (byte = 0..255):
+// prmt under the exponent of 2^23, then subtract 2^23.
+__device__ __forceinline__ void bytes_to_float4(uint32_t w, float (&f)[4]) {
+#pragma unroll
+    for (uint32_t i = 0; i < 4; ++i) {
+        uint32_t r;
+        asm("prmt.b32 %0, %1, %2, %3;" : "=r"(r) : "r"(w), "r"(0x4B000000u), "r"(0x7440u | i));
+        f[i] = __uint_as_float(r) - 8388608.0f;
+    }
+}
+
+// Columns of the MMA's N8 side: with TP tokens per tile (1, 2, 4 or 8),
+// column n carries token n % TP of the n / TP-th scale group of the current
+// chain, so a chain of S = 8 / TP scale groups accumulates unscaled in one
+// fp32 fragment; the B fragment of a K16 step is non-zero only in the columns
+// of that step's group.  The A operand is the bf16 value 128 + code (no
+// subtract): the chain also accumulates sum_k x_k per column with an all-ones
+// A (C1), and the group's result is ds * (C - off * C1) with off = 128 + bias
+// (Q6_K: 160; Q4_K: 128, plus its min term -m * C1).
+//
+// Visit order of the scale groups (v = 0..GROUPS-1) follows the packed words:
+//   Q4_K: v = sub-block (quarter v/2, nibble v&1), two K16 steps each;
+//   Q6_K: v = 8h + 4jj + grp -> 16-weight group 8h + 2grp + jj, one step each.
+template <int TYPE>
+__device__ __forceinline__ constexpr uint32_t group_of_visit(uint32_t v) {
+    return TYPE == 12 ? v : 8 * (v >> 3) + 2 * (v & 3) + ((v >> 2) & 1);
+}
+
+template <int TYPE, int TP, int NT>
+__device__ __forceinline__ void compute_stage(const uint8_t *st, uint32_t m_count, uint32_t g, uint32_t t,
+                                              uint32_t lane, float *wt, float (&acc)[NT][4]) {
+    using SG = StageGeo<TYPE>;
+    constexpr uint32_t S = 8 / TP;
+    constexpr uint32_t GROUPS = TYPE == 12 ? 8 : 16;
+    const uint32_t rg = row_slot(g), rg8 = row_slot(g + 8);   // slots inside the 16-row piece
+    const uint32_t half = lane & 1, rr = lane >> 1;
+    // Scale table, written by all lanes: row rr, half `half` of its groups.
+    //   Q4_K: float2 (d*sc_g, dmin*m_g) [16][8];  Q6_K: float d*sc_i [16][16].
+    __syncwarp();
+    if constexpr (TYPE == 12) {
+        const uint32_t dm = lds32(st + SG::dm + rr * 4);
+        const float d = half_bits_to_float((uint16_t)(dm & 0xffffu)), dmin = half_bits_to_float((uint16_t)(dm >> 16));
+        const uint32_t w0 = lds32(st + SG::sc + rr * 12), w1 = lds32(st + SG::sc + rr * 12 + 4),
+                       w2 = lds32(st + SG::sc + rr * 12 + 8);
+        // byte lanes: sc0..3 = w0 & 63, m0..3 = w1 & 63,
+        // sc4..7 = (w2 & 15) | (w0 >> 6) << 4, m4..7 = (w2 >> 4) | (w1 >> 6) << 4
+        const uint32_t scw = half ? ((w2 & 0x0F0F0F0Fu) | ((w0 >> 2) & 0x30303030u)) : (w0 & 0x3F3F3F3Fu);
+        const uint32_t mnw = half ? (((w2 >> 4) & 0x0F0F0F0Fu) | ((w1 >> 2) & 0x30303030u)) : (w1 & 0x3F3F3F3Fu);
+        float scf[4], mnf[4];
+        bytes_to_float4(scw, scf);
+        bytes_to_float4(mnw, mnf);
+        float4 *o = reinterpret_cast<float4 *>(wt + rr * 16 + half * 8);
+        o[0] = make_float4(d * scf[0], dmin * mnf[0], d * scf[1], dmin * mnf[1]);
+        o[1] = make_float4(d * scf[2], dmin * mnf[2], d * scf[3], dmin * mnf[3]);
+    } else {
+        const float d = half_bits_to_float(*reinterpret_cast<const uint16_t *>(st + SG::d + rr * 2));
+        const uint2 sw = *reinterpret_cast<const uint2 *>(st + SG::sc + rr * 16 + 8 * half);
+        float a[4], b[4];
+        bytes_to_float4(sw.x ^ 0x80808080u, a);   // int8 + 128 as unsigned bytes
+        bytes_to_float4(sw.y ^ 0x80808080u, b);
+        float4 *o = reinterpret_cast<float4 *>(wt + rr * 16 + half * 8);
+        o[0] = make_float4(d * (a[0] - 128.f), d * (a[1] - 128.f), d * (a[2] - 128.f), d * (a[3] - 128.f));
+        o[1] = make_float4(d * (b[0] - 128.f), d * (b[1] - 128.f), d * (b[2] - 128.f), d * (b[3] - 128.f));
+    }
+    __syncwarp();
+    const uint16_t *xst = reinterpret_cast<const uint16_t *>(st + SG::w_bytes);
+    const uint16_t *xrow[NT];
+#pragma unroll
+    for (int nt = 0; nt < NT; ++nt) xrow[nt] = xst + min(8 * nt + g % TP, m_count - 1) * 256;
+    const uint32_t my_j = g / TP;
+    const uint32_t ones = 0x3F803F80u;
+    constexpr float off = TYPE == 12 ? 128.f : 160.f;
+    float cq[NT][4], c1[NT][4];
+
+    // One K16 step of scale group visit v: A from code words (rows g, g+8).
+    auto step = [&](uint32_t v, uint32_t cg, uint32_t cg8, uint32_t kloc, bool chain_start) {
+        const uint32_t j = v % S;
+        if (chain_start) {
+#pragma unroll
+            for (int nt = 0; nt < NT; ++nt)
+#pragma unroll
+                for (int i = 0; i < 4; ++i) cq[nt][i] = c1[nt][i] = 0.f;
+        }
+        const uint32_t a0 = code_pair(cg, 0x4140u), a1 = code_pair(cg8, 0x4140u);
+        const uint32_t a2 = code_pair(cg, 0x4342u), a3 = code_pair(cg8, 0x4342u);
+#pragma unroll
+        for (int nt = 0; nt < NT; ++nt) {
+            const uint2 xv = *reinterpret_cast<const uint2 *>(xrow[nt] + kloc);
+            const bool on = my_j == j;
+            const uint32_t b0 = on ? xv.x : 0u, b1 = on ? xv.y : 0u;
+            mma16816(cq[nt], a0, a1, a2, a3, b0, b1, cq[nt]);
+            mma16816(c1[nt], ones, ones, ones, ones, b0, b1, c1[nt]);
+        }
+    };
+    // Scale the finished chain `chain` into the accumulators.
+    auto close_chain = [&](uint32_t chain) {
+#pragma unroll
+        for (uint32_t ci = 0; ci < 2; ++ci) {
+            const uint32_t G = group_of_visit<TYPE>(chain * S + (2 * t + ci) / TP);
+            if constexpr (TYPE == 12) {
+                const float2 a = reinterpret_cast<const float2 *>(wt)[g * 8 + G];
+                const float2 b = reinterpret_cast<const float2 *>(wt)[(g + 8) * 8 + G];
+#pragma unroll
+                for (int nt = 0; nt < NT; ++nt) {
+                    acc[nt][ci] = fmaf(a.x, fmaf(-off, c1[nt][ci], cq[nt][ci]), fmaf(-a.y, c1[nt][ci], acc[nt][ci]));
+                    acc[nt][2 + ci] = fmaf(b.x, fmaf(-off, c1[nt][2 + ci], cq[nt][2 + ci]),
+                                           fmaf(-b.y, c1[nt][2 + ci], acc[nt][2 + ci]));
+                }
+            } else {
+                const float a = wt[g * 16 + G], b = wt[(g + 8) * 16 + G];
+#pragma unroll
+                for (int nt = 0; nt < NT; ++nt) {
+                    acc[nt][ci] = fmaf(a, fmaf(-off, c1[nt][ci], cq[nt][ci]), acc[nt][ci]);
+                    acc[nt][2 + ci] = fmaf(b, fmaf(-off, c1[nt][2 + ci], cq[nt][2 + ci]), acc[nt][2 + ci]);
+                }
+            }
+        }
+    };
+
+    if constexpr (TYPE == 12) {
+#pragma unroll
+        for (uint32_t q = 0; q < 4; ++q) {
+            const uint2 wg = *reinterpret_cast<const uint2 *>(st + SG::qs + q * 512 + rg * 32 + 8 * t);
+            const uint2 wg8 = *reinterpret_cast<const uint2 *>(st + SG::qs + q * 512 + rg8 * 32 + 8 * t);
+#pragma unroll
+            for (uint32_t nib = 0; nib < 2; ++nib) {
+                const uint32_t v = 2 * q + nib;
+#pragma unroll
+                for (uint32_t sp = 0; sp < 2; ++sp) {
+                    const uint32_t w = sp ? wg.y : wg.x, w8 = sp ? wg8.y : wg8.x;
+                    step(v, (w >> (4 * nib)) & 0x0F0F0F0Fu, (w8 >> (4 * nib)) & 0x0F0F0F0Fu,
+                         32 * v + 8 * t + 4 * sp, sp == 0 && v % S == 0);
+                }
+                if (v % S == S - 1) close_chain(v / S);
+            }
+        }
+    } else {
+#pragma unroll
+        for (uint32_t h = 0; h < 2; ++h) {
+#pragma unroll
+            for (uint32_t jj = 0; jj < 2; ++jj) {
+                const uint32_t o0 = SG::ql + (h * 2) * 512 + 16 * jj + 4 * t;
+                const uint32_t o1 = o0 + 512, oh = SG::qh + h * 512 + 16 * jj + 4 * t;
+                const uint32_t l0 = lds32(st + o0 + rg * 32), l1 = lds32(st + o1 + rg * 32), hq = lds32(st + oh + rg * 32);
+                const uint32_t l08 = lds32(st + o0 + rg8 * 32), l18 = lds32(st + o1 + rg8 * 32),
+                               hq8 = lds32(st + oh + rg8 * 32);
+                // high-bit planes for groups 0..3, already at bits 4..5 of each byte
+                const uint32_t hb[4] = {(hq << 4) & 0x30303030u, (hq << 2) & 0x30303030u, hq & 0x30303030u,
+                                        (hq >> 2) & 0x30303030u};
+                const uint32_t hb8[4] = {(hq8 << 4) & 0x30303030u, (hq8 << 2) & 0x30303030u, hq8 & 0x30303030u,
+                                         (hq8 >> 2) & 0x30303030u};
+                const uint32_t lw[4] = {l0, l1, l0 >> 4, l1 >> 4}, lw8[4] = {l08, l18, l08 >> 4, l18 >> 4};
+#pragma unroll
+                for (uint32_t grp = 0; grp < 4; ++grp) {
+                    const uint32_t v = 8 * h + 4 * jj + grp;
+                    step(v, (lw[grp] & 0x0F0F0F0Fu) | hb[grp], (lw8[grp] & 0x0F0F0F0Fu) | hb8[grp],
+                         128 * h + 32 * grp + 16 * jj + 4 * t, v % S == 0);
+                    if (v % S == S - 1) close_chain(v / S);
+                }
+            }
+        }
+    }
+}
+
+constexpr uint32_t kGemvStages = 3;
+
+template <int TYPE, int TP, int NT, int DT>
 __global__ void __launch_bounds__(kWarps * 32) gemv_kernel(WeightView w, const uint16_t *__restrict__ x,
                                                            uint32_t m_begin, uint32_t m_count, uint64_t k,
                                                            void *__restrict__ y, uint64_t ldy,
                                                            uint32_t kb_per_slice, float *__restrict__ partials,
-                                                           uint32_t *__restrict__ counters) {
+                                                           uint32_t *__restrict__ counters, uint32_t *status) {
+    using SG = StageGeo<TYPE>;
     constexpr uint32_t chunk = TYPE == 12 ? kQ4KChunk : kQ6KChunk;
+    extern __shared__ __align__(128) uint8_t dyn[];
     __shared__ float red[kWarps][32][4 * NT];
     __shared__ __align__(16) float tab[kWarps][16 * 16];
+    __shared__ __align__(8) uint64_t bars[kWarps][kGemvStages];
     const uint32_t warp = threadIdx.x >> 5, lane = threadIdx.x & 31, g = lane >> 2, t = lane & 3;
     const uint32_t row0 = blockIdx.x * 16, panel = row0 / kPanelRows, r0 = row0 % kPanelRows;
     const uint32_t n_slices = gridDim.y, kb_begin = blockIdx.y * kb_per_slice;
     const uint32_t kb_end = min(w.kb, kb_begin + kb_per_slice);
-    const uint32_t sg = row_slot(r0 + g), sg8 = row_slot(r0 + g + 8);
     const uint8_t *pbase = w.chunks + (uint64_t)panel * w.kb * chunk;
-    const uint16_t *xr[NT];
-#pragma unroll
-    for (int nt = 0; nt < NT; ++nt)
-        xr[nt] = (8 * nt + g < m_count) ? x + (uint64_t)(m_begin + 8 * nt + g) * k : nullptr;
+    const uint32_t stage_bytes = (SG::w_bytes + m_count * 512 + 127) / 128 * 128;
+    uint8_t *mine = dyn + (size_t)warp * kGemvStages * stage_bytes;
+    float *wt = tab[warp];
+    if (lane == 0)
+        for (uint32_t i = 0; i < kGemvStages; ++i) mbar_init(s_u32(&bars[warp][i]), 1);
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    __syncwarp();
+
+    // This warp's super-blocks: kb_begin + warp + kWarps * i
+    const uint32_t first = kb_begin + warp;
+    const uint32_t count = first < kb_end ? (kb_end - first + kWarps - 1) / kWarps : 0;
+    // Weights do not depend on the previous kernel: prefetch them first, then
+    // wait for it (it may still be writing X, the workspace or Y).
+    if (lane == 0) {
+        for (uint32_t i = 0; i < min(count, kGemvStages - 1); ++i) {
+            const uint32_t kb = first + kWarps * i;
+            issue_w<TYPE>(mine + i * stage_bytes, s_u32(&bars[warp][i]), pbase + (uint64_t)kb * chunk, r0, m_count);
+        }
+    }
+    if (threadIdx.x == 0) pdl_launch_dependents();
+    pdl_wait();
+    if (lane == 0)
+        for (uint32_t i = 0; i < min(count, kGemvStages - 1); ++i)
+            issue_x<TYPE>(mine + i * stage_bytes, s_u32(&bars[warp][i]), x, k, m_begin, m_count, first + kWarps * i);
     float acc[NT][4];
 #pragma unroll
     for (int nt = 0; nt < NT; ++nt)
 #pragma unroll
         for (int i = 0; i < 4; ++i) acc[nt][i] = 0.f;
-    float *wt = tab[warp];
-
-    for (uint32_t kb = kb_begin + warp; kb < kb_end; kb += kWarps) {
-        const uint8_t *c = pbase + (uint64_t)kb * chunk;
-        const uint64_t kbase = (uint64_t)kb * 256;
+    bool ok = true;
+    for (uint32_t i = 0; i < count; ++i) {
+        const uint32_t slot = i % kGemvStages, parity = (i / kGemvStages) & 1;
+        // refill the slot computed in the previous iteration (all lanes are past it)
+        if (lane == 0 && i + kGemvStages - 1 < count) {
+            const uint32_t j = i + kGemvStages - 1, kb = first + kWarps * j;
+            uint8_t *sj = mine + (j % kGemvStages) * stage_bytes;
+            const uint32_t bj = s_u32(&bars[warp][j % kGemvStages]);
+            issue_w<TYPE>(sj, bj, pbase + (uint64_t)kb * chunk, r0, m_count);
+            issue_x<TYPE>(sj, bj, x, k, m_begin, m_count, kb);
+        }
+        if (!mbar_wait(s_u32(&bars[warp][slot]), parity, status)) { ok = false; break; }
+        compute_stage<TYPE, TP, NT>(mine + slot * stage_bytes, m_count, g, t, lane, wt, acc);
         __syncwarp();
-        if (TYPE == 12) {
-            // scale table: rows r0..r0+15 x 8 sub-blocks of (d*sc, dmin*m)
-            {
-                const uint32_t rr = r0 + (lane >> 1), half = lane & 1;
-                const uint32_t dm = __ldg(reinterpret_cast<const uint32_t *>(c + kQ4Dm + rr * 4));
-                const float d = half_bits_to_float((uint16_t)(dm & 0xffffu));
-                const float dmin = half_bits_to_float((uint16_t)(dm >> 16));
-                uint32_t sw[3];
-                const uint32_t *sp = reinterpret_cast<const uint32_t *>(c + kQ4Sc + rr * 12);
-                sw[0] = __ldg(sp); sw[1] = __ldg(sp + 1); sw[2] = __ldg(sp + 2);
-                const uint8_t *sc = reinterpret_cast<const uint8_t *>(sw);
-                float2 *o = reinterpret_cast<float2 *>(wt) + (lane >> 1) * 8 + half * 4;
-#pragma unroll
-                for (uint32_t i = 0; i < 4; ++i) {
-                    uint32_t s, m;
-                    q4k_scale_min(half * 4 + i, sc, s, m);
-                    o[i] = make_float2(d * (float)s, dmin * (float)m);
-                }
-            }
-            __syncwarp();
-            const uint32_t bias = 0x43004300u;     // bf16x2 (128, 128)
-            const uint32_t ones = 0x3F803F80u;     // bf16x2 (1, 1)
-#pragma unroll
-            for (uint32_t s = 0; s < 4; ++s) {
-                uint32_t wg[2], wg8[2];
-#pragma unroll
-                for (uint32_t jj = 0; jj < 2; ++jj) {
-                    wg[jj] = ldg32(c + kQ4Qs + s * 4096 + sg * 32 + 16 * jj + 4 * t);
-                    wg8[jj] = ldg32(c + kQ4Qs + s * 4096 + sg8 * 32 + 16 * jj + 4 * t);
-                }
-#pragma unroll
-                for (uint32_t nib = 0; nib < 2; ++nib) {
-                    const uint32_t G = 2 * s + nib;
-                    float cq[NT][4], c1[NT][4];
-#pragma unroll
-                    for (int nt = 0; nt < NT; ++nt)
-#pragma unroll
-                        for (int i = 0; i < 4; ++i) cq[nt][i] = c1[nt][i] = 0.f;
-#pragma unroll
-                    for (uint32_t jj = 0; jj < 2; ++jj) {
-                        const AFrag a = a_frag((wg[jj] >> (4 * nib)) & 0x0F0F0F0Fu,
-                                               (wg8[jj] >> (4 * nib)) & 0x0F0F0F0Fu, bias);
-                        uint32_t b[NT][2];
-                        x_frag<NT>(xr, kbase + 32 * G + 16 * jj + 4 * t, b);
-#pragma unroll
-                        for (int nt = 0; nt < NT; ++nt) {
-                            mma16816(cq[nt], a.r0, a.r1, a.r2, a.r3, b[nt][0], b[nt][1], cq[nt]);
-                            mma16816(c1[nt], ones, ones, ones, ones, b[nt][0], b[nt][1], c1[nt]);
-                        }
-                    }
-                    const float2 sgv = reinterpret_cast<const float2 *>(wt)[g * 8 + G];
-                    const float2 sg8v = reinterpret_cast<const float2 *>(wt)[(g + 8) * 8 + G];
-#pragma unroll
-                    for (int nt = 0; nt < NT; ++nt) {
-                        acc[nt][0] = fmaf(sgv.x, cq[nt][0], fmaf(-sgv.y, c1[nt][0], acc[nt][0]));
-                        acc[nt][1] = fmaf(sgv.x, cq[nt][1], fmaf(-sgv.y, c1[nt][1], acc[nt][1]));
-                        acc[nt][2] = fmaf(sg8v.x, cq[nt][2], fmaf(-sg8v.y, c1[nt][2], acc[nt][2]));
-                        acc[nt][3] = fmaf(sg8v.x, cq[nt][3], fmaf(-sg8v.y, c1[nt][3], acc[nt][3]));
-                    }
-                }
-            }
-        } else {
-            // scale table: rows r0..r0+15 x 16 sub-blocks of d*sc
-            {
-                const uint32_t rr = r0 + (lane >> 1), half = lane & 1;
-                const float d = half_bits_to_float(__ldg(reinterpret_cast<const uint16_t *>(c + kQ6D + rr * 2)));
-                const uint2 sw = __ldg(reinterpret_cast<const uint2 *>(c + kQ6Sc + rr * 16 + 8 * half));
-                const uint32_t words[2] = {sw.x, sw.y};
-                float *o = wt + (lane >> 1) * 16 + half * 8;
-#pragma unroll
-                for (uint32_t i = 0; i < 8; ++i)
-                    o[i] = d * (float)(int8_t)((words[i >> 2] >> (8 * (i & 3))) & 0xffu);
-            }
-            __syncwarp();
-            const uint32_t bias = 0x43204320u;     // bf16x2 (160, 160) = 128 + 32
-#pragma unroll
-            for (uint32_t h = 0; h < 2; ++h) {
-                uint32_t hg[2], hg8[2];
-#pragma unroll
-                for (uint32_t jj = 0; jj < 2; ++jj) {
-                    hg[jj] = ldg32(c + kQ6Qh + (h * kPanelRows + sg) * 32 + 16 * jj + 4 * t);
-                    hg8[jj] = ldg32(c + kQ6Qh + (h * kPanelRows + sg8) * 32 + 16 * jj + 4 * t);
-                }
-#pragma unroll
-                for (uint32_t part = 0; part < 2; ++part) {
-                    uint32_t lg[2], lg8[2];
-#pragma unroll
-                    for (uint32_t jj = 0; jj < 2; ++jj) {
-                        lg[jj] = ldg32(c + kQ6Ql + ((h * 2 + part) * kPanelRows + sg) * 32 + 16 * jj + 4 * t);
-                        lg8[jj] = ldg32(c + kQ6Ql + ((h * 2 + part) * kPanelRows + sg8) * 32 + 16 * jj + 4 * t);
-                    }
-#pragma unroll
-                    for (uint32_t nib = 0; nib < 2; ++nib) {
-                        const uint32_t grp = part + 2 * nib;
-#pragma unroll
-                        for (uint32_t jj = 0; jj < 2; ++jj) {
-                            const uint32_t cg = ((lg[jj] >> (4 * nib)) & 0x0F0F0F0Fu) |
-                                                (((hg[jj] >> (2 * grp)) & 0x03030303u) << 4);
-                            const uint32_t cg8 = ((lg8[jj] >> (4 * nib)) & 0x0F0F0F0Fu) |
-                                                 (((hg8[jj] >> (2 * grp)) & 0x03030303u) << 4);
-                            const AFrag a = a_frag(cg, cg8, bias);
-                            uint32_t b[NT][2];
-                            x_frag<NT>(xr, kbase + 128 * h + 32 * grp + 16 * jj + 4 * t, b);
-                            const uint32_t sb = 8 * h + 2 * grp + jj;
-                            const float dg = wt[g * 16 + sb], dg8 = wt[(g + 8) * 16 + sb];
-#pragma unroll
-                            for (int nt = 0; nt < NT; ++nt) {
-                                float cq[4] = {0.f, 0.f, 0.f, 0.f};
-                                mma16816(cq, a.r0, a.r1, a.r2, a.r3, b[nt][0], b[nt][1], cq);
-                                acc[nt][0] = fmaf(dg, cq[0], acc[nt][0]);
-                                acc[nt][1] = fmaf(dg, cq[1], acc[nt][1]);
-                                acc[nt][2] = fmaf(dg8, cq[2], acc[nt][2]);
-                                acc[nt][3] = fmaf(dg8, cq[3], acc[nt][3]);
-                            }
-                        }
-                    }
-                }
+    }
+    if (!ok) {
+        // wait (bounded) for this warp's copies still in flight before exiting
+        for (uint32_t s2 = 0; s2 < kGemvStages; ++s2) {
+            // the last use of slot s2 was iteration j = largest j < count with j % S == s2
+            if (s2 < count) {
+                const uint32_t j = s2 + ((count - 1 - s2) / kGemvStages) * kGemvStages;
+                mbar_wait(s_u32(&bars[warp][s2]), (j / kGemvStages) & 1, status);
             }
         }
     }
+    // Columns of one token are spread over the quad (TP < 8): sum them so that
+    // every lane holds the full value of its (row, token) pairs.
+    if constexpr (TP == 1) {   // all 8 columns are token 0: fold the thread's two columns
+#pragma unroll
+        for (int nt = 0; nt < NT; ++nt) {
+            acc[nt][0] += acc[nt][1];
+            acc[nt][2] += acc[nt][3];
+            acc[nt][1] = acc[nt][0];
+            acc[nt][3] = acc[nt][2];
+        }
+    }
+    if constexpr (TP <= 2) {
+#pragma unroll
+        for (int nt = 0; nt < NT; ++nt)
+#pragma unroll
+            for (int i = 0; i < 4; ++i) {
+                acc[nt][i] += __shfl_xor_sync(0xffffffffu, acc[nt][i], 1);
+                acc[nt][i] += __shfl_xor_sync(0xffffffffu, acc[nt][i], 2);
+            }
+    } else if constexpr (TP == 4) {
+#pragma unroll
+        for (int nt = 0; nt < NT; ++nt)
+#pragma unroll
+            for (int i = 0; i < 4; ++i) acc[nt][i] += __shfl_xor_sync(0xffffffffu, acc[nt][i], 2);
+    }
 
-    // Reduce the warps' partial fragments; then either store Y directly (one
-    // K slice) or publish the partial and let the tile's last CTA finish.
+    // Reduce the warps' fragments; then either store Y directly (one K slice)
+    // or publish the partial and let the tile's last CTA finish.
 #pragma unroll
     for (int nt = 0; nt < NT; ++nt)
 #pragma unroll
         for (int i = 0; i < 4; ++i) red[warp][lane][4 * nt + i] = acc[nt][i];
     __syncthreads();
     __shared__ uint32_t last;
-    float v[4 * NT];
     if (warp == 0) {
+        float v[4 * NT];
 #pragma unroll
         for (int j = 0; j < 4 * NT; ++j) {
-            float s = 0.f;
+            float sum = 0.f;
 #pragma unroll
-            for (int ww = 0; ww < kWarps; ++ww) s += red[ww][lane][j];
-            v[j] = s;
+            for (int ww2 = 0; ww2 < kWarps; ++ww2) sum += red[ww2][lane][j];
+            v[j] = sum;
         }
+        bool store = n_slices == 1;
         if (n_slices > 1) {
             // partials[slice][tile][lane][4*NT]
             float *dst = partials + (((uint64_t)blockIdx.y * gridDim.x + blockIdx.x) * 32 + lane) * (4 * NT);
@@ -269,16 +444,20 @@ __global__ void __launch_bounds__(kWarps * 32) gemv_kernel(WeightView w, const u
                     for (int j = 0; j < 4 * NT; ++j) v[j] += __ldcg(src + j);
                 }
                 if (lane == 0) counters[blockIdx.x] = 0u;
+                store = true;
             }
         }
-        if (n_slices == 1 || last) {
+        if (store) {
 #pragma unroll
             for (int nt = 0; nt < NT; ++nt) {
 #pragma unroll
                 for (int i = 0; i < 4; ++i) {
-                    const uint32_t tok = 8 * nt + 2 * t + (i & 1);
+                    // column 2t + (i & 1) carries token (column % TP); the lanes
+                    // whose column < TP are the designated writers
+                    const uint32_t col = 2 * t + (i & 1);
+                    const uint32_t tok = 8 * nt + col % TP;
                     const uint32_t row = row0 + g + 8 * (i >> 1);
-                    if (tok < m_count && row < w.n) {
+                    if (col < TP && tok < m_count && row < w.n) {
                         const uint64_t off = (uint64_t)(m_begin + tok) * ldy + row;
                         if (DT == 0) static_cast<float *>(y)[off] = v[4 * nt + i];
                         else static_cast<__nv_bfloat16 *>(y)[off] = __float2bfloat16_rn(v[4 * nt + i]);
@@ -289,28 +468,55 @@ __global__ void __launch_bounds__(kWarps * 32) gemv_kernel(WeightView w, const u
     }
 }
 
-template <int TYPE, int NT>
+template <int TYPE, int TP, int NT>
 cudaError_t launch_typed(const SegmentView &seg, const uint16_t *x, uint64_t k, void *y, uint64_t ldy,
                          int out_dtype, const GemvSplit &sp, cudaStream_t s) {
     const dim3 grid((seg.w.n + 15) / 16, sp.n_slices);
     const uint32_t mc = seg.m_end - seg.m_begin;
-    if (out_dtype == 0)
-        gemv_kernel<TYPE, NT, 0><<<grid, kWarps * 32, 0, s>>>(seg.w, x, seg.m_begin, mc, k, y, ldy, sp.kb_per_slice,
-                                                               sp.partials, sp.counters);
-    else
-        gemv_kernel<TYPE, NT, 2><<<grid, kWarps * 32, 0, s>>>(seg.w, x, seg.m_begin, mc, k, y, ldy, sp.kb_per_slice,
-                                                               sp.partials, sp.counters);
-    return cudaGetLastError();
+    const size_t stage = (StageGeo<TYPE>::w_bytes + (size_t)mc * 512 + 127) / 128 * 128;
+    const size_t smem = stage * kGemvStages * kWarps;
+    auto kern = out_dtype == 0 ? gemv_kernel<TYPE, TP, NT, 0> : gemv_kernel<TYPE, TP, NT, 2>;
+    // Opt in once per instantiation to the largest stage set (16 tokens).
+    static bool configured[2] = {false, false};
+    if (!configured[out_dtype == 0]) {
+        const int most = (int)((StageGeo<TYPE>::w_bytes + 16 * 512 + 127) / 128 * 128 * kGemvStages * kWarps);
+        cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, most);
+        if (e != cudaSuccess) return e;
+        configured[out_dtype == 0] = true;
+    }
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = grid;
+    cfg.blockDim = dim3(kWarps * 32);
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = s;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    return cudaLaunchKernelEx(&cfg, kern, seg.w, x, seg.m_begin, mc, k, y, ldy, sp.kb_per_slice, sp.partials,
+                              sp.counters, sp.status);
+}
+
+template <int TYPE>
+cudaError_t launch_m(const SegmentView &seg, const uint16_t *x, uint64_t k, void *y, uint64_t ldy, int out_dtype,
+                     const GemvSplit &sp, cudaStream_t s) {
+    const uint32_t m = seg.m_end - seg.m_begin;
+    if (m <= 1) return launch_typed<TYPE, 1, 1>(seg, x, k, y, ldy, out_dtype, sp, s);
+    if (m <= 2) return launch_typed<TYPE, 2, 1>(seg, x, k, y, ldy, out_dtype, sp, s);
+    if (m <= 4) return launch_typed<TYPE, 4, 1>(seg, x, k, y, ldy, out_dtype, sp, s);
+    if (m <= 8) return launch_typed<TYPE, 8, 1>(seg, x, k, y, ldy, out_dtype, sp, s);
+    return launch_typed<TYPE, 8, 2>(seg, x, k, y, ldy, out_dtype, sp, s);
 }
 
 }  // namespace
 
 GemvSplit gemv_split(const WeightView &w) {
-    // Aim for >= 8 CTAs per SM of work, one super-block per warp (K slices of
-    // 4 super-blocks); two per warp when the grid is large anyway.
+    // K slices of 16 super-blocks (4 per warp, pipelined), fewer when the
+    // grid would not fill the machine.
     const uint32_t tiles = (w.n + 15) / 16;
-    uint32_t per = 4;
-    if ((uint64_t)tiles * ((w.kb + 7) / 8) >= 148u * 8u) per = 8;
+    uint32_t per = 16;
+    while (per > kWarps && (uint64_t)tiles * ((w.kb + per - 1) / per) < 148u * 3u) per /= 2;
     GemvSplit sp;
     sp.kb_per_slice = per;
     sp.n_slices = (w.kb + per - 1) / per;
@@ -328,11 +534,8 @@ cudaError_t launch_gemv(const SegmentView &seg, const uint16_t *x, uint64_t k, v
     const uint32_t m = seg.m_end - seg.m_begin;
     if (m > 16) return cudaErrorInvalidValue;
     if (sp.n_slices > 1 && (!sp.partials || !sp.counters)) return cudaErrorInvalidValue;
-    if (seg.w.type == 12)
-        return m <= 8 ? launch_typed<12, 1>(seg, x, k, y, ldy, out_dtype, sp, s)
-                      : launch_typed<12, 2>(seg, x, k, y, ldy, out_dtype, sp, s);
-    return m <= 8 ? launch_typed<14, 1>(seg, x, k, y, ldy, out_dtype, sp, s)
-                  : launch_typed<14, 2>(seg, x, k, y, ldy, out_dtype, sp, s);
+    return seg.w.type == 12 ? launch_m<12>(seg, x, k, y, ldy, out_dtype, sp, s)
+                            : launch_m<14>(seg, x, k, y, ldy, out_dtype, sp, s);
 }
 
 }  // namespace tc

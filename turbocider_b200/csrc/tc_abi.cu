@@ -353,6 +353,7 @@ int tc_cuda_qlinear(tc_cuda_ctx *ctx, const tc_cuda_weight *const *weights, uint
     }
     for (const auto &sv : gemv) {
         tc::GemvSplit sp = tc::gemv_split(sv.w);
+        sp.status = ctx->status;
         if (sp.n_slices > 1) {
             int rc = ensure_gemv_workspace(ctx, tc::gemv_workspace_floats(sv.w), (sv.w.n + 15) / 16);
             if (rc) return rc;

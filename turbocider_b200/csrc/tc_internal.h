@@ -57,6 +57,7 @@ struct GemvSplit {
     uint32_t kb_per_slice = 0, n_slices = 1;
     float *partials = nullptr;
     uint32_t *counters = nullptr;
+    uint32_t *status = nullptr;
 };
 GemvSplit gemv_split(const WeightView &w);
 size_t gemv_workspace_floats(const WeightView &w);
