@@ -142,6 +142,22 @@ int tc_cuda_qlinear(tc_cuda_ctx *ctx, const tc_cuda_weight *const *weights, uint
  *   0 automatic, 1 warp GEMV (any M), 2 tensor-core GEMM (any M). */
 int tc_cuda_set_path(tc_cuda_ctx *ctx, int path);
 
+/* Allocation-free small-M quantised linear.  No counterpart in the reference.
+ * For callers that must not allocate device memory while they run a linear
+ * (a pre-sized memory arena, code under an allocator callback, a loop that
+ * cannot take cudaMalloc's implicit synchronisation): computes
+ * Y[m, N] = X[m, K] * W^T for 1 <= m <= 16 with the split-K GEMV of
+ * tc_cuda_qlinear, whose scratch (K-slice partials, per-tile counters, status
+ * word) here lives in a 4 MiB file-scope device array instead of a cudaMalloc'd
+ * context workspace.  No context argument; X bf16 [m, K] (16-byte aligned), Y
+ * f32 or bf16 with row stride ldy (0 = N), all device memory, enqueued on
+ * `stream`.  The first call on a device looks up the array's address (make it
+ * before any stream capture); shapes whose scratch exceeds 4 MiB are rejected;
+ * every call shares the array, so calls that may overlap on the GPU must be
+ * serialised by the caller.  Allocates nothing. */
+int tc_cuda_qlinear_small_static(const tc_cuda_weight *weight, const void *x, uint32_t m, void *y, uint64_t ldy,
+                                 int out_dtype, void *stream);
+
 /* Host-side GGUF K-quant quantiser (not in the reference, which ships no
  * encoder): quantise a row-major fp32 [rows, cols] matrix (cols % 256 == 0) to
  * raw GGUF blocks of `ggml_type` (Q4_K or Q6_K) using `threads` CPU threads.

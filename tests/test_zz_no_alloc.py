@@ -1,0 +1,56 @@
+"""GPU test of the allocation-free entry point tc_cuda_qlinear_small_static.
+
+It serves callers that cannot allocate device memory while running a linear
+(pre-sized memory arenas, allocator callbacks, loops that cannot absorb
+cudaMalloc's synchronisation): the split-K GEMV runs with its scratch in a
+fixed static device array.  Its output must match the existing entry point
+(tc_cuda_qlinear, same kernel with a cudaMalloc'd workspace) within the GEMV
+tolerance used elsewhere (rel-L2 <= 1e-5), on two calls in a row -- the second
+call sees the array as the first one left it.  This file is collected last.
+"""
+from __future__ import annotations
+
+import numpy as np
+import pytest
+
+import kq_cases
+from oracle import oracle
+
+pytestmark = pytest.mark.gpu
+
+
+@pytest.mark.parametrize("typ,n,k,m", [(14, 3072, 12288, 4), (12, 1000, 4096, 1), (14, 512, 2048, 16),
+                                       (12, 2048, 3072, 2)])
+def test_static_scratch_matches_qlinear_twice(ctx, typ, n, k, m):
+    import torch
+    from turbocider_b200 import cuda as tcc
+    raw = tcc.quantize(typ, kq_cases.synthetic_weight(n, k, seed=n + m))
+    w = tcc.Weight.upload(ctx, typ, n, k, raw)
+    xb = kq_cases.synthetic_x_bf16(m, k, seed=m + 3)
+    x = torch.from_numpy(xb.view(np.int16)).view(torch.bfloat16).cuda()
+    ref = tcc.qlinear(ctx, w, x, out_dtype=tcc.F32).cpu().numpy()
+    for _ in range(2):
+        y = torch.full((m, n), float("nan"), device="cuda", dtype=torch.float32)
+        tcc.qlinear_small_static(w, x, out_dtype=tcc.F32, out=y)
+        torch.cuda.synchronize()
+        got = y.cpu().numpy()
+        assert np.isfinite(got).all()
+        assert oracle.rel_l2(got, ref) <= 1e-5
+    yb = tcc.qlinear_small_static(w, x, out_dtype=tcc.BF16)
+    assert oracle.rel_l2(yb.float().cpu().numpy(), ref) <= 3e-3
+    assert ctx.status() == 0
+
+
+def test_static_scratch_rejects_oversize_and_bad_rows(ctx):
+    import torch
+    from turbocider_b200 import cuda as tcc
+    # 22016 rows x K 8448 needs 3 K slices x 1376 row tiles of partials: > 4 MiB
+    n, k = 22016, 8448
+    raw = tcc.quantize(12, kq_cases.synthetic_weight(n, k, seed=5))
+    w = tcc.Weight.upload(ctx, 12, n, k, raw)
+    x = torch.zeros(1, k, device="cuda", dtype=torch.bfloat16)
+    with pytest.raises(tcc.BackendError, match="static scratch holds"):
+        tcc.qlinear_small_static(w, x)
+    x17 = torch.zeros(17, k, device="cuda", dtype=torch.bfloat16)
+    with pytest.raises(tcc.BackendError, match="1..16 rows"):
+        tcc.qlinear_small_static(w, x17)

@@ -87,6 +87,8 @@ int ensure_gemv_workspace(tc_cuda_ctx *ctx, size_t floats, size_t counters) {
 
 }  // namespace
 
+void tc::set_last_error(const std::string &reason) { g_error = reason; }
+
 extern "C" {
 
 uint32_t tc_cuda_abi_version(void) { return TC_CUDA_ABI_VERSION; }

@@ -2,6 +2,7 @@
 // launchers.  Nothing here crosses the public ABI.
 #pragma once
 #include <cstdint>
+#include <string>
 #include <cuda_runtime.h>
 
 struct tc_cuda_ctx {
@@ -28,6 +29,9 @@ struct tc_cuda_weight {
 };
 
 namespace tc {
+
+// Sets the thread-local message returned by tc_cuda_last_error().
+void set_last_error(const std::string &reason);
 
 // Geometry handed to the kernels for one weight.
 struct WeightView {

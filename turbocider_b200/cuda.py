@@ -54,6 +54,7 @@ EXPORTS = {
                                   _u64, C.c_int, C.c_int, _vp]),
     "tc_cuda_set_path": (C.c_int, [_vp, C.c_int]),
     "tc_quantize": (C.c_int, [_u32, _vp, _u64, _u64, _vp, _u64, C.c_int]),
+    "tc_cuda_qlinear_small_static": (C.c_int, [_vp, _vp, _u32, _vp, _u64, C.c_int, _vp]),
 }
 
 
@@ -225,4 +226,16 @@ def qlinear(ctx: Context, weights, x, seg_offsets=None, seg_weight=None, out_dty
                           device=x.device)
     _check(lib().tc_cuda_qlinear(ctx.handle, handles, len(ws), offs, sw, n_seg, x.data_ptr(), out.data_ptr(),
                                  out.stride(0), out_dtype, stage, _stream_ptr(stream)))
+    return out
+
+
+def qlinear_small_static(weight: Weight, x, out_dtype: int = BF16, out=None, stream=None):
+    """Y = X * W^T for 1..16 rows of X through the allocation-free entry point
+    (static device scratch instead of a context workspace)."""
+    import torch
+    if out is None:
+        out = torch.empty((x.shape[0], weight.n), dtype=torch.float32 if out_dtype == F32 else torch.bfloat16,
+                          device=x.device)
+    _check(lib().tc_cuda_qlinear_small_static(weight.handle, x.data_ptr(), x.shape[0], out.data_ptr(),
+                                              out.stride(0), out_dtype, _stream_ptr(stream)))
     return out
