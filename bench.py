@@ -137,7 +137,7 @@ def run_reference(args):
         return 0
     threads = os.cpu_count() or 1
     linears = make_cpu_linears(0)
-    m_sample = args.cpu_rows
+    m_sample = args.cpu_rows or 2048
     for _ in range(args.warmup):
         cpu_reference_sample(m_sample, linears, threads)
     times, flops, kind = [], 0.0, "port"
@@ -357,10 +357,17 @@ def run_ours(args):
     cpu = None
     if rank == 0 and world == 1 and not args.no_extras:
         gemv = gemv_measure(ctx, device, hbm_peak)
-        t, f, kind = cpu_reference_sample(args.cpu_rows, make_cpu_linears(0), os.cpu_count() or 1)
-        cpu = {"value": round(f / t / 1e12, 4), "unit": "TFLOPS", "cores": os.cpu_count() or 1, "kind": kind,
+        # bounded CPU sample: layer 0 at cpu_rows rows, repeated until >= 10 s of work
+        linears, threads = make_cpu_linears(0), os.cpu_count() or 1
+        cpu_rows = args.cpu_rows or M_TOKENS
+        t = f = 0.0
+        reps = 0
+        while t < 10.0 and reps < 20:
+            dt, df, kind = cpu_reference_sample(cpu_rows, linears, threads)
+            t, f, reps = t + dt, f + df, reps + 1
+        cpu = {"value": round(f / t / 1e12, 4), "unit": "TFLOPS", "cores": threads, "kind": kind,
                "sample": f"layer 0 of the stack (5 linears): decode_cpu_into->f32 + fp32 torch matmul at "
-                         f"{args.cpu_rows} of {M_TOKENS} rows; {t:.1f} s"}
+                         f"{cpu_rows} of {M_TOKENS} rows, {reps} repetitions, {t:.1f} s"}
 
     traffic = None
     tfile = ROOT / "profiles" / "gemm_traffic.json"
@@ -408,7 +415,8 @@ def main():
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--layers", type=int, default=LAYERS)
-    ap.add_argument("--cpu-rows", type=int, default=1024)
+    ap.add_argument("--cpu-rows", type=int, default=None,
+                    help="rows of X in the CPU sample (default: 2048 per reference-arm step, all rows for cpu_baseline)")
     ap.add_argument("--no-extras", action="store_true", help="skip the GEMV and CPU-baseline legs")
     args = ap.parse_args()
     if args.warmup < 3 and args.impl == "ours":
