@@ -89,7 +89,7 @@ int tc_cuda_weight_upload(tc_cuda_ctx *ctx, uint32_t ggml_type, uint64_t n, uint
                           uint64_t n_count, tc_cuda_weight **weight);
 
 /* As tc_cuda_weight_upload, but the raw rows are already in device memory
- * (e.g. a staging slot filled by tc_cuda_stage_copy) and the re-layout is
+ * (e.g. a staging buffer the caller filled with cudaMemcpyAsync) and the re-layout is
  * enqueued on `stream` without synchronising.  `weight` must have been
  * created by tc_cuda_weight_create with the same type and shape. */
 int tc_cuda_weight_create(tc_cuda_ctx *ctx, uint32_t ggml_type, uint64_t n, uint64_t k,
@@ -132,14 +132,16 @@ int tc_cuda_decode(tc_cuda_ctx *ctx, uint32_t ggml_type, const void *source, uin
  *   seg_weight   int32 [n_seg] host array: which weight segment s uses (e.g.
  *            image vs text stream);  NULL = weight 0 for every segment.
  * Dispatch: the warp GEMV for segments with at most 16 rows, the tcgen05
- * tensor-core GEMM otherwise.  `stage` selects the GEMM's operand precision
+ * tensor-core GEMM otherwise (2-CTA 256 x 256 tiles once a segment has more
+ * than 128 rows).  `stage` selects the GEMM's operand precision
  * (TC_STAGE_BF16 uses X as given; TC_STAGE_F16 converts X to fp16 first). */
 int tc_cuda_qlinear(tc_cuda_ctx *ctx, const tc_cuda_weight *const *weights, uint32_t n_weights,
                     const int32_t *seg_offsets, const int32_t *seg_weight, uint32_t n_seg,
                     const void *x, void *y, uint64_t ldy, int out_dtype, int stage, void *stream);
 
 /* Force one kernel family for a call (testing and benchmarking):
- *   0 automatic, 1 warp GEMV (any M), 2 tensor-core GEMM (any M). */
+ *   0 automatic, 1 warp GEMV (any M), 2 tensor-core GEMM (any M),
+ *   3 tensor-core GEMM with one-CTA tiles only (no 2-CTA pairs). */
 int tc_cuda_set_path(tc_cuda_ctx *ctx, int path);
 
 /* Allocation-free small-M quantised linear.  No counterpart in the reference.

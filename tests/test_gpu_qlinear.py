@@ -75,15 +75,44 @@ def test_gemm_fp16_staging_meets_1e3_vs_f32_decode(ctx, typ):
     assert e <= 1e-3
 
 
+@pytest.mark.parametrize("path", [2, 3])
 @pytest.mark.parametrize("typ", [12, 14])
 @pytest.mark.parametrize("m,n,k", [(17, 200, 512), (129, 384, 1024), (300, 256, 768), (64, 130, 256),
-                                   (1000, 640, 2560)])
-def test_gemm_ragged_edges(ctx, typ, m, n, k):
-    """M and N not multiples of the tile, every BN variant (64/128/256)."""
+                                   (1000, 640, 2560), (520, 1920, 512)])
+def test_gemm_ragged_edges(ctx, typ, m, n, k, path):
+    """M and N not multiples of the tile: every one-CTA BN variant (64/128/256,
+    path 3) and the 2-CTA 256 x 256 tile (path 2, M > 128), including odd panel
+    counts (N = 384, 640, 1920 -> 3, 5, 15 panels of 128 rows)."""
     from turbocider_b200 import cuda as tcc
     raw, w, xb, x = _setup(ctx, typ, n, k, m, wseed=m + n)
-    y = _run(ctx, w, x, tcc.F32, path=2)
+    y = _run(ctx, w, x, tcc.F32, path=path)
     assert oracle.rel_l2(y, oracle.qlinear_ref(xb, raw, typ, n, k, "bf16")) <= TIGHT
+
+
+@pytest.mark.parametrize("typ", [12, 14])
+@pytest.mark.parametrize("ldy", [640, 648, 645])
+def test_gemm_bf16_out_row_stride(ctx, typ, ldy):
+    """bf16 output into a wider buffer (row stride ldy): TMA-stored tiles when
+    the row pitch is a multiple of 16 bytes (640, 648), plain stores otherwise
+    (645); columns past N stay untouched."""
+    import torch
+    from turbocider_b200 import cuda as tcc
+    m, n, k = 300, 640, 768
+    raw, w, xb, x = _setup(ctx, typ, n, k, m, wseed=ldy)
+    big = torch.full((m, ldy), 7.0, dtype=torch.bfloat16, device=x.device)
+    out = big[:, :n]
+    tcc.qlinear(ctx, w, x, out=out)
+    assert ctx.status() == 0
+    y = out.float().cpu().numpy().astype(np.float64)
+    assert oracle.rel_l2(y, oracle.qlinear_ref(xb, raw, typ, n, k, "bf16")) <= 3e-3
+    if ldy > n:
+        assert bool((big[:, n:] == 7.0).all())
+    ctx.set_path(3)
+    try:
+        y1 = tcc.qlinear(ctx, w, x).float().cpu().numpy().astype(np.float64)
+    finally:
+        ctx.set_path(0)
+    assert oracle.rel_l2(y, y1) <= 3e-3
 
 
 @pytest.mark.parametrize("typ", [12, 14])
@@ -153,3 +182,25 @@ def test_full_size_config5_sampled_rows(ctx, typ, n, k):
     rows = np.random.default_rng(0).choice(m, 64, replace=False)
     ref = oracle.qlinear_ref(xb[rows], raw, typ, n, k, "bf16")
     assert oracle.rel_l2(y[rows], ref) <= TIGHT
+
+
+@pytest.mark.parametrize("typ", [12, 14])
+@pytest.mark.parametrize("m", [64, 300])
+def test_gemm_f16_staging_range_check(ctx, typ, m):
+    """fp16 staging flags TC_STATUS_F16_OVERFLOW when a sub-block's values
+    can leave the fp16 range (d = 65504), and stays quiet for in-range scales
+    and for bf16 staging; m = 64 runs the one-CTA kernel, m = 300 the pair."""
+    import torch
+    from turbocider_b200 import cuda as tcc
+    k = 1024
+    x = torch.randn(m, k, device="cuda").to(torch.bfloat16)
+    for scale, expect in ((65504.0, True), (0.03125, False)):
+        raw = np.frombuffer(kq_cases.extreme_case(typ, scale), dtype=np.uint8)
+        raw = np.tile(raw.reshape(2, -1), (128, 1)).reshape(-1)   # 256 rows x 1024
+        w = tcc.Weight.upload(ctx, typ, 256, k, raw)
+        tcc.qlinear(ctx, w, x, stage=tcc.STAGE_F16, out_dtype=tcc.F32)
+        bits = ctx.status()
+        assert bool(bits & tcc.STATUS_F16_OVERFLOW) == expect, (scale, bits)
+        tcc.qlinear(ctx, w, x, stage=tcc.STAGE_BF16, out_dtype=tcc.F32)
+        assert ctx.status() == 0
+        w.free()

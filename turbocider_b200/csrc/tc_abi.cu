@@ -285,7 +285,7 @@ int tc_cuda_decode(tc_cuda_ctx *ctx, uint32_t type, const void *source, uint64_t
 
 int tc_cuda_set_path(tc_cuda_ctx *ctx, int path) {
     if (!ctx) return fail("null context");
-    if (path < 0 || path > 2) return fail("invalid path selector");
+    if (path < 0 || path > 3) return fail("invalid path selector");
     ctx->path = path;
     return ok();
 }
@@ -329,7 +329,7 @@ int tc_cuda_qlinear(tc_cuda_ctx *ctx, const tc_cuda_weight *const *weights, uint
         const tc_cuda_weight *w = weights[seg_weight ? seg_weight[i] : 0];
         const tc::SegmentView sv{b, e, view_of(w)};
         const bool small = (e - b) <= 16;
-        if ((small && ctx->path != 2) || ctx->path == 1) {
+        if ((small && ctx->path < 2) || ctx->path == 1) {
             // The GEMV handles at most 16 rows per launch; longer forced
             // segments are cut into 16-row pieces.
             for (uint32_t m = b; m < e; m += 16) gemv.push_back({m, std::min(e, m + 16), sv.w});
@@ -349,7 +349,8 @@ int tc_cuda_qlinear(tc_cuda_ctx *ctx, const tc_cuda_weight *const *weights, uint
         for (size_t i = 0; i < gemm[t].size(); i += 32) {
             const uint32_t cnt = (uint32_t)std::min<size_t>(32, gemm[t].size() - i);
             cudaError_t e = tc::launch_gemm(gemm[t].data() + i, cnt, xg, m_total, k, y, ldy, out_dtype,
-                                            stage == TC_STAGE_F16, ctx->sm_count, ctx->status, s);
+                                            stage == TC_STAGE_F16, ctx->sm_count, ctx->status,
+                                            ctx->path != 3, s);
             if (e != cudaSuccess) return cuda_fail("GEMM launch", e);
         }
     }

@@ -15,7 +15,7 @@ struct tc_cuda_ctx {
     size_t gemv_partials_floats = 0;
     uint32_t *gemv_counters = nullptr;  // per-16-row-tile arrival counters, kept at 0
     size_t gemv_counters_n = 0;
-    int path = 0;                    // 0 auto, 1 GEMV, 2 GEMM
+    int path = 0;                    // 0 auto, 1 GEMV, 2 GEMM, 3 GEMM with one-CTA tiles only
 };
 
 struct tc_cuda_weight {
@@ -69,9 +69,14 @@ cudaError_t launch_gemv(const SegmentView &seg, const uint16_t *x, uint64_t k, v
                         uint64_t ldy, int out_dtype, const GemvSplit &split, cudaStream_t s);
 cudaError_t launch_x_to_f16(const uint16_t *x, uint16_t *x16, uint64_t count, uint32_t *status,
                             cudaStream_t s);
-// Tensor-core GEMM over a list of segments that share type, N and K.
+// Tensor-core GEMM over a list of segments that share type, N and K.  Uses
+// 2-CTA (cta_group::2) 256 x 256 tiles when a segment has more than 128 rows
+// and allow_pair is set, one-CTA 128 x {64, 128, 256} tiles otherwise.
 cudaError_t launch_gemm(const SegmentView *segs, uint32_t n_seg, const uint16_t *x,
                         uint64_t m_total, uint64_t k, void *y, uint64_t ldy, int out_dtype,
-                        int stage_f16, int sm_count, uint32_t *status, cudaStream_t s);
+                        int stage_f16, int sm_count, uint32_t *status, int allow_pair, cudaStream_t s);
+cudaError_t launch_gemm_pair(const SegmentView *segs, uint32_t n_seg, const uint16_t *x,
+                             uint64_t m_total, uint64_t k, void *y, uint64_t ldy, int out_dtype,
+                             int stage_f16, uint32_t *status, cudaStream_t s);
 
 }  // namespace tc
