@@ -1,40 +1,51 @@
-// Quantised GEMM on CTA pairs (tcgen05 cta_group::2, sm_100a):
+// Quantised GEMM on CTA pairs with the weight operand in tensor memory
+// (tcgen05 cta_group::2, sm_100a):
 //     Y[m, n] = sum_k X[m, k] * W[n, k],  W in GGUF Q4_K / Q6_K, X bf16 (or fp16).
 //
-// A cluster of two CTAs computes one 256-token x 256-weight-row tile with
-// MMAs of shape M = 256 (tokens) x N = 256 (weight rows) x K = 16, issued by a
-// single thread of CTA 0 (the leader) for both SMs:
-//   A = activations, K-major, 128-byte swizzle: each CTA holds its own 128
-//       tokens x 64 K per stage, loaded by TMA;
-//   B = dequantised weights: each CTA unpacks its own 128-row weight panel
-//       (one packed chunk = 128 rows x 256 K) into the swizzled bf16 tile, bit-
-//       exact to the reference decoder; the MMA reads B's halves from both CTAs.
-// Compared with a one-CTA 128 x 256 tile doing the same MMA work per SM, each
-// CTA streams half the activation bytes from L2 per stage (16 KB instead of
-// 32 KB), which leaves room for a 4-deep pipeline in shared memory.
-// D lands in each CTA's TMEM as [128 lanes = its tokens] x [256 columns =
-// weight rows], two accumulators of 256 columns each (all 512 TMEM columns),
-// so the epilogue of tile i overlaps the main loop of tile i+1.  An epilogue
-// thread owns one token and 32 consecutive outputs per TMEM load: it packs
-// them into a 64-byte-swizzled staging tile and the warp writes whole lines
-// with a TMA store (plain stores for f32 output and ragged edges).
+// A cluster of two CTAs computes one 256-weight-row x 256-token tile with
+// MMAs of shape M = 256 (weight rows) x N = 256 (tokens) x K = 16, issued by
+// one thread of CTA 0 (the leader) for both SMs:
+//   A = dequantised weights, in TMEM: each CTA holds its own 128-row weight
+//       panel as 128 lanes x 32 columns (64 K of bf16 / fp16 pairs) per stage,
+//       written by the dequant warps with tcgen05.st straight from registers;
+//   B = activations, in shared memory: each CTA loads its own 128 tokens x 64 K
+//       per stage by TMA (K-major, 128-byte swizzle); the MMA reads both halves.
+// Unpacked weights never touch shared memory.  Per 64-K stage an SM's shared
+// memory serves only the activation copy and its MMA read (16 KB each), the
+// packed bytes (about 4.5 KB) and the dequant warps' code reads; with the
+// weight tile staged in shared memory instead, its stores and MMA reads made
+// the shared-memory pipe, not the tensor core, the limit.
+//
+// TMEM (512 columns per CTA): columns 0-255 hold the accumulator D as
+// [128 lanes = this CTA's weight rows] x [256 columns = the tile's tokens];
+// columns 256-447 hold a 6-slot ring of A stages (32 columns each).  There is
+// room for one accumulator only: the epilogue copies it to a shared-memory
+// staging area (tcgen05.ld, then 2-byte stores that are conflict-free because
+// a warp's 32 lanes hold 32 consecutive outputs of one token), releases it to
+// the MMA right away, and writes Y from the staging area with TMA stores while
+// the next tile accumulates.  (Splitting each k-step into two N = 128 MMAs to
+// double-buffer halves of D measured slower than this single short stall.)
+//
+// Dequant mapping: one thread per weight row.  The 16 dequant warps form four
+// groups of four (one warp per TMEM lane quarter); group q unpacks the q-th
+// 64-K quarter of every packed chunk (128 rows x 256 K), 64 weights per thread,
+// reading its sub-block scales directly from the packed bytes -- bit-exact to
+// the reference decoder (native/core/gguf_decode.cpp:77-105).
 //
 // Warp roles (22 warps, both CTAs):
-//   warp 0     producer: bulk copy of the packed chunk, TMA of the activations;
-//   warp 1     TMEM allocator (cta_group::2, both CTAs); in the leader, the
-//              MMA-issuing thread;
-//   warps 2-5  epilogue;
+//   warp 0     producer: bulk copy of each packed chunk, TMA of the activations;
+//   warp 1     TMEM allocator (cta_group::2); in the leader, the MMA-issuing
+//              thread; in the peer, a relay that forwards "this CTA's stage is
+//              complete" to the leader's `full` barrier (one remote arrival per
+//              stage, kept off the dequant warps);
+//   warps 2-5  epilogue: tcgen05.ld of 32 tokens per thread-row, stores of Y;
 //   warps 6-21 dequantisers.
-// Per stage, each CTA's dequant warps arrive on a local `dq_done` barrier and
-// its activation copy completes a local `x_full`; the leader's MMA thread
-// waits on its own two barriers and on `full`, to which the peer CTA's warp 1
-// relays one remote arrival per stage once the peer's two barriers complete
-// (a remote arrival takes a DSMEM round trip; keeping it off the dequant
-// warps keeps them unpacking).  The leader's MMA completion is committed to
-// both CTAs' barriers (tcgen05.commit with a CTA mask).  No TMA load uses cluster multicast: every copy lands in the CTA
-// that issued it and signals that CTA's own barrier.  Every wait is bounded;
-// on timeout both CTAs raise their abort flags, set TC_STATUS_TIMEOUT, drain
-// their own copies and MMAs, free TMEM and return.
+// The leader's MMA completion is committed to both CTAs' barriers
+// (tcgen05.commit with a CTA mask).  No TMA load uses cluster multicast:
+// every copy lands in the CTA that issued it and signals that CTA's own
+// barrier.  Every wait is bounded; on timeout both CTAs raise their abort
+// flags, set TC_STATUS_TIMEOUT, drain their own copies and MMAs, free TMEM and
+// return.
 #include <cuda.h>
 #include <cudaTypedefs.h>
 
@@ -47,12 +58,13 @@ namespace tc {
 namespace {
 
 constexpr int kThreads = 704;
-constexpr int kDequantWarp0 = 6, kDequantWarps = 16, kDequantThreads = 512;
+constexpr int kDequantWarp0 = 6, kDequantWarps = 16;
 constexpr int kEpiWarps = 4;
-constexpr int kStages = 4;       // activation + B-tile pipeline depth (64 K each)
-constexpr int kWStages = 2;      // packed chunk pipeline depth (256 K each)
+constexpr int kStages = 6;       // activation (smem) + A (TMEM) ring, 64 K per stage
+constexpr int kWStages = 2;      // packed chunk ring (256 K per chunk)
 constexpr int kMaxSeg = 32;
-constexpr uint32_t kTileM = 256, kHalfM = 128, kTileN = 256;
+constexpr uint32_t kTileRows = 256, kTileTokens = 256, kHalf = 128;
+constexpr uint32_t kACol0 = 256, kAStageCols = 32;
 
 struct PairSeg {
     uint32_t m_begin, m_end, tile_begin, pad;
@@ -64,28 +76,21 @@ struct PairParams {
     void *y;
     uint64_t ldy;
     uint32_t *status;
-    uint32_t y_tma;   // bf16 Y through TMA stores (16-byte aligned base and row pitch)
-    uint32_t y_vec;   // 16-byte vector stores allowed on the plain-store path
+    uint32_t y_tma;   // bf16 Y written by TMA stores (16-byte aligned base and row pitch)
 };
 
 template <int TYPE>
 struct PairLayout {
-    static constexpr uint32_t x_stage = kHalfM * 128;   // 128 tokens x 64 K x 2 B
-    static constexpr uint32_t b_stage = 128 * 128;      // 128 weight rows x 64 K x 2 B
-    static constexpr uint32_t e_piece = 32 * 64;        // 32 tokens x 32 outputs x 2 B
-    static constexpr uint32_t e_bufs = TYPE == 12 ? 2 : 1;   // per epilogue warp (Q6_K: smem-bound)
+    static constexpr uint32_t x_stage = kHalf * 128;   // 128 tokens x 64 K x 2 B
     static constexpr uint32_t w_stage = chunk_bytes(TYPE);
     static constexpr uint32_t x_off = 0;
-    static constexpr uint32_t b_off = x_off + kStages * x_stage;
-    static constexpr uint32_t e_off = b_off + kStages * b_stage;
-    static constexpr uint32_t w_off = e_off + kEpiWarps * e_bufs * e_piece;
-    static constexpr uint32_t t_off = (w_off + kWStages * w_stage + 127) / 128 * 128;
-    static constexpr uint32_t table_bytes = 128 * 80;
-    static constexpr uint32_t n_tables = 3;
-    static constexpr uint32_t bar_off = t_off + n_tables * table_bytes;
-    // x_full[S] dq_done[S] full[S] st_empty[S] w_full[W] w_empty[W] t_ready[3]
-    // acc_full[2] acc_empty[2] fin
-    static constexpr uint32_t n_bars = 4 * kStages + 2 * kWStages + n_tables + 5;
+    static constexpr uint32_t w_off = x_off + kStages * x_stage;
+    // Epilogue staging per warp: eight 32-token x 32-output bf16 boxes (16 KB).
+    static constexpr uint32_t e_box = 32 * 64, e_warp = 8 * e_box;
+    static constexpr uint32_t e_off = (w_off + kWStages * w_stage + 1023) / 1024 * 1024;
+    static constexpr uint32_t bar_off = e_off + kEpiWarps * e_warp;
+    // x_full[S] a_full[S] full[S] st_empty[S] w_full[W] w_empty[W] acc_full acc_empty fin
+    static constexpr uint32_t n_bars = 4 * kStages + 2 * kWStages + 3;
     static constexpr uint32_t misc_off = bar_off + n_bars * 8;
     static constexpr uint32_t bytes = misc_off + 16 + 1024;  // + alignment slack
     static constexpr uint32_t tmem_cols = 512;
@@ -105,16 +110,17 @@ __device__ __forceinline__ uint32_t cluster_addr(uint32_t saddr, uint32_t rank) 
     return r;
 }
 // Arrive on a barrier of either CTA of the pair (default .release.cta
-// semantics).  The data this arrival publishes is this CTA's own shared memory
-// (dequantised B tile, or TMEM already read back), which the CTA-scope release
-// has completed before the arrival is sent; a cluster-scope release would add
-// a full memory barrier (hundreds of cycles) to every pipeline stage.
+// semantics).  What the arrival publishes lives in the arriving CTA (its
+// activation stage and TMEM A stage, or TMEM already read back), completed
+// before the arrival is sent; a cluster-scope release would add a full memory
+// barrier to every stage.
 __device__ __forceinline__ void bar_arrive_cluster(uint32_t caddr) {
     asm volatile("mbarrier.arrive.shared::cluster.b64 _, [%0];" ::"r"(caddr) : "memory");
 }
 __device__ __forceinline__ void cluster_sync() {
     asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
 }
+
 // Abort state of one CTA: its own flag and the peer's flag (cluster address).
 struct Abort {
     volatile uint32_t *flag;
@@ -141,17 +147,18 @@ __device__ __forceinline__ bool pwait(uint32_t b, uint32_t parity, const Abort &
 }
 
 // Instruction descriptor, kind::f16, cta_group::2: D fp32, A/B bf16 (or fp16),
-// both K-major, M = 256, N = 256.
+// A from TMEM, B K-major, M = 256, N = 256.
 template <bool F16>
 __device__ __forceinline__ constexpr uint32_t pair_idesc() {
-    return (1u << 4) | ((F16 ? 0u : 1u) << 7) | ((F16 ? 0u : 1u) << 10) | ((kTileN >> 3) << 17) |
-           ((kTileM >> 4) << 24);
+    return (1u << 4) | ((F16 ? 0u : 1u) << 7) | ((F16 ? 0u : 1u) << 10) | ((kTileTokens >> 3) << 17) |
+           ((kTileRows >> 4) << 24);
 }
-__device__ __forceinline__ void mma_pair(uint32_t d_tmem, uint64_t a, uint64_t b, uint32_t idesc, uint32_t acc) {
+__device__ __forceinline__ void mma_pair_ts(uint32_t d_tmem, uint32_t a_tmem, uint64_t b, uint32_t idesc,
+                                            uint32_t acc) {
     asm volatile(
         "{\n .reg .pred p;\n setp.ne.b32 p, %4, 0;\n"
-        " tcgen05.mma.cta_group::2.kind::f16 [%0], %1, %2, %3, p;\n}\n"
-        ::"r"(d_tmem), "l"(a), "l"(b), "r"(idesc), "r"(acc));
+        " tcgen05.mma.cta_group::2.kind::f16 [%0], [%1], %2, %3, p;\n}\n"
+        ::"r"(d_tmem), "r"(a_tmem), "l"(b), "r"(idesc), "r"(acc));
 }
 // Arrive (once the leader's MMAs issued so far complete) on the barrier at
 // offset `b` in both CTAs of the pair.
@@ -160,18 +167,121 @@ __device__ __forceinline__ void commit_both(uint32_t b) {
         "tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.multicast::cluster.b64 [%0], %1;"
         ::"r"(b), "h"((uint16_t)3) : "memory");
 }
+// 16 consecutive 32-bit TMEM columns of this thread's lane.
+__device__ __forceinline__ void tmem_st16(uint32_t taddr, const uint32_t (&v)[16]) {
+    asm volatile(
+        "tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], {%1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, "
+        "%14, %15, %16};"
+        ::"r"(taddr), "r"(v[0]), "r"(v[1]), "r"(v[2]), "r"(v[3]), "r"(v[4]), "r"(v[5]), "r"(v[6]), "r"(v[7]),
+          "r"(v[8]), "r"(v[9]), "r"(v[10]), "r"(v[11]), "r"(v[12]), "r"(v[13]), "r"(v[14]), "r"(v[15])
+        : "memory");
+}
+__device__ __forceinline__ void tmem_st_wait() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
 __device__ __forceinline__ void tma_store_2d(const CUtensorMap *map, uint32_t src, int x, int y) {
     asm volatile("cp.async.bulk.tensor.2d.global.shared::cta.bulk_group [%0, {%2, %3}], [%1];"
                  ::"l"(reinterpret_cast<uint64_t>(map)), "r"(src), "r"(x), "r"(y) : "memory");
 }
 __device__ __forceinline__ void bulk_commit() { asm volatile("cp.async.bulk.commit_group;" ::: "memory"); }
-__device__ __forceinline__ void bulk_wait_read1() { asm volatile("cp.async.bulk.wait_group.read 1;" ::: "memory"); }
 __device__ __forceinline__ void bulk_wait_read0() { asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory"); }
 __device__ __forceinline__ void bulk_wait_all() { asm volatile("cp.async.bulk.wait_group 0;" ::: "memory"); }
-__device__ __forceinline__ uint32_t bf16x2(uint32_t lo, uint32_t hi) {
-    uint32_t r;
-    asm("cvt.rn.bf16x2.f32 %0, %1, %2;" : "=r"(r) : "f"(__uint_as_float(hi)), "f"(__uint_as_float(lo)));
-    return r;
+__device__ __forceinline__ uint32_t lds32(const uint8_t *p) { return *reinterpret_cast<const uint32_t *>(p); }
+__device__ __forceinline__ uint4 lds128(const uint8_t *p) { return *reinterpret_cast<const uint4 *>(p); }
+
+// The 32-byte code slice of one row, as 8 words in K order.  The two 16-byte
+// halves are read in an order set by bit 2 of the row slot, so the eight rows
+// served by one shared-memory wavefront fall in eight different bank groups.
+__device__ __forceinline__ void load_row32(const uint8_t *p, uint32_t slot, uint32_t (&w)[8]) {
+    const uint32_t h = (slot >> 2) & 1u;
+    const uint4 a = lds128(p + 16 * h), b = lds128(p + 16 * (h ^ 1u));
+    const uint4 lo = h ? b : a, hi = h ? a : b;
+    w[0] = lo.x; w[1] = lo.y; w[2] = lo.z; w[3] = lo.w;
+    w[4] = hi.x; w[5] = hi.y; w[6] = hi.z; w[7] = hi.w;
+}
+
+// One thread's share of a stage: weight row r, the q-th 64-K quarter of the
+// packed chunk `wc`, written to the TMEM A stage at `ta` (this thread's lane)
+// as 32 columns of packed pairs (column j = weights 2j, 2j+1 of the quarter).
+// Q4_K: byte j of the row's quarter holds weight j (low nibble, sub-block 2q)
+// and weight 32 + j (high nibble, sub-block 2q + 1).  Q6_K: half h = q / 2,
+// parts of ql and the 2-bit planes of qh give weights j and 32 + j.
+template <int TYPE, bool F16>
+__device__ __forceinline__ void unpack_row(const uint8_t *wc, uint32_t q, uint32_t r, uint32_t ta, bool &ovf) {
+    constexpr float kF16Inf = 65520.0f;   // smallest magnitude that rounds to inf
+    const uint32_t slot = row_slot(r);
+    uint32_t out[16];
+    if (TYPE == 12) {
+        const uint32_t dm = lds32(wc + kQ4Dm + r * 4);
+        const float d = half_bits_to_float((uint16_t)(dm & 0xffffu)), dmin = half_bits_to_float((uint16_t)(dm >> 16));
+        const uint8_t *scp = wc + kQ4Sc + r * 12;
+        uint32_t s0, m0, s1, m1;
+        const uint32_t sw0 = lds32(scp), sw1 = lds32(scp + 4), sw2 = lds32(scp + 8);
+        q4k_scale_min_w(2 * q, sw0, sw1, sw2, s0, m0);
+        q4k_scale_min_w(2 * q + 1, sw0, sw1, sw2, s1, m1);
+        const float a0 = d * (float)s0, b0 = dmin * (float)m0, a1 = d * (float)s1, b1 = dmin * (float)m1;
+        if (F16)
+            ovf |= fmaxf(fabsf(b0), fabsf(fmaf(a0, 15.0f, -b0))) >= kF16Inf ||
+                   fmaxf(fabsf(b1), fabsf(fmaf(a1, 15.0f, -b1))) >= kF16Inf;
+        uint32_t w[8];
+        load_row32(wc + kQ4Qs + q * 4096 + slot * 32, slot, w);
+        const uint64_t off2 = f2splat(-8388608.0f);
+        {
+            const uint64_t sc2 = f2splat(a0), mn2 = f2splat(-b0);
+#pragma unroll
+            for (int i = 0; i < 8; ++i) {
+                const uint2 v = four_values<12, F16>(w[i] & 0x0F0F0F0Fu, sc2, off2, mn2);
+                out[2 * i] = v.x;
+                out[2 * i + 1] = v.y;
+            }
+            tmem_st16(ta, out);
+        }
+        {
+            // High nibbles are read in place (16 q): the scale is pre-divided
+            // by 16, a power of two, so every product stays exact.
+            const uint64_t sc2 = f2splat(a1 * 0.0625f), mn2 = f2splat(-b1);
+#pragma unroll
+            for (int i = 0; i < 8; ++i) {
+                const uint2 v = four_values<12, F16>(w[i] & 0xF0F0F0F0u, sc2, off2, mn2);
+                out[2 * i] = v.x;
+                out[2 * i + 1] = v.y;
+            }
+            tmem_st16(ta + 16, out);
+        }
+    } else {
+        const uint32_t h = q >> 1, shift = (q & 1) * 4, g0 = 2 * (q & 1);
+        const float d = half_bits_to_float(*reinterpret_cast<const uint16_t *>(wc + kQ6D + r * 2));
+        const uint32_t sc4 = lds32(wc + kQ6Sc + r * 16 + 8 * h + 2 * g0);   // 4 int8 scales
+        const float sa0 = d * (float)(int8_t)(sc4 & 0xff), sa1 = d * (float)(int8_t)((sc4 >> 8) & 0xff);
+        const float sb0 = d * (float)(int8_t)((sc4 >> 16) & 0xff), sb1 = d * (float)(int8_t)(sc4 >> 24);
+        if (F16)
+            ovf |= 32.0f * fmaxf(fmaxf(fabsf(sa0), fabsf(sa1)), fmaxf(fabsf(sb0), fabsf(sb1))) >= kF16Inf;
+        const uint64_t off2 = f2splat(-8388640.0f);  // -(2^23 + 32)
+        uint32_t qh[8], l[8];
+        load_row32(wc + kQ6Qh + (h * kPanelRows + slot) * 32, slot, qh);
+        load_row32(wc + kQ6Ql + ((h * 2 + 0) * kPanelRows + slot) * 32, slot, l);
+        {
+            const uint64_t s0 = f2splat(sa0), s1 = f2splat(sa1);
+#pragma unroll
+            for (int i = 0; i < 8; ++i) {
+                const uint32_t c = ((l[i] >> shift) & 0x0F0F0F0Fu) | (((qh[i] >> (2 * g0)) & 0x03030303u) << 4);
+                const uint2 v = four_values<14, F16>(c, i < 4 ? s0 : s1, off2, 0);
+                out[2 * i] = v.x;
+                out[2 * i + 1] = v.y;
+            }
+            tmem_st16(ta, out);
+        }
+        load_row32(wc + kQ6Ql + ((h * 2 + 1) * kPanelRows + slot) * 32, slot, l);
+        {
+            const uint64_t s0 = f2splat(sb0), s1 = f2splat(sb1);
+#pragma unroll
+            for (int i = 0; i < 8; ++i) {
+                const uint32_t c = ((l[i] >> shift) & 0x0F0F0F0Fu) | (((qh[i] >> (2 * g0 + 2)) & 0x03030303u) << 4);
+                const uint2 v = four_values<14, F16>(c, i < 4 ? s0 : s1, off2, 0);
+                out[2 * i] = v.x;
+                out[2 * i + 1] = v.y;
+            }
+            tmem_st16(ta + 16, out);
+        }
+    }
 }
 
 // ------------------------------------------------------------ tiles
@@ -183,40 +293,8 @@ __device__ __forceinline__ PairTile pair_tile(const PairParams &p, uint32_t t) {
     uint32_t s = 0;
     while (s + 1 < p.n_seg && t >= p.seg[s + 1].tile_begin) ++s;
     const uint32_t local = t - p.seg[s].tile_begin;
-    return {p.seg[s].m_begin + (local / p.pair_panels) * kTileM, p.seg[s].m_end, local % p.pair_panels, p.seg[s].w};
-}
-
-// Plain stores of one token's 32 outputs (ragged edges, f32 output, or Y
-// without TMA-compatible alignment).
-template <bool OUT_F32>
-__device__ __forceinline__ void store_row(const PairParams &p, uint32_t m, uint32_t n0, const uint32_t (&v)[32]) {
-    if (OUT_F32) {
-        float *y = static_cast<float *>(p.y) + (uint64_t)m * p.ldy;
-#pragma unroll
-        for (uint32_t j = 0; j < 32; j += 4) {
-            if (p.y_vec && n0 + j + 4 <= p.n) {
-                *reinterpret_cast<uint4 *>(y + n0 + j) = make_uint4(v[j], v[j + 1], v[j + 2], v[j + 3]);
-            } else {
-#pragma unroll
-                for (uint32_t c = 0; c < 4; ++c)
-                    if (n0 + j + c < p.n) y[n0 + j + c] = __uint_as_float(v[j + c]);
-            }
-        }
-    } else {
-        __nv_bfloat16 *y = static_cast<__nv_bfloat16 *>(p.y) + (uint64_t)m * p.ldy;
-#pragma unroll
-        for (uint32_t j = 0; j < 32; j += 8) {
-            if (p.y_vec && n0 + j + 8 <= p.n) {
-                *reinterpret_cast<uint4 *>(y + n0 + j) =
-                    make_uint4(bf16x2(v[j], v[j + 1]), bf16x2(v[j + 2], v[j + 3]), bf16x2(v[j + 4], v[j + 5]),
-                               bf16x2(v[j + 6], v[j + 7]));
-            } else {
-#pragma unroll
-                for (uint32_t c = 0; c < 8; ++c)
-                    if (n0 + j + c < p.n) y[n0 + j + c] = __float2bfloat16_rn(__uint_as_float(v[j + c]));
-            }
-        }
-    }
+    return {p.seg[s].m_begin + (local / p.pair_panels) * kTileTokens, p.seg[s].m_end, local % p.pair_panels,
+            p.seg[s].w};
 }
 
 // ------------------------------------------------------------ the kernel
@@ -233,39 +311,33 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
     const uint32_t pair = blockIdx.x >> 1, n_pairs = gridDim.x >> 1;
 
     const uint32_t bars = su32(smem + L::bar_off);
-    constexpr uint32_t kT = L::n_tables;
     auto x_full = [&](uint32_t i) { return bars + 8 * i; };
-    auto dq_done = [&](uint32_t i) { return bars + 8 * (kStages + i); };
+    auto a_full = [&](uint32_t i) { return bars + 8 * (kStages + i); };
     auto full = [&](uint32_t i) { return bars + 8 * (2 * kStages + i); };
     auto st_empty = [&](uint32_t i) { return bars + 8 * (3 * kStages + i); };
     auto w_full = [&](uint32_t i) { return bars + 8 * (4 * kStages + i); };
     auto w_empty = [&](uint32_t i) { return bars + 8 * (4 * kStages + kWStages + i); };
-    auto t_ready = [&](uint32_t i) { return bars + 8 * (4 * kStages + 2 * kWStages + i); };
-    auto acc_full = [&](uint32_t i) { return bars + 8 * (4 * kStages + 2 * kWStages + kT + i); };
-    auto acc_empty = [&](uint32_t i) { return bars + 8 * (4 * kStages + 2 * kWStages + kT + 2 + i); };
-    const uint32_t fin = bars + 8 * (4 * kStages + 2 * kWStages + kT + 4);
-    auto table = [&](uint32_t i) { return reinterpret_cast<float *>(smem + L::t_off + i * L::table_bytes); };
-    // Tiles of this pair: pair, pair + n_pairs, ...
-    const uint32_t my_tiles = p.n_tiles > pair ? (p.n_tiles - pair + n_pairs - 1) / n_pairs : 0;
+    const uint32_t acc_full = bars + 8 * (4 * kStages + 2 * kWStages);
+    const uint32_t acc_empty = acc_full + 8, fin = acc_full + 16;
     uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(smem + L::misc_off);
     volatile uint32_t *abort_flag = tmem_slot + 1;
+    // Tiles of this pair: pair, pair + n_pairs, ...; 4 stages per packed chunk.
+    const uint32_t my_tiles = p.n_tiles > pair ? (p.n_tiles - pair + n_pairs - 1) / n_pairs : 0;
+    const uint32_t n_chunks = my_tiles * p.kb;
 
     if (threadIdx.x == 0) {
         for (int i = 0; i < kStages; ++i) {
             bar_init(x_full(i), 1);
-            bar_init(dq_done(i), kDequantWarps);
-            bar_init(full(i), 1);                   // leader's copy: the peer's relay
+            bar_init(a_full(i), 4);        // the four warps of one dequant group
+            bar_init(full(i), 1);          // leader's copy: the peer's relay
             bar_init(st_empty(i), 1);
         }
         for (int i = 0; i < kWStages; ++i) {
             bar_init(w_full(i), 1);
             bar_init(w_empty(i), kDequantWarps);
         }
-        for (uint32_t i = 0; i < kT; ++i) bar_init(t_ready(i), kDequantThreads);
-        for (int i = 0; i < 2; ++i) {
-            bar_init(acc_full(i), 1);
-            bar_init(acc_empty(i), 2 * kEpiWarps);  // leader's copy is the one used
-        }
+        bar_init(acc_full, 1);
+        bar_init(acc_empty, 2 * kEpiWarps);   // leader's copy is the one used
         bar_init(fin, 1);
         *abort_flag = 0u;
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
@@ -286,12 +358,12 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
         // ---------------------------------------------------- producer
         if (lane == 0) {
             // X (and the Y the epilogue writes) may belong to the previous
-            // kernel in the stream: wait for it before the first activation load.
+            // kernel in the stream: wait for it before the first load.
             asm volatile("griddepcontrol.wait;" ::: "memory");
-            uint32_t st = 0, ph = 0, ws = 0, wph = 0;
             uint32_t x_last[kStages], w_last[kWStages];
             bool x_used[kStages] = {}, w_used[kWStages] = {};
             bool ok = true;
+            uint32_t c = 0;
             for (uint32_t t = pair; ok && t < p.n_tiles; t += n_pairs) {
                 const PairTile T = pair_tile(p, t);
                 // A missing second panel (odd panel count) re-reads the last
@@ -299,20 +371,20 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
                 uint32_t panel = 2 * T.pp + rank;
                 if (panel >= p.panels) panel = p.panels - 1;
                 const uint8_t *pw = T.w + (uint64_t)panel * p.kb * kChunk;
-                const int my_m = (int)(T.m0 + rank * kHalfM);
-                for (uint32_t kb = 0; ok && kb < p.kb; ++kb) {
+                const int my_m = (int)(T.m0 + rank * kHalf);
+                for (uint32_t kb = 0; ok && kb < p.kb; ++kb, ++c) {
+                    const uint32_t ws = c % kWStages, wph = (c / kWStages) & 1;
                     if (!(ok = pwait(w_empty(ws), wph ^ 1, ab))) break;
                     bar_expect_tx(w_full(ws), kChunk);
                     bulk_load(su32(smem + L::w_off + ws * L::w_stage), pw + (uint64_t)kb * kChunk, kChunk, w_full(ws));
                     w_last[ws] = wph; w_used[ws] = true;
-                    if (++ws == kWStages) { ws = 0; wph ^= 1; }
                     for (uint32_t q = 0; q < 4; ++q) {
+                        const uint32_t i = 4 * c + q, st = i % kStages, ph = (i / kStages) & 1;
                         if (!(ok = pwait(st_empty(st), ph ^ 1, ab))) break;
                         bar_expect_tx(x_full(st), L::x_stage);
                         tma_load_2d(su32(smem + L::x_off + st * L::x_stage), &xmap, x_full(st),
                                     (int)(kb * 256 + q * 64), my_m);
                         x_last[st] = ph; x_used[st] = true;
-                        if (++st == kStages) { st = 0; ph ^= 1; }
                     }
                 }
             }
@@ -324,141 +396,128 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
         }
         __syncwarp();
     } else if (warp == 1) {
-        // ---------------------------------------------------- MMA issuer (leader)
         if (lane == 0 && rank == 0) {
+            // ---------------------------------------------------- MMA issuer (leader)
             constexpr uint32_t idesc = pair_idesc<F16>();
-            uint32_t st = 0, ph = 0, acc = 0, aph = 0;
             bool ok = true;
-            for (uint32_t t = pair; ok && t < p.n_tiles; t += n_pairs) {
-                if (!(ok = pwait(acc_empty(acc), aph ^ 1, ab))) break;
+            uint32_t i = 0;   // stage counter
+            for (uint32_t tt = 0; ok && tt < my_tiles; ++tt) {
+                if (!(ok = pwait(acc_empty, (tt & 1) ^ 1, ab))) break;
                 tc_fence_after();
-                const uint32_t d_tmem = tmem + acc * kTileN;
-                for (uint32_t kb = 0; ok && kb < p.kb; ++kb) {
-                    for (uint32_t q = 0; q < 4; ++q) {
-                        if (!(ok = pwait(x_full(st), ph, ab))) break;
-                        if (!(ok = pwait(dq_done(st), ph, ab))) break;
-                        if (!(ok = pwait(full(st), ph, ab))) break;   // the peer's stage
-                        tc_fence_after();
-                        const uint32_t a_addr = su32(smem + L::x_off + st * L::x_stage);
-                        const uint32_t b_addr = su32(smem + L::b_off + st * L::b_stage);
+                for (uint32_t s = 0; ok && s < 4 * p.kb; ++s, ++i) {
+                    const uint32_t st = i % kStages, ph = (i / kStages) & 1;
+                    if (!(ok = pwait(x_full(st), ph, ab))) break;
+                    if (!(ok = pwait(a_full(st), ph, ab))) break;
+                    if (!(ok = pwait(full(st), ph, ab))) break;   // the peer's stage
+                    tc_fence_after();
+                    const uint32_t a_col = tmem + kACol0 + st * kAStageCols;
+                    const uint32_t b_addr = su32(smem + L::x_off + st * L::x_stage);
 #pragma unroll
-                        for (uint32_t kk = 0; kk < 4; ++kk)
-                            mma_pair(d_tmem, sw128_desc(a_addr + kk * 32), sw128_desc(b_addr + kk * 32), idesc,
-                                     (kb | q | kk) ? 1u : 0u);
-                        commit_both(st_empty(st));
-                        if (++st == kStages) { st = 0; ph ^= 1; }
-                    }
+                    for (uint32_t kk = 0; kk < 4; ++kk)
+                        mma_pair_ts(tmem, a_col + 8 * kk, sw128_desc(b_addr + kk * 32), idesc, (s | kk) ? 1u : 0u);
+                    commit_both(st_empty(st));
                 }
                 if (!ok) break;
-                commit_both(acc_full(acc));
-                acc ^= 1;
-                if (acc == 0) aph ^= 1;
+                commit_both(acc_full);
             }
             // Every MMA issued by this thread has completed (in both CTAs)
             // before either CTA frees its TMEM.
             commit_both(fin);
         } else if (lane == 0) {
             // ---------------------------------------------------- relay (peer)
-            // Forwards "this CTA's stage is complete" to the leader's `full`.
-            uint32_t st = 0, ph = 0;
-            const uint32_t n_stages = my_tiles * p.kb * 4;
-            for (uint32_t i = 0; i < n_stages; ++i) {
+            for (uint32_t i = 0; i < 4 * n_chunks; ++i) {
+                const uint32_t st = i % kStages, ph = (i / kStages) & 1;
                 if (!pwait(x_full(st), ph, ab)) break;
-                if (!pwait(dq_done(st), ph, ab)) break;
+                if (!pwait(a_full(st), ph, ab)) break;
                 bar_arrive_cluster(cluster_addr(full(st), 0));
-                if (++st == kStages) { st = 0; ph ^= 1; }
             }
         }
         if (lane == 0) pwait(fin, 0, ab, false);
         __syncwarp();
     } else if (warp >= (uint32_t)kDequantWarp0) {
         // ---------------------------------------------------- dequantisers
-        // Chunks (128 weight rows x 256 K) are unpacked in order.  The scale
-        // table of chunk c + 1 is built during chunk c's last stage, into the
-        // next of three table buffers (a buffer is rewritten only after every
-        // thread has passed the chunk that read it), so a chunk never starts
-        // with a CTA-wide wait on a table that was just built.  Waits are
-        // warp-uniform (__all_sync): the warp synchronises after every stage
-        // and leaves together on abort.
-        const uint32_t dt = threadIdx.x - kDequantWarp0 * 32, dw = dt / 32;
-        const uint32_t r = 8 * dw + (lane >> 3) + 4 * ((lane >> 2) & 1);
-        const uint32_t n_chunks = my_tiles * p.kb;
-        uint32_t st = 0, ph = 0;
-        bool ok = true, ovf = false;
-        auto build = [&](uint32_t c) -> bool {
-            const uint32_t ws = c % kWStages;
-            if (!__all_sync(0xffffffffu, pwait(w_full(ws), (c / kWStages) & 1, ab))) return false;
-            build_table<TYPE, F16>(smem + L::w_off + ws * L::w_stage, table(c % kT), dt, ovf);
-            bar_arrive(t_ready(c % kT));
-            return true;
-        };
-        if (n_chunks) ok = build(0);
-        for (uint32_t c = 0; ok && c < n_chunks; ++c) {
-            const uint8_t *wc = smem + L::w_off + (c % kWStages) * L::w_stage;
-            const float *tab = table(c % kT);
-            if (!(ok = __all_sync(0xffffffffu, pwait(t_ready(c % kT), (c / kT) & 1, ab)))) break;
-            for (uint32_t q = 0; q < 4; ++q) {
-                if (q == 3 && c + 1 < n_chunks && !(ok = build(c + 1))) break;
-                if (!(ok = __all_sync(0xffffffffu, pwait(st_empty(st), ph ^ 1, ab)))) break;
-                dequant_task<TYPE, F16>(wc, tab, q, r, lane & 3, smem + L::b_off + st * L::b_stage);
-                fence_proxy_async();
-                __syncwarp();
-                if (lane == 0) bar_arrive(dq_done(st));
-                if (++st == kStages) { st = 0; ph ^= 1; }
-            }
-            if (!ok) break;
+        // Group q = (warp - 6) / 4 unpacks quarter q of every chunk: stage
+        // 4c + q.  Waits are warp-uniform (__all_sync) because tcgen05.st is
+        // a warp-collective; on abort the whole warp leaves.
+        const uint32_t q = (warp - kDequantWarp0) / 4, quarter = warp & 3;
+        const uint32_t r = 32 * quarter + lane;            // weight row = TMEM lane
+        const uint32_t t_lane = tmem + ((32 * quarter) << 16) + kACol0;
+        bool ovf = false;
+        for (uint32_t c = 0; c < n_chunks; ++c) {
+            const uint32_t ws = c % kWStages, i = 4 * c + q, st = i % kStages, ph = (i / kStages) & 1;
+            if (!__all_sync(0xffffffffu, pwait(w_full(ws), (c / kWStages) & 1, ab))) break;
+            if (!__all_sync(0xffffffffu, pwait(st_empty(st), ph ^ 1, ab))) break;
+            tc_fence_after();
+            unpack_row<TYPE, F16>(smem + L::w_off + ws * L::w_stage, q, r, t_lane + st * kAStageCols, ovf);
+            tmem_st_wait();
+            tc_fence_before();
             __syncwarp();
-            if (lane == 0) bar_arrive(w_empty(c % kWStages));
+            if (lane == 0) {
+                bar_arrive(w_empty(ws));
+                bar_arrive(a_full(st));
+            }
         }
         if (F16 && ovf) atomicOr(p.status, kStatusF16);
     } else {
         // ---------------------------------------------------- epilogue
+        // Thread = weight row n of this CTA's panel; D column c = token m0 + c
+        // (columns 0-127: CTA 0's activation rows, 128-255: CTA 1's).  The
+        // accumulator is read out in eight 32-token pieces; a piece that lies
+        // inside the segment goes to this warp's staging box (bf16, [token]
+        // [32 outputs]) for a TMA store, a piece at a ragged segment end (and
+        // f32 output) is stored directly, the warp's 32 lanes writing 32
+        // consecutive outputs of one token.  TMEM is released before the TMA
+        // stores are issued.
         const uint32_t quad = warp & 3;   // TMEM lanes 32*quad .. +31
-        uint32_t acc = 0, aph = 0, piece = 0;
-        uint8_t *stage = smem + L::e_off + quad * L::e_bufs * L::e_piece;
-        for (uint32_t t = pair; t < p.n_tiles; t += n_pairs) {
-            const PairTile T = pair_tile(p, t);
-            if (!__all_sync(0xffffffffu, pwait(acc_full(acc), aph, ab))) break;
+        uint8_t *stage = smem + L::e_off + quad * L::e_warp;
+        for (uint32_t tt = 0; tt < my_tiles; ++tt) {
+            const PairTile T = pair_tile(p, pair + tt * n_pairs);
+            const uint32_t n0 = (2 * T.pp + rank) * 128 + quad * 32, n = n0 + lane;
+            if (!__all_sync(0xffffffffu, pwait(acc_full, tt & 1, ab))) break;
             tc_fence_after();
-            const uint32_t row0 = T.m0 + rank * kHalfM + quad * 32;   // this warp's first token
-            const bool rows_all = row0 + 32 <= T.m_end, rows_any = row0 < T.m_end;
-            const uint32_t taddr = tmem + ((quad * 32) << 16) + acc * kTileN;
+            if (!OUT_F32 && p.y_tma) {
+                if (lane == 0) bulk_wait_read0();   // the last tile's stores have read the staging area
+                __syncwarp();
+            }
+            const uint32_t taddr = tmem + ((quad * 32) << 16);
+            uint32_t tma_pieces = 0;   // bit j: piece j goes out by TMA
 #pragma unroll 1
-            for (uint32_t c0 = 0; c0 < kTileN; c0 += 32) {
-                const uint32_t n0 = T.pp * kTileN + c0;
-                if (!rows_any || n0 >= p.n) continue;
+            for (uint32_t j = 0; j < kTileTokens / 32; ++j) {
+                const uint32_t t0 = T.m0 + 32 * j;
+                if (t0 >= T.m_end || n0 >= p.n) break;   // past the segment / a missing second panel
                 uint32_t v[32];
-                tmem_ld32(taddr + c0, v);
-                if (!OUT_F32 && p.y_tma && rows_all) {
-                    uint8_t *buf = stage + (piece % L::e_bufs) * L::e_piece;
-                    if (lane == 0) {   // the store that last used `buf` has read it
-                        if (L::e_bufs == 2) bulk_wait_read1();
-                        else bulk_wait_read0();
-                    }
-                    __syncwarp();
-                    uint8_t *row = buf + lane * 64;
-                    const uint32_t sw = (lane >> 1) & 3;   // 64-byte swizzle of the TMA box
+                tmem_ld32(taddr + 32 * j, v);
+                if (!OUT_F32 && p.y_tma && t0 + 32 <= T.m_end) {
+                    tma_pieces |= 1u << j;
+                    __nv_bfloat16 *sb = reinterpret_cast<__nv_bfloat16 *>(stage + j * L::e_box) + lane;
 #pragma unroll
-                    for (uint32_t j = 0; j < 4; ++j)
-                        *reinterpret_cast<uint4 *>(row + ((j ^ sw) << 4)) =
-                            make_uint4(bf16x2(v[8 * j], v[8 * j + 1]), bf16x2(v[8 * j + 2], v[8 * j + 3]),
-                                       bf16x2(v[8 * j + 4], v[8 * j + 5]), bf16x2(v[8 * j + 6], v[8 * j + 7]));
-                    fence_proxy_async();
-                    __syncwarp();
-                    if (lane == 0) {
-                        tma_store_2d(&ymap, su32(buf), (int)n0, (int)row0);
-                        bulk_commit();
+                    for (uint32_t c = 0; c < 32; ++c) sb[c * 32] = __float2bfloat16_rn(__uint_as_float(v[c]));
+                } else if (n < p.n) {
+#pragma unroll
+                    for (uint32_t c = 0; c < 32; ++c) {
+                        const uint32_t m = t0 + c;
+                        if (m < T.m_end) {
+                            const uint64_t off = (uint64_t)m * p.ldy + n;
+                            if (OUT_F32) static_cast<float *>(p.y)[off] = __uint_as_float(v[c]);
+                            else static_cast<__nv_bfloat16 *>(p.y)[off] = __float2bfloat16_rn(__uint_as_float(v[c]));
+                        }
                     }
-                    ++piece;
-                } else if (row0 + lane < T.m_end) {
-                    store_row<OUT_F32>(p, row0 + lane, n0, v);
                 }
             }
+            // Every TMEM load has completed (tcgen05.ld waits): hand D back.
             tc_fence_before();
             __syncwarp();
-            if (lane == 0) bar_arrive_cluster(cluster_addr(acc_empty(acc), 0));
-            acc ^= 1;
-            if (acc == 0) aph ^= 1;
+            if (lane == 0) bar_arrive_cluster(cluster_addr(acc_empty, 0));
+            if (tma_pieces) {
+                fence_proxy_async();
+                __syncwarp();
+                if (lane == 0) {
+                    for (uint32_t j = 0; j < kTileTokens / 32; ++j)
+                        if (tma_pieces & (1u << j))
+                            tma_store_2d(&ymap, su32(stage + j * L::e_box), (int)n0, (int)(T.m0 + 32 * j));
+                    bulk_commit();
+                }
+            }
         }
         if (lane == 0) bulk_wait_all();
         __syncwarp();
@@ -517,8 +576,6 @@ cudaError_t launch_pair_inst(const CUtensorMap &xm, const CUtensorMap &ym, const
 
 }  // namespace
 
-bool gemm_pair_supported(uint32_t n_seg) { return n_seg <= (uint32_t)kMaxSeg; }
-
 cudaError_t launch_gemm_pair(const SegmentView *segs, uint32_t n_seg, const uint16_t *x, uint64_t m_total,
                              uint64_t k, void *y, uint64_t ldy, int out_dtype, int stage_f16, uint32_t *status,
                              cudaStream_t s) {
@@ -536,38 +593,34 @@ cudaError_t launch_gemm_pair(const SegmentView *segs, uint32_t n_seg, const uint
     uint32_t tiles = 0;
     for (uint32_t i = 0; i < n_seg; ++i) {
         p.seg[i] = {segs[i].m_begin, segs[i].m_end, tiles, 0u, segs[i].w.chunks};
-        tiles += (segs[i].m_end - segs[i].m_begin + kTileM - 1) / kTileM * p.pair_panels;
+        tiles += (segs[i].m_end - segs[i].m_begin + kTileTokens - 1) / kTileTokens * p.pair_panels;
     }
     p.n_tiles = tiles;
     if (!tiles) return cudaSuccess;
 
     auto enc = encode_fn();
     if (!enc) return cudaErrorNotSupported;
-    CUtensorMap xm, ym;
-    {
-        const cuuint64_t dims[2] = {k, m_total};
-        const cuuint64_t strides[1] = {k * 2};
-        const cuuint32_t box[2] = {64u, kHalfM};
-        const cuuint32_t estr[2] = {1u, 1u};
-        const CUresult r = enc(&xm, stage_f16 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2,
-                               const_cast<uint16_t *>(x), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
-                               CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
-                               CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
-        if (r != CUDA_SUCCESS) return cudaErrorInvalidValue;
-    }
+    CUtensorMap xm;
+    const cuuint64_t dims[2] = {k, m_total};
+    const cuuint64_t strides[1] = {k * 2};
+    const cuuint32_t box[2] = {64u, kHalf};
+    const cuuint32_t estr[2] = {1u, 1u};
+    const CUresult r = enc(&xm, stage_f16 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2,
+                           const_cast<uint16_t *>(x), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                           CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                           CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r != CUDA_SUCCESS) return cudaErrorInvalidValue;
     const int out_f32 = out_dtype == 0;
-    const uint64_t esize = out_f32 ? 4 : 2;
-    p.y_vec = ((reinterpret_cast<uintptr_t>(y) & 15u) == 0 && (ldy * esize) % 16 == 0) ? 1u : 0u;
+    CUtensorMap ym;
     memset(&ym, 0, sizeof(ym));
-    if (!out_f32 && p.y_vec) {
-        const cuuint64_t dims[2] = {p.n, m_total};
-        const cuuint64_t strides[1] = {ldy * 2};
-        const cuuint32_t box[2] = {32u, 32u};
-        const cuuint32_t estr[2] = {1u, 1u};
-        const CUresult r = enc(&ym, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, y, dims, strides, box, estr,
-                               CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_64B,
-                               CU_TENSOR_MAP_L2_PROMOTION_NONE, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
-        p.y_tma = r == CUDA_SUCCESS ? 1u : 0u;
+    if (!out_f32 && (reinterpret_cast<uintptr_t>(y) & 15u) == 0 && (ldy * 2) % 16 == 0) {
+        const cuuint64_t ydims[2] = {p.n, m_total};
+        const cuuint64_t ystrides[1] = {ldy * 2};
+        const cuuint32_t ybox[2] = {32u, 32u};
+        const CUresult ry = enc(&ym, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, y, ydims, ystrides, ybox, estr,
+                                CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE,
+                                CU_TENSOR_MAP_L2_PROMOTION_NONE, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+        p.y_tma = ry == CUDA_SUCCESS ? 1u : 0u;
     }
     const uint32_t type = segs[0].w.type;
     if (type == 12) {
