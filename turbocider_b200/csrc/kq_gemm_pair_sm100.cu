@@ -18,7 +18,7 @@
 //
 // TMEM (512 columns per CTA): columns 0-255 hold the accumulator D as
 // [128 lanes = this CTA's weight rows] x [256 columns = the tile's tokens];
-// columns 256-447 hold a 6-slot ring of A stages (32 columns each).  There is
+// columns 256 onwards hold the ring of A stages (32 columns each).  There is
 // room for one accumulator only: the epilogue copies it to a shared-memory
 // staging area (tcgen05.ld, then 2-byte stores that are conflict-free because
 // a warp's 32 lanes hold 32 consecutive outputs of one token), releases it to
@@ -32,14 +32,17 @@
 // reading its sub-block scales directly from the packed bytes -- bit-exact to
 // the reference decoder (native/core/gguf_decode.cpp:77-105).
 //
-// Warp roles (22 warps, both CTAs):
-//   warp 0     producer: bulk copy of each packed chunk, TMA of the activations;
+// Warp roles (23 warps, both CTAs):
+//   warp 0     activation producer (TMA);
 //   warp 1     TMEM allocator (cta_group::2); in the leader, the MMA-issuing
 //              thread; in the peer, a relay that forwards "this CTA's stage is
 //              complete" to the leader's `full` barrier (one remote arrival per
 //              stage, kept off the dequant warps);
 //   warps 2-5  epilogue: tcgen05.ld of 32 tokens per thread-row, stores of Y;
-//   warps 6-21 dequantisers.
+//   warps 6-21 dequantisers;
+//   warp 22    packed-chunk producer: one bulk copy per chunk as soon as its
+//              slot frees (never queued behind activation copies that wait on
+//              the MMA), plus an L2 prefetch of the chunk two ahead.
 // The leader's MMA completion is committed to both CTAs' barriers
 // (tcgen05.commit with a CTA mask).  No TMA load uses cluster multicast:
 // every copy lands in the CTA that issued it and signals that CTA's own
@@ -57,10 +60,14 @@
 namespace tc {
 namespace {
 
-constexpr int kThreads = 704;
+constexpr int kThreads = 736;
+constexpr int kWProdWarp = 22;   // packed-chunk producer
 constexpr int kDequantWarp0 = 6, kDequantWarps = 16;
 constexpr int kEpiWarps = 4;
-constexpr int kStages = 6;       // activation (smem) + A (TMEM) ring, 64 K per stage
+// Stage ring (activations in shared memory + A in TMEM, 64 K per stage):
+// as deep as shared memory allows next to the packed-chunk ring and the
+// 64 KB epilogue staging area -- 7 stages for Q4_K, 6 for Q6_K.
+constexpr int stages_for(int type) { return type == 12 ? 7 : 6; }
 constexpr int kWStages = 2;      // packed chunk ring (256 K per chunk)
 constexpr int kMaxSeg = 32;
 constexpr uint32_t kTileRows = 256, kTileTokens = 256, kHalf = 128;
@@ -84,17 +91,19 @@ struct PairLayout {
     static constexpr uint32_t x_stage = kHalf * 128;   // 128 tokens x 64 K x 2 B
     static constexpr uint32_t w_stage = chunk_bytes(TYPE);
     static constexpr uint32_t x_off = 0;
-    static constexpr uint32_t w_off = x_off + kStages * x_stage;
+    static constexpr int kS = stages_for(TYPE);
+    static constexpr uint32_t w_off = x_off + kS * x_stage;
     // Epilogue staging per warp: eight 32-token x 32-output bf16 boxes (16 KB).
     static constexpr uint32_t e_box = 32 * 64, e_warp = 8 * e_box;
     static constexpr uint32_t e_off = (w_off + kWStages * w_stage + 1023) / 1024 * 1024;
     static constexpr uint32_t bar_off = e_off + kEpiWarps * e_warp;
     // x_full[S] a_full[S] full[S] st_empty[S] w_full[W] w_empty[W] acc_full acc_empty fin
-    static constexpr uint32_t n_bars = 4 * kStages + 2 * kWStages + 3;
+    static constexpr uint32_t n_bars = 4 * kS + 2 * kWStages + 3;
     static constexpr uint32_t misc_off = bar_off + n_bars * 8;
     static constexpr uint32_t bytes = misc_off + 16 + 1024;  // + alignment slack
     static constexpr uint32_t tmem_cols = 512;
     static_assert(bytes <= 232448, "shared memory per CTA exceeds the sm_100 limit");
+    static_assert(kACol0 + kS * kAStageCols <= tmem_cols, "TMEM budget");
 };
 
 // ------------------------------------------------------------ cluster PTX
@@ -175,6 +184,10 @@ __device__ __forceinline__ void tmem_st16(uint32_t taddr, const uint32_t (&v)[16
         ::"r"(taddr), "r"(v[0]), "r"(v[1]), "r"(v[2]), "r"(v[3]), "r"(v[4]), "r"(v[5]), "r"(v[6]), "r"(v[7]),
           "r"(v[8]), "r"(v[9]), "r"(v[10]), "r"(v[11]), "r"(v[12]), "r"(v[13]), "r"(v[14]), "r"(v[15])
         : "memory");
+}
+// Hint: bring `bytes` at `src` into L2 (no completion tracking).
+__device__ __forceinline__ void l2_prefetch(const void *src, uint32_t bytes) {
+    asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(src), "r"(bytes) : "memory");
 }
 __device__ __forceinline__ void tmem_st_wait() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
 __device__ __forceinline__ void tma_store_2d(const CUtensorMap *map, uint32_t src, int x, int y) {
@@ -304,6 +317,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
                      const __grid_constant__ PairParams p) {
     using L = PairLayout<TYPE>;
     constexpr uint32_t kChunk = chunk_bytes(TYPE);
+    constexpr int kStages = L::kS;
     extern __shared__ uint8_t smem_raw[];
     uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
     const uint32_t warp = threadIdx.x / 32, lane = threadIdx.x % 32;
@@ -355,44 +369,57 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
 
     if (threadIdx.x == 0) asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
     if (warp == 0) {
-        // ---------------------------------------------------- producer
+        // ---------------------------------------------------- activation producer
         if (lane == 0) {
             // X (and the Y the epilogue writes) may belong to the previous
             // kernel in the stream: wait for it before the first load.
             asm volatile("griddepcontrol.wait;" ::: "memory");
-            uint32_t x_last[kStages], w_last[kWStages];
-            bool x_used[kStages] = {}, w_used[kWStages] = {};
+            uint32_t x_last[kStages];
+            bool x_used[kStages] = {};
             bool ok = true;
-            uint32_t c = 0;
+            uint32_t i = 0;   // stage counter
             for (uint32_t t = pair; ok && t < p.n_tiles; t += n_pairs) {
-                const PairTile T = pair_tile(p, t);
-                // A missing second panel (odd panel count) re-reads the last
-                // panel; its outputs fall past N and are never stored.
-                uint32_t panel = 2 * T.pp + rank;
-                if (panel >= p.panels) panel = p.panels - 1;
-                const uint8_t *pw = T.w + (uint64_t)panel * p.kb * kChunk;
-                const int my_m = (int)(T.m0 + rank * kHalf);
-                for (uint32_t kb = 0; ok && kb < p.kb; ++kb, ++c) {
-                    const uint32_t ws = c % kWStages, wph = (c / kWStages) & 1;
-                    if (!(ok = pwait(w_empty(ws), wph ^ 1, ab))) break;
-                    bar_expect_tx(w_full(ws), kChunk);
-                    bulk_load(su32(smem + L::w_off + ws * L::w_stage), pw + (uint64_t)kb * kChunk, kChunk, w_full(ws));
-                    w_last[ws] = wph; w_used[ws] = true;
-                    for (uint32_t q = 0; q < 4; ++q) {
-                        const uint32_t i = 4 * c + q, st = i % kStages, ph = (i / kStages) & 1;
-                        if (!(ok = pwait(st_empty(st), ph ^ 1, ab))) break;
-                        bar_expect_tx(x_full(st), L::x_stage);
-                        tma_load_2d(su32(smem + L::x_off + st * L::x_stage), &xmap, x_full(st),
-                                    (int)(kb * 256 + q * 64), my_m);
-                        x_last[st] = ph; x_used[st] = true;
-                    }
+                const int my_m = (int)(pair_tile(p, t).m0 + rank * kHalf);
+                for (uint32_t s = 0; ok && s < 4 * p.kb; ++s, ++i) {
+                    const uint32_t st = i % kStages, ph = (i / kStages) & 1;
+                    if (!(ok = pwait(st_empty(st), ph ^ 1, ab))) break;
+                    bar_expect_tx(x_full(st), L::x_stage);
+                    tma_load_2d(su32(smem + L::x_off + st * L::x_stage), &xmap, x_full(st), (int)(s * 64), my_m);
+                    x_last[st] = ph; x_used[st] = true;
                 }
             }
             // Drain: every copy this thread issued has landed before exit.
-            for (int i = 0; i < kStages; ++i)
-                if (x_used[i]) pwait(x_full(i), x_last[i], ab, false);
-            for (int i = 0; i < kWStages; ++i)
-                if (w_used[i]) pwait(w_full(i), w_last[i], ab, false);
+            for (int k = 0; k < kStages; ++k)
+                if (x_used[k]) pwait(x_full(k), x_last[k], ab, false);
+        }
+        __syncwarp();
+    } else if (warp == (uint32_t)kWProdWarp) {
+        // ---------------------------------------------------- packed-chunk producer
+        if (lane == 0) {
+            asm volatile("griddepcontrol.wait;" ::: "memory");
+            uint32_t w_last[kWStages];
+            bool w_used[kWStages] = {};
+            bool ok = true;
+            // Chunk c of this pair's sequence: tile c / kb, K block c % kb.
+            // A missing second panel (odd panel count) re-reads the last
+            // panel; its outputs fall past N and are never stored.
+            auto chunk_src = [&](uint32_t c) -> const uint8_t * {
+                const PairTile T = pair_tile(p, pair + (c / p.kb) * n_pairs);
+                uint32_t panel = 2 * T.pp + rank;
+                if (panel >= p.panels) panel = p.panels - 1;
+                return T.w + ((uint64_t)panel * p.kb + c % p.kb) * kChunk;
+            };
+            for (uint32_t c = 0; c < kWStages && c < n_chunks; ++c) l2_prefetch(chunk_src(c), kChunk);
+            for (uint32_t c = 0; ok && c < n_chunks; ++c) {
+                const uint32_t ws = c % kWStages, wph = (c / kWStages) & 1;
+                if (c + kWStages < n_chunks) l2_prefetch(chunk_src(c + kWStages), kChunk);
+                if (!(ok = pwait(w_empty(ws), wph ^ 1, ab))) break;
+                bar_expect_tx(w_full(ws), kChunk);
+                bulk_load(su32(smem + L::w_off + ws * L::w_stage), chunk_src(c), kChunk, w_full(ws));
+                w_last[ws] = wph; w_used[ws] = true;
+            }
+            for (int k = 0; k < kWStages; ++k)
+                if (w_used[k]) pwait(w_full(k), w_last[k], ab, false);
         }
         __syncwarp();
     } else if (warp == 1) {
@@ -434,7 +461,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
         }
         if (lane == 0) pwait(fin, 0, ab, false);
         __syncwarp();
-    } else if (warp >= (uint32_t)kDequantWarp0) {
+    } else if (warp >= (uint32_t)kDequantWarp0 && warp < (uint32_t)kWProdWarp) {
         // ---------------------------------------------------- dequantisers
         // Group q = (warp - 6) / 4 unpacks quarter q of every chunk: stage
         // 4c + q.  Waits are warp-uniform (__all_sync) because tcgen05.st is
