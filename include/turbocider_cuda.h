@@ -44,8 +44,15 @@ enum { TC_GGML_Q4_K = 12, TC_GGML_Q5_K = 13, TC_GGML_Q6_K = 14 };
  * (reference native/core/gguf_decode.hpp:18). */
 enum { TC_DTYPE_F32 = 0, TC_DTYPE_F16 = 1, TC_DTYPE_BF16 = 2 };
 
-/* Staging precision of the dequantised weight inside the tensor-core GEMM. */
-enum { TC_STAGE_BF16 = 0, TC_STAGE_F16 = 1 };
+/* Staging precision of the dequantised weight inside the tensor-core GEMM,
+ * and the type of X:
+ *   TC_STAGE_BF16     X bf16, W staged bf16 (rel-L2 ~1.7e-3 vs an fp32 decode);
+ *   TC_STAGE_F16      X bf16, converted to fp16 into the context workspace,
+ *                     W staged fp16 (rel-L2 ~2e-4);
+ *   TC_STAGE_F16_X16  X already fp16 (the reference's GGUF execution runs fp16
+ *                     activations), W staged fp16, no conversion pass; every
+ *                     segment takes the tensor-core GEMM. */
+enum { TC_STAGE_BF16 = 0, TC_STAGE_F16 = 1, TC_STAGE_F16_X16 = 2 };
 
 /* Status-word bits (tc_cuda_status). */
 enum {
@@ -122,7 +129,8 @@ int tc_cuda_decode(tc_cuda_ctx *ctx, uint32_t ggml_type, const void *source, uin
 
 /* Quantised linear Y[M, N] = X[M, K] * W^T (fp32 accumulate) -- the operator
  * behind Weights::project (reference native/backends/mlx.cpp:668-679).
- *   X        bf16 [M, K] row-major, device; M = seg_offsets[n_seg].
+ *   X        bf16 [M, K] row-major, device (fp16 with TC_STAGE_F16_X16);
+ *            M = seg_offsets[n_seg].
  *   Y        [M, N] row-major, device, dtype out_dtype (TC_DTYPE_BF16 or
  *            TC_DTYPE_F32); row stride ldy elements (0 = N).
  *   weights  n_weights uploaded weights with identical N, K;
@@ -133,8 +141,8 @@ int tc_cuda_decode(tc_cuda_ctx *ctx, uint32_t ggml_type, const void *source, uin
  *            image vs text stream);  NULL = weight 0 for every segment.
  * Dispatch: the warp GEMV for segments with at most 16 rows, the tcgen05
  * tensor-core GEMM otherwise (2-CTA 256 x 256 tiles once a segment has more
- * than 128 rows).  `stage` selects the GEMM's operand precision
- * (TC_STAGE_BF16 uses X as given; TC_STAGE_F16 converts X to fp16 first). */
+ * than 128 rows).  `stage` selects the GEMM's operand precision and X's type
+ * (TC_STAGE_*). */
 int tc_cuda_qlinear(tc_cuda_ctx *ctx, const tc_cuda_weight *const *weights, uint32_t n_weights,
                     const int32_t *seg_offsets, const int32_t *seg_weight, uint32_t n_seg,
                     const void *x, void *y, uint64_t ldy, int out_dtype, int stage, void *stream);

@@ -164,13 +164,17 @@ def staged_weight(raw, ggml_type: int, n: int, k: int, staging: str, which: str 
     return bits.view(np.float16).astype(np.float64)
 
 
-def qlinear_ref(x_bf16_bits: np.ndarray, raw, ggml_type: int, n: int, k: int, staging: str = "f32",
-                which: str = "port") -> np.ndarray:
-    """fp64 oracle of Y = X * W^T.  X is given as bf16 bit patterns [M, K]; with
-    staging "f16" it is first rounded to fp16 (as the kernel's fp16 mode)."""
-    x = bf16_bits_to_f32(x_bf16_bits)
-    if staging == "f16":
-        x = x.astype(np.float16)
+def qlinear_ref(x_bits: np.ndarray, raw, ggml_type: int, n: int, k: int, staging: str = "f32",
+                which: str = "port", x_dtype: str = "bf16") -> np.ndarray:
+    """fp64 oracle of Y = X * W^T.  X is given as bf16 bit patterns [M, K]
+    (x_dtype "f16": fp16 bit patterns); with staging "f16" a bf16 X is first
+    rounded to fp16 (as the kernel's fp16 mode)."""
+    if x_dtype == "f16":
+        x = np.asarray(x_bits, dtype=np.uint16).view(np.float16)
+    else:
+        x = bf16_bits_to_f32(x_bits)
+        if staging == "f16":
+            x = x.astype(np.float16)
     w = staged_weight(raw, ggml_type, n, k, staging, which)
     return x.astype(np.float64) @ w.T
 

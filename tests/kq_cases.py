@@ -117,3 +117,9 @@ def synthetic_x_bf16(m: int, k: int, seed: int = 1) -> np.ndarray:
     x = np.random.default_rng(seed).standard_normal((m, k), dtype=np.float32)
     b = x.view(np.uint32)
     return ((b + 0x7FFF + ((b >> 16) & 1)) >> 16).astype(np.uint16)
+
+
+def synthetic_x_f16(m: int, k: int, seed: int = 1) -> np.ndarray:
+    """X ~ N(0, 1) as fp16 bit patterns [m, k] (round-to-nearest-even)."""
+    x = np.random.default_rng(seed).standard_normal((m, k), dtype=np.float32)
+    return x.astype(np.float16).view(np.uint16)

@@ -204,3 +204,32 @@ def test_gemm_f16_staging_range_check(ctx, typ, m):
         tcc.qlinear(ctx, w, x, stage=tcc.STAGE_BF16, out_dtype=tcc.F32)
         assert ctx.status() == 0
         w.free()
+
+
+@pytest.mark.parametrize("typ", [12, 14])
+@pytest.mark.parametrize("m,n,k", [(300, 640, 768), (40, 512, 1024), (3, 256, 512), (1024, 1920, 1024)])
+def test_gemm_f16_activations_meet_1e3(ctx, typ, m, n, k):
+    """TC_STAGE_F16_X16: fp16 X as given, W staged fp16, every segment on the
+    tensor-core GEMM (also the 3-row one).  Bound: rel-L2 <= 1e-3 against the
+    dequant + fp32 matmul oracle and <= TIGHT against the
+    oracle that stages W in fp16 too."""
+    import torch
+    from turbocider_b200 import cuda as tcc
+    raw = tcc.quantize(typ, kq_cases.synthetic_weight(n, k, seed=m + 7))
+    w = tcc.Weight.upload(ctx, typ, n, k, raw)
+    xh = kq_cases.synthetic_x_f16(m, k, seed=m)
+    x = torch.from_numpy(xh.view(np.int16)).view(torch.float16).cuda()
+    y = tcc.qlinear(ctx, w, x, out_dtype=tcc.F32, stage=tcc.STAGE_F16_X16).cpu().numpy().astype(np.float64)
+    assert ctx.status() == 0
+    assert oracle.rel_l2(y, oracle.qlinear_ref(xh, raw, typ, n, k, "f16", x_dtype="f16")) <= TIGHT
+    e = oracle.rel_l2(y, oracle.qlinear_ref(xh, raw, typ, n, k, "f32", x_dtype="f16"))
+    print(f"type {typ} m {m}: fp16 activations vs f32 decode {e:.2e}")
+    assert e <= 1e-3
+    yb = tcc.qlinear(ctx, w, x, out_dtype=tcc.BF16, stage=tcc.STAGE_F16_X16).float().cpu().numpy()
+    assert oracle.rel_l2(yb, y) <= 3e-3
+    with pytest.raises(tcc.BackendError, match="bf16 X"):
+        ctx.set_path(1)
+        try:
+            tcc.qlinear(ctx, w, x, stage=tcc.STAGE_F16_X16)
+        finally:
+            ctx.set_path(0)

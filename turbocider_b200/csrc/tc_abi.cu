@@ -296,7 +296,9 @@ int tc_cuda_qlinear(tc_cuda_ctx *ctx, const tc_cuda_weight *const *weights, uint
     if (!ctx || !weights || !n_weights || !x || !y || !seg_offsets) return fail("null argument");
     if (!n_seg) return fail("no segments");
     if (out_dtype != TC_DTYPE_F32 && out_dtype != TC_DTYPE_BF16) return fail("output dtype must be f32 or bf16");
-    if (stage != TC_STAGE_BF16 && stage != TC_STAGE_F16) return fail("invalid staging precision");
+    if (stage != TC_STAGE_BF16 && stage != TC_STAGE_F16 && stage != TC_STAGE_F16_X16)
+        return fail("invalid staging precision");
+    if (stage == TC_STAGE_F16_X16 && ctx->path == 1) return fail("the warp GEMV takes bf16 X");
     const tc_cuda_weight *w0 = weights[0];
     if (!w0) return fail("null weight");
     for (uint32_t i = 0; i < n_weights; ++i) {
@@ -328,7 +330,9 @@ int tc_cuda_qlinear(tc_cuda_ctx *ctx, const tc_cuda_weight *const *weights, uint
         if (b == e) continue;
         const tc_cuda_weight *w = weights[seg_weight ? seg_weight[i] : 0];
         const tc::SegmentView sv{b, e, view_of(w)};
-        const bool small = (e - b) <= 16;
+        // fp16 X (TC_STAGE_F16_X16) always takes the tensor-core GEMM: the
+        // warp GEMV works in bf16 code space.
+        const bool small = (e - b) <= 16 && stage != TC_STAGE_F16_X16;
         if ((small && ctx->path < 2) || ctx->path == 1) {
             // The GEMV handles at most 16 rows per launch; longer forced
             // segments are cut into 16-row pieces.
@@ -349,7 +353,7 @@ int tc_cuda_qlinear(tc_cuda_ctx *ctx, const tc_cuda_weight *const *weights, uint
         for (size_t i = 0; i < gemm[t].size(); i += 32) {
             const uint32_t cnt = (uint32_t)std::min<size_t>(32, gemm[t].size() - i);
             cudaError_t e = tc::launch_gemm(gemm[t].data() + i, cnt, xg, m_total, k, y, ldy, out_dtype,
-                                            stage == TC_STAGE_F16, ctx->sm_count, ctx->status,
+                                            stage != TC_STAGE_BF16, ctx->sm_count, ctx->status,
                                             ctx->path != 3, s);
             if (e != cudaSuccess) return cuda_fail("GEMM launch", e);
         }

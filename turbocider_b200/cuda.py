@@ -18,7 +18,7 @@ LIB_PATH = Path(__file__).resolve().parent / "libturbocider_cuda.so"
 
 Q4_K, Q5_K, Q6_K = 12, 13, 14
 F32, F16, BF16 = 0, 1, 2
-STAGE_BF16, STAGE_F16 = 0, 1
+STAGE_BF16, STAGE_F16, STAGE_F16_X16 = 0, 1, 2
 STATUS_NONFINITE_SCALE, STATUS_F16_OVERFLOW, STATUS_TIMEOUT, STATUS_GEOMETRY = 1, 2, 4, 8
 BLOCK_BYTES = {Q4_K: 144, Q6_K: 210}
 
