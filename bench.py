@@ -373,10 +373,13 @@ def run_ours(args):
                "sample": f"layer 0 of the stack (5 linears): decode_cpu_into->f32 + fp32 torch matmul at "
                          f"{cpu_rows} of {M_TOKENS} rows, {reps} repetitions, {t:.1f} s"}
 
+    # DRAM bytes per GEMM launch from the committed ncu summary (mean over one layer)
     traffic = None
-    tfile = ROOT / "profiles" / "gemm_traffic.json"
+    tfile = ROOT / "profiles" / "gemm_pair_config5_layer.md"
     if tfile.exists():
-        traffic = json.loads(tfile.read_text()).get("bytes_per_launch")
+        import re
+        mt = re.search(r"traffic_bytes_per_launch_mean: (\d+)", tfile.read_text())
+        traffic = int(mt.group(1)) if mt else None
     if rank == 0:
         peak = tc_sustained
         line = {"metric": METRIC, "value": round(value, 2), "unit": "TFLOPS", "n_gpus": world, "steps": args.steps,
@@ -393,7 +396,7 @@ def run_ours(args):
                 "gpu_launches": len(timing) * args.steps,
                 "roofline": {"bound": "tensor", "achieved": round(achieved, 2), "peak": peak, "unit": "TFLOP/s",
                              "frac": round(achieved / peak, 4), "traffic": traffic,
-                             "kernel": "gemm_kernel (tcgen05 Q4_K/Q6_K)", "peak_source": f"{peak_src} sustained"},
+                             "kernel": "pair_gemm_kernel (tcgen05 cta_group::2, A in TMEM)", "peak_source": f"{peak_src} sustained"},
                 "e2e": {"value": round(e2e_value, 2), "unit": "TFLOPS",
                         "h2d_bytes_per_step": int(h_xh.numel() * 2 + h_xf.numel() * 2),
                         "d2h_bytes_per_step": int(h_y.numel() * 2), "steps": e2e_steps},
