@@ -163,16 +163,17 @@ def run_reference(args):
 
 # ---------------------------------------------------------------- GPU arm
 def build_weights(ctx, rank, world, layers, device):
-    """Upload every layer's weight shard (rows [r N/g, (r+1) N/g)) to HBM."""
+    """Upload every layer's weight shard (turbocider_b200.shard.shard_rows) to HBM."""
     import torch
     from turbocider_b200 import cuda as tcc
+    from turbocider_b200 import shard
     threads = max(1, (os.cpu_count() or 8) // max(1, world))
     raw_cache = {}
     for d in range(min(DISTINCT_LAYERS, layers)):
         for i, (name, n, k, typ) in enumerate(layer_linears(d)):
             g = torch.Generator(device=device).manual_seed(1000 * d + i)
-            rows = n // world
-            w = torch.randn(n, k, generator=g, device=device)[rank * rows:(rank + 1) * rows].mul_(0.02)
+            b, rows = shard.shard_rows(n, world, rank)
+            w = torch.randn(n, k, generator=g, device=device)[b:b + rows].mul_(0.02)
             raw_cache[(d, name)] = (tcc.quantize(typ, w.cpu().numpy(), threads=threads), rows, k, typ)
             del w
     weights = []
@@ -261,10 +262,11 @@ def run_ours(args):
     compute = torch.cuda.Stream(device)
     comm = torch.cuda.Stream(device)
     names = [l[0] for l in layer_linears(0)]
-    nloc = {name: n // world for name, n, _, _ in layer_linears(0)}
+    from turbocider_b200 import shard
+    nloc = {name: shard.rows_per_rank(n, world) for name, n, _, _ in layer_linears(0)}
     # double-buffered local outputs and gathered outputs per linear
     y_loc = {(name, b): torch.empty(m, nloc[name], device=device, dtype=torch.bfloat16) for name in names for b in (0, 1)}
-    y_all = ({(name, b): torch.empty(world, m, nloc[name], device=device, dtype=torch.bfloat16)
+    y_all = ({(name, b): torch.empty(world * m, nloc[name], device=device, dtype=torch.bfloat16)
               for name in names for b in (0, 1)} if world > 1 else {})
     gathered = {(name, b): None for name in names for b in (0, 1)}
 
@@ -283,7 +285,7 @@ def run_ours(args):
                 if timing is not None:
                     e1 = torch.cuda.Event(enable_timing=True)
                     e1.record(compute)
-                    timing.append((e0, e1, 2.0 * m * nloc[name] * weights[layer][name].k))
+                    timing.append((e0, e1, 2.0 * m * weights[layer][name].n * weights[layer][name].k))
                 if world > 1:
                     done = torch.cuda.Event()
                     done.record(compute)
