@@ -250,6 +250,10 @@ def run_ours(args):
     hbm_peak, tc_burst, tc_sustained, peak_src = peaks()
     layers = args.layers
     ctx = tcc.Context(local)
+    reserve = args.reserve_sms or 0
+    if reserve:
+        # leave SMs free for the NCCL all-gather that runs beside each GEMM
+        ctx.set_sm_limit(torch.cuda.get_device_properties(device).multi_processor_count - reserve)
     weights = build_weights(ctx, rank, world, layers, device)
 
     m = M_TOKENS
@@ -391,7 +395,9 @@ def run_ours(args):
                 "config": {"workload": "config5_zimage_6b_linear_stack", "layers": layers, "m_tokens": m,
                            "operands": "X fp16, W dequantised to fp16 in TMEM, fp32 accumulate, bf16 Y",
                            "hidden": HIDDEN, "ffn": FFN, "mix": "Q4_K_M (w2 Q6_K in even layers)",
-                           "parallelism": f"N-shard x{world} + NCCL all-gather" if world > 1 else "single GPU",
+                           "parallelism": (f"N-shard x{world} + NCCL all-gather"
+                                           + (f" ({reserve} SMs left to it)" if reserve else "")
+                                           if world > 1 else "single GPU"),
                            "l2": "inputs larger than L2 (3 GB of packed weights streamed per step)",
                            "weights": f"{layers} distinct HBM buffers per tensor, contents cycle over "
                                       f"{DISTINCT_LAYERS} seeds"},
@@ -428,6 +434,8 @@ def main():
     ap.add_argument("--cpu-rows", type=int, default=None,
                     help="rows of X in the CPU sample (default: 2048 per reference-arm step, all rows for cpu_baseline)")
     ap.add_argument("--no-extras", action="store_true", help="skip the GEMV and CPU-baseline legs")
+    ap.add_argument("--reserve-sms", type=int, default=None,
+                    help="SMs kept free of the GEMM for the all-gather (default 0: measured no gain at N=2)")
     args = ap.parse_args()
     if args.warmup < 3 and args.impl == "ours":
         args.warmup = 3

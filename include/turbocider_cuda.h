@@ -152,6 +152,12 @@ int tc_cuda_qlinear(tc_cuda_ctx *ctx, const tc_cuda_weight *const *weights, uint
  *   3 tensor-core GEMM with one-CTA tiles only (no 2-CTA pairs). */
 int tc_cuda_set_path(tc_cuda_ctx *ctx, int path);
 
+/* Cap the SMs the tensor-core GEMM's persistent grid may occupy (0 = all, the
+ * default).  The GEMM holds one CTA per SM for its whole run; with N-column
+ * sharding a communication kernel (the all-gather of the previous linear's
+ * output) runs beside it, and it needs free SMs to make progress. */
+int tc_cuda_set_sm_limit(tc_cuda_ctx *ctx, int sms);
+
 /* Allocation-free small-M quantised linear.  No counterpart in the reference.
  * For callers that must not allocate device memory while they run a linear
  * (a pre-sized memory arena, code under an allocator callback, a loop that

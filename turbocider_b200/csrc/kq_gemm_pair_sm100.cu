@@ -572,7 +572,8 @@ PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
 }
 
 template <int TYPE, bool F16, bool OUT_F32>
-cudaError_t launch_pair_inst(const CUtensorMap &xm, const CUtensorMap &ym, const PairParams &p, cudaStream_t s) {
+cudaError_t launch_pair_inst(const CUtensorMap &xm, const CUtensorMap &ym, const PairParams &p, int sm_count,
+                             cudaStream_t s) {
     using L = PairLayout<TYPE>;
     auto kernel = pair_gemm_kernel<TYPE, F16, OUT_F32>;
     static int max_clusters = 0;   // co-resident 2-CTA clusters on this GPU
@@ -587,7 +588,8 @@ cudaError_t launch_pair_inst(const CUtensorMap &xm, const CUtensorMap &ym, const
         if (e != cudaSuccess) return e;
         if (max_clusters < 1) return cudaErrorInvalidConfiguration;
     }
-    const uint32_t pairs = p.n_tiles < (uint32_t)max_clusters ? p.n_tiles : (uint32_t)max_clusters;
+    uint32_t pairs = p.n_tiles < (uint32_t)max_clusters ? p.n_tiles : (uint32_t)max_clusters;
+    if (sm_count >= 2 && pairs > (uint32_t)sm_count / 2) pairs = (uint32_t)sm_count / 2;
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(2 * pairs);
     cfg.blockDim = dim3(kThreads);
@@ -604,8 +606,8 @@ cudaError_t launch_pair_inst(const CUtensorMap &xm, const CUtensorMap &ym, const
 }  // namespace
 
 cudaError_t launch_gemm_pair(const SegmentView *segs, uint32_t n_seg, const uint16_t *x, uint64_t m_total,
-                             uint64_t k, void *y, uint64_t ldy, int out_dtype, int stage_f16, uint32_t *status,
-                             cudaStream_t s) {
+                             uint64_t k, void *y, uint64_t ldy, int out_dtype, int stage_f16, int sm_count,
+                             uint32_t *status, cudaStream_t s) {
     if (n_seg == 0) return cudaSuccess;
     if (n_seg > (uint32_t)kMaxSeg) return cudaErrorInvalidValue;
     PairParams p{};
@@ -651,11 +653,11 @@ cudaError_t launch_gemm_pair(const SegmentView *segs, uint32_t n_seg, const uint
     }
     const uint32_t type = segs[0].w.type;
     if (type == 12) {
-        if (stage_f16) return out_f32 ? launch_pair_inst<12, true, true>(xm, ym, p, s) : launch_pair_inst<12, true, false>(xm, ym, p, s);
-        return out_f32 ? launch_pair_inst<12, false, true>(xm, ym, p, s) : launch_pair_inst<12, false, false>(xm, ym, p, s);
+        if (stage_f16) return out_f32 ? launch_pair_inst<12, true, true>(xm, ym, p, sm_count, s) : launch_pair_inst<12, true, false>(xm, ym, p, sm_count, s);
+        return out_f32 ? launch_pair_inst<12, false, true>(xm, ym, p, sm_count, s) : launch_pair_inst<12, false, false>(xm, ym, p, sm_count, s);
     }
-    if (stage_f16) return out_f32 ? launch_pair_inst<14, true, true>(xm, ym, p, s) : launch_pair_inst<14, true, false>(xm, ym, p, s);
-    return out_f32 ? launch_pair_inst<14, false, true>(xm, ym, p, s) : launch_pair_inst<14, false, false>(xm, ym, p, s);
+    if (stage_f16) return out_f32 ? launch_pair_inst<14, true, true>(xm, ym, p, sm_count, s) : launch_pair_inst<14, true, false>(xm, ym, p, sm_count, s);
+    return out_f32 ? launch_pair_inst<14, false, true>(xm, ym, p, sm_count, s) : launch_pair_inst<14, false, false>(xm, ym, p, sm_count, s);
 }
 
 }  // namespace tc

@@ -334,7 +334,7 @@ cudaError_t launch_gemm(const SegmentView *segs, uint32_t n_seg, const uint16_t 
     for (uint32_t i = 0; i < n_seg; ++i) max_rows = max(max_rows, segs[i].m_end - segs[i].m_begin);
     const int bn = max_rows <= 64 ? 64 : max_rows <= 128 ? 128 : 256;
     if (bn == 256 && allow_pair)
-        return launch_gemm_pair(segs, n_seg, x, m_total, k, y, ldy, out_dtype, stage_f16, status, s);
+        return launch_gemm_pair(segs, n_seg, x, m_total, k, y, ldy, out_dtype, stage_f16, sm_count, status, s);
     GemmParams p{};
     p.n_seg = n_seg;
     p.kb = segs[0].w.kb;

@@ -290,6 +290,13 @@ int tc_cuda_set_path(tc_cuda_ctx *ctx, int path) {
     return ok();
 }
 
+int tc_cuda_set_sm_limit(tc_cuda_ctx *ctx, int sms) {
+    if (!ctx) return fail("null context");
+    if (sms < 0) return fail("negative SM limit");
+    ctx->sm_limit = sms;
+    return ok();
+}
+
 int tc_cuda_qlinear(tc_cuda_ctx *ctx, const tc_cuda_weight *const *weights, uint32_t n_weights,
                     const int32_t *seg_offsets, const int32_t *seg_weight, uint32_t n_seg, const void *x, void *y,
                     uint64_t ldy, int out_dtype, int stage, void *stream) {
@@ -353,7 +360,9 @@ int tc_cuda_qlinear(tc_cuda_ctx *ctx, const tc_cuda_weight *const *weights, uint
         for (size_t i = 0; i < gemm[t].size(); i += 32) {
             const uint32_t cnt = (uint32_t)std::min<size_t>(32, gemm[t].size() - i);
             cudaError_t e = tc::launch_gemm(gemm[t].data() + i, cnt, xg, m_total, k, y, ldy, out_dtype,
-                                            stage != TC_STAGE_BF16, ctx->sm_count, ctx->status,
+                                            stage != TC_STAGE_BF16,
+                                            ctx->sm_limit > 0 ? std::min(ctx->sm_limit, ctx->sm_count) : ctx->sm_count,
+                                            ctx->status,
                                             ctx->path != 3, s);
             if (e != cudaSuccess) return cuda_fail("GEMM launch", e);
         }

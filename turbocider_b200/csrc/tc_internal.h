@@ -16,6 +16,7 @@ struct tc_cuda_ctx {
     uint32_t *gemv_counters = nullptr;  // per-16-row-tile arrival counters, kept at 0
     size_t gemv_counters_n = 0;
     int path = 0;                    // 0 auto, 1 GEMV, 2 GEMM, 3 GEMM with one-CTA tiles only
+    int sm_limit = 0;                // SMs the tensor-core GEMM may occupy (0 = all)
 };
 
 struct tc_cuda_weight {
@@ -77,6 +78,6 @@ cudaError_t launch_gemm(const SegmentView *segs, uint32_t n_seg, const uint16_t 
                         int stage_f16, int sm_count, uint32_t *status, int allow_pair, cudaStream_t s);
 cudaError_t launch_gemm_pair(const SegmentView *segs, uint32_t n_seg, const uint16_t *x,
                              uint64_t m_total, uint64_t k, void *y, uint64_t ldy, int out_dtype,
-                             int stage_f16, uint32_t *status, cudaStream_t s);
+                             int stage_f16, int sm_count, uint32_t *status, cudaStream_t s);
 
 }  // namespace tc

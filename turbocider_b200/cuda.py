@@ -53,6 +53,7 @@ EXPORTS = {
     "tc_cuda_qlinear": (C.c_int, [_vp, C.POINTER(_vp), _u32, C.POINTER(_i32), C.POINTER(_i32), _u32, _vp, _vp,
                                   _u64, C.c_int, C.c_int, _vp]),
     "tc_cuda_set_path": (C.c_int, [_vp, C.c_int]),
+    "tc_cuda_set_sm_limit": (C.c_int, [_vp, C.c_int]),
     "tc_quantize": (C.c_int, [_u32, _vp, _u64, _u64, _vp, _u64, C.c_int]),
     "tc_cuda_qlinear_small_static": (C.c_int, [_vp, _vp, _u32, _vp, _u64, C.c_int, _vp]),
 }
@@ -117,6 +118,10 @@ class Context:
 
     def set_path(self, path: int):
         _check(lib().tc_cuda_set_path(self._h, path))
+
+    def set_sm_limit(self, sms: int):
+        """SMs the tensor-core GEMM may occupy (0 = all)."""
+        _check(lib().tc_cuda_set_sm_limit(self._h, sms))
 
     def close(self):
         if self._h:
