@@ -174,6 +174,39 @@ int tc_cuda_set_sm_limit(tc_cuda_ctx *ctx, int sms);
 int tc_cuda_qlinear_small_static(const tc_cuda_weight *weight, const void *x, uint32_t m, void *y, uint64_t ldy,
                                  int out_dtype, void *stream);
 
+/* ---------------------------------------------------------------- GGUF files
+ * Directory parser and payload reader for GGUF v2/v3 containers, with the
+ * reference's acceptance rules and error texts (read_directory,
+ * native/core/gguf_directory.hpp:199-271): magic and version, metadata with
+ * parse limits, tensor table (rank <= 4, block-aligned rows, known GGML type),
+ * general.alignment, payload bounds and overlap.  Host only, no GPU work. */
+typedef struct tc_gguf tc_gguf;
+
+/* Open and parse `path`; `limit` is NULL (or a test hook shrinking one parse
+ * limit: "retained", "directory", "string", "count", "array").  The file
+ * stays open for tc_gguf_read until tc_gguf_close. */
+int tc_gguf_open(const char *path, const char *limit, tc_gguf **file);
+void tc_gguf_close(tc_gguf *file);
+int tc_gguf_info(const tc_gguf *file, uint32_t *version, uint32_t *alignment, uint64_t *n_tensors,
+                 uint64_t *data_offset, uint64_t *n_metadata);
+/* Tensor `index`: NUL-terminated name (name_cap bytes available), GGML type,
+ * rank, dims[4] (dims[0] = contiguous extent K; unused dims = 1), absolute
+ * file offset and payload bytes (cf. TensorDescriptor, gguf_directory.hpp:63-71). */
+int tc_gguf_tensor(const tc_gguf *file, uint64_t index, char *name, uint64_t name_cap, uint32_t *ggml_type,
+                   uint32_t *rank, uint64_t *dims, uint64_t *file_offset, uint64_t *bytes);
+int tc_gguf_find(const tc_gguf *file, const char *name, uint64_t *index);
+/* Metadata entry `key`: GGUF value type, raw unsigned bits, sign-extended
+ * value, float value, string text (type 8), element count (type 9 arrays). */
+int tc_gguf_meta(const tc_gguf *file, const char *key, uint32_t *type, uint64_t *u, int64_t *i, double *f,
+                 char *text, uint64_t text_cap, uint64_t *array_count);
+/* Read rows [row_begin, row_begin + rows) of a tensor's payload (raw GGUF
+ * blocks, row pitch dims[0] / block_elements * block_bytes) into host memory
+ * (pinned memory lets the following upload run at full PCIe rate). */
+int tc_gguf_read(const tc_gguf *file, uint64_t index, uint64_t row_begin, uint64_t rows, void *dst,
+                 uint64_t dst_bytes);
+/* Validate a split set (validate_split_set, gguf_directory.hpp:273-304). */
+int tc_gguf_validate_split(const tc_gguf *const *shards, uint32_t n);
+
 /* Host-side GGUF K-quant quantiser (not in the reference, which ships no
  * encoder): quantise a row-major fp32 [rows, cols] matrix (cols % 256 == 0) to
  * raw GGUF blocks of `ggml_type` (Q4_K or Q6_K) using `threads` CPU threads.

@@ -56,6 +56,17 @@ EXPORTS = {
     "tc_cuda_set_sm_limit": (C.c_int, [_vp, C.c_int]),
     "tc_quantize": (C.c_int, [_u32, _vp, _u64, _u64, _vp, _u64, C.c_int]),
     "tc_cuda_qlinear_small_static": (C.c_int, [_vp, _vp, _u32, _vp, _u64, C.c_int, _vp]),
+    "tc_gguf_open": (C.c_int, [C.c_char_p, C.c_char_p, C.POINTER(_vp)]),
+    "tc_gguf_close": (None, [_vp]),
+    "tc_gguf_info": (C.c_int, [_vp, C.POINTER(_u32), C.POINTER(_u32), C.POINTER(_u64), C.POINTER(_u64),
+                               C.POINTER(_u64)]),
+    "tc_gguf_tensor": (C.c_int, [_vp, _u64, C.c_char_p, _u64, C.POINTER(_u32), C.POINTER(_u32), C.POINTER(_u64),
+                                 C.POINTER(_u64), C.POINTER(_u64)]),
+    "tc_gguf_find": (C.c_int, [_vp, C.c_char_p, C.POINTER(_u64)]),
+    "tc_gguf_meta": (C.c_int, [_vp, C.c_char_p, C.POINTER(_u32), C.POINTER(_u64), C.POINTER(C.c_int64),
+                               C.POINTER(C.c_double), C.c_char_p, _u64, C.POINTER(_u64)]),
+    "tc_gguf_read": (C.c_int, [_vp, _u64, _u64, _u64, _vp, _u64]),
+    "tc_gguf_validate_split": (C.c_int, [C.POINTER(_vp), _u32]),
 }
 
 
@@ -244,3 +255,86 @@ def qlinear_small_static(weight: Weight, x, out_dtype: int = BF16, out=None, str
     _check(lib().tc_cuda_qlinear_small_static(weight.handle, x.data_ptr(), x.shape[0], out.data_ptr(),
                                               out.stride(0), out_dtype, _stream_ptr(stream)))
     return out
+
+
+class GGUFError(BackendError):
+    """A GGUF file the reader rejects (message as the reference's gguf_invalid: ...)."""
+
+
+class GGUFFile:
+    """A parsed GGUF container (tc_gguf_*): directory, metadata lookup and
+    row-range payload reads into host memory."""
+
+    def __init__(self, path, limit: str | None = None):
+        self._h = _vp()
+        rc = lib().tc_gguf_open(str(path).encode(), limit.encode() if limit else None, C.byref(self._h))
+        _check(rc, GGUFError)
+        v, a, n, d, nm = _u32(), _u32(), _u64(), _u64(), _u64()
+        _check(lib().tc_gguf_info(self._h, C.byref(v), C.byref(a), C.byref(n), C.byref(d), C.byref(nm)), GGUFError)
+        self.version, self.alignment, self.data_offset = v.value, a.value, d.value
+        self.tensors = [self._tensor(i) for i in range(n.value)]
+        self.n_metadata = nm.value
+
+    def _tensor(self, i: int) -> dict:
+        name = C.create_string_buffer(4096)
+        t, r, off, nb = _u32(), _u32(), _u64(), _u64()
+        dims = (_u64 * 4)()
+        _check(lib().tc_gguf_tensor(self._h, i, name, 4096, C.byref(t), C.byref(r), dims, C.byref(off),
+                                    C.byref(nb)), GGUFError)
+        d = list(dims)[:r.value]
+        rows = 1
+        for x in d[1:]:
+            rows *= x
+        return {"name": name.value.decode(), "type": t.value, "dims": d, "rows": rows, "columns": d[0],
+                "file_offset": off.value, "bytes": nb.value}
+
+    def tensor(self, name: str) -> dict:
+        idx = _u64()
+        _check(lib().tc_gguf_find(self._h, name.encode(), C.byref(idx)), GGUFError)
+        return dict(self.tensors[idx.value], index=idx.value)
+
+    def meta(self, key: str):
+        t, u, i, f, cnt = _u32(), _u64(), C.c_int64(), C.c_double(), _u64()
+        text = C.create_string_buffer(1 << 20)
+        _check(lib().tc_gguf_meta(self._h, key.encode(), C.byref(t), C.byref(u), C.byref(i), C.byref(f), text,
+                                  1 << 20, C.byref(cnt)), GGUFError)
+        kind = t.value
+        if kind == 8:
+            return text.value.decode()
+        if kind == 9:
+            return ("array", cnt.value)
+        if kind in (6, 12):
+            return f.value
+        if kind in (1, 3, 5, 11):
+            return i.value
+        return u.value
+
+    def read(self, name_or_index, row_begin: int = 0, rows: int | None = None, out=None) -> np.ndarray:
+        """Raw block bytes of rows [row_begin, +rows) into `out` (a uint8
+        numpy array or a pinned torch uint8 tensor; allocated if None)."""
+        info = self.tensors[name_or_index] if isinstance(name_or_index, int) else self.tensor(name_or_index)
+        idx = name_or_index if isinstance(name_or_index, int) else info["index"]
+        rows = info["rows"] - row_begin if rows is None else rows
+        nbytes = info["bytes"] // info["rows"] * rows
+        if out is None:
+            out = np.empty(nbytes, dtype=np.uint8)
+        ptr = out.data_ptr() if hasattr(out, "data_ptr") else out.ctypes.data
+        size = out.numel() if hasattr(out, "numel") else out.nbytes
+        _check(lib().tc_gguf_read(self._h, idx, row_begin, rows, ptr, size), GGUFError)
+        return out
+
+    @staticmethod
+    def validate_split(files) -> None:
+        arr = (_vp * len(files))(*[f._h for f in files])
+        _check(lib().tc_gguf_validate_split(arr, len(files)), GGUFError)
+
+    def close(self):
+        if self._h:
+            lib().tc_gguf_close(self._h)
+            self._h = _vp()
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
