@@ -105,6 +105,21 @@ int tc_cuda_weight_fill_device(tc_cuda_ctx *ctx, tc_cuda_weight *weight, const v
                                uint64_t raw_bytes, void *stream);
 void tc_cuda_weight_free(tc_cuda_weight *weight);
 
+/* Streaming from pinned host memory (cf. the reference's streamed GGUF
+ * weights: GgufPackedBank / GgufWeightPager, native/runtime/streaming/).
+ * tc_relayout_host re-lays rows [n_begin, n_begin + n_count) (0 = to the end)
+ * of a raw GGUF matrix [n, k] into the panel layout of an n_count-row weight,
+ * on `threads` CPU threads, checking every d/dmin is finite; tc_panel_bytes
+ * is the size of that layout.  tc_cuda_weight_copy_panels then copies panel
+ * bytes (pinned host or device memory, exactly weight_info's device_bytes)
+ * into a weight made by tc_cuda_weight_create, asynchronously on `stream`,
+ * with no kernel (so it overlaps a running GEMM). */
+uint64_t tc_panel_bytes(uint32_t ggml_type, uint64_t n, uint64_t k);
+int tc_relayout_host(uint32_t ggml_type, const void *raw, uint64_t raw_bytes, uint64_t n, uint64_t k,
+                     uint64_t n_begin, uint64_t n_count, void *panels, uint64_t panel_bytes, int threads);
+int tc_cuda_weight_copy_panels(tc_cuda_ctx *ctx, tc_cuda_weight *weight, const void *panels, uint64_t bytes,
+                               void *stream);
+
 /* Shape queries of an uploaded weight. */
 int tc_cuda_weight_info(const tc_cuda_weight *weight, uint32_t *ggml_type, uint64_t *n,
                         uint64_t *k, uint64_t *device_bytes);

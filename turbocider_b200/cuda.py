@@ -56,6 +56,9 @@ EXPORTS = {
     "tc_cuda_set_sm_limit": (C.c_int, [_vp, C.c_int]),
     "tc_quantize": (C.c_int, [_u32, _vp, _u64, _u64, _vp, _u64, C.c_int]),
     "tc_cuda_qlinear_small_static": (C.c_int, [_vp, _vp, _u32, _vp, _u64, C.c_int, _vp]),
+    "tc_panel_bytes": (_u64, [_u32, _u64, _u64]),
+    "tc_relayout_host": (C.c_int, [_u32, _vp, _u64, _u64, _u64, _u64, _u64, _vp, _u64, C.c_int]),
+    "tc_cuda_weight_copy_panels": (C.c_int, [_vp, _vp, _vp, _u64, _vp]),
     "tc_gguf_open": (C.c_int, [C.c_char_p, C.c_char_p, C.POINTER(_vp)]),
     "tc_gguf_close": (None, [_vp]),
     "tc_gguf_info": (C.c_int, [_vp, C.POINTER(_u32), C.POINTER(_u32), C.POINTER(_u64), C.POINTER(_u64),
@@ -107,6 +110,28 @@ def quantize(ggml_type: int, w: np.ndarray, threads: int | None = None) -> np.nd
                            threads or os.cpu_count() or 1)
     if rc != 0:
         raise BackendError("tc_quantize rejected the input (type, shape or nonfinite values)")
+    return out
+
+
+def panel_bytes(ggml_type: int, n: int, k: int) -> int:
+    """Bytes of the panel layout of an [n, k] weight (0 = unsupported)."""
+    return int(lib().tc_panel_bytes(ggml_type, n, k))
+
+
+def relayout_host(ggml_type: int, raw, n: int, k: int, n_begin: int = 0, n_count: int = 0, out=None,
+                  threads: int | None = None):
+    """Panel layout of rows [n_begin, +n_count) of a raw GGUF matrix, built on
+    the CPU (uint8 numpy array in, uint8 numpy array or pinned torch tensor out)."""
+    raw = np.ascontiguousarray(np.frombuffer(raw, dtype=np.uint8) if isinstance(raw, (bytes, bytearray))
+                               else raw).view(np.uint8).reshape(-1)
+    rows = n_count or (n - n_begin)
+    size = panel_bytes(ggml_type, rows, k)
+    if out is None:
+        out = np.empty(size, dtype=np.uint8)
+    ptr = out.data_ptr() if hasattr(out, "data_ptr") else out.ctypes.data
+    cap = out.numel() if hasattr(out, "numel") else out.nbytes
+    _check(lib().tc_relayout_host(ggml_type, raw.ctypes.data, raw.nbytes, n, k, n_begin, n_count, ptr, cap,
+                                  threads or os.cpu_count() or 1), DecodeError)
     return out
 
 
@@ -169,6 +194,12 @@ class Weight:
         h = _vp()
         _check(lib().tc_cuda_weight_create(ctx.handle, ggml_type, n, k, C.byref(h)))
         return cls(ctx, h)
+
+    def copy_panels(self, panels, stream=None):
+        """Asynchronous copy of panel-layout bytes (tc_relayout_host output,
+        pinned host or device torch uint8 tensor) into this weight."""
+        _check(lib().tc_cuda_weight_copy_panels(self.ctx.handle, self._h, panels.data_ptr(), panels.numel(),
+                                                _stream_ptr(stream)))
 
     def fill_device(self, raw_device, stream=None):
         """Re-layout raw GGUF rows already in device memory (torch uint8 tensor)."""
