@@ -23,9 +23,12 @@
 // Work split: CTA (x, y) = (16 weight rows, one K slice of 4 super-blocks),
 // 4 warps each taking one super-block, so that thousands of short CTAs keep
 // every SM's loads in flight (the CTA count is independent of the SM count).
-// Each warp issues all loads of its super-block first; the CTA stages its X
-// slice in shared memory meanwhile (rows padded so token rows use distinct
-// banks).  A CTA
+// Each warp streams its super-blocks' packed fields through a 3-stage ring of
+// bulk copies.  With one token (TP = 1) the stage also carries that token's
+// 256 columns of X (512 B); with more tokens X is read straight from global
+// memory instead (at most 16 rows x K, the same for every row tile, so it
+// stays in L1 / L2): staging M rows per stage would shrink the number of
+// resident CTAs as M grows (one CTA of 4 warps per SM at M = 16).  A CTA
 // sums its warps through shared memory; with several K slices it stores the
 // 16 x M partial in the context workspace, and the last CTA of the row tile to
 // finish (per-tile arrival counter) adds the slices in slice order -- a fixed
@@ -60,11 +63,10 @@ __device__ __forceinline__ void mma16816(float (&d)[4], uint32_t a0, uint32_t a1
 
 // ---------------------------------------------------------------- staging
 // Per-warp stage in shared memory: the packed fields of 16 weight rows for one
-// super-block (contiguous pieces of the panel chunk, one bulk copy each) and
-// the matching 256 columns of X for each token.
+// super-block (contiguous pieces of the panel chunk, one bulk copy each).
 //   Q4_K: qs [4][16 rows][32] | sc [16][12] | dm [16][4]              = 2304 B
 //   Q6_K: ql [4 = h*2+part][16][32] | qh [2][16][32] | sc [16][16] | d [16][2] = 3360 B
-// followed by X [m][256] bf16.  Row r of a piece is at row_slot(r0 + r) - r0.
+// Row r of a piece is at row_slot(r0 + r) - r0.
 template <int TYPE> struct StageGeo;
 template <> struct StageGeo<12> {
     static constexpr uint32_t w_bytes = 2304, qs = 0, sc = 2048, dm = 2240;
@@ -107,12 +109,11 @@ __device__ __noinline__ bool mbar_wait(uint32_t b, uint32_t parity, uint32_t *st
 }
 
 // Lane 0 of a warp: enqueue the weight copies of one super-block into stage
-// buffer st (the stage's barrier expects the X bytes too; issue_x adds them).
-template <int TYPE>
-__device__ __forceinline__ void issue_w(uint8_t *st, uint32_t bar, const uint8_t *chunk, uint32_t r0,
-                                        uint32_t m_count) {
+// buffer st.
+template <int TYPE, bool STAGE_X>
+__device__ __forceinline__ void issue_w(uint8_t *st, uint32_t bar, const uint8_t *chunk, uint32_t r0) {
     using SG = StageGeo<TYPE>;
-    mbar_expect(bar, SG::w_bytes + m_count * 512);
+    mbar_expect(bar, SG::w_bytes + (STAGE_X ? 512u : 0u));
     const uint32_t d = s_u32(st);
     if constexpr (TYPE == 12) {
 #pragma unroll
@@ -130,12 +131,11 @@ __device__ __forceinline__ void issue_w(uint8_t *st, uint32_t bar, const uint8_t
         bulk_g2s(d + SG::d, chunk + kQ6D + r0 * 2, 32, bar);
     }
 }
+// Lane 0: the single token's 256 columns of X for super-block kb (TP = 1).
 template <int TYPE>
-__device__ __forceinline__ void issue_x(uint8_t *st, uint32_t bar, const uint16_t *x, uint64_t k, uint32_t m_begin,
-                                        uint32_t m_count, uint32_t kb) {
-    const uint32_t d = s_u32(st) + StageGeo<TYPE>::w_bytes;
-    for (uint32_t tok = 0; tok < m_count; ++tok)
-        bulk_g2s(d + tok * 512, x + (uint64_t)(m_begin + tok) * k + (uint64_t)kb * 256, 512, bar);
+__device__ __forceinline__ void issue_x1(uint8_t *st, uint32_t bar, const uint16_t *x, uint64_t k, uint32_t m,
+                                         uint32_t kb) {
+    bulk_g2s(s_u32(st) + StageGeo<TYPE>::w_bytes, x + (uint64_t)m * k + (uint64_t)kb * 256, 512, bar);
 }
 // Programmatic dependent launch: let the next kernel in the stream start its
 // prologue, and wait for the previous one before touching its outputs.
@@ -173,8 +173,9 @@ __device__ __forceinline__ constexpr uint32_t group_of_visit(uint32_t v) {
 }
 
 template <int TYPE, int TP, int NT>
-__device__ __forceinline__ void compute_stage(const uint8_t *st, uint32_t m_count, uint32_t g, uint32_t t,
-                                              uint32_t lane, float *wt, float (&acc)[NT][4]) {
+__device__ __forceinline__ void compute_stage(const uint8_t *st, const uint16_t *__restrict__ x, uint64_t k,
+                                              uint32_t m_begin, uint32_t kb, uint32_t m_count, uint32_t g,
+                                              uint32_t t, uint32_t lane, float *wt, float (&acc)[NT][4]) {
     using SG = StageGeo<TYPE>;
     constexpr uint32_t S = 8 / TP;
     constexpr uint32_t GROUPS = TYPE == 12 ? 8 : 16;
@@ -209,10 +210,11 @@ __device__ __forceinline__ void compute_stage(const uint8_t *st, uint32_t m_coun
         o[1] = make_float4(d * (b[0] - 128.f), d * (b[1] - 128.f), d * (b[2] - 128.f), d * (b[3] - 128.f));
     }
     __syncwarp();
-    const uint16_t *xst = reinterpret_cast<const uint16_t *>(st + SG::w_bytes);
-    const uint16_t *xrow[NT];
+    const uint16_t *xrow[NT];   // this thread's tokens, columns of this super-block
 #pragma unroll
-    for (int nt = 0; nt < NT; ++nt) xrow[nt] = xst + min(8 * nt + g % TP, m_count - 1) * 256;
+    for (int nt = 0; nt < NT; ++nt)
+        xrow[nt] = TP == 1 ? reinterpret_cast<const uint16_t *>(st + SG::w_bytes)
+                           : x + (uint64_t)(m_begin + min(8 * nt + g % TP, m_count - 1)) * k + (uint64_t)kb * 256;
     const uint32_t my_j = g / TP;
     const uint32_t ones = 0x3F803F80u;
     constexpr float off = TYPE == 12 ? 128.f : 160.f;
@@ -231,7 +233,8 @@ __device__ __forceinline__ void compute_stage(const uint8_t *st, uint32_t m_coun
         const uint32_t a2 = code_pair(cg, 0x4342u), a3 = code_pair(cg8, 0x4342u);
 #pragma unroll
         for (int nt = 0; nt < NT; ++nt) {
-            const uint2 xv = *reinterpret_cast<const uint2 *>(xrow[nt] + kloc);
+            const uint2 xv = TP == 1 ? *reinterpret_cast<const uint2 *>(xrow[nt] + kloc)
+                                     : __ldg(reinterpret_cast<const uint2 *>(xrow[nt] + kloc));
             const bool on = my_j == j;
             const uint32_t b0 = on ? xv.x : 0u, b1 = on ? xv.y : 0u;
             mma16816(cq[nt], a0, a1, a2, a3, b0, b1, cq[nt]);
@@ -327,7 +330,8 @@ __global__ void __launch_bounds__(kWarps * 32) gemv_kernel(WeightView w, const u
     const uint32_t n_slices = gridDim.y, kb_begin = blockIdx.y * kb_per_slice;
     const uint32_t kb_end = min(w.kb, kb_begin + kb_per_slice);
     const uint8_t *pbase = w.chunks + (uint64_t)panel * w.kb * chunk;
-    const uint32_t stage_bytes = (SG::w_bytes + m_count * 512 + 127) / 128 * 128;
+    constexpr bool kStageX = TP == 1;
+    constexpr uint32_t stage_bytes = (SG::w_bytes + (kStageX ? 512u : 0u) + 127) / 128 * 128;
     uint8_t *mine = dyn + (size_t)warp * kGemvStages * stage_bytes;
     float *wt = tab[warp];
     if (lane == 0)
@@ -343,14 +347,14 @@ __global__ void __launch_bounds__(kWarps * 32) gemv_kernel(WeightView w, const u
     if (lane == 0) {
         for (uint32_t i = 0; i < min(count, kGemvStages - 1); ++i) {
             const uint32_t kb = first + kWarps * i;
-            issue_w<TYPE>(mine + i * stage_bytes, s_u32(&bars[warp][i]), pbase + (uint64_t)kb * chunk, r0, m_count);
+            issue_w<TYPE, kStageX>(mine + i * stage_bytes, s_u32(&bars[warp][i]), pbase + (uint64_t)kb * chunk, r0);
         }
     }
     if (threadIdx.x == 0) pdl_launch_dependents();
     pdl_wait();
-    if (lane == 0)
+    if (kStageX && lane == 0)
         for (uint32_t i = 0; i < min(count, kGemvStages - 1); ++i)
-            issue_x<TYPE>(mine + i * stage_bytes, s_u32(&bars[warp][i]), x, k, m_begin, m_count, first + kWarps * i);
+            issue_x1<TYPE>(mine + i * stage_bytes, s_u32(&bars[warp][i]), x, k, m_begin, first + kWarps * i);
     float acc[NT][4];
 #pragma unroll
     for (int nt = 0; nt < NT; ++nt)
@@ -364,11 +368,12 @@ __global__ void __launch_bounds__(kWarps * 32) gemv_kernel(WeightView w, const u
             const uint32_t j = i + kGemvStages - 1, kb = first + kWarps * j;
             uint8_t *sj = mine + (j % kGemvStages) * stage_bytes;
             const uint32_t bj = s_u32(&bars[warp][j % kGemvStages]);
-            issue_w<TYPE>(sj, bj, pbase + (uint64_t)kb * chunk, r0, m_count);
-            issue_x<TYPE>(sj, bj, x, k, m_begin, m_count, kb);
+            issue_w<TYPE, kStageX>(sj, bj, pbase + (uint64_t)kb * chunk, r0);
+            if (kStageX) issue_x1<TYPE>(sj, bj, x, k, m_begin, kb);
         }
         if (!mbar_wait(s_u32(&bars[warp][slot]), parity, status)) { ok = false; break; }
-        compute_stage<TYPE, TP, NT>(mine + slot * stage_bytes, m_count, g, t, lane, wt, acc);
+        compute_stage<TYPE, TP, NT>(mine + slot * stage_bytes, x, k, m_begin, first + kWarps * i, m_count, g, t,
+                                    lane, wt, acc);
         __syncwarp();
     }
     if (!ok) {
@@ -473,13 +478,13 @@ cudaError_t launch_typed(const SegmentView &seg, const uint16_t *x, uint64_t k, 
                          int out_dtype, const GemvSplit &sp, cudaStream_t s) {
     const dim3 grid((seg.w.n + 15) / 16, sp.n_slices);
     const uint32_t mc = seg.m_end - seg.m_begin;
-    const size_t stage = (StageGeo<TYPE>::w_bytes + (size_t)mc * 512 + 127) / 128 * 128;
+    const size_t stage = (StageGeo<TYPE>::w_bytes + (TP == 1 ? 512u : 0u) + 127) / 128 * 128;
     const size_t smem = stage * kGemvStages * kWarps;
     auto kern = out_dtype == 0 ? gemv_kernel<TYPE, TP, NT, 0> : gemv_kernel<TYPE, TP, NT, 2>;
     // Opt in once per instantiation to the largest stage set (16 tokens).
     static bool configured[2] = {false, false};
     if (!configured[out_dtype == 0]) {
-        const int most = (int)((StageGeo<TYPE>::w_bytes + 16 * 512 + 127) / 128 * 128 * kGemvStages * kWarps);
+        const int most = (int)((StageGeo<TYPE>::w_bytes + (TP == 1 ? 512u : 0u) + 127) / 128 * 128 * kGemvStages * kWarps);
         cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, most);
         if (e != cudaSuccess) return e;
         configured[out_dtype == 0] = true;
