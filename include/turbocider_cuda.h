@@ -162,6 +162,16 @@ int tc_cuda_qlinear(tc_cuda_ctx *ctx, const tc_cuda_weight *const *weights, uint
                     const int32_t *seg_offsets, const int32_t *seg_weight, uint32_t n_seg,
                     const void *x, void *y, uint64_t ldy, int out_dtype, int stage, void *stream);
 
+/* Batched small-M linear: Y_i[m, N_i] = X[m, K] * W_i^T for n_weights
+ * (1..64) weights that share K and X (e.g. every block's AdaLN modulation
+ * linear, which all take the timestep embedding), m = 1..16 rows of bf16 X.
+ * One GEMV launch per weight type streams all of them, so a call moves the
+ * sum of the weights' bytes instead of paying a launch per weight.  ys[i] is
+ * the output of weight i (f32 or bf16, row stride ldys[i], NULL / 0 = N_i). */
+int tc_cuda_qlinear_batched(tc_cuda_ctx *ctx, const tc_cuda_weight *const *weights, uint32_t n_weights,
+                            const void *x, uint32_t m, void *const *ys, const uint64_t *ldys, int out_dtype,
+                            void *stream);
+
 /* Force one kernel family for a call (testing and benchmarking):
  *   0 automatic, 1 warp GEMV (any M), 2 tensor-core GEMM (any M),
  *   3 tensor-core GEMM with one-CTA tiles only (no 2-CTA pairs). */
@@ -183,7 +193,8 @@ int tc_cuda_set_sm_limit(tc_cuda_ctx *ctx, int sms);
  * context workspace.  No context argument; X bf16 [m, K] (16-byte aligned), Y
  * f32 or bf16 with row stride ldy (0 = N), all device memory, enqueued on
  * `stream`.  The first call on a device looks up the array's address (make it
- * before any stream capture); shapes whose scratch exceeds 4 MiB are rejected;
+ * before any stream capture); the K-split rule keeps every shape's scratch
+ * under about 0.9 MiB, and a size check rejects anything over 4 MiB;
  * every call shares the array, so calls that may overlap on the GPU must be
  * serialised by the caller.  Allocates nothing. */
 int tc_cuda_qlinear_small_static(const tc_cuda_weight *weight, const void *x, uint32_t m, void *y, uint64_t ldy,

@@ -233,3 +233,27 @@ def test_gemm_f16_activations_meet_1e3(ctx, typ, m, n, k):
             tcc.qlinear(ctx, w, x, stage=tcc.STAGE_F16_X16)
         finally:
             ctx.set_path(0)
+
+
+@pytest.mark.parametrize("m", [1, 4, 16])
+def test_batched_gemv_matches_oracle(ctx, m):
+    """tc_cuda_qlinear_batched: Q4_K and Q6_K weights of different N sharing
+    K and X, one launch per type; each output against the fp32-decode oracle."""
+    import torch
+    from turbocider_b200 import cuda as tcc
+    k = 1024
+    specs = [(12, 512), (14, 384), (12, 100), (14, 1536), (12, 48)]
+    raws, ws = [], []
+    for i, (typ, n) in enumerate(specs):
+        raw = tcc.quantize(typ, kq_cases.synthetic_weight(n, k, seed=200 + i))
+        raws.append(raw)
+        ws.append(tcc.Weight.upload(ctx, typ, n, k, raw))
+    xb = kq_cases.synthetic_x_bf16(m, k, seed=m)
+    x = torch.from_numpy(xb.view(np.int16)).view(torch.bfloat16).cuda()
+    outs = tcc.qlinear_batched(ctx, ws, x, out_dtype=tcc.F32)
+    assert ctx.status() == 0
+    for (typ, n), raw, y in zip(specs, raws, outs):
+        got = y.cpu().numpy().astype(np.float64)
+        assert oracle.rel_l2(got, oracle.qlinear_ref(xb, raw, typ, n, k, "f32")) <= 1e-5
+    with pytest.raises(tcc.BackendError, match="1..16 rows"):
+        tcc.qlinear_batched(ctx, ws, torch.zeros(17, k, dtype=torch.bfloat16, device="cuda"))

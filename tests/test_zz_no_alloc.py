@@ -41,16 +41,27 @@ def test_static_scratch_matches_qlinear_twice(ctx, typ, n, k, m):
     assert ctx.status() == 0
 
 
-def test_static_scratch_rejects_oversize_and_bad_rows(ctx):
+def test_static_scratch_covers_large_shapes_and_rejects_bad_rows(ctx):
+    """The GEMV splits K only while there are fewer than 444 row tiles, so its
+    scratch stays below ~0.9 MiB for every shape (slices x tiles < 888 tiles
+    of 1 KiB partials); the 4 MiB array's size check remains as a guard.  A
+    large weight (1376 row tiles, one K slice) runs and matches the context
+    path; row counts outside 1..16 are rejected."""
     import torch
     from turbocider_b200 import cuda as tcc
-    # 22016 rows x K 8448 needs 3 K slices x 1376 row tiles of partials: > 4 MiB
     n, k = 22016, 8448
     raw = tcc.quantize(12, kq_cases.synthetic_weight(n, k, seed=5))
     w = tcc.Weight.upload(ctx, 12, n, k, raw)
-    x = torch.zeros(1, k, device="cuda", dtype=torch.bfloat16)
-    with pytest.raises(tcc.BackendError, match="static scratch holds"):
-        tcc.qlinear_small_static(w, x)
+    x = torch.randn(1, k, device="cuda").to(torch.bfloat16)
+    ref = tcc.qlinear(ctx, w, x, out_dtype=tcc.F32).cpu().numpy()
+    got = tcc.qlinear_small_static(w, x, out_dtype=tcc.F32).cpu().numpy()
+    assert oracle.rel_l2(got, ref) <= 1e-5
+    for n2, k2 in ((3072, 12288), (128, 256), (9000, 1024)):
+        w2 = tcc.Weight.upload(ctx, 14, n2, k2, tcc.quantize(14, kq_cases.synthetic_weight(n2, k2, seed=n2)))
+        x2 = torch.randn(16, k2, device="cuda").to(torch.bfloat16)
+        ref2 = tcc.qlinear(ctx, w2, x2, out_dtype=tcc.F32).cpu().numpy()
+        assert oracle.rel_l2(tcc.qlinear_small_static(w2, x2, out_dtype=tcc.F32).cpu().numpy(), ref2) <= 1e-5
+        w2.free()
     x17 = torch.zeros(17, k, device="cuda", dtype=torch.bfloat16)
     with pytest.raises(tcc.BackendError, match="1..16 rows"):
         tcc.qlinear_small_static(w, x17)

@@ -155,14 +155,23 @@ __device__ __forceinline__ void bytes_to_float4(uint32_t w, float (&f)[4]) {
     }
 }
 
+// Q6_K codes as exact signed bf16 pairs (q0 - 32, q1 - 32): the 128 + q of
+// code_pair minus 160, one bf16x2 subtract whose result (-32..31) is exact.
+__device__ __forceinline__ uint32_t centred_pair(uint32_t codes, uint32_t sel) {
+    uint32_t r;
+    asm("sub.rn.bf16x2 %0, %1, %2;" : "=r"(r) : "r"(code_pair(codes, sel)), "r"(0x43204320u));
+    return r;
+}
+
 // Columns of the MMA's N8 side: with TP tokens per tile (1, 2, 4 or 8),
 // column n carries token n % TP of the n / TP-th scale group of the current
 // chain, so a chain of S = 8 / TP scale groups accumulates unscaled in one
 // fp32 fragment; the B fragment of a K16 step is non-zero only in the columns
 // of that step's group.  The A operand is the bf16 value 128 + code (no
-// subtract): the chain also accumulates sum_k x_k per column with an all-ones
-// A (C1), and the group's result is ds * (C - off * C1) with off = 128 + bias
-// (Q6_K: 160; Q4_K: 128, plus its min term -m * C1).
+// subtract) for Q4_K: the chain also accumulates sum_k x_k per column with an
+// all-ones A (C1), and the group's result is d*sc * (C - 128 C1) - dmin*m C1.
+// Q6_K has no per-group min, so its A is the centred code q - 32 itself
+// (centred_pair) and the group's result is d*sc * C: one MMA per step.
 //
 // Visit order of the scale groups (v = 0..GROUPS-1) follows the packed words:
 //   Q4_K: v = sub-block (quarter v/2, nibble v&1), two K16 steps each;
@@ -178,7 +187,6 @@ __device__ __forceinline__ void compute_stage(const uint8_t *st, const uint16_t 
                                               uint32_t t, uint32_t lane, float *wt, float (&acc)[NT][4]) {
     using SG = StageGeo<TYPE>;
     constexpr uint32_t S = 8 / TP;
-    constexpr uint32_t GROUPS = TYPE == 12 ? 8 : 16;
     const uint32_t rg = row_slot(g), rg8 = row_slot(g + 8);   // slots inside the 16-row piece
     const uint32_t half = lane & 1, rr = lane >> 1;
     // Scale table, written by all lanes: row rr, half `half` of its groups.
@@ -217,7 +225,7 @@ __device__ __forceinline__ void compute_stage(const uint8_t *st, const uint16_t 
                            : x + (uint64_t)(m_begin + min(8 * nt + g % TP, m_count - 1)) * k + (uint64_t)kb * 256;
     const uint32_t my_j = g / TP;
     const uint32_t ones = 0x3F803F80u;
-    constexpr float off = TYPE == 12 ? 128.f : 160.f;
+    constexpr float off = 128.f;   // Q4_K: the code-space offset of code_pair
     float cq[NT][4], c1[NT][4];
 
     // One K16 step of scale group visit v: A from code words (rows g, g+8).
@@ -229,8 +237,14 @@ __device__ __forceinline__ void compute_stage(const uint8_t *st, const uint16_t 
 #pragma unroll
                 for (int i = 0; i < 4; ++i) cq[nt][i] = c1[nt][i] = 0.f;
         }
-        const uint32_t a0 = code_pair(cg, 0x4140u), a1 = code_pair(cg8, 0x4140u);
-        const uint32_t a2 = code_pair(cg, 0x4342u), a3 = code_pair(cg8, 0x4342u);
+        uint32_t a0, a1, a2, a3;
+        if constexpr (TYPE == 12) {
+            a0 = code_pair(cg, 0x4140u); a1 = code_pair(cg8, 0x4140u);
+            a2 = code_pair(cg, 0x4342u); a3 = code_pair(cg8, 0x4342u);
+        } else {
+            a0 = centred_pair(cg, 0x4140u); a1 = centred_pair(cg8, 0x4140u);
+            a2 = centred_pair(cg, 0x4342u); a3 = centred_pair(cg8, 0x4342u);
+        }
 #pragma unroll
         for (int nt = 0; nt < NT; ++nt) {
             const uint2 xv = TP == 1 ? *reinterpret_cast<const uint2 *>(xrow[nt] + kloc)
@@ -238,7 +252,7 @@ __device__ __forceinline__ void compute_stage(const uint8_t *st, const uint16_t 
             const bool on = my_j == j;
             const uint32_t b0 = on ? xv.x : 0u, b1 = on ? xv.y : 0u;
             mma16816(cq[nt], a0, a1, a2, a3, b0, b1, cq[nt]);
-            mma16816(c1[nt], ones, ones, ones, ones, b0, b1, c1[nt]);
+            if constexpr (TYPE == 12) mma16816(c1[nt], ones, ones, ones, ones, b0, b1, c1[nt]);
         }
     };
     // Scale the finished chain `chain` into the accumulators.
@@ -259,8 +273,8 @@ __device__ __forceinline__ void compute_stage(const uint8_t *st, const uint16_t 
                 const float a = wt[g * 16 + G], b = wt[(g + 8) * 16 + G];
 #pragma unroll
                 for (int nt = 0; nt < NT; ++nt) {
-                    acc[nt][ci] = fmaf(a, fmaf(-off, c1[nt][ci], cq[nt][ci]), acc[nt][ci]);
-                    acc[nt][2 + ci] = fmaf(b, fmaf(-off, c1[nt][2 + ci], cq[nt][2 + ci]), acc[nt][2 + ci]);
+                    acc[nt][ci] = fmaf(a, cq[nt][ci], acc[nt][ci]);
+                    acc[nt][2 + ci] = fmaf(b, cq[nt][2 + ci], acc[nt][2 + ci]);
                 }
             }
         }
@@ -313,11 +327,14 @@ __device__ __forceinline__ void compute_stage(const uint8_t *st, const uint16_t 
 
 constexpr uint32_t kGemvStages = 3;
 
+// Weights of one launch: blockIdx.x runs over the 16-row tiles of all of
+// them (entry e owns tiles [tile_begin, next entry's tile_begin)); they share
+// K, type and X, each has its own Y.
 template <int TYPE, int TP, int NT, int DT>
-__global__ void __launch_bounds__(kWarps * 32) gemv_kernel(WeightView w, const uint16_t *__restrict__ x,
-                                                           uint32_t m_begin, uint32_t m_count, uint64_t k,
-                                                           void *__restrict__ y, uint64_t ldy,
-                                                           uint32_t kb_per_slice, float *__restrict__ partials,
+__global__ void __launch_bounds__(kWarps * 32) gemv_kernel(const __grid_constant__ GemvBatch b,
+                                                           const uint16_t *__restrict__ x, uint32_t m_begin,
+                                                           uint32_t m_count, uint64_t k, uint32_t kb_per_slice,
+                                                           float *__restrict__ partials,
                                                            uint32_t *__restrict__ counters, uint32_t *status) {
     using SG = StageGeo<TYPE>;
     constexpr uint32_t chunk = TYPE == 12 ? kQ4KChunk : kQ6KChunk;
@@ -325,11 +342,16 @@ __global__ void __launch_bounds__(kWarps * 32) gemv_kernel(WeightView w, const u
     __shared__ float red[kWarps][32][4 * NT];
     __shared__ __align__(16) float tab[kWarps][16 * 16];
     __shared__ __align__(8) uint64_t bars[kWarps][kGemvStages];
+    uint32_t ei = 0;
+    while (ei + 1 < b.n_entries && blockIdx.x >= b.e[ei + 1].tile_begin) ++ei;
+    const GemvEntry &w = b.e[ei];
+    void *const y = w.y;
+    const uint64_t ldy = w.ldy;
     const uint32_t warp = threadIdx.x >> 5, lane = threadIdx.x & 31, g = lane >> 2, t = lane & 3;
-    const uint32_t row0 = blockIdx.x * 16, panel = row0 / kPanelRows, r0 = row0 % kPanelRows;
+    const uint32_t row0 = (blockIdx.x - w.tile_begin) * 16, panel = row0 / kPanelRows, r0 = row0 % kPanelRows;
     const uint32_t n_slices = gridDim.y, kb_begin = blockIdx.y * kb_per_slice;
-    const uint32_t kb_end = min(w.kb, kb_begin + kb_per_slice);
-    const uint8_t *pbase = w.chunks + (uint64_t)panel * w.kb * chunk;
+    const uint32_t kb_end = min(b.kb, kb_begin + kb_per_slice);
+    const uint8_t *pbase = w.chunks + (uint64_t)panel * b.kb * chunk;
     constexpr bool kStageX = TP == 1;
     constexpr uint32_t stage_bytes = (SG::w_bytes + (kStageX ? 512u : 0u) + 127) / 128 * 128;
     uint8_t *mine = dyn + (size_t)warp * kGemvStages * stage_bytes;
@@ -474,10 +496,9 @@ __global__ void __launch_bounds__(kWarps * 32) gemv_kernel(WeightView w, const u
 }
 
 template <int TYPE, int TP, int NT>
-cudaError_t launch_typed(const SegmentView &seg, const uint16_t *x, uint64_t k, void *y, uint64_t ldy,
-                         int out_dtype, const GemvSplit &sp, cudaStream_t s) {
-    const dim3 grid((seg.w.n + 15) / 16, sp.n_slices);
-    const uint32_t mc = seg.m_end - seg.m_begin;
+cudaError_t launch_typed(const GemvBatch &bt, uint32_t tiles, uint32_t m_begin, uint32_t mc, const uint16_t *x,
+                         uint64_t k, int out_dtype, const GemvSplit &sp, cudaStream_t s) {
+    const dim3 grid(tiles, sp.n_slices);
     const size_t stage = (StageGeo<TYPE>::w_bytes + (TP == 1 ? 512u : 0u) + 127) / 128 * 128;
     const size_t smem = stage * kGemvStages * kWarps;
     auto kern = out_dtype == 0 ? gemv_kernel<TYPE, TP, NT, 0> : gemv_kernel<TYPE, TP, NT, 2>;
@@ -499,48 +520,64 @@ cudaError_t launch_typed(const SegmentView &seg, const uint16_t *x, uint64_t k, 
     attr[0].val.programmaticStreamSerializationAllowed = 1;
     cfg.attrs = attr;
     cfg.numAttrs = 1;
-    return cudaLaunchKernelEx(&cfg, kern, seg.w, x, seg.m_begin, mc, k, y, ldy, sp.kb_per_slice, sp.partials,
-                              sp.counters, sp.status);
+    return cudaLaunchKernelEx(&cfg, kern, bt, x, m_begin, mc, k, sp.kb_per_slice, sp.partials, sp.counters,
+                              sp.status);
 }
 
 template <int TYPE>
-cudaError_t launch_m(const SegmentView &seg, const uint16_t *x, uint64_t k, void *y, uint64_t ldy, int out_dtype,
-                     const GemvSplit &sp, cudaStream_t s) {
-    const uint32_t m = seg.m_end - seg.m_begin;
-    if (m <= 1) return launch_typed<TYPE, 1, 1>(seg, x, k, y, ldy, out_dtype, sp, s);
-    if (m <= 2) return launch_typed<TYPE, 2, 1>(seg, x, k, y, ldy, out_dtype, sp, s);
-    if (m <= 4) return launch_typed<TYPE, 4, 1>(seg, x, k, y, ldy, out_dtype, sp, s);
-    if (m <= 8) return launch_typed<TYPE, 8, 1>(seg, x, k, y, ldy, out_dtype, sp, s);
-    return launch_typed<TYPE, 8, 2>(seg, x, k, y, ldy, out_dtype, sp, s);
+cudaError_t launch_m(const GemvBatch &bt, uint32_t tiles, uint32_t m_begin, uint32_t m, const uint16_t *x,
+                     uint64_t k, int out_dtype, const GemvSplit &sp, cudaStream_t s) {
+    if (m <= 1) return launch_typed<TYPE, 1, 1>(bt, tiles, m_begin, m, x, k, out_dtype, sp, s);
+    if (m <= 2) return launch_typed<TYPE, 2, 1>(bt, tiles, m_begin, m, x, k, out_dtype, sp, s);
+    if (m <= 4) return launch_typed<TYPE, 4, 1>(bt, tiles, m_begin, m, x, k, out_dtype, sp, s);
+    if (m <= 8) return launch_typed<TYPE, 8, 1>(bt, tiles, m_begin, m, x, k, out_dtype, sp, s);
+    return launch_typed<TYPE, 8, 2>(bt, tiles, m_begin, m, x, k, out_dtype, sp, s);
 }
 
 }  // namespace
 
-GemvSplit gemv_split(const WeightView &w) {
-    // K slices of 16 super-blocks (4 per warp, pipelined), fewer when the
-    // grid would not fill the machine.
-    const uint32_t tiles = (w.n + 15) / 16;
-    uint32_t per = 16;
-    while (per > kWarps && (uint64_t)tiles * ((w.kb + per - 1) / per) < 148u * 3u) per /= 2;
+GemvSplit gemv_split_tiles(uint32_t tiles, uint32_t kb) {
+    // Enough CTAs for about three per SM, with as few K slices as that allows
+    // (each slice costs a partial store and a share of the fixup): a single
+    // weight of a few hundred row tiles splits K three ways, a batch of
+    // thousands of tiles runs whole rows per CTA.  Slices hold a multiple of
+    // the 4 warps' super-blocks.
+    const uint32_t want = 148u * 3u;
+    uint32_t slices = tiles >= want ? 1u : (want + tiles - 1) / tiles;
+    slices = max(1u, min(slices, (kb + kWarps - 1) / kWarps));
+    uint32_t per = (kb + slices - 1) / slices;
+    per = (per + kWarps - 1) / kWarps * kWarps;
     GemvSplit sp;
     sp.kb_per_slice = per;
-    sp.n_slices = (w.kb + per - 1) / per;
+    sp.n_slices = (kb + per - 1) / per;
     return sp;
 }
+GemvSplit gemv_split(const WeightView &w) { return gemv_split_tiles((w.n + 15) / 16, w.kb); }
 
-size_t gemv_workspace_floats(const WeightView &w) {
-    const GemvSplit sp = gemv_split(w);
-    return sp.n_slices > 1 ? (size_t)sp.n_slices * ((w.n + 15) / 16) * 32 * 8 : 0;
+size_t gemv_workspace_floats_tiles(uint32_t tiles, uint32_t kb) {
+    const GemvSplit sp = gemv_split_tiles(tiles, kb);
+    return sp.n_slices > 1 ? (size_t)sp.n_slices * tiles * 32 * 8 : 0;
+}
+size_t gemv_workspace_floats(const WeightView &w) { return gemv_workspace_floats_tiles((w.n + 15) / 16, w.kb); }
+
+cudaError_t launch_gemv_batch(const GemvBatch &bt, uint32_t type, uint32_t tiles, uint32_t m_begin, uint32_t m,
+                              const uint16_t *x, uint64_t k, int out_dtype, const GemvSplit &sp, cudaStream_t s) {
+    if (!m || !tiles) return cudaSuccess;
+    if (m > 16 || bt.n_entries == 0 || bt.n_entries > kMaxGemvBatch) return cudaErrorInvalidValue;
+    if (sp.n_slices > 1 && (!sp.partials || !sp.counters)) return cudaErrorInvalidValue;
+    return type == 12 ? launch_m<12>(bt, tiles, m_begin, m, x, k, out_dtype, sp, s)
+                      : launch_m<14>(bt, tiles, m_begin, m, x, k, out_dtype, sp, s);
 }
 
 cudaError_t launch_gemv(const SegmentView &seg, const uint16_t *x, uint64_t k, void *y, uint64_t ldy,
                         int out_dtype, const GemvSplit &sp, cudaStream_t s) {
     if (seg.m_end <= seg.m_begin) return cudaSuccess;
-    const uint32_t m = seg.m_end - seg.m_begin;
-    if (m > 16) return cudaErrorInvalidValue;
-    if (sp.n_slices > 1 && (!sp.partials || !sp.counters)) return cudaErrorInvalidValue;
-    return seg.w.type == 12 ? launch_m<12>(seg, x, k, y, ldy, out_dtype, sp, s)
-                            : launch_m<14>(seg, x, k, y, ldy, out_dtype, sp, s);
+    GemvBatch bt{};
+    bt.n_entries = 1;
+    bt.kb = seg.w.kb;
+    bt.e[0] = {seg.w.chunks, y, ldy, seg.w.n, 0u};
+    return launch_gemv_batch(bt, seg.w.type, (seg.w.n + 15) / 16, seg.m_begin, seg.m_end - seg.m_begin, x, k,
+                             out_dtype, sp, s);
 }
 
 }  // namespace tc

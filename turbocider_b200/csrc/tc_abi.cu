@@ -290,6 +290,51 @@ int tc_cuda_set_path(tc_cuda_ctx *ctx, int path) {
     return ok();
 }
 
+int tc_cuda_qlinear_batched(tc_cuda_ctx *ctx, const tc_cuda_weight *const *weights, uint32_t n_weights,
+                            const void *x, uint32_t m, void *const *ys, const uint64_t *ldys, int out_dtype,
+                            void *stream) {
+    if (!ctx || !weights || !x || !ys) return fail("null argument");
+    if (!n_weights || n_weights > tc::kMaxGemvBatch) return fail("1..64 weights per batched call");
+    if (m < 1 || m > 16) return fail("the batched GEMV takes 1..16 rows of X");
+    if (out_dtype != TC_DTYPE_F32 && out_dtype != TC_DTYPE_BF16) return fail("output dtype must be f32 or bf16");
+    if (reinterpret_cast<uintptr_t>(x) % 16) return fail("X must be 16-byte aligned");
+    const uint64_t k = weights[0] ? weights[0]->k : 0;
+    for (uint32_t i = 0; i < n_weights; ++i) {
+        const tc_cuda_weight *w = weights[i];
+        if (!w || !ys[i]) return fail("null weight or output");
+        if (w->k != k) return fail("weights of one batched call must share K");
+        if (w->device != ctx->device) return fail("weight lives on another device");
+        if (ldys && ldys[i] && ldys[i] < w->n) return fail("invalid/overlapping row stride");
+    }
+    DeviceGuard guard(ctx->device);
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+    // One launch per weight type (the kernel is specialised on it).
+    for (const uint32_t type : {uint32_t(TC_GGML_Q4_K), uint32_t(TC_GGML_Q6_K)}) {
+        tc::GemvBatch bt{};
+        uint32_t tiles = 0;
+        for (uint32_t i = 0; i < n_weights; ++i) {
+            const tc_cuda_weight *w = weights[i];
+            if (w->type != type) continue;
+            bt.e[bt.n_entries++] = {w->chunks, ys[i], ldys && ldys[i] ? ldys[i] : w->n, (uint32_t)w->n, tiles};
+            tiles += (uint32_t)((w->n + 15) / 16);
+        }
+        if (!bt.n_entries) continue;
+        bt.kb = (uint32_t)(k / 256);
+        tc::GemvSplit sp = tc::gemv_split_tiles(tiles, bt.kb);
+        sp.status = ctx->status;
+        if (sp.n_slices > 1) {
+            int rc = ensure_gemv_workspace(ctx, tc::gemv_workspace_floats_tiles(tiles, bt.kb), tiles);
+            if (rc) return rc;
+            sp.partials = ctx->gemv_partials;
+            sp.counters = ctx->gemv_counters;
+        }
+        cudaError_t e = tc::launch_gemv_batch(bt, type, tiles, 0, m, static_cast<const uint16_t *>(x), k, out_dtype,
+                                              sp, s);
+        if (e != cudaSuccess) return cuda_fail("batched GEMV launch", e);
+    }
+    return ok();
+}
+
 int tc_cuda_set_sm_limit(tc_cuda_ctx *ctx, int sms) {
     if (!ctx) return fail("null context");
     if (sms < 0) return fail("negative SM limit");

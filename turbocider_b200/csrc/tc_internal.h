@@ -66,6 +66,22 @@ struct GemvSplit {
 };
 GemvSplit gemv_split(const WeightView &w);
 size_t gemv_workspace_floats(const WeightView &w);
+GemvSplit gemv_split_tiles(uint32_t tiles, uint32_t kb);
+size_t gemv_workspace_floats_tiles(uint32_t tiles, uint32_t kb);
+// Several weights with the same K, type and X in one GEMV launch.
+constexpr uint32_t kMaxGemvBatch = 64;
+struct GemvEntry {
+    const uint8_t *chunks;
+    void *y;
+    uint64_t ldy;
+    uint32_t n, tile_begin;   // rows; first 16-row tile of this weight in the launch
+};
+struct GemvBatch {
+    uint32_t n_entries, kb;
+    GemvEntry e[kMaxGemvBatch];
+};
+cudaError_t launch_gemv_batch(const GemvBatch &bt, uint32_t type, uint32_t tiles, uint32_t m_begin, uint32_t m,
+                              const uint16_t *x, uint64_t k, int out_dtype, const GemvSplit &sp, cudaStream_t s);
 cudaError_t launch_gemv(const SegmentView &seg, const uint16_t *x, uint64_t k, void *y,
                         uint64_t ldy, int out_dtype, const GemvSplit &split, cudaStream_t s);
 cudaError_t launch_x_to_f16(const uint16_t *x, uint16_t *x16, uint64_t count, uint32_t *status,

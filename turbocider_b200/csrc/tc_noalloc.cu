@@ -26,7 +26,8 @@
 //     they are read;
 //   * calls whose kernels may overlap on the GPU (different streams, or
 //     different host threads) race on the array -- serialise them;
-//   * sizes whose scratch exceeds kScratchBytes are rejected with an error.
+//   * sizes whose scratch exceeds kScratchBytes are rejected with an error
+//     (a guard: the GEMV's K-split rule keeps every shape under ~0.9 MiB).
 // Nothing here calls cudaMalloc, cudaFree or any allocating library routine.
 #include <mutex>
 #include <string>

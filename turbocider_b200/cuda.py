@@ -53,6 +53,8 @@ EXPORTS = {
     "tc_cuda_qlinear": (C.c_int, [_vp, C.POINTER(_vp), _u32, C.POINTER(_i32), C.POINTER(_i32), _u32, _vp, _vp,
                                   _u64, C.c_int, C.c_int, _vp]),
     "tc_cuda_set_path": (C.c_int, [_vp, C.c_int]),
+    "tc_cuda_qlinear_batched": (C.c_int, [_vp, C.POINTER(_vp), _u32, _vp, _u32, C.POINTER(_vp), C.POINTER(_u64),
+                                          C.c_int, _vp]),
     "tc_cuda_set_sm_limit": (C.c_int, [_vp, C.c_int]),
     "tc_quantize": (C.c_int, [_u32, _vp, _u64, _u64, _vp, _u64, C.c_int]),
     "tc_cuda_qlinear_small_static": (C.c_int, [_vp, _vp, _u32, _vp, _u64, C.c_int, _vp]),
@@ -274,6 +276,21 @@ def qlinear(ctx: Context, weights, x, seg_offsets=None, seg_weight=None, out_dty
     _check(lib().tc_cuda_qlinear(ctx.handle, handles, len(ws), offs, sw, n_seg, x.data_ptr(), out.data_ptr(),
                                  out.stride(0), out_dtype, stage, _stream_ptr(stream)))
     return out
+
+
+def qlinear_batched(ctx: Context, weights, x, out_dtype: int = BF16, outs=None, stream=None):
+    """[X * W_i^T for W_i in weights] in one GEMV launch per weight type (1..16
+    rows of bf16 X, weights sharing K)."""
+    import torch
+    if outs is None:
+        outs = [torch.empty((x.shape[0], w.n), dtype=torch.float32 if out_dtype == F32 else torch.bfloat16,
+                            device=x.device) for w in weights]
+    handles = (_vp * len(weights))(*[w.handle for w in weights])
+    ys = (_vp * len(outs))(*[o.data_ptr() for o in outs])
+    lds = (_u64 * len(outs))(*[o.stride(0) for o in outs])
+    _check(lib().tc_cuda_qlinear_batched(ctx.handle, handles, len(weights), x.data_ptr(), x.shape[0], ys, lds,
+                                         out_dtype, _stream_ptr(stream)))
+    return outs
 
 
 def qlinear_small_static(weight: Weight, x, out_dtype: int = BF16, out=None, stream=None):
