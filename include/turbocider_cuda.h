@@ -1,7 +1,7 @@
 #ifndef TURBOCIDER_CUDA_H
 #define TURBOCIDER_CUDA_H
 /*
- * TurboCider CUDA backend for B200 (sm_100a): GGUF K-quant (Q4_K / Q6_K)
+ * TurboCider CUDA backend for B200 (sm_100a): GGUF K-quant (Q4_K / Q5_K / Q6_K)
  * dequantise-and-matmul, exported as a plain C ABI.
  *
  * This backend sits beside the reference's native backends.  Its operator
@@ -23,7 +23,7 @@
  *     every launch is asynchronous on that stream;
  *   - calls on one context are serialised by the caller.
  *
- * Ratios: Q4_K = 256 weights / 144 bytes, Q6_K = 256 weights / 210 bytes
+ * Ratios: Q4_K = 256 weights / 144 bytes, Q5_K = 256 / 176, Q6_K = 256 / 210
  * (reference native/core/gguf_directory.hpp:21-26).
  */
 #include <stddef.h>
@@ -83,8 +83,8 @@ void tc_cuda_free(tc_cuda_ctx *ctx);
 int tc_cuda_status(tc_cuda_ctx *ctx, uint32_t *bits, int clear);
 
 /* Upload a GGUF tensor [N rows, K columns] (ne[0] = K contiguous) of type
- * Q4_K or Q6_K from host memory and keep it resident in HBM in the kernels'
- * panel layout.  `raw_host` holds whole rows, row pitch K/256*block_bytes, as
+ * Q4_K, Q5_K or Q6_K from host memory and keep it resident in HBM in the
+ * kernels' panel layout.  `raw_host` holds whole rows, row pitch K/256*block_bytes, as
  * in the GGUF payload.  Rows [n_begin, n_begin + n_count) are uploaded (an
  * N-column shard); n_count = 0 means all rows.  The blocks' bytes are moved,
  * never re-encoded; every d/dmin is checked finite (the reference rejects
@@ -94,6 +94,21 @@ int tc_cuda_status(tc_cuda_ctx *ctx, uint32_t *bits, int clear);
 int tc_cuda_weight_upload(tc_cuda_ctx *ctx, uint32_t ggml_type, uint64_t n, uint64_t k,
                           const void *raw_host, uint64_t raw_bytes, uint64_t n_begin,
                           uint64_t n_count, tc_cuda_weight **weight);
+
+/* Upload the two halves of a SwiGLU projection as ONE weight for the fused
+ * TC_EPI_SWIGLU epilogue of tc_cuda_qlinear_ex: `gate_raw` and `up_raw` are
+ * raw GGUF matrices [f, k] of the same type (two tensors such as Z-Image's
+ * w1 / w3, or the two halves of a gate_up tensor [2f, k], up_raw = gate_raw +
+ * f rows, as in reference native/models/qwen21/transformer.cpp:971-976).
+ * Output columns [col_begin, col_begin + col_count) (col_count = 0: to the
+ * end; a multiple of 8 unless it reaches f) are taken from both halves and
+ * interleaved in groups of 8 rows (8 gate rows, then the same 8 up rows), so
+ * that one tile holds both factors of each output.  The weight has
+ * 2 * col_count rows; tc_cuda_dequant shows them in that interleaved order.
+ * Synchronous; checks every d/dmin finite. */
+int tc_cuda_weight_upload_glu(tc_cuda_ctx *ctx, uint32_t ggml_type, uint64_t f, uint64_t k,
+                              const void *gate_raw, const void *up_raw, uint64_t raw_bytes_each,
+                              uint64_t col_begin, uint64_t col_count, tc_cuda_weight **weight);
 
 /* As tc_cuda_weight_upload, but the raw rows are already in device memory
  * (e.g. a staging buffer the caller filled with cudaMemcpyAsync) and the re-layout is
@@ -146,8 +161,8 @@ int tc_cuda_decode(tc_cuda_ctx *ctx, uint32_t ggml_type, const void *source, uin
  * behind Weights::project (reference native/backends/mlx.cpp:668-679).
  *   X        bf16 [M, K] row-major, device (fp16 with TC_STAGE_F16_X16);
  *            M = seg_offsets[n_seg].
- *   Y        [M, N] row-major, device, dtype out_dtype (TC_DTYPE_BF16 or
- *            TC_DTYPE_F32); row stride ldy elements (0 = N).
+ *   Y        [M, N] row-major, device, dtype out_dtype (TC_DTYPE_BF16,
+ *            TC_DTYPE_F16 or TC_DTYPE_F32); row stride ldy elements (0 = N).
  *   weights  n_weights uploaded weights with identical N, K;
  *   seg_offsets  int32 [n_seg + 1] host array, 0 = seg_offsets[0] <= ... :
  *            rows of X that belong to request segment s (ragged packing of
@@ -162,12 +177,61 @@ int tc_cuda_qlinear(tc_cuda_ctx *ctx, const tc_cuda_weight *const *weights, uint
                     const int32_t *seg_offsets, const int32_t *seg_weight, uint32_t n_seg,
                     const void *x, void *y, uint64_t ldy, int out_dtype, int stage, void *stream);
 
+/* Fused epilogue of tc_cuda_qlinear_ex, applied in fp32 to each accumulator
+ * value before the one rounding to out_dtype, in this order:
+ *   TC_EPI_BIAS          t = acc + bias[row]             (mlx.cpp:687-688)
+ *   TC_EPI_GELU_TANH     t = 0.5 t (1 + tanh(sqrt(2/pi) (t + 0.044715 t^3)))
+ *   TC_EPI_GELU_ERF      t = 0.5 t (1 + erf(t / sqrt(2)))
+ *   TC_EPI_SWIGLU        t = silu(t_gate) * t_up        (transformer.cpp:971-976;
+ *                        the weight must come from tc_cuda_weight_upload_glu;
+ *                        the output has col_count = rows / 2 columns)
+ *   TC_EPI_GATE_RESIDUAL y = residual[m][c] + gate[g][c] * t, g the gate row
+ *                        of m's segment (the AdaLN gated residual
+ *                        hidden + gate * proj, transformer.cpp:950, :980;
+ *                        the caller applies any tanh to the gate vector).
+ * bias: f32 [rows] in the weight's row order; for a SwiGLU weight the gate
+ *   bias of output column c is bias[c] and its up bias bias[bias_up_offset + c].
+ * gate: f32 [n_gate_rows][ld_gate]; seg_gate: host int32 [n_seg] gate row of
+ *   each segment (NULL: segment s uses row s).
+ * residual: [M][ld_residual] in out_dtype; may be Y itself (in-place update:
+ *   each element is read and then written by the same thread).
+ * The reference rounds after the product and again after each following
+ * operation; here every step is fp32 with one rounding at the end. */
+enum {
+    TC_EPI_BIAS = 1u << 0,
+    TC_EPI_GELU_TANH = 1u << 1,
+    TC_EPI_GELU_ERF = 1u << 2,
+    TC_EPI_SWIGLU = 1u << 3,
+    TC_EPI_GATE_RESIDUAL = 1u << 4
+};
+typedef struct tc_epilogue {
+    uint32_t flags;
+    uint32_t n_gate_rows;
+    const float *bias;
+    uint64_t bias_up_offset;
+    const float *gate;
+    uint64_t ld_gate;
+    const int32_t *seg_gate;
+    const void *residual;
+    uint64_t ld_residual;
+} tc_epilogue;
+
+/* tc_cuda_qlinear with a fused epilogue (NULL = none, the same as
+ * tc_cuda_qlinear) and any of the three output dtypes (TC_DTYPE_F16 is the
+ * reference's output dtype for fp16 activations: mlx.cpp:668-679 returns
+ * X's dtype).  For a SwiGLU weight Y has rows/2 columns and ldy counts those. */
+int tc_cuda_qlinear_ex(tc_cuda_ctx *ctx, const tc_cuda_weight *const *weights, uint32_t n_weights,
+                       const int32_t *seg_offsets, const int32_t *seg_weight, uint32_t n_seg,
+                       const void *x, void *y, uint64_t ldy, int out_dtype, int stage,
+                       const tc_epilogue *epilogue, void *stream);
+
 /* Batched small-M linear: Y_i[m, N_i] = X[m, K] * W_i^T for n_weights
  * (1..64) weights that share K and X (e.g. every block's AdaLN modulation
  * linear, which all take the timestep embedding), m = 1..16 rows of bf16 X.
  * One GEMV launch per weight type streams all of them, so a call moves the
  * sum of the weights' bytes instead of paying a launch per weight.  ys[i] is
- * the output of weight i (f32 or bf16, row stride ldys[i], NULL / 0 = N_i). */
+ * the output of weight i (f32, f16 or bf16, row stride ldys[i], NULL / 0 =
+ * N_i).  SwiGLU weights are not accepted here. */
 int tc_cuda_qlinear_batched(tc_cuda_ctx *ctx, const tc_cuda_weight *const *weights, uint32_t n_weights,
                             const void *x, uint32_t m, void *const *ys, const uint64_t *ldys, int out_dtype,
                             void *stream);
@@ -191,7 +255,7 @@ int tc_cuda_set_sm_limit(tc_cuda_ctx *ctx, int sms);
  * tc_cuda_qlinear, whose scratch (K-slice partials, per-tile counters, status
  * word) here lives in a 4 MiB file-scope device array instead of a cudaMalloc'd
  * context workspace.  No context argument; X bf16 [m, K] (16-byte aligned), Y
- * f32 or bf16 with row stride ldy (0 = N), all device memory, enqueued on
+ * f32, f16 or bf16 with row stride ldy (0 = N), all device memory, enqueued on
  * `stream`.  The first call on a device looks up the array's address (make it
  * before any stream capture); the K-split rule keeps every shape's scratch
  * under about 0.9 MiB, and a size check rejects anything over 4 MiB;

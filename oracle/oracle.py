@@ -179,6 +179,33 @@ def qlinear_ref(x_bits: np.ndarray, raw, ggml_type: int, n: int, k: int, staging
     return x.astype(np.float64) @ w.T
 
 
+def epilogue_ref(acc: np.ndarray, bias=None, activation: str | None = None, glu: bool = False,
+                 gate=None, residual=None, gate_rows=None) -> np.ndarray:
+    """fp64 restatement of the fused epilogue on a product acc [M, rows]:
+    bias add (reference native/backends/mlx.cpp:687-688), GELU (tanh or erf
+    form), SwiGLU silu(gate) * up over the halves [gate | up] of a gate_up
+    product (native/models/qwen21/transformer.cpp:971-976), then the gated
+    residual residual + gate[g(m)] * t (transformer.cpp:950, :980).  acc's
+    columns are in logical order (gate rows then up rows for glu); gate_rows
+    [M] gives each row's gate vector index."""
+    from math import erf, pi, sqrt
+    t = np.asarray(acc, dtype=np.float64).copy()
+    if bias is not None:
+        t = t + np.asarray(bias, dtype=np.float64)[None, :]
+    if glu:
+        f = t.shape[1] // 2
+        g, u = t[:, :f], t[:, f:]
+        t = g / (1.0 + np.exp(-g)) * u
+    elif activation == "gelu_tanh":
+        t = 0.5 * t * (1.0 + np.tanh(sqrt(2.0 / pi) * (t + 0.044715 * t ** 3)))
+    elif activation == "gelu_erf":
+        t = 0.5 * t * (1.0 + np.vectorize(erf)(t / sqrt(2.0)))
+    if gate is not None:
+        gv = np.asarray(gate, dtype=np.float64)[np.asarray(gate_rows)]
+        t = np.asarray(residual, dtype=np.float64) + gv * t
+    return t
+
+
 def rel_l2(a, b) -> float:
     a = np.asarray(a, dtype=np.float64)
     b = np.asarray(b, dtype=np.float64)

@@ -78,9 +78,25 @@ def test_q6k_quantiser_pinned(golden):
     assert oracle.rel_l2(dec, w) < 0.03
 
 
+def test_q5k_quantiser_between_q4k_and_q6k():
+    """Q5_K blocks from tc_quantize decode identically through the port and the
+    reference decoder, and their error sits between Q4_K's and Q6_K's."""
+    w = kq_cases.synthetic_weight(64, 2048, seed=5)
+    err = {}
+    for typ in (12, 13, 14):
+        raw = tcc.quantize(typ, w)
+        assert raw.nbytes == 64 * 8 * tcc.BLOCK_BYTES[typ]
+        dec = oracle.decode_parallel(raw, typ, 64, 2048, 0, which="port")
+        ref = oracle.decode_parallel(raw, typ, 64, 2048, 0, which="ref")
+        assert np.array_equal(dec.view(np.uint32), ref.view(np.uint32))
+        err[typ] = oracle.rel_l2(dec, w)
+    assert err[14] < err[13] < err[12]
+    assert err[13] < 0.05
+
+
 def test_quantiser_threads_do_not_change_bytes():
     w = kq_cases.synthetic_weight(33, 512, seed=7)
-    for typ in (12, 14):
+    for typ in (12, 13, 14):
         assert np.array_equal(tcc.quantize(typ, w, threads=1), tcc.quantize(typ, w, threads=5))
 
 
@@ -92,4 +108,4 @@ def test_quantiser_rejects_bad_input():
     with pytest.raises(tcc.BackendError):
         tcc.quantize(14, bad)
     with pytest.raises(KeyError):
-        tcc.quantize(13, np.zeros((1, 256), np.float32))
+        tcc.quantize(10, np.zeros((1, 256), np.float32))

@@ -115,7 +115,7 @@ def test_decode_geometry_errors(ctx):
         tcc.decode(ctx, 12, raw, 2, 512, 0, 2, 0, 512, 0, tgt[:100], 2048, 4)
 
 
-@pytest.mark.parametrize("typ", [12, 14])
+@pytest.mark.parametrize("typ", [12, 13, 14])
 @pytest.mark.parametrize("n,k", [(200, 512), (128, 256), (384, 3072)])
 def test_panel_dequant_bit_exact(ctx, typ, n, k):
     from turbocider_b200 import cuda as tcc
@@ -145,7 +145,7 @@ def test_panel_dequant_shard(ctx):
 
 def test_upload_rejects_nonfinite_scale(ctx):
     from turbocider_b200 import cuda as tcc
-    for typ in (12, 14):
+    for typ in (12, 13, 14):
         raw = bytearray(tcc.quantize(typ, kq_cases.synthetic_weight(4, 512, seed=9)))
         off = 208 if typ == 14 else 2
         raw[off + tcc.BLOCK_BYTES[typ] * 5:off + tcc.BLOCK_BYTES[typ] * 5 + 2] = (0x7C00).to_bytes(2, "little")

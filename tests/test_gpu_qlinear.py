@@ -47,7 +47,7 @@ def _run(ctx, weight, x, out_dtype, stage=0, path=0, seg=None, seg_w=None, weigh
     return y.float().cpu().numpy().astype(np.float64)
 
 
-@pytest.mark.parametrize("typ", [12, 14])
+@pytest.mark.parametrize("typ", [12, 13, 14])
 def test_gemm_config1_shape(ctx, typ):
     """Config 1 (M=256, N=3072, K=3072) through the tcgen05 GEMM."""
     from turbocider_b200 import cuda as tcc
@@ -63,7 +63,7 @@ def test_gemm_config1_shape(ctx, typ):
     assert oracle.rel_l2(yb, oracle.qlinear_ref(xb, raw, typ, n, k, "bf16")) <= 3e-3
 
 
-@pytest.mark.parametrize("typ", [12, 14])
+@pytest.mark.parametrize("typ", [12, 13, 14])
 def test_gemm_fp16_staging_meets_1e3_vs_f32_decode(ctx, typ):
     from turbocider_b200 import cuda as tcc
     n, k, m = 1024, 2048, 384
@@ -76,7 +76,7 @@ def test_gemm_fp16_staging_meets_1e3_vs_f32_decode(ctx, typ):
 
 
 @pytest.mark.parametrize("path", [2, 3])
-@pytest.mark.parametrize("typ", [12, 14])
+@pytest.mark.parametrize("typ", [12, 13, 14])
 @pytest.mark.parametrize("m,n,k", [(17, 200, 512), (129, 384, 1024), (300, 256, 768), (64, 130, 256),
                                    (1000, 640, 2560), (520, 1920, 512)])
 def test_gemm_ragged_edges(ctx, typ, m, n, k, path):
@@ -89,7 +89,7 @@ def test_gemm_ragged_edges(ctx, typ, m, n, k, path):
     assert oracle.rel_l2(y, oracle.qlinear_ref(xb, raw, typ, n, k, "bf16")) <= TIGHT
 
 
-@pytest.mark.parametrize("typ", [12, 14])
+@pytest.mark.parametrize("typ", [12, 13, 14])
 @pytest.mark.parametrize("ldy", [640, 648, 645])
 def test_gemm_bf16_out_row_stride(ctx, typ, ldy):
     """bf16 output into a wider buffer (row stride ldy): TMA-stored tiles when
@@ -115,7 +115,7 @@ def test_gemm_bf16_out_row_stride(ctx, typ, ldy):
     assert oracle.rel_l2(y, y1) <= 3e-3
 
 
-@pytest.mark.parametrize("typ", [12, 14])
+@pytest.mark.parametrize("typ", [12, 13, 14])
 @pytest.mark.parametrize("m", [1, 2, 3, 4, 16])
 def test_gemv_config2_shape(ctx, typ, m):
     """Config 2 (K=12288, N=3072, M in {1..16}) through the warp GEMV."""
@@ -162,6 +162,28 @@ def test_ragged_segments_two_weights(ctx):
     del yb
 
 
+def test_ragged_segments_three_types(ctx):
+    """Segments on Q4_K, Q5_K and Q6_K weights of one shape in one call (the
+    Q4_K_M mix puts different types behind the same projection in different
+    blocks); the pair kernel, the one-CTA kernel and the GEMV each get one."""
+    import torch
+    from turbocider_b200 import cuda as tcc
+    n, k = 512, 1024
+    segs = [0, 300, 340, 344, 600]
+    types = [12, 13, 14]
+    raws = [tcc.quantize(t, kq_cases.synthetic_weight(n, k, seed=40 + t)) for t in types]
+    ws = [tcc.Weight.upload(ctx, t, n, k, r) for t, r in zip(types, raws)]
+    xb = kq_cases.synthetic_x_bf16(segs[-1], k, seed=41)
+    x = torch.from_numpy(xb.view(np.int16)).view(torch.bfloat16).cuda()
+    seg_w = [1, 2, 0, 1]
+    y = _run(ctx, None, x, tcc.F32, seg=segs, seg_w=seg_w, weights=ws)
+    for i, wi in enumerate(seg_w):
+        a, b = segs[i], segs[i + 1]
+        staging = "f32" if b - a <= 16 else "bf16"
+        ref = oracle.qlinear_ref(xb[a:b], raws[wi], types[wi], n, k, staging)
+        assert oracle.rel_l2(y[a:b], ref) <= (1e-5 if staging == "f32" else TIGHT), (i, types[wi])
+
+
 def test_empty_and_zero_segments(ctx):
     import torch
     from turbocider_b200 import cuda as tcc
@@ -172,7 +194,7 @@ def test_empty_and_zero_segments(ctx):
         tcc.qlinear(ctx, w, x, seg_offsets=[0, 100, 50])
 
 
-@pytest.mark.parametrize("typ,n,k", [(12, 10240, 3840), (14, 3840, 10240)])
+@pytest.mark.parametrize("typ,n,k", [(12, 10240, 3840), (14, 3840, 10240), (13, 3840, 10240)])
 def test_full_size_config5_sampled_rows(ctx, typ, n, k):
     """Config 5 sizes (M = 8448): every output column of 64 sampled rows."""
     from turbocider_b200 import cuda as tcc
@@ -184,7 +206,7 @@ def test_full_size_config5_sampled_rows(ctx, typ, n, k):
     assert oracle.rel_l2(y[rows], ref) <= TIGHT
 
 
-@pytest.mark.parametrize("typ", [12, 14])
+@pytest.mark.parametrize("typ", [12, 13, 14])
 @pytest.mark.parametrize("m", [64, 300])
 def test_gemm_f16_staging_range_check(ctx, typ, m):
     """fp16 staging flags TC_STATUS_F16_OVERFLOW when a sub-block's values
@@ -206,7 +228,7 @@ def test_gemm_f16_staging_range_check(ctx, typ, m):
         w.free()
 
 
-@pytest.mark.parametrize("typ", [12, 14])
+@pytest.mark.parametrize("typ", [12, 13, 14])
 @pytest.mark.parametrize("m,n,k", [(300, 640, 768), (40, 512, 1024), (3, 256, 512), (1024, 1920, 1024)])
 def test_gemm_f16_activations_meet_1e3(ctx, typ, m, n, k):
     """TC_STAGE_F16_X16: fp16 X as given, W staged fp16, every segment on the
@@ -237,12 +259,13 @@ def test_gemm_f16_activations_meet_1e3(ctx, typ, m, n, k):
 
 @pytest.mark.parametrize("m", [1, 4, 16])
 def test_batched_gemv_matches_oracle(ctx, m):
-    """tc_cuda_qlinear_batched: Q4_K and Q6_K weights of different N sharing
-    K and X, one launch per type; each output against the fp32-decode oracle."""
+    """tc_cuda_qlinear_batched: Q4_K, Q5_K and Q6_K weights of different N
+    sharing K and X, one launch per type; each output against the fp32-decode
+    oracle."""
     import torch
     from turbocider_b200 import cuda as tcc
     k = 1024
-    specs = [(12, 512), (14, 384), (12, 100), (14, 1536), (12, 48)]
+    specs = [(12, 512), (14, 384), (13, 256), (12, 100), (14, 1536), (12, 48), (13, 700)]
     raws, ws = [], []
     for i, (typ, n) in enumerate(specs):
         raw = tcc.quantize(typ, kq_cases.synthetic_weight(n, k, seed=200 + i))

@@ -13,7 +13,7 @@ from oracle import oracle
 pytestmark = pytest.mark.gpu
 
 
-@pytest.mark.parametrize("typ", [12, 14])
+@pytest.mark.parametrize("typ", [12, 13, 14])
 def test_host_relayout_equals_device_relayout(ctx, typ):
     import torch
     from turbocider_b200 import cuda as tcc

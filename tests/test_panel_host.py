@@ -34,6 +34,13 @@ def unlayout(typ: int, panels: np.ndarray, n: int, k: int) -> np.ndarray:
                 blk[4:16] = ch[16384 + rr * 12:16384 + rr * 12 + 12]
                 for q in range(4):
                     blk[16 + 32 * q:48 + 32 * q] = ch[q * 4096 + s * 32:q * 4096 + s * 32 + 32]
+            elif typ == 13:
+                # qs [4][128][32] @0 | qh [128][32] @16384 | sc [128][12] @20480 | dm [128][4] @22016
+                blk[0:4] = ch[22016 + rr * 4:22016 + rr * 4 + 4]
+                blk[4:16] = ch[20480 + rr * 12:20480 + rr * 12 + 12]
+                blk[16:48] = ch[16384 + s * 32:16384 + s * 32 + 32]
+                for q in range(4):
+                    blk[48 + 32 * q:80 + 32 * q] = ch[q * 4096 + s * 32:q * 4096 + s * 32 + 32]
             else:
                 for h in range(2):
                     for part in range(2):
@@ -46,7 +53,7 @@ def unlayout(typ: int, panels: np.ndarray, n: int, k: int) -> np.ndarray:
     return out.reshape(n, -1)
 
 
-@pytest.mark.parametrize("typ", [12, 14])
+@pytest.mark.parametrize("typ", [12, 13, 14])
 @pytest.mark.parametrize("n,k,n_begin,n_count", [(300, 512, 0, 0), (256, 768, 64, 130), (5, 256, 0, 0)])
 def test_relayout_host_places_every_byte(typ, n, k, n_begin, n_count):
     raw = tcc.quantize(typ, kq_cases.synthetic_weight(n, k, seed=n + k)).reshape(n, -1)
@@ -60,11 +67,11 @@ def test_relayout_host_places_every_byte(typ, n, k, n_begin, n_count):
     assert not full[rows:].any()
 
 
-@pytest.mark.parametrize("typ", [12, 14])
+@pytest.mark.parametrize("typ", [12, 13, 14])
 def test_relayout_host_rejects_nonfinite_scale(typ):
     raw = bytearray(kq_cases.extreme_case(typ, 1.0))
     off = 208 if typ == 14 else 0
     raw[off:off + 2] = (0x7C00).to_bytes(2, "little")   # +inf
     with pytest.raises(tcc.DecodeError, match="nonfinite"):
         tcc.relayout_host(typ, bytes(raw), 2, 1024)
-    assert tcc.panel_bytes(13, 128, 256) == 0
+    assert tcc.panel_bytes(10, 128, 256) == 0

@@ -20,7 +20,7 @@ __device__ __forceinline__ uint16_t ld16(const uint8_t *p) { return (uint16_t)(p
 // warp.  Rows past N are written as zero blocks.
 __global__ void relayout_kernel(uint32_t type, const uint8_t *__restrict__ raw, uint64_t n,
                                 uint32_t kb, uint8_t *__restrict__ chunks, uint32_t panels,
-                                uint32_t *status) {
+                                uint32_t *status, uint64_t glu_c) {
     const uint64_t idx = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x;
     const uint64_t total = (uint64_t)panels * kb * kPanelRows;
     if (idx >= total) return;
@@ -31,7 +31,10 @@ __global__ void relayout_kernel(uint32_t type, const uint8_t *__restrict__ raw, 
     const uint64_t row = panel * kPanelRows + r;
     uint8_t *chunk = chunks + pk * chunk_bytes(type);
     const uint32_t bb = block_bytes(type);
-    const uint8_t *blk = row < n ? raw + (row * kb + col) * bb : nullptr;
+    // SwiGLU weights: panel row 16 g + i holds gate row 8 g + i (i < 8) or up
+    // row 8 g + i - 8, the up rows following the glu_c gate rows in `raw`.
+    const uint64_t src = glu_c ? (row >> 4) * 8 + (row & 7) + ((row & 8) ? glu_c : 0) : row;
+    const uint8_t *blk = row < n ? raw + (src * kb + col) * bb : nullptr;
     if (type == 12) {
         // qs quarters: 4 x 32 bytes
         for (uint32_t s = 0; s < 4; ++s) {
@@ -47,6 +50,19 @@ __global__ void relayout_kernel(uint32_t type, const uint8_t *__restrict__ raw, 
         for (uint32_t i = 0; i < 12; ++i) sc[i] = blk ? blk[4 + i] : 0;
         uint16_t d = blk ? ld16(blk) : 0, dmin = blk ? ld16(blk + 2) : 0;
         *reinterpret_cast<uint32_t *>(chunk + kQ4Dm + r * 4) = (uint32_t)d | ((uint32_t)dmin << 16);
+        if (!half_bits_finite(d) || !half_bits_finite(dmin)) atomicOr(status, kNonfinite);
+    } else if (type == 13) {
+        // qs quarters (block bytes 48..175), the qh plane (16..47), scales, d/dmin
+        for (uint32_t s = 0; s < 4; ++s) {
+            uint8_t *dst = chunk + kQ5Qs + s * 4096 + row_slot(r) * 32;
+            for (uint32_t i = 0; i < 32; ++i) dst[i] = blk ? blk[48 + 32 * s + i] : 0;
+        }
+        uint8_t *qh = chunk + kQ5Qh + row_slot(r) * 32;
+        for (uint32_t i = 0; i < 32; ++i) qh[i] = blk ? blk[16 + i] : 0;
+        uint8_t *sc = chunk + kQ5Sc + r * 12;
+        for (uint32_t i = 0; i < 12; ++i) sc[i] = blk ? blk[4 + i] : 0;
+        uint16_t d = blk ? ld16(blk) : 0, dmin = blk ? ld16(blk + 2) : 0;
+        *reinterpret_cast<uint32_t *>(chunk + kQ5Dm + r * 4) = (uint32_t)d | ((uint32_t)dmin << 16);
         if (!half_bits_finite(d) || !half_bits_finite(dmin)) atomicOr(status, kNonfinite);
     } else {
         // ql: [h][part][row][32]
@@ -131,6 +147,11 @@ __global__ void dequant_panel_kernel(WeightView w, uint8_t *__restrict__ dst, ui
         Q4Fields f{chunk + kQ4Qs + (G / 2) * 4096 + row_slot(r) * 32, chunk + kQ4Sc + r * 12,
                    (uint16_t)(dm & 0xffffu), (uint16_t)(dm >> 16)};
         q4k_group(f, G, v, bad);
+    } else if (w.type == 13) {
+        const uint32_t dm = *reinterpret_cast<const uint32_t *>(chunk + kQ5Dm + r * 4);
+        Q4Fields f{chunk + kQ5Qs + (G / 2) * 4096 + row_slot(r) * 32, chunk + kQ5Sc + r * 12,
+                   (uint16_t)(dm & 0xffffu), (uint16_t)(dm >> 16), chunk + kQ5Qh + row_slot(r) * 32};
+        q4k_group(f, G, v, bad);
     } else {
         const uint32_t h = G / 4, g = G % 4;
         Q6Fields f{chunk + kQ6Ql + ((h * 2 + (g & 1)) * kPanelRows + row_slot(r)) * 32,
@@ -212,10 +233,10 @@ inline unsigned blocks_for(uint64_t threads, unsigned per) { return (unsigned)((
 }  // namespace
 
 cudaError_t launch_relayout(uint32_t type, const uint8_t *raw, uint64_t n, uint32_t kb,
-                            uint8_t *chunks, uint32_t panels, uint32_t *status, cudaStream_t s) {
+                            uint8_t *chunks, uint32_t panels, uint32_t *status, cudaStream_t s, uint64_t glu_c) {
     const uint64_t total = (uint64_t)panels * kb * kPanelRows;
     if (!total) return cudaSuccess;
-    relayout_kernel<<<blocks_for(total, 256), 256, 0, s>>>(type, raw, n, kb, chunks, panels, status);
+    relayout_kernel<<<blocks_for(total, 256), 256, 0, s>>>(type, raw, n, kb, chunks, panels, status, glu_c);
     return cudaGetLastError();
 }
 

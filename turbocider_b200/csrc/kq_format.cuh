@@ -47,12 +47,16 @@ namespace tc {
 
 constexpr uint32_t kBlockWeights = 256;
 constexpr uint32_t kPanelRows = 128;
-constexpr uint32_t kQ4KBytes = 144, kQ6KBytes = 210;
+constexpr uint32_t kQ4KBytes = 144, kQ5KBytes = 176, kQ6KBytes = 210;
 constexpr uint32_t kQ4KChunk = kPanelRows * kQ4KBytes;  // 18432
+constexpr uint32_t kQ5KChunk = kPanelRows * kQ5KBytes;  // 22528
 constexpr uint32_t kQ6KChunk = kPanelRows * kQ6KBytes;  // 26880
 
 // Q4_K chunk field offsets
 constexpr uint32_t kQ4Qs = 0, kQ4Sc = 16384, kQ4Dm = 17920;
+// Q5_K chunk field offsets: Q4_K's fields plus the fifth-bit plane qh (32
+// bytes per row, bit g of qh[j] belongs to weight j of sub-block g)
+constexpr uint32_t kQ5Qs = 0, kQ5Qh = 16384, kQ5Sc = 20480, kQ5Dm = 22016;
 // Q6_K chunk field offsets
 constexpr uint32_t kQ6Ql = 0, kQ6Qh = 16384, kQ6Sc = 24576, kQ6D = 26624;
 
@@ -61,10 +65,10 @@ __host__ __device__ constexpr uint32_t row_slot(uint32_t r) {
 }
 
 __host__ __device__ constexpr uint32_t block_bytes(uint32_t type) {
-    return type == 12 ? kQ4KBytes : type == 14 ? kQ6KBytes : type == 13 ? 176u : 0u;
+    return type == 12 ? kQ4KBytes : type == 14 ? kQ6KBytes : type == 13 ? kQ5KBytes : 0u;
 }
 __host__ __device__ constexpr uint32_t chunk_bytes(uint32_t type) {
-    return type == 12 ? kQ4KChunk : type == 14 ? kQ6KChunk : 0u;
+    return type == 12 ? kQ4KChunk : type == 14 ? kQ6KChunk : type == 13 ? kQ5KChunk : 0u;
 }
 
 // fp16 bits -> fp32, exact (hardware conversion; equals the reference's

@@ -54,6 +54,7 @@
 
 #include <cstring>
 
+#include "kq_epilogue.cuh"
 #include "kq_sm100.cuh"
 #include "tc_internal.h"
 
@@ -74,7 +75,7 @@ constexpr uint32_t kTileRows = 256, kTileTokens = 256, kHalf = 128;
 constexpr uint32_t kACol0 = 256, kAStageCols = 32;
 
 struct PairSeg {
-    uint32_t m_begin, m_end, tile_begin, pad;
+    uint32_t m_begin, m_end, tile_begin, gate_row;
     const uint8_t *w;
 };
 struct PairParams {
@@ -83,7 +84,8 @@ struct PairParams {
     void *y;
     uint64_t ldy;
     uint32_t *status;
-    uint32_t y_tma;   // bf16 Y written by TMA stores (16-byte aligned base and row pitch)
+    uint32_t y_tma;   // 16-bit Y written by TMA stores (16-byte aligned base and row pitch)
+    EpiView epi;      // fused epilogue (flags 0: plain store); out_f16: fp16 rather than bf16
 };
 
 template <int TYPE>
@@ -215,45 +217,55 @@ __device__ __forceinline__ void load_row32(const uint8_t *p, uint32_t slot, uint
 // packed chunk `wc`, written to the TMEM A stage at `ta` (this thread's lane)
 // as 32 columns of packed pairs (column j = weights 2j, 2j+1 of the quarter).
 // Q4_K: byte j of the row's quarter holds weight j (low nibble, sub-block 2q)
-// and weight 32 + j (high nibble, sub-block 2q + 1).  Q6_K: half h = q / 2,
+// and weight 32 + j (high nibble, sub-block 2q + 1).  Q5_K: the same, plus
+// bits 2q and 2q + 1 of qh[j] as each code's fifth bit.  Q6_K: half h = q / 2,
 // parts of ql and the 2-bit planes of qh give weights j and 32 + j.
 template <int TYPE, bool F16>
 __device__ __forceinline__ void unpack_row(const uint8_t *wc, uint32_t q, uint32_t r, uint32_t ta, bool &ovf) {
     constexpr float kF16Inf = 65520.0f;   // smallest magnitude that rounds to inf
     const uint32_t slot = row_slot(r);
     uint32_t out[16];
-    if (TYPE == 12) {
-        const uint32_t dm = lds32(wc + kQ4Dm + r * 4);
+    if (affine_type(TYPE)) {
+        constexpr bool kQ5 = TYPE == 13;
+        constexpr uint32_t kDm = kQ5 ? kQ5Dm : kQ4Dm, kSc = kQ5 ? kQ5Sc : kQ4Sc, kQs = kQ5 ? kQ5Qs : kQ4Qs;
+        constexpr float kQMax = kQ5 ? 31.0f : 15.0f;
+        const uint32_t dm = lds32(wc + kDm + r * 4);
         const float d = half_bits_to_float((uint16_t)(dm & 0xffffu)), dmin = half_bits_to_float((uint16_t)(dm >> 16));
-        const uint8_t *scp = wc + kQ4Sc + r * 12;
+        const uint8_t *scp = wc + kSc + r * 12;
         uint32_t s0, m0, s1, m1;
         const uint32_t sw0 = lds32(scp), sw1 = lds32(scp + 4), sw2 = lds32(scp + 8);
         q4k_scale_min_w(2 * q, sw0, sw1, sw2, s0, m0);
         q4k_scale_min_w(2 * q + 1, sw0, sw1, sw2, s1, m1);
         const float a0 = d * (float)s0, b0 = dmin * (float)m0, a1 = d * (float)s1, b1 = dmin * (float)m1;
         if (F16)
-            ovf |= fmaxf(fabsf(b0), fabsf(fmaf(a0, 15.0f, -b0))) >= kF16Inf ||
-                   fmaxf(fabsf(b1), fabsf(fmaf(a1, 15.0f, -b1))) >= kF16Inf;
-        uint32_t w[8];
-        load_row32(wc + kQ4Qs + q * 4096 + slot * 32, slot, w);
+            ovf |= fmaxf(fabsf(b0), fabsf(fmaf(a0, kQMax, -b0))) >= kF16Inf ||
+                   fmaxf(fabsf(b1), fabsf(fmaf(a1, kQMax, -b1))) >= kF16Inf;
+        uint32_t w[8], hb[8];
+        load_row32(wc + kQs + q * 4096 + slot * 32, slot, w);
+        if (kQ5) load_row32(wc + kQ5Qh + slot * 32, slot, hb);
         const uint64_t off2 = f2splat(-8388608.0f);
         {
             const uint64_t sc2 = f2splat(a0), mn2 = f2splat(-b0);
 #pragma unroll
             for (int i = 0; i < 8; ++i) {
-                const uint2 v = four_values<12, F16>(w[i] & 0x0F0F0F0Fu, sc2, off2, mn2);
+                const uint32_t c = kQ5 ? (w[i] & 0x0F0F0F0Fu) | (((hb[i] >> (2 * q)) & 0x01010101u) << 4)
+                                       : w[i] & 0x0F0F0F0Fu;
+                const uint2 v = four_values<TYPE, F16>(c, sc2, off2, mn2);
                 out[2 * i] = v.x;
                 out[2 * i + 1] = v.y;
             }
             tmem_st16(ta, out);
         }
         {
-            // High nibbles are read in place (16 q): the scale is pre-divided
-            // by 16, a power of two, so every product stays exact.
-            const uint64_t sc2 = f2splat(a1 * 0.0625f), mn2 = f2splat(-b1);
+            // Q4_K high nibbles are read in place (16 q) with the scale
+            // pre-divided by 16, a power of two, so every product stays exact;
+            // Q5_K's 5-bit codes are shifted down instead.
+            const uint64_t sc2 = f2splat(kQ5 ? a1 : a1 * 0.0625f), mn2 = f2splat(-b1);
 #pragma unroll
             for (int i = 0; i < 8; ++i) {
-                const uint2 v = four_values<12, F16>(w[i] & 0xF0F0F0F0u, sc2, off2, mn2);
+                const uint32_t c = kQ5 ? ((w[i] >> 4) & 0x0F0F0F0Fu) | (((hb[i] >> (2 * q + 1)) & 0x01010101u) << 4)
+                                       : w[i] & 0xF0F0F0F0u;
+                const uint2 v = four_values<TYPE, F16>(c, sc2, off2, mn2);
                 out[2 * i] = v.x;
                 out[2 * i + 1] = v.y;
             }
@@ -301,13 +313,17 @@ __device__ __forceinline__ void unpack_row(const uint8_t *wc, uint32_t q, uint32
 struct PairTile {
     uint32_t m0, m_end, pp;   // first token, segment end, pair-panel (256 weight rows)
     const uint8_t *w;
+    uint32_t gate_row;
 };
 __device__ __forceinline__ PairTile pair_tile(const PairParams &p, uint32_t t) {
     uint32_t s = 0;
     while (s + 1 < p.n_seg && t >= p.seg[s + 1].tile_begin) ++s;
     const uint32_t local = t - p.seg[s].tile_begin;
     return {p.seg[s].m_begin + (local / p.pair_panels) * kTileTokens, p.seg[s].m_end, local % p.pair_panels,
-            p.seg[s].w};
+            p.seg[s].w, p.seg[s].gate_row};
+}
+__device__ __forceinline__ uint16_t to16(float v, bool f16) {
+    return f16 ? __half_as_ushort(__float2half_rn(v)) : __bfloat16_as_ushort(__float2bfloat16_rn(v));
 }
 
 // ------------------------------------------------------------ the kernel
@@ -508,6 +524,19 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
             }
             const uint32_t taddr = tmem + ((quad * 32) << 16);
             uint32_t tma_pieces = 0;   // bit j: piece j goes out by TMA
+            const bool f16 = p.epi.out_f16;
+            if (p.epi.flags) {
+                // fused epilogue: direct stores (SwiGLU halves the columns)
+                const EpiRow er = epi_row(p.epi, min(n, p.n - 1), T.gate_row);
+#pragma unroll 1
+                for (uint32_t j = 0; j < kTileTokens / 32; ++j) {
+                    const uint32_t t0 = T.m0 + 32 * j;
+                    if (t0 >= T.m_end || n0 >= p.n) break;
+                    uint32_t v[32];
+                    tmem_ld32(taddr + 32 * j, v);
+                    epi_piece<OUT_F32>(p.epi, er, v, n < p.n, t0, T.m_end, p.y, p.ldy);
+                }
+            } else {
 #pragma unroll 1
             for (uint32_t j = 0; j < kTileTokens / 32; ++j) {
                 const uint32_t t0 = T.m0 + 32 * j;
@@ -516,9 +545,9 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
                 tmem_ld32(taddr + 32 * j, v);
                 if (!OUT_F32 && p.y_tma && t0 + 32 <= T.m_end) {
                     tma_pieces |= 1u << j;
-                    __nv_bfloat16 *sb = reinterpret_cast<__nv_bfloat16 *>(stage + j * L::e_box) + lane;
+                    uint16_t *sb = reinterpret_cast<uint16_t *>(stage + j * L::e_box) + lane;
 #pragma unroll
-                    for (uint32_t c = 0; c < 32; ++c) sb[c * 32] = __float2bfloat16_rn(__uint_as_float(v[c]));
+                    for (uint32_t c = 0; c < 32; ++c) sb[c * 32] = to16(__uint_as_float(v[c]), f16);
                 } else if (n < p.n) {
 #pragma unroll
                     for (uint32_t c = 0; c < 32; ++c) {
@@ -526,10 +555,11 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
                         if (m < T.m_end) {
                             const uint64_t off = (uint64_t)m * p.ldy + n;
                             if (OUT_F32) static_cast<float *>(p.y)[off] = __uint_as_float(v[c]);
-                            else static_cast<__nv_bfloat16 *>(p.y)[off] = __float2bfloat16_rn(__uint_as_float(v[c]));
+                            else static_cast<uint16_t *>(p.y)[off] = to16(__uint_as_float(v[c]), f16);
                         }
                     }
                 }
+            }
             }
             // Every TMEM load has completed (tcgen05.ld waits): hand D back.
             tc_fence_before();
@@ -607,7 +637,7 @@ cudaError_t launch_pair_inst(const CUtensorMap &xm, const CUtensorMap &ym, const
 
 cudaError_t launch_gemm_pair(const SegmentView *segs, uint32_t n_seg, const uint16_t *x, uint64_t m_total,
                              uint64_t k, void *y, uint64_t ldy, int out_dtype, int stage_f16, int sm_count,
-                             uint32_t *status, cudaStream_t s) {
+                             uint32_t *status, cudaStream_t s, const EpiView *epi) {
     if (n_seg == 0) return cudaSuccess;
     if (n_seg > (uint32_t)kMaxSeg) return cudaErrorInvalidValue;
     PairParams p{};
@@ -619,9 +649,11 @@ cudaError_t launch_gemm_pair(const SegmentView *segs, uint32_t n_seg, const uint
     p.y = y;
     p.ldy = ldy;
     p.status = status;
+    if (epi) p.epi = *epi;
+    p.epi.out_f16 = out_dtype == 1;
     uint32_t tiles = 0;
     for (uint32_t i = 0; i < n_seg; ++i) {
-        p.seg[i] = {segs[i].m_begin, segs[i].m_end, tiles, 0u, segs[i].w.chunks};
+        p.seg[i] = {segs[i].m_begin, segs[i].m_end, tiles, segs[i].gate_row, segs[i].w.chunks};
         tiles += (segs[i].m_end - segs[i].m_begin + kTileTokens - 1) / kTileTokens * p.pair_panels;
     }
     p.n_tiles = tiles;
@@ -642,11 +674,12 @@ cudaError_t launch_gemm_pair(const SegmentView *segs, uint32_t n_seg, const uint
     const int out_f32 = out_dtype == 0;
     CUtensorMap ym;
     memset(&ym, 0, sizeof(ym));
-    if (!out_f32 && (reinterpret_cast<uintptr_t>(y) & 15u) == 0 && (ldy * 2) % 16 == 0) {
+    if (!out_f32 && !p.epi.flags && (reinterpret_cast<uintptr_t>(y) & 15u) == 0 && (ldy * 2) % 16 == 0) {
         const cuuint64_t ydims[2] = {p.n, m_total};
         const cuuint64_t ystrides[1] = {ldy * 2};
         const cuuint32_t ybox[2] = {32u, 32u};
-        const CUresult ry = enc(&ym, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, y, ydims, ystrides, ybox, estr,
+        const CUresult ry = enc(&ym, out_dtype == 1 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16,
+                                2, y, ydims, ystrides, ybox, estr,
                                 CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE,
                                 CU_TENSOR_MAP_L2_PROMOTION_NONE, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
         p.y_tma = ry == CUDA_SUCCESS ? 1u : 0u;
@@ -655,6 +688,10 @@ cudaError_t launch_gemm_pair(const SegmentView *segs, uint32_t n_seg, const uint
     if (type == 12) {
         if (stage_f16) return out_f32 ? launch_pair_inst<12, true, true>(xm, ym, p, sm_count, s) : launch_pair_inst<12, true, false>(xm, ym, p, sm_count, s);
         return out_f32 ? launch_pair_inst<12, false, true>(xm, ym, p, sm_count, s) : launch_pair_inst<12, false, false>(xm, ym, p, sm_count, s);
+    }
+    if (type == 13) {
+        if (stage_f16) return out_f32 ? launch_pair_inst<13, true, true>(xm, ym, p, sm_count, s) : launch_pair_inst<13, true, false>(xm, ym, p, sm_count, s);
+        return out_f32 ? launch_pair_inst<13, false, true>(xm, ym, p, sm_count, s) : launch_pair_inst<13, false, false>(xm, ym, p, sm_count, s);
     }
     if (stage_f16) return out_f32 ? launch_pair_inst<14, true, true>(xm, ym, p, sm_count, s) : launch_pair_inst<14, true, false>(xm, ym, p, sm_count, s);
     return out_f32 ? launch_pair_inst<14, false, true>(xm, ym, p, sm_count, s) : launch_pair_inst<14, false, false>(xm, ym, p, sm_count, s);

@@ -28,6 +28,7 @@
 #include <cuda.h>
 #include <cudaTypedefs.h>
 
+#include "kq_epilogue.cuh"
 #include "kq_sm100.cuh"
 #include "tc_internal.h"
 
@@ -41,7 +42,7 @@ constexpr int kWStages = 2;     // packed chunk pipeline depth (256 K each)
 constexpr int kMaxSeg = 32;
 
 struct GemmSeg {
-    uint32_t m_begin, m_end, tile_begin, pad;
+    uint32_t m_begin, m_end, tile_begin, gate_row;
     const uint8_t *w;
 };
 struct GemmParams {
@@ -50,6 +51,7 @@ struct GemmParams {
     void *y;
     uint64_t ldy;
     uint32_t *status;
+    EpiView epi;      // fused epilogue (flags 0: plain store); out_f16: fp16 rather than bf16
 };
 
 template <int TYPE, int BN>
@@ -74,13 +76,15 @@ struct Layout {
 struct Tile {
     uint32_t m0, m_end, panel;
     const uint8_t *w;
+    uint32_t gate_row;
 };
 template <int BN>
 __device__ __forceinline__ Tile tile_of(const GemmParams &p, uint32_t t) {
     uint32_t s = 0;
     while (s + 1 < p.n_seg && t >= p.seg[s + 1].tile_begin) ++s;
     const uint32_t local = t - p.seg[s].tile_begin;
-    return {p.seg[s].m_begin + (local / p.panels) * BN, p.seg[s].m_end, local % p.panels, p.seg[s].w};
+    return {p.seg[s].m_begin + (local / p.panels) * BN, p.seg[s].m_end, local % p.panels, p.seg[s].w,
+            p.seg[s].gate_row};
 }
 
 
@@ -249,6 +253,16 @@ __global__ void __launch_bounds__(kThreads, 1)
             tc_fence_after();
             const uint32_t n = T.panel * 128 + quad * 32 + lane;
             const uint32_t taddr = tmem + ((quad * 32) << 16) + acc * BN;
+            const bool f16 = p.epi.out_f16;
+            if (p.epi.flags) {
+                const EpiRow er = epi_row(p.epi, min(n, p.n - 1), T.gate_row);
+#pragma unroll 1
+                for (uint32_t c0 = 0; c0 < (uint32_t)BN; c0 += 32) {
+                    uint32_t v[32];
+                    tmem_ld32(taddr + c0, v);
+                    epi_piece<OUT_F32>(p.epi, er, v, n < p.n, T.m0 + c0, T.m_end, p.y, p.ldy);
+                }
+            } else {
 #pragma unroll 1
             for (uint32_t c0 = 0; c0 < (uint32_t)BN; c0 += 32) {
                 uint32_t v[32];
@@ -260,10 +274,12 @@ __global__ void __launch_bounds__(kThreads, 1)
                         if (m < T.m_end) {
                             const uint64_t off = (uint64_t)m * p.ldy + n;
                             if (OUT_F32) static_cast<float *>(p.y)[off] = __uint_as_float(v[c]);
+                            else if (f16) static_cast<__half *>(p.y)[off] = __float2half_rn(__uint_as_float(v[c]));
                             else static_cast<__nv_bfloat16 *>(p.y)[off] = __float2bfloat16_rn(__uint_as_float(v[c]));
                         }
                     }
                 }
+            }
             }
             tc_fence_before();
             bar_arrive(acc_empty(acc));
@@ -327,14 +343,14 @@ cudaError_t launch_bn(const CUtensorMap &map, const GemmParams &p, int f16, int 
 
 cudaError_t launch_gemm(const SegmentView *segs, uint32_t n_seg, const uint16_t *x, uint64_t m_total, uint64_t k,
                         void *y, uint64_t ldy, int out_dtype, int stage_f16, int sm_count, uint32_t *status,
-                        int allow_pair, cudaStream_t s) {
+                        int allow_pair, cudaStream_t s, const EpiView *epi) {
     if (n_seg == 0) return cudaSuccess;
     if (n_seg > (uint32_t)kMaxSeg) return cudaErrorInvalidValue;
     uint32_t max_rows = 0;
     for (uint32_t i = 0; i < n_seg; ++i) max_rows = max(max_rows, segs[i].m_end - segs[i].m_begin);
     const int bn = max_rows <= 64 ? 64 : max_rows <= 128 ? 128 : 256;
     if (bn == 256 && allow_pair)
-        return launch_gemm_pair(segs, n_seg, x, m_total, k, y, ldy, out_dtype, stage_f16, sm_count, status, s);
+        return launch_gemm_pair(segs, n_seg, x, m_total, k, y, ldy, out_dtype, stage_f16, sm_count, status, s, epi);
     GemmParams p{};
     p.n_seg = n_seg;
     p.kb = segs[0].w.kb;
@@ -343,9 +359,11 @@ cudaError_t launch_gemm(const SegmentView *segs, uint32_t n_seg, const uint16_t 
     p.y = y;
     p.ldy = ldy;
     p.status = status;
+    if (epi) p.epi = *epi;
+    p.epi.out_f16 = out_dtype == 1;
     uint32_t tiles = 0;
     for (uint32_t i = 0; i < n_seg; ++i) {
-        p.seg[i] = {segs[i].m_begin, segs[i].m_end, tiles, 0u, segs[i].w.chunks};
+        p.seg[i] = {segs[i].m_begin, segs[i].m_end, tiles, segs[i].gate_row, segs[i].w.chunks};
         tiles += (segs[i].m_end - segs[i].m_begin + bn - 1) / bn * p.panels;
     }
     p.n_tiles = tiles;
@@ -369,6 +387,11 @@ cudaError_t launch_gemm(const SegmentView *segs, uint32_t n_seg, const uint16_t 
         if (bn == 64) return launch_bn<12, 64>(map, p, stage_f16, out_f32, sm_count, s);
         if (bn == 128) return launch_bn<12, 128>(map, p, stage_f16, out_f32, sm_count, s);
         return launch_bn<12, 256>(map, p, stage_f16, out_f32, sm_count, s);
+    }
+    if (type == 13) {
+        if (bn == 64) return launch_bn<13, 64>(map, p, stage_f16, out_f32, sm_count, s);
+        if (bn == 128) return launch_bn<13, 128>(map, p, stage_f16, out_f32, sm_count, s);
+        return launch_bn<13, 256>(map, p, stage_f16, out_f32, sm_count, s);
     }
     if (bn == 64) return launch_bn<14, 64>(map, p, stage_f16, out_f32, sm_count, s);
     if (bn == 128) return launch_bn<14, 128>(map, p, stage_f16, out_f32, sm_count, s);

@@ -37,6 +37,7 @@
 // Launches use programmatic dependent launch: weight prefetch overlaps the
 // tail of the previous kernel in the stream; X, the workspace and Y are
 // touched only after griddepcontrol.wait.
+#include "kq_epilogue.cuh"
 #include "kq_format.cuh"
 #include "tc_internal.h"
 
@@ -70,6 +71,10 @@ __device__ __forceinline__ void mma16816(float (&d)[4], uint32_t a0, uint32_t a1
 template <int TYPE> struct StageGeo;
 template <> struct StageGeo<12> {
     static constexpr uint32_t w_bytes = 2304, qs = 0, sc = 2048, dm = 2240;
+};
+//   Q5_K: qs [4][16][32] | qh [16][32] | sc [16][12] | dm [16][4]     = 2816 B
+template <> struct StageGeo<13> {
+    static constexpr uint32_t w_bytes = 2816, qs = 0, qh = 2048, sc = 2560, dm = 2752;
 };
 template <> struct StageGeo<14> {
     static constexpr uint32_t w_bytes = 3360, ql = 0, qh = 2048, sc = 3072, d = 3328;
@@ -120,6 +125,12 @@ __device__ __forceinline__ void issue_w(uint8_t *st, uint32_t bar, const uint8_t
         for (uint32_t q = 0; q < 4; ++q) bulk_g2s(d + SG::qs + q * 512, chunk + kQ4Qs + q * 4096 + r0 * 32, 512, bar);
         bulk_g2s(d + SG::sc, chunk + kQ4Sc + r0 * 12, 192, bar);
         bulk_g2s(d + SG::dm, chunk + kQ4Dm + r0 * 4, 64, bar);
+    } else if constexpr (TYPE == 13) {
+#pragma unroll
+        for (uint32_t q = 0; q < 4; ++q) bulk_g2s(d + SG::qs + q * 512, chunk + kQ5Qs + q * 4096 + r0 * 32, 512, bar);
+        bulk_g2s(d + SG::qh, chunk + kQ5Qh + r0 * 32, 512, bar);
+        bulk_g2s(d + SG::sc, chunk + kQ5Sc + r0 * 12, 192, bar);
+        bulk_g2s(d + SG::dm, chunk + kQ5Dm + r0 * 4, 64, bar);
     } else {
 #pragma unroll
         for (uint32_t hp = 0; hp < 4; ++hp)
@@ -178,7 +189,7 @@ __device__ __forceinline__ uint32_t centred_pair(uint32_t codes, uint32_t sel) {
 //   Q6_K: v = 8h + 4jj + grp -> 16-weight group 8h + 2grp + jj, one step each.
 template <int TYPE>
 __device__ __forceinline__ constexpr uint32_t group_of_visit(uint32_t v) {
-    return TYPE == 12 ? v : 8 * (v >> 3) + 2 * (v & 3) + ((v >> 2) & 1);
+    return TYPE != 14 ? v : 8 * (v >> 3) + 2 * (v & 3) + ((v >> 2) & 1);
 }
 
 template <int TYPE, int TP, int NT>
@@ -192,7 +203,7 @@ __device__ __forceinline__ void compute_stage(const uint8_t *st, const uint16_t 
     // Scale table, written by all lanes: row rr, half `half` of its groups.
     //   Q4_K: float2 (d*sc_g, dmin*m_g) [16][8];  Q6_K: float d*sc_i [16][16].
     __syncwarp();
-    if constexpr (TYPE == 12) {
+    if constexpr (TYPE != 14) {
         const uint32_t dm = lds32(st + SG::dm + rr * 4);
         const float d = half_bits_to_float((uint16_t)(dm & 0xffffu)), dmin = half_bits_to_float((uint16_t)(dm >> 16));
         const uint32_t w0 = lds32(st + SG::sc + rr * 12), w1 = lds32(st + SG::sc + rr * 12 + 4),
@@ -238,7 +249,7 @@ __device__ __forceinline__ void compute_stage(const uint8_t *st, const uint16_t 
                 for (int i = 0; i < 4; ++i) cq[nt][i] = c1[nt][i] = 0.f;
         }
         uint32_t a0, a1, a2, a3;
-        if constexpr (TYPE == 12) {
+        if constexpr (TYPE != 14) {
             a0 = code_pair(cg, 0x4140u); a1 = code_pair(cg8, 0x4140u);
             a2 = code_pair(cg, 0x4342u); a3 = code_pair(cg8, 0x4342u);
         } else {
@@ -252,7 +263,7 @@ __device__ __forceinline__ void compute_stage(const uint8_t *st, const uint16_t 
             const bool on = my_j == j;
             const uint32_t b0 = on ? xv.x : 0u, b1 = on ? xv.y : 0u;
             mma16816(cq[nt], a0, a1, a2, a3, b0, b1, cq[nt]);
-            if constexpr (TYPE == 12) mma16816(c1[nt], ones, ones, ones, ones, b0, b1, c1[nt]);
+            if constexpr (TYPE != 14) mma16816(c1[nt], ones, ones, ones, ones, b0, b1, c1[nt]);
         }
     };
     // Scale the finished chain `chain` into the accumulators.
@@ -260,7 +271,7 @@ __device__ __forceinline__ void compute_stage(const uint8_t *st, const uint16_t 
 #pragma unroll
         for (uint32_t ci = 0; ci < 2; ++ci) {
             const uint32_t G = group_of_visit<TYPE>(chain * S + (2 * t + ci) / TP);
-            if constexpr (TYPE == 12) {
+            if constexpr (TYPE != 14) {
                 const float2 a = reinterpret_cast<const float2 *>(wt)[g * 8 + G];
                 const float2 b = reinterpret_cast<const float2 *>(wt)[(g + 8) * 8 + G];
 #pragma unroll
@@ -280,7 +291,13 @@ __device__ __forceinline__ void compute_stage(const uint8_t *st, const uint16_t 
         }
     };
 
-    if constexpr (TYPE == 12) {
+    if constexpr (TYPE != 14) {
+        // Q5_K: the fifth bit of code j of sub-block v is bit v of qh[j]
+        uint2 hq = make_uint2(0u, 0u), hq8 = make_uint2(0u, 0u);
+        if constexpr (TYPE == 13) {
+            hq = *reinterpret_cast<const uint2 *>(st + StageGeo<13>::qh + rg * 32 + 8 * t);
+            hq8 = *reinterpret_cast<const uint2 *>(st + StageGeo<13>::qh + rg8 * 32 + 8 * t);
+        }
 #pragma unroll
         for (uint32_t q = 0; q < 4; ++q) {
             const uint2 wg = *reinterpret_cast<const uint2 *>(st + SG::qs + q * 512 + rg * 32 + 8 * t);
@@ -291,8 +308,12 @@ __device__ __forceinline__ void compute_stage(const uint8_t *st, const uint16_t 
 #pragma unroll
                 for (uint32_t sp = 0; sp < 2; ++sp) {
                     const uint32_t w = sp ? wg.y : wg.x, w8 = sp ? wg8.y : wg8.x;
-                    step(v, (w >> (4 * nib)) & 0x0F0F0F0Fu, (w8 >> (4 * nib)) & 0x0F0F0F0Fu,
-                         32 * v + 8 * t + 4 * sp, sp == 0 && v % S == 0);
+                    uint32_t c = (w >> (4 * nib)) & 0x0F0F0F0Fu, c8 = (w8 >> (4 * nib)) & 0x0F0F0F0Fu;
+                    if constexpr (TYPE == 13) {
+                        c |= (((sp ? hq.y : hq.x) >> v) & 0x01010101u) << 4;
+                        c8 |= (((sp ? hq8.y : hq8.x) >> v) & 0x01010101u) << 4;
+                    }
+                    step(v, c, c8, 32 * v + 8 * t + 4 * sp, sp == 0 && v % S == 0);
                 }
                 if (v % S == S - 1) close_chain(v / S);
             }
@@ -337,7 +358,7 @@ __global__ void __launch_bounds__(kWarps * 32) gemv_kernel(const __grid_constant
                                                            float *__restrict__ partials,
                                                            uint32_t *__restrict__ counters, uint32_t *status) {
     using SG = StageGeo<TYPE>;
-    constexpr uint32_t chunk = TYPE == 12 ? kQ4KChunk : kQ6KChunk;
+    constexpr uint32_t chunk = chunk_bytes(TYPE);
     extern __shared__ __align__(128) uint8_t dyn[];
     __shared__ float red[kWarps][32][4 * NT];
     __shared__ __align__(16) float tab[kWarps][16 * 16];
@@ -474,7 +495,32 @@ __global__ void __launch_bounds__(kWarps * 32) gemv_kernel(const __grid_constant
                 store = true;
             }
         }
-        if (store) {
+        if (store && b.epi.flags) {
+            // Fused epilogue.  A thread holds rows g and g + 8 of the tile for
+            // the same token: for a SwiGLU weight the gate row and its up row.
+            const EpiView &e = b.epi;
+            const bool glu = e.flags & TC_EPI_SWIGLU;
+#pragma unroll
+            for (int nt = 0; nt < NT; ++nt) {
+#pragma unroll
+                for (int i = 0; i < 4; ++i) {
+                    const uint32_t col = 2 * t + (i & 1);
+                    const uint32_t tok = 8 * nt + col % TP;
+                    const uint32_t row = row0 + g + 8 * (i >> 1);
+                    if (glu && i >= 2) continue;   // up rows are read with their gate row
+                    if (col < TP && tok < m_count && row < w.n) {
+                        const EpiRow er = epi_row(e, row, b.gate_row);
+                        float val = v[4 * nt + i] + er.bias;
+                        if (glu) val = silu(val) * (v[4 * nt + i + 2] + epi_row(e, row + 8, b.gate_row).bias);
+                        else val = epi_act(e.flags, val);
+                        const uint64_t m = m_begin + tok;
+                        if (e.flags & TC_EPI_GATE_RESIDUAL)
+                            val = load_out(e.res, m * e.ld_res + er.col, DT == 0, DT == 1) + er.gate * val;
+                        store_out(y, m * ldy + er.col, val, DT == 0, DT == 1);
+                    }
+                }
+            }
+        } else if (store) {
 #pragma unroll
             for (int nt = 0; nt < NT; ++nt) {
 #pragma unroll
@@ -486,8 +532,7 @@ __global__ void __launch_bounds__(kWarps * 32) gemv_kernel(const __grid_constant
                     const uint32_t row = row0 + g + 8 * (i >> 1);
                     if (col < TP && tok < m_count && row < w.n) {
                         const uint64_t off = (uint64_t)(m_begin + tok) * ldy + row;
-                        if (DT == 0) static_cast<float *>(y)[off] = v[4 * nt + i];
-                        else static_cast<__nv_bfloat16 *>(y)[off] = __float2bfloat16_rn(v[4 * nt + i]);
+                        store_out(y, off, v[4 * nt + i], DT == 0, DT == 1);
                     }
                 }
             }
@@ -501,14 +546,15 @@ cudaError_t launch_typed(const GemvBatch &bt, uint32_t tiles, uint32_t m_begin, 
     const dim3 grid(tiles, sp.n_slices);
     const size_t stage = (StageGeo<TYPE>::w_bytes + (TP == 1 ? 512u : 0u) + 127) / 128 * 128;
     const size_t smem = stage * kGemvStages * kWarps;
-    auto kern = out_dtype == 0 ? gemv_kernel<TYPE, TP, NT, 0> : gemv_kernel<TYPE, TP, NT, 2>;
+    auto kern = out_dtype == 0 ? gemv_kernel<TYPE, TP, NT, 0>
+                : out_dtype == 1 ? gemv_kernel<TYPE, TP, NT, 1> : gemv_kernel<TYPE, TP, NT, 2>;
     // Opt in once per instantiation to the largest stage set (16 tokens).
-    static bool configured[2] = {false, false};
-    if (!configured[out_dtype == 0]) {
+    static bool configured[3] = {false, false, false};
+    if (!configured[out_dtype]) {
         const int most = (int)((StageGeo<TYPE>::w_bytes + (TP == 1 ? 512u : 0u) + 127) / 128 * 128 * kGemvStages * kWarps);
         cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, most);
         if (e != cudaSuccess) return e;
-        configured[out_dtype == 0] = true;
+        configured[out_dtype] = true;
     }
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = grid;
@@ -560,24 +606,30 @@ size_t gemv_workspace_floats_tiles(uint32_t tiles, uint32_t kb) {
 }
 size_t gemv_workspace_floats(const WeightView &w) { return gemv_workspace_floats_tiles((w.n + 15) / 16, w.kb); }
 
-cudaError_t launch_gemv_batch(const GemvBatch &bt, uint32_t type, uint32_t tiles, uint32_t m_begin, uint32_t m,
-                              const uint16_t *x, uint64_t k, int out_dtype, const GemvSplit &sp, cudaStream_t s) {
+cudaError_t launch_gemv_batch(const GemvBatch &bt_in, uint32_t type, uint32_t tiles, uint32_t m_begin, uint32_t m,
+                              const uint16_t *x, uint64_t k, int out_dtype, const GemvSplit &sp, cudaStream_t s,
+                              const EpiView *epi, uint32_t gate_row) {
     if (!m || !tiles) return cudaSuccess;
+    if (out_dtype < 0 || out_dtype > 2) return cudaErrorInvalidValue;
+    GemvBatch bt = bt_in;
+    bt.epi = epi ? *epi : EpiView{};
+    bt.gate_row = gate_row;
     if (m > 16 || bt.n_entries == 0 || bt.n_entries > kMaxGemvBatch) return cudaErrorInvalidValue;
     if (sp.n_slices > 1 && (!sp.partials || !sp.counters)) return cudaErrorInvalidValue;
-    return type == 12 ? launch_m<12>(bt, tiles, m_begin, m, x, k, out_dtype, sp, s)
-                      : launch_m<14>(bt, tiles, m_begin, m, x, k, out_dtype, sp, s);
+    if (type == 12) return launch_m<12>(bt, tiles, m_begin, m, x, k, out_dtype, sp, s);
+    if (type == 13) return launch_m<13>(bt, tiles, m_begin, m, x, k, out_dtype, sp, s);
+    return launch_m<14>(bt, tiles, m_begin, m, x, k, out_dtype, sp, s);
 }
 
 cudaError_t launch_gemv(const SegmentView &seg, const uint16_t *x, uint64_t k, void *y, uint64_t ldy,
-                        int out_dtype, const GemvSplit &sp, cudaStream_t s) {
+                        int out_dtype, const GemvSplit &sp, cudaStream_t s, const EpiView *epi) {
     if (seg.m_end <= seg.m_begin) return cudaSuccess;
     GemvBatch bt{};
     bt.n_entries = 1;
     bt.kb = seg.w.kb;
     bt.e[0] = {seg.w.chunks, y, ldy, seg.w.n, 0u};
     return launch_gemv_batch(bt, seg.w.type, (seg.w.n + 15) / 16, seg.m_begin, seg.m_end - seg.m_begin, x, k,
-                             out_dtype, sp, s);
+                             out_dtype, sp, s, epi, seg.gate_row);
 }
 
 }  // namespace tc

@@ -157,27 +157,35 @@ __device__ __forceinline__ uint32_t magic_byte(uint32_t w, uint32_t i) {
 //   Q6_K row r: d*sc_i for the 16 sub-blocks.
 // Thread dt writes 16 bytes of row dt % 128 (conflict-free with the odd
 // 80-byte stride, as are the reads of the dequant tasks).
+// Q4_K and Q5_K share the per-sub-block (scale, min) form d*sc*q - dmin*m
+// (gguf_decode.cpp:77-90); Q6_K is scale-only.
+__device__ __forceinline__ constexpr bool affine_type(int type) { return type == 12 || type == 13; }
+
 // With fp16 staging the range check is done here, once per sub-block: the
 // decode is affine in the code, so the largest magnitude a sub-block can
-// produce sits at an end code (Q4_K: q = 0 or 15; Q6_K: q - 32 = -32);
-// `ovf` is raised when that value would round to inf in fp16.
+// produce sits at an end code (Q4_K: q = 0 or 15; Q5_K: 0 or 31; Q6_K:
+// q - 32 = -32); `ovf` is raised when that value would round to inf in fp16.
+// Q5_K's odd sub-blocks are not pre-divided: their 5-bit codes are shifted
+// down to the low bits instead of being read in place.
 template <int TYPE, bool F16>
 __device__ __forceinline__ void build_table(const uint8_t *wc, float *tab, uint32_t dt, bool &ovf) {
     constexpr float kF16Inf = 65520.0f;   // smallest magnitude that rounds to inf
     const uint32_t r = dt & 127, j = dt >> 7;
     float4 v;
-    if (TYPE == 12) {
-        const uint32_t dm = *reinterpret_cast<const uint32_t *>(wc + kQ4Dm + r * 4);
+    if (affine_type(TYPE)) {
+        constexpr uint32_t kDm = TYPE == 12 ? kQ4Dm : kQ5Dm, kSc = TYPE == 12 ? kQ4Sc : kQ5Sc;
+        constexpr float kQMax = TYPE == 12 ? 15.0f : 31.0f, kOddScale = TYPE == 12 ? 0.0625f : 1.0f;
+        const uint32_t dm = *reinterpret_cast<const uint32_t *>(wc + kDm + r * 4);
         const float d = half_bits_to_float((uint16_t)(dm & 0xffffu)), dmin = half_bits_to_float((uint16_t)(dm >> 16));
-        const uint8_t *sc = wc + kQ4Sc + r * 12;
+        const uint8_t *sc = wc + kSc + r * 12;
         uint32_t s0, m0, s1, m1;
         q4k_scale_min(2 * j, sc, s0, m0);
         q4k_scale_min(2 * j + 1, sc, s1, m1);
-        v = make_float4(d * (float)s0, dmin * (float)m0, d * (float)s1 * 0.0625f, dmin * (float)m1);
+        v = make_float4(d * (float)s0, dmin * (float)m0, d * (float)s1 * kOddScale, dmin * (float)m1);
         if (F16) {
             const float a1 = d * (float)s1;
-            ovf |= fmaxf(fabsf(v.y), fabsf(fmaf(v.x, 15.0f, -v.y))) >= kF16Inf ||
-                   fmaxf(fabsf(v.w), fabsf(fmaf(a1, 15.0f, -v.w))) >= kF16Inf;
+            ovf |= fmaxf(fabsf(v.y), fabsf(fmaf(v.x, kQMax, -v.y))) >= kF16Inf ||
+                   fmaxf(fabsf(v.w), fabsf(fmaf(a1, kQMax, -v.w))) >= kF16Inf;
         }
     } else {
         const float d = half_bits_to_float(*reinterpret_cast<const uint16_t *>(wc + kQ6D + r * 2));
@@ -211,7 +219,7 @@ __device__ __forceinline__ uint2 four_values(uint32_t codes, uint64_t scale2, ui
     const uint64_t p0 = f2add(f2pack(magic_byte(codes, 0), magic_byte(codes, 1)), off2);
     const uint64_t p1 = f2add(f2pack(magic_byte(codes, 2), magic_byte(codes, 3)), off2);
     uint64_t v0, v1;
-    if (TYPE == 12) { v0 = f2fma(scale2, p0, min2); v1 = f2fma(scale2, p1, min2); }
+    if (affine_type(TYPE)) { v0 = f2fma(scale2, p0, min2); v1 = f2fma(scale2, p1, min2); }
     else { v0 = f2mul(scale2, p0); v1 = f2mul(scale2, p1); }
     return make_uint2(pack_pair<F16>(v0), pack_pair<F16>(v1));
 }
@@ -235,6 +243,19 @@ __device__ __forceinline__ void dequant_task(const uint8_t *wc, const float *tab
         lo1 = four_values<12, F16>(b.y & 0x0F0F0F0Fu, dl, off2, ml);
         hi0 = four_values<12, F16>(b.x & 0xF0F0F0F0u, dh, off2, mh);
         hi1 = four_values<12, F16>(b.y & 0xF0F0F0F0u, dh, off2, mh);
+    } else if (TYPE == 13) {
+        // Q5_K: low nibble | fifth bit (bit 2q of qh) for sub-block 2q, high
+        // nibble shifted down | bit 2q+1 for sub-block 2q+1 (codes 0..31).
+        const uint2 b = *reinterpret_cast<const uint2 *>(wc + kQ5Qs + q * 4096 + slot * 32 + t * 8);
+        const uint2 hb = *reinterpret_cast<const uint2 *>(wc + kQ5Qh + slot * 32 + t * 8);
+        const float4 s = *reinterpret_cast<const float4 *>(trow + 16 * q);
+        const uint64_t off2 = f2splat(-8388608.0f);
+        const uint64_t dl = f2splat(s.x), ml = f2splat(-s.y), dh = f2splat(s.z), mh = f2splat(-s.w);
+        const uint32_t bl = 2 * q, bh = 2 * q + 1;
+        lo0 = four_values<13, F16>((b.x & 0x0F0F0F0Fu) | (((hb.x >> bl) & 0x01010101u) << 4), dl, off2, ml);
+        lo1 = four_values<13, F16>((b.y & 0x0F0F0F0Fu) | (((hb.y >> bl) & 0x01010101u) << 4), dl, off2, ml);
+        hi0 = four_values<13, F16>(((b.x >> 4) & 0x0F0F0F0Fu) | (((hb.x >> bh) & 0x01010101u) << 4), dh, off2, mh);
+        hi1 = four_values<13, F16>(((b.y >> 4) & 0x0F0F0F0Fu) | (((hb.y >> bh) & 0x01010101u) << 4), dh, off2, mh);
     } else {
         const uint32_t h = q >> 1, shift = (q & 1) * 4, g0 = 2 * (q & 1);
         const uint2 la = *reinterpret_cast<const uint2 *>(wc + kQ6Ql + ((h * 2 + 0) * kPanelRows + slot) * 32 + t * 8);

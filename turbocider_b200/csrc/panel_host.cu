@@ -44,6 +44,12 @@ bool chunk_host(uint32_t type, const uint8_t *rows, uint64_t n, uint32_t kb, uin
             std::memcpy(chunk + kQ4Sc + r * 12, blk + 4, 12);
             std::memcpy(chunk + kQ4Dm + r * 4, blk, 4);   // d, dmin (little endian, as on the device)
             ok &= finite_half(rd16(blk)) && finite_half(rd16(blk + 2));
+        } else if (type == 13) {
+            for (uint32_t s = 0; s < 4; ++s) std::memcpy(chunk + kQ5Qs + s * 4096 + slot * 32, blk + 48 + 32 * s, 32);
+            std::memcpy(chunk + kQ5Qh + slot * 32, blk + 16, 32);
+            std::memcpy(chunk + kQ5Sc + r * 12, blk + 4, 12);
+            std::memcpy(chunk + kQ5Dm + r * 4, blk, 4);
+            ok &= finite_half(rd16(blk)) && finite_half(rd16(blk + 2));
         } else {
             for (uint32_t h = 0; h < 2; ++h)
                 for (uint32_t part = 0; part < 2; ++part)
@@ -62,7 +68,9 @@ bool chunk_host(uint32_t type, const uint8_t *rows, uint64_t n, uint32_t kb, uin
 extern "C" {
 
 uint64_t tc_panel_bytes(uint32_t ggml_type, uint64_t n, uint64_t k) {
-    if ((ggml_type != TC_GGML_Q4_K && ggml_type != TC_GGML_Q6_K) || !n || !k || k % 256) return 0;
+    if ((ggml_type != TC_GGML_Q4_K && ggml_type != TC_GGML_Q5_K && ggml_type != TC_GGML_Q6_K) || !n || !k ||
+        k % 256)
+        return 0;
     return (n + tc::kPanelRows - 1) / tc::kPanelRows * (k / 256) * tc::chunk_bytes(ggml_type);
 }
 

@@ -98,6 +98,45 @@ void quantize_q4k_block(const float *w, uint8_t *p) {
     }
 }
 
+// Q5_K: the Q4_K fit with 31 code levels; the fifth bit of weight j of
+// sub-block g goes to bit g of qh[j] (block bytes 16..47), the low nibbles to
+// qs (bytes 48..175) as in Q4_K.
+void quantize_q5k_block(const float *w, uint8_t *p) {
+    float a[8], b[8];
+    for (int g = 0; g < 8; ++g) {
+        float lo = w[32 * g], hi = w[32 * g];
+        for (int j = 1; j < 32; ++j) { lo = std::min(lo, w[32 * g + j]); hi = std::max(hi, w[32 * g + j]); }
+        b[g] = std::max(0.f, -lo);
+        a[g] = std::max(0.f, (hi + b[g]) / 31.f);
+    }
+    const float amax = *std::max_element(a, a + 8), bmax = *std::max_element(b, b + 8);
+    const uint16_t dh = f32_to_f16_bits(amax / 63.f), mh = f32_to_f16_bits(bmax / 63.f);
+    const float d = f16_bits_to_f32(dh), dmin = f16_bits_to_f32(mh);
+    uint32_t sc[8], mn[8];
+    for (int g = 0; g < 8; ++g) {
+        sc[g] = d > 0 ? (uint32_t)std::clamp(nearest(a[g] / d), 0, 63) : 0u;
+        mn[g] = dmin > 0 ? (uint32_t)std::clamp(nearest(b[g] / dmin), 0, 63) : 0u;
+    }
+    std::memset(p, 0, 176);
+    p[0] = (uint8_t)(dh & 0xff); p[1] = (uint8_t)(dh >> 8);
+    p[2] = (uint8_t)(mh & 0xff); p[3] = (uint8_t)(mh >> 8);
+    uint8_t *s = p + 4;
+    for (int g = 0; g < 4; ++g) {
+        s[g] = (uint8_t)(sc[g] | ((sc[g + 4] >> 4) << 6));
+        s[g + 4] = (uint8_t)(mn[g] | ((mn[g + 4] >> 4) << 6));
+        s[g + 8] = (uint8_t)((sc[g + 4] & 15u) | ((mn[g + 4] & 15u) << 4));
+    }
+    uint8_t *qh = p + 16, *qs = p + 48;
+    for (int g = 0; g < 8; ++g) {
+        const float A = d * (float)sc[g], B = dmin * (float)mn[g];
+        for (int j = 0; j < 32; ++j) {
+            const int q = A > 0 ? std::clamp(nearest((w[32 * g + j] + B) / A), 0, 31) : 0;
+            qs[(g / 2) * 32 + j] |= (uint8_t)((q & 15) << ((g & 1) * 4));
+            qh[j] |= (uint8_t)((q >> 4) << g);
+        }
+    }
+}
+
 void quantize_q6k_block(const float *w, uint8_t *p) {
     float c[16];
     for (int s = 0; s < 16; ++s) {
@@ -129,9 +168,9 @@ void quantize_q6k_block(const float *w, uint8_t *p) {
 extern "C" int tc_quantize(uint32_t type, const float *w, uint64_t rows, uint64_t cols, void *blocks,
                            uint64_t blocks_bytes, int threads) {
     if (!w || !blocks) return TC_CUDA_FAIL;
-    if (type != TC_GGML_Q4_K && type != TC_GGML_Q6_K) return TC_CUDA_FAIL;
+    if (type != TC_GGML_Q4_K && type != TC_GGML_Q5_K && type != TC_GGML_Q6_K) return TC_CUDA_FAIL;
     if (!rows || !cols || cols % 256) return TC_CUDA_FAIL;
-    const uint64_t bb = type == TC_GGML_Q4_K ? 144 : 210, per_row = cols / 256;
+    const uint64_t bb = type == TC_GGML_Q4_K ? 144 : type == TC_GGML_Q5_K ? 176 : 210, per_row = cols / 256;
     if (blocks_bytes / bb / per_row < rows) return TC_CUDA_FAIL;
     const int nt = std::max(1, std::min<int>(threads, 256));
     auto *out = static_cast<uint8_t *>(blocks);
@@ -144,6 +183,7 @@ extern "C" int tc_quantize(uint32_t type, const float *w, uint64_t rows, uint64_
                 const float *src = w + r * cols + b * 256;
                 uint8_t *dst = out + (r * per_row + b) * bb;
                 if (type == TC_GGML_Q4_K) quantize_q4k_block(src, dst);
+                else if (type == TC_GGML_Q5_K) quantize_q5k_block(src, dst);
                 else quantize_q6k_block(src, dst);
             }
     };

@@ -44,7 +44,9 @@ struct DeviceGuard {
     }
 };
 
-bool supported_type(uint32_t type) { return type == TC_GGML_Q4_K || type == TC_GGML_Q6_K; }
+bool supported_type(uint32_t type) {
+    return type == TC_GGML_Q4_K || type == TC_GGML_Q5_K || type == TC_GGML_Q6_K;
+}
 
 tc::WeightView view_of(const tc_cuda_weight *w) {
     return {w->chunks, w->type, w->kb, w->panels, (uint32_t)w->n};
@@ -182,30 +184,23 @@ int tc_cuda_weight_fill_device(tc_cuda_ctx *ctx, tc_cuda_weight *w, const void *
     return ok();
 }
 
-int tc_cuda_weight_upload(tc_cuda_ctx *ctx, uint32_t type, uint64_t n, uint64_t k, const void *raw_host,
-                          uint64_t raw_bytes, uint64_t n_begin, uint64_t n_count, tc_cuda_weight **out) {
-    if (!ctx || !out || !raw_host) return fail("null context, source or out-parameter");
-    *out = nullptr;
-    if (!supported_type(type)) return fail("gguf_decode: unsupported tensor type");
-    if (!n || !k || k % tc::kBlockWeights) return fail("invalid source geometry");
-    if (n_count == 0) n_count = n - std::min(n_begin, n);
-    if (n_begin >= n || n_count > n - n_begin) return fail("row slice out of bounds");
-    const uint64_t row_bytes = k / tc::kBlockWeights * tc::block_bytes(type);
-    if (raw_bytes / row_bytes < n) return fail("packed source too short");
-    tc_cuda_weight *w = nullptr;
-    int rc = tc_cuda_weight_create(ctx, type, n_count, k, &w);
-    if (rc) return rc;
+}  // extern "C"
+
+namespace {
+// Copy `n_src` host row ranges of `bytes_each` into one device staging buffer,
+// re-lay them into w's panels (glu_c > 0: gate then up rows, interleaved) and
+// check every scale finite.  Frees w on failure; synchronous.
+int upload_rows(tc_cuda_ctx *ctx, tc_cuda_weight *w, const uint8_t *const *src, int n_src, uint64_t bytes_each,
+                uint64_t glu_c, tc_cuda_weight **out) {
     DeviceGuard guard(ctx->device);
     void *staging = nullptr;
-    const uint64_t shard_bytes = n_count * row_bytes;
-    cudaError_t e = cudaMalloc(&staging, shard_bytes);
-    if (e == cudaSuccess)
-        e = cudaMemcpy(staging, static_cast<const uint8_t *>(raw_host) + n_begin * row_bytes, shard_bytes,
-                       cudaMemcpyHostToDevice);
+    cudaError_t e = cudaMalloc(&staging, bytes_each * n_src);
+    for (int i = 0; i < n_src && e == cudaSuccess; ++i)
+        e = cudaMemcpy(static_cast<uint8_t *>(staging) + i * bytes_each, src[i], bytes_each, cudaMemcpyHostToDevice);
     if (e == cudaSuccess) e = cudaMemset(ctx->status + 1, 0, sizeof(uint32_t));
     if (e == cudaSuccess)
-        e = tc::launch_relayout(type, static_cast<const uint8_t *>(staging), n_count, w->kb, w->chunks, w->panels,
-                                ctx->status + 1, nullptr);
+        e = tc::launch_relayout(w->type, static_cast<const uint8_t *>(staging), w->n, w->kb, w->chunks, w->panels,
+                                ctx->status + 1, nullptr, glu_c);
     uint32_t bits = 0;
     if (e == cudaSuccess) e = cudaMemcpy(&bits, ctx->status + 1, sizeof(uint32_t), cudaMemcpyDeviceToHost);
     if (staging) cudaFree(staging);
@@ -219,6 +214,47 @@ int tc_cuda_weight_upload(tc_cuda_ctx *ctx, uint32_t type, uint64_t n, uint64_t 
     }
     *out = w;
     return ok();
+}
+}  // namespace
+
+extern "C" {
+
+int tc_cuda_weight_upload(tc_cuda_ctx *ctx, uint32_t type, uint64_t n, uint64_t k, const void *raw_host,
+                          uint64_t raw_bytes, uint64_t n_begin, uint64_t n_count, tc_cuda_weight **out) {
+    if (!ctx || !out || !raw_host) return fail("null context, source or out-parameter");
+    *out = nullptr;
+    if (!supported_type(type)) return fail("gguf_decode: unsupported tensor type");
+    if (!n || !k || k % tc::kBlockWeights) return fail("invalid source geometry");
+    if (n_count == 0) n_count = n - std::min(n_begin, n);
+    if (n_begin >= n || n_count > n - n_begin) return fail("row slice out of bounds");
+    const uint64_t row_bytes = k / tc::kBlockWeights * tc::block_bytes(type);
+    if (raw_bytes / row_bytes < n) return fail("packed source too short");
+    tc_cuda_weight *w = nullptr;
+    int rc = tc_cuda_weight_create(ctx, type, n_count, k, &w);
+    if (rc) return rc;
+    const uint8_t *src = static_cast<const uint8_t *>(raw_host) + n_begin * row_bytes;
+    return upload_rows(ctx, w, &src, 1, n_count * row_bytes, 0, out);
+}
+
+int tc_cuda_weight_upload_glu(tc_cuda_ctx *ctx, uint32_t type, uint64_t f, uint64_t k, const void *gate_raw,
+                              const void *up_raw, uint64_t raw_bytes_each, uint64_t col_begin, uint64_t col_count,
+                              tc_cuda_weight **out) {
+    if (!ctx || !out || !gate_raw || !up_raw) return fail("null context, source or out-parameter");
+    *out = nullptr;
+    if (!supported_type(type)) return fail("gguf_decode: unsupported tensor type");
+    if (!f || !k || k % tc::kBlockWeights) return fail("invalid source geometry");
+    if (col_count == 0) col_count = f - std::min(col_begin, f);
+    if (col_begin >= f || col_count > f - col_begin) return fail("row slice out of bounds");
+    if (col_count % 8) return fail("SwiGLU column count must be a multiple of 8");
+    const uint64_t row_bytes = k / tc::kBlockWeights * tc::block_bytes(type);
+    if (raw_bytes_each / row_bytes < f) return fail("packed source too short");
+    tc_cuda_weight *w = nullptr;
+    int rc = tc_cuda_weight_create(ctx, type, 2 * col_count, k, &w);
+    if (rc) return rc;
+    w->glu = 1;
+    const uint8_t *src[2] = {static_cast<const uint8_t *>(gate_raw) + col_begin * row_bytes,
+                             static_cast<const uint8_t *>(up_raw) + col_begin * row_bytes};
+    return upload_rows(ctx, w, src, 2, col_count * row_bytes, col_count, out);
 }
 
 void tc_cuda_weight_free(tc_cuda_weight *w) {
@@ -296,7 +332,7 @@ int tc_cuda_qlinear_batched(tc_cuda_ctx *ctx, const tc_cuda_weight *const *weigh
     if (!ctx || !weights || !x || !ys) return fail("null argument");
     if (!n_weights || n_weights > tc::kMaxGemvBatch) return fail("1..64 weights per batched call");
     if (m < 1 || m > 16) return fail("the batched GEMV takes 1..16 rows of X");
-    if (out_dtype != TC_DTYPE_F32 && out_dtype != TC_DTYPE_BF16) return fail("output dtype must be f32 or bf16");
+    if (out_dtype < TC_DTYPE_F32 || out_dtype > TC_DTYPE_BF16) return fail("invalid output dtype");
     if (reinterpret_cast<uintptr_t>(x) % 16) return fail("X must be 16-byte aligned");
     const uint64_t k = weights[0] ? weights[0]->k : 0;
     for (uint32_t i = 0; i < n_weights; ++i) {
@@ -304,12 +340,13 @@ int tc_cuda_qlinear_batched(tc_cuda_ctx *ctx, const tc_cuda_weight *const *weigh
         if (!w || !ys[i]) return fail("null weight or output");
         if (w->k != k) return fail("weights of one batched call must share K");
         if (w->device != ctx->device) return fail("weight lives on another device");
+        if (w->glu) return fail("a SwiGLU weight needs TC_EPI_SWIGLU (tc_cuda_qlinear_ex)");
         if (ldys && ldys[i] && ldys[i] < w->n) return fail("invalid/overlapping row stride");
     }
     DeviceGuard guard(ctx->device);
     cudaStream_t s = static_cast<cudaStream_t>(stream);
     // One launch per weight type (the kernel is specialised on it).
-    for (const uint32_t type : {uint32_t(TC_GGML_Q4_K), uint32_t(TC_GGML_Q6_K)}) {
+    for (const uint32_t type : {uint32_t(TC_GGML_Q4_K), uint32_t(TC_GGML_Q5_K), uint32_t(TC_GGML_Q6_K)}) {
         tc::GemvBatch bt{};
         uint32_t tiles = 0;
         for (uint32_t i = 0; i < n_weights; ++i) {
@@ -345,9 +382,16 @@ int tc_cuda_set_sm_limit(tc_cuda_ctx *ctx, int sms) {
 int tc_cuda_qlinear(tc_cuda_ctx *ctx, const tc_cuda_weight *const *weights, uint32_t n_weights,
                     const int32_t *seg_offsets, const int32_t *seg_weight, uint32_t n_seg, const void *x, void *y,
                     uint64_t ldy, int out_dtype, int stage, void *stream) {
+    return tc_cuda_qlinear_ex(ctx, weights, n_weights, seg_offsets, seg_weight, n_seg, x, y, ldy, out_dtype, stage,
+                              nullptr, stream);
+}
+
+int tc_cuda_qlinear_ex(tc_cuda_ctx *ctx, const tc_cuda_weight *const *weights, uint32_t n_weights,
+                       const int32_t *seg_offsets, const int32_t *seg_weight, uint32_t n_seg, const void *x, void *y,
+                       uint64_t ldy, int out_dtype, int stage, const tc_epilogue *epilogue, void *stream) {
     if (!ctx || !weights || !n_weights || !x || !y || !seg_offsets) return fail("null argument");
     if (!n_seg) return fail("no segments");
-    if (out_dtype != TC_DTYPE_F32 && out_dtype != TC_DTYPE_BF16) return fail("output dtype must be f32 or bf16");
+    if (out_dtype < TC_DTYPE_F32 || out_dtype > TC_DTYPE_BF16) return fail("invalid output dtype");
     if (stage != TC_STAGE_BF16 && stage != TC_STAGE_F16 && stage != TC_STAGE_F16_X16)
         return fail("invalid staging precision");
     if (stage == TC_STAGE_F16_X16 && ctx->path == 1) return fail("the warp GEMV takes bf16 X");
@@ -357,9 +401,38 @@ int tc_cuda_qlinear(tc_cuda_ctx *ctx, const tc_cuda_weight *const *weights, uint
         if (!weights[i]) return fail("null weight");
         if (weights[i]->n != w0->n || weights[i]->k != w0->k) return fail("weights of one call must share N and K");
         if (weights[i]->device != ctx->device) return fail("weight lives on another device");
+        if (weights[i]->glu != w0->glu) return fail("SwiGLU and plain weights cannot share a call");
     }
-    if (ldy == 0) ldy = w0->n;
-    if (ldy < w0->n) return fail("invalid/overlapping row stride");
+    const uint32_t flags = epilogue ? epilogue->flags : 0u;
+    const uint32_t known = TC_EPI_BIAS | TC_EPI_GELU_TANH | TC_EPI_GELU_ERF | TC_EPI_SWIGLU | TC_EPI_GATE_RESIDUAL;
+    if (flags & ~known) return fail("unknown epilogue flag");
+    if (__builtin_popcount(flags & (TC_EPI_GELU_TANH | TC_EPI_GELU_ERF | TC_EPI_SWIGLU)) > 1)
+        return fail("at most one activation per epilogue");
+    if (bool(flags & TC_EPI_SWIGLU) != bool(w0->glu))
+        return fail(w0->glu ? "a SwiGLU weight needs TC_EPI_SWIGLU" : "TC_EPI_SWIGLU needs a weight from tc_cuda_weight_upload_glu");
+    const uint64_t n_out = w0->glu ? w0->n / 2 : w0->n;
+    if (ldy == 0) ldy = n_out;
+    if (ldy < n_out) return fail("invalid/overlapping row stride");
+    tc::EpiView epi;
+    epi.flags = flags;
+    if (flags & TC_EPI_BIAS) {
+        if (!epilogue->bias) return fail("TC_EPI_BIAS needs a bias vector");
+        epi.bias = epilogue->bias;
+        epi.bias_up = epilogue->bias_up_offset;
+        if (w0->glu && epi.bias_up < n_out) return fail("SwiGLU up-bias offset overlaps the gate biases");
+    }
+    if (flags & TC_EPI_GATE_RESIDUAL) {
+        if (!epilogue->gate || !epilogue->residual) return fail("TC_EPI_GATE_RESIDUAL needs gate and residual");
+        epi.gate = epilogue->gate;
+        epi.ld_gate = epilogue->ld_gate ? epilogue->ld_gate : n_out;
+        epi.res = epilogue->residual;
+        epi.ld_res = epilogue->ld_residual ? epilogue->ld_residual : n_out;
+        if (epi.ld_gate < n_out || epi.ld_res < n_out) return fail("invalid/overlapping row stride");
+        for (uint32_t s = 0; s < n_seg; ++s) {
+            const int64_t g = epilogue->seg_gate ? epilogue->seg_gate[s] : (int64_t)s;
+            if (g < 0 || g >= (int64_t)epilogue->n_gate_rows) return fail("segment gate row out of range");
+        }
+    }
     if (seg_offsets[0] != 0) return fail("seg_offsets[0] must be 0");
     for (uint32_t s = 0; s < n_seg; ++s) {
         if (seg_offsets[s + 1] < seg_offsets[s]) return fail("seg_offsets must be non-decreasing");
@@ -375,40 +448,41 @@ int tc_cuda_qlinear(tc_cuda_ctx *ctx, const tc_cuda_weight *const *weights, uint
 
     // Split segments: small ones to the GEMV, the rest to the tensor-core GEMM
     // (one launch per weight type).
-    std::vector<tc::SegmentView> gemm[2];
+    std::vector<tc::SegmentView> gemm[3];   // Q4_K, Q6_K, Q5_K
     std::vector<tc::SegmentView> gemv;
     for (uint32_t i = 0; i < n_seg; ++i) {
         const uint32_t b = (uint32_t)seg_offsets[i], e = (uint32_t)seg_offsets[i + 1];
         if (b == e) continue;
         const tc_cuda_weight *w = weights[seg_weight ? seg_weight[i] : 0];
-        const tc::SegmentView sv{b, e, view_of(w)};
+        tc::SegmentView sv{b, e, view_of(w)};
+        if (flags & TC_EPI_GATE_RESIDUAL) sv.gate_row = (uint32_t)(epilogue->seg_gate ? epilogue->seg_gate[i] : i);
         // fp16 X (TC_STAGE_F16_X16) always takes the tensor-core GEMM: the
         // warp GEMV works in bf16 code space.
         const bool small = (e - b) <= 16 && stage != TC_STAGE_F16_X16;
         if ((small && ctx->path < 2) || ctx->path == 1) {
             // The GEMV handles at most 16 rows per launch; longer forced
             // segments are cut into 16-row pieces.
-            for (uint32_t m = b; m < e; m += 16) gemv.push_back({m, std::min(e, m + 16), sv.w});
+            for (uint32_t m = b; m < e; m += 16) gemv.push_back({m, std::min(e, m + 16), sv.w, sv.gate_row});
         } else {
-            gemm[w->type == TC_GGML_Q4_K ? 0 : 1].push_back(sv);
+            gemm[w->type == TC_GGML_Q4_K ? 0 : w->type == TC_GGML_Q5_K ? 2 : 1].push_back(sv);
         }
     }
     const uint16_t *xg = static_cast<const uint16_t *>(x);
-    if (stage == TC_STAGE_F16 && (!gemm[0].empty() || !gemm[1].empty())) {
+    if (stage == TC_STAGE_F16 && (!gemm[0].empty() || !gemm[1].empty() || !gemm[2].empty())) {
         int rc = ensure_workspace(ctx, m_total * k * 2);
         if (rc) return rc;
         cudaError_t e = tc::launch_x_to_f16(xg, static_cast<uint16_t *>(ctx->workspace), m_total * k, ctx->status, s);
         if (e != cudaSuccess) return cuda_fail("fp16 staging launch", e);
         xg = static_cast<const uint16_t *>(ctx->workspace);
     }
-    for (int t = 0; t < 2; ++t) {
+    for (int t = 0; t < 3; ++t) {
         for (size_t i = 0; i < gemm[t].size(); i += 32) {
             const uint32_t cnt = (uint32_t)std::min<size_t>(32, gemm[t].size() - i);
             cudaError_t e = tc::launch_gemm(gemm[t].data() + i, cnt, xg, m_total, k, y, ldy, out_dtype,
                                             stage != TC_STAGE_BF16,
                                             ctx->sm_limit > 0 ? std::min(ctx->sm_limit, ctx->sm_count) : ctx->sm_count,
                                             ctx->status,
-                                            ctx->path != 3, s);
+                                            ctx->path != 3, s, &epi);
             if (e != cudaSuccess) return cuda_fail("GEMM launch", e);
         }
     }
@@ -421,7 +495,7 @@ int tc_cuda_qlinear(tc_cuda_ctx *ctx, const tc_cuda_weight *const *weights, uint
             sp.partials = ctx->gemv_partials;
             sp.counters = ctx->gemv_counters;
         }
-        cudaError_t e = tc::launch_gemv(sv, static_cast<const uint16_t *>(x), k, y, ldy, out_dtype, sp, s);
+        cudaError_t e = tc::launch_gemv(sv, static_cast<const uint16_t *>(x), k, y, ldy, out_dtype, sp, s, &epi);
         if (e != cudaSuccess) return cuda_fail("GEMV launch", e);
     }
     return ok();

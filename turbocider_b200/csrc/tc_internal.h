@@ -21,7 +21,8 @@ struct tc_cuda_ctx {
 
 struct tc_cuda_weight {
     int device = 0;
-    uint32_t type = 0;               // 12 = Q4_K, 14 = Q6_K
+    uint32_t type = 0;               // 12 = Q4_K, 13 = Q5_K, 14 = Q6_K
+    uint32_t glu = 0;                // rows are 8-row gate / up groups (tc_cuda_weight_upload_glu)
     uint64_t n = 0, k = 0;
     uint32_t kb = 0;                 // super-blocks per row, K / 256
     uint32_t panels = 0;             // ceil(N / 128)
@@ -45,10 +46,26 @@ struct WeightView {
 struct SegmentView {
     uint32_t m_begin, m_end;         // rows of X / Y
     WeightView w;
+    uint32_t gate_row = 0;           // row of the epilogue's gate vectors
 };
 
+// Fused epilogue (device pointers), flags = TC_EPI_* bits; flags == 0 is a
+// plain store.  out_f16 selects fp16 over bf16 for 16-bit outputs.
+struct EpiView {
+    uint32_t flags = 0, out_f16 = 0;
+    const float *bias = nullptr;     // by weight row; SwiGLU: gate c at c, up c at bias_up + c
+    uint64_t bias_up = 0;
+    const float *gate = nullptr;     // [rows][ld_gate], over output columns
+    uint64_t ld_gate = 0;
+    const void *res = nullptr;       // [M][ld_res] in the output dtype
+    uint64_t ld_res = 0;
+};
+
+// glu_c > 0: the source holds glu_c gate rows then glu_c up rows, and panel
+// row 16 g + i takes gate row 8 g + i (i < 8) or up row 8 g + i - 8.
 cudaError_t launch_relayout(uint32_t type, const uint8_t *raw, uint64_t n, uint32_t kb,
-                            uint8_t *chunks, uint32_t panels, uint32_t *status, cudaStream_t s);
+                            uint8_t *chunks, uint32_t panels, uint32_t *status, cudaStream_t s,
+                            uint64_t glu_c = 0);
 cudaError_t launch_dequant_panel(const WeightView &w, int dtype, void *dst, uint64_t ld,
                                  uint32_t *status, cudaStream_t s);
 cudaError_t launch_decode_raw(uint32_t type, const uint8_t *src, uint64_t row_bytes,
@@ -79,11 +96,17 @@ struct GemvEntry {
 struct GemvBatch {
     uint32_t n_entries, kb;
     GemvEntry e[kMaxGemvBatch];
+    EpiView epi;          // fused epilogue of every entry (flags 0: plain store)
+    uint32_t gate_row;    // gate vector row of the launch's segment
 };
+// out_dtype: TC_DTYPE_F32 / F16 / BF16.  epi (optional) applies to every
+// entry, with gate row `gate_row`.
 cudaError_t launch_gemv_batch(const GemvBatch &bt, uint32_t type, uint32_t tiles, uint32_t m_begin, uint32_t m,
-                              const uint16_t *x, uint64_t k, int out_dtype, const GemvSplit &sp, cudaStream_t s);
+                              const uint16_t *x, uint64_t k, int out_dtype, const GemvSplit &sp, cudaStream_t s,
+                              const EpiView *epi = nullptr, uint32_t gate_row = 0);
 cudaError_t launch_gemv(const SegmentView &seg, const uint16_t *x, uint64_t k, void *y,
-                        uint64_t ldy, int out_dtype, const GemvSplit &split, cudaStream_t s);
+                        uint64_t ldy, int out_dtype, const GemvSplit &split, cudaStream_t s,
+                        const EpiView *epi = nullptr);
 cudaError_t launch_x_to_f16(const uint16_t *x, uint16_t *x16, uint64_t count, uint32_t *status,
                             cudaStream_t s);
 // Tensor-core GEMM over a list of segments that share type, N and K.  Uses
@@ -91,9 +114,11 @@ cudaError_t launch_x_to_f16(const uint16_t *x, uint16_t *x16, uint64_t count, ui
 // and allow_pair is set, one-CTA 128 x {64, 128, 256} tiles otherwise.
 cudaError_t launch_gemm(const SegmentView *segs, uint32_t n_seg, const uint16_t *x,
                         uint64_t m_total, uint64_t k, void *y, uint64_t ldy, int out_dtype,
-                        int stage_f16, int sm_count, uint32_t *status, int allow_pair, cudaStream_t s);
+                        int stage_f16, int sm_count, uint32_t *status, int allow_pair, cudaStream_t s,
+                        const EpiView *epi = nullptr);
 cudaError_t launch_gemm_pair(const SegmentView *segs, uint32_t n_seg, const uint16_t *x,
                              uint64_t m_total, uint64_t k, void *y, uint64_t ldy, int out_dtype,
-                             int stage_f16, int sm_count, uint32_t *status, cudaStream_t s);
+                             int stage_f16, int sm_count, uint32_t *status, cudaStream_t s,
+                             const EpiView *epi = nullptr);
 
 }  // namespace tc

@@ -79,8 +79,9 @@ extern "C" int tc_cuda_qlinear_small_static(const tc_cuda_weight *weight, const 
                                             uint64_t ldy, int out_dtype, void *stream) {
     if (!weight || !x || !y) return fail("null weight, X or Y");
     if (m == 0 || m > 16) return fail("tc_cuda_qlinear_small_static handles 1..16 rows of X");
-    if (out_dtype != TC_DTYPE_F32 && out_dtype != TC_DTYPE_BF16) return fail("output dtype must be f32 or bf16");
+    if (out_dtype < TC_DTYPE_F32 || out_dtype > TC_DTYPE_BF16) return fail("invalid output dtype");
     if (reinterpret_cast<uintptr_t>(x) % 16) return fail("X must be 16-byte aligned");
+    if (weight->glu) return fail("a SwiGLU weight needs TC_EPI_SWIGLU (tc_cuda_qlinear_ex)");
     if (ldy == 0) ldy = weight->n;
     if (ldy < weight->n) return fail("invalid/overlapping row stride");
 

@@ -20,7 +20,8 @@ Q4_K, Q5_K, Q6_K = 12, 13, 14
 F32, F16, BF16 = 0, 1, 2
 STAGE_BF16, STAGE_F16, STAGE_F16_X16 = 0, 1, 2
 STATUS_NONFINITE_SCALE, STATUS_F16_OVERFLOW, STATUS_TIMEOUT, STATUS_GEOMETRY = 1, 2, 4, 8
-BLOCK_BYTES = {Q4_K: 144, Q6_K: 210}
+EPI_BIAS, EPI_GELU_TANH, EPI_GELU_ERF, EPI_SWIGLU, EPI_GATE_RESIDUAL = 1, 2, 4, 8, 16
+BLOCK_BYTES = {Q4_K: 144, Q5_K: 176, Q6_K: 210}
 
 _lib = None
 
@@ -34,6 +35,13 @@ class DecodeError(BackendError):
 
 
 _vp, _u32, _u64, _i32 = C.c_void_p, C.c_uint32, C.c_uint64, C.c_int32
+
+
+class Epilogue(C.Structure):
+    """struct tc_epilogue (include/turbocider_cuda.h)."""
+    _fields_ = [("flags", _u32), ("n_gate_rows", _u32), ("bias", _vp), ("bias_up_offset", _u64), ("gate", _vp),
+                ("ld_gate", _u64), ("seg_gate", C.POINTER(_i32)), ("residual", _vp), ("ld_residual", _u64)]
+
 
 EXPORTS = {
     # name: (restype, argtypes)
@@ -52,6 +60,9 @@ EXPORTS = {
                                  _u64, _u64, _vp]),
     "tc_cuda_qlinear": (C.c_int, [_vp, C.POINTER(_vp), _u32, C.POINTER(_i32), C.POINTER(_i32), _u32, _vp, _vp,
                                   _u64, C.c_int, C.c_int, _vp]),
+    "tc_cuda_qlinear_ex": (C.c_int, [_vp, C.POINTER(_vp), _u32, C.POINTER(_i32), C.POINTER(_i32), _u32, _vp, _vp,
+                                     _u64, C.c_int, C.c_int, C.POINTER(Epilogue), _vp]),
+    "tc_cuda_weight_upload_glu": (C.c_int, [_vp, _u32, _u64, _u64, _vp, _vp, _u64, _u64, _u64, C.POINTER(_vp)]),
     "tc_cuda_set_path": (C.c_int, [_vp, C.c_int]),
     "tc_cuda_qlinear_batched": (C.c_int, [_vp, C.POINTER(_vp), _u32, _vp, _u32, C.POINTER(_vp), C.POINTER(_u64),
                                           C.c_int, _vp]),
@@ -176,11 +187,28 @@ class Context:
 class Weight:
     """A K-quant weight resident in HBM (panel layout)."""
 
-    def __init__(self, ctx: Context, handle):
+    def __init__(self, ctx: Context, handle, glu: bool = False):
         self.ctx, self._h = ctx, handle
         t, n, k, b = _u32(), _u64(), _u64(), _u64()
         _check(lib().tc_cuda_weight_info(handle, C.byref(t), C.byref(n), C.byref(k), C.byref(b)))
         self.ggml_type, self.n, self.k, self.device_bytes = t.value, n.value, k.value, b.value
+        self.glu = glu
+        self.n_out = n.value // 2 if glu else n.value   # output columns
+
+    @classmethod
+    def upload_glu(cls, ctx: Context, ggml_type: int, f: int, k: int, gate_raw, up_raw, col_begin: int = 0,
+                   col_count: int = 0):
+        """Gate and up halves of a SwiGLU projection ([f, k] raw GGUF rows each)
+        as one interleaved weight for the fused SwiGLU epilogue."""
+        def flat(r):
+            return np.ascontiguousarray(np.frombuffer(r, dtype=np.uint8) if isinstance(r, (bytes, bytearray))
+                                        else r).view(np.uint8).reshape(-1)
+        g, u = flat(gate_raw), flat(up_raw)
+        h = _vp()
+        _check(lib().tc_cuda_weight_upload_glu(ctx.handle, ggml_type, f, k, g.ctypes.data, u.ctypes.data,
+                                               min(g.nbytes, u.nbytes), col_begin, col_count, C.byref(h)),
+               DecodeError)
+        return cls(ctx, h, glu=True)
 
     @classmethod
     def upload(cls, ctx: Context, ggml_type: int, n: int, k: int, raw, n_begin: int = 0, n_count: int = 0):
@@ -255,10 +283,25 @@ def decode(ctx: Context, ggml_type: int, source, source_rows: int, source_column
             raise DecodeError("FP16 conversion overflow")
 
 
+def _torch_dtype(out_dtype: int):
+    import torch
+    return {F32: torch.float32, F16: torch.float16, BF16: torch.bfloat16}[out_dtype]
+
+
 def qlinear(ctx: Context, weights, x, seg_offsets=None, seg_weight=None, out_dtype: int = BF16,
-            stage: int = STAGE_BF16, out=None, stream=None):
-    """Y = X * W^T through tc_cuda_qlinear.  `weights` is a Weight or a list of
-    them; seg_offsets / seg_weight describe ragged request segments along M."""
+            stage: int = STAGE_BF16, out=None, stream=None, bias=None, activation: str | None = None,
+            gate=None, residual=None, seg_gate=None, bias_up_offset: int | None = None):
+    """Y = X * W^T through tc_cuda_qlinear_ex.  `weights` is a Weight or a list
+    of them; seg_offsets / seg_weight describe ragged request segments along M.
+
+    Fused epilogue (all optional; f32 device tensors unless noted):
+      bias        [rows] (SwiGLU weight: gate biases then up biases, up at
+                  bias_up_offset, default n_out);
+      activation  "gelu_tanh" | "gelu_erf" (SwiGLU weights always apply
+                  silu(gate) * up);
+      gate, residual  y = residual + gate[seg_gate[s]] * t; gate [G, n_out]
+                  f32, residual [M, n_out] in the output dtype (may be `out`).
+    """
     import torch
     ws = weights if isinstance(weights, (list, tuple)) else [weights]
     m = x.shape[0]
@@ -269,12 +312,30 @@ def qlinear(ctx: Context, weights, x, seg_offsets=None, seg_weight=None, out_dty
     offs = (_i32 * len(seg_offsets))(*seg_offsets)
     sw = (_i32 * n_seg)(*seg_weight) if seg_weight is not None else None
     handles = (_vp * len(ws))(*[w.handle for w in ws])
-    n = ws[0].n
+    n_out = getattr(ws[0], "n_out", ws[0].n)
     if out is None:
-        out = torch.empty((m, n), dtype=torch.float32 if out_dtype == F32 else torch.bfloat16,
-                          device=x.device)
-    _check(lib().tc_cuda_qlinear(ctx.handle, handles, len(ws), offs, sw, n_seg, x.data_ptr(), out.data_ptr(),
-                                 out.stride(0), out_dtype, stage, _stream_ptr(stream)))
+        out = torch.empty((m, n_out), dtype=_torch_dtype(out_dtype), device=x.device)
+    epi = Epilogue()
+    if bias is not None:
+        epi.flags |= EPI_BIAS
+        epi.bias = bias.data_ptr()
+        epi.bias_up_offset = n_out if bias_up_offset is None else bias_up_offset
+    if activation is not None:
+        epi.flags |= {"gelu_tanh": EPI_GELU_TANH, "gelu_erf": EPI_GELU_ERF}[activation]
+    if getattr(ws[0], "glu", False):
+        epi.flags |= EPI_SWIGLU
+    if gate is not None or residual is not None:
+        epi.flags |= EPI_GATE_RESIDUAL
+        epi.gate = gate.data_ptr() if gate is not None else None
+        epi.ld_gate = gate.stride(0) if gate is not None else 0
+        epi.n_gate_rows = gate.shape[0] if gate is not None else 0
+        epi.residual = residual.data_ptr() if residual is not None else None
+        epi.ld_residual = residual.stride(0) if residual is not None else 0
+        if seg_gate is not None:
+            epi.seg_gate = (_i32 * n_seg)(*seg_gate)
+    _check(lib().tc_cuda_qlinear_ex(ctx.handle, handles, len(ws), offs, sw, n_seg, x.data_ptr(), out.data_ptr(),
+                                    out.stride(0), out_dtype, stage, C.byref(epi) if epi.flags else None,
+                                    _stream_ptr(stream)))
     return out
 
 
@@ -283,8 +344,7 @@ def qlinear_batched(ctx: Context, weights, x, out_dtype: int = BF16, outs=None, 
     rows of bf16 X, weights sharing K)."""
     import torch
     if outs is None:
-        outs = [torch.empty((x.shape[0], w.n), dtype=torch.float32 if out_dtype == F32 else torch.bfloat16,
-                            device=x.device) for w in weights]
+        outs = [torch.empty((x.shape[0], w.n), dtype=_torch_dtype(out_dtype), device=x.device) for w in weights]
     handles = (_vp * len(weights))(*[w.handle for w in weights])
     ys = (_vp * len(outs))(*[o.data_ptr() for o in outs])
     lds = (_u64 * len(outs))(*[o.stride(0) for o in outs])
@@ -298,8 +358,7 @@ def qlinear_small_static(weight: Weight, x, out_dtype: int = BF16, out=None, str
     (static device scratch instead of a context workspace)."""
     import torch
     if out is None:
-        out = torch.empty((x.shape[0], weight.n), dtype=torch.float32 if out_dtype == F32 else torch.bfloat16,
-                          device=x.device)
+        out = torch.empty((x.shape[0], weight.n), dtype=_torch_dtype(out_dtype), device=x.device)
     _check(lib().tc_cuda_qlinear_small_static(weight.handle, x.data_ptr(), x.shape[0], out.data_ptr(),
                                               out.stride(0), out_dtype, _stream_ptr(stream)))
     return out
