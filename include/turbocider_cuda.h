@@ -37,8 +37,13 @@ extern "C" {
 
 enum { TC_CUDA_OK = 0, TC_CUDA_FAIL = 1, TC_CUDA_CANCELLED = 2 };
 
-/* GGML on-disk type ids (reference native/core/gguf_directory.hpp:21-26). */
-enum { TC_GGML_Q4_K = 12, TC_GGML_Q5_K = 13, TC_GGML_Q6_K = 14 };
+/* GGML on-disk type ids (reference native/core/gguf_directory.hpp:21-26).
+ * The quantised linear takes the K-quants; tc_cuda_decode takes every
+ * registered type. */
+enum {
+    TC_GGML_F32 = 0, TC_GGML_F16 = 1, TC_GGML_Q4_0 = 2, TC_GGML_Q4_1 = 3, TC_GGML_Q5_0 = 6, TC_GGML_Q5_1 = 7,
+    TC_GGML_Q8_0 = 8, TC_GGML_Q4_K = 12, TC_GGML_Q5_K = 13, TC_GGML_Q6_K = 14, TC_GGML_BF16 = 30
+};
 
 /* Target / output dtypes; same numbering as tc::gguf::DecodeDType
  * (reference native/core/gguf_decode.hpp:18). */
@@ -59,7 +64,8 @@ enum {
     TC_STATUS_NONFINITE_SCALE = 1u << 0, /* a d/dmin master scale is inf/nan   */
     TC_STATUS_F16_OVERFLOW    = 1u << 1, /* a value does not fit fp16          */
     TC_STATUS_TIMEOUT         = 1u << 2, /* a bounded pipeline wait gave up    */
-    TC_STATUS_GEOMETRY        = 1u << 3  /* a kernel saw an impossible tile    */
+    TC_STATUS_GEOMETRY        = 1u << 3, /* a kernel saw an impossible tile    */
+    TC_STATUS_BF16_OVERFLOW   = 1u << 4  /* a value rounds past the bf16 range */
 };
 
 typedef struct tc_cuda_ctx tc_cuda_ctx;
@@ -147,10 +153,12 @@ int tc_cuda_dequant(tc_cuda_ctx *ctx, const tc_cuda_weight *weight, int dtype, v
 
 /* Device mirror of decode_cpu_into (gguf_decode.cpp:433-445 and the probe ABI
  * tc_gguf_test_decode, gguf_core_probe.cpp:32-50): decode the slice
- * [row_begin, +rows) x [column_begin, +columns) of a raw GGUF K-quant matrix
- * in device memory into a strided device target (byte strides).  Geometry is
- * validated on the host with the reference's rules and messages; value
- * errors (nonfinite scale, fp16 overflow) are reported in the status word. */
+ * [row_begin, +rows) x [column_begin, +columns) of a raw GGUF matrix of any
+ * registered type (F32, F16, BF16, Q4_0, Q4_1, Q5_0, Q5_1, Q8_0, Q4_K, Q5_K,
+ * Q6_K) in device memory into a strided device target (byte strides, no
+ * alignment needed).  Geometry is validated on the host with the reference's
+ * rules and messages; value errors (nonfinite input or scale, fp16 / bf16
+ * overflow) are reported in the status word. */
 int tc_cuda_decode(tc_cuda_ctx *ctx, uint32_t ggml_type, const void *source, uint64_t source_bytes,
                    uint64_t source_rows, uint64_t source_columns, uint64_t row_begin,
                    uint64_t rows, uint64_t column_begin, uint64_t columns, int dtype,

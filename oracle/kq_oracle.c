@@ -112,9 +112,44 @@ static void q4k_scale_min(unsigned g, const uint8_t *s, unsigned *sc, unsigned *
     }
 }
 
-/* One super-block to 256 fp32 values: Q4_K/Q5_K gguf_decode.cpp:77-90,
- * Q6_K gguf_decode.cpp:91-105.  Returns nonzero on a nonfinite master scale. */
+static uint32_t rd32(const uint8_t *p) {
+    return (uint32_t)p[0] | ((uint32_t)p[1] << 8) | ((uint32_t)p[2] << 16) | ((uint32_t)p[3] << 24);
+}
+
+/* One block to fp32 values.  F32 / F16 / BF16 single elements:
+ * gguf_decode.cpp:56-58; Q4_0 / Q4_1 / Q5_0 / Q5_1 / Q8_0 (32 weights):
+ * :59-76; Q4_K / Q5_K super-blocks: :77-90; Q6_K: :91-105.  Every value must
+ * be finite (:110).  Returns nonzero (with the reference's message) otherwise. */
 int kq_decode_block(uint32_t type, const uint8_t *p, float *out) {
+    static const char *nonfinite = "nonfinite weight/scale or conversion overflow";
+    if (type == 0 || type == 1 || type == 30) {
+        out[0] = type == 0 ? bits_f32(rd32(p)) : type == 1 ? kq_half_to_float(rd16(p))
+                                                            : bits_f32((uint32_t)rd16(p) << 16);
+        return isfinite(out[0]) ? 0 : fail(nonfinite);
+    }
+    if (type == 2 || type == 3 || type == 6 || type == 7 || type == 8) {
+        const float d = kq_half_to_float(rd16(p));
+        if (!isfinite(d)) return fail(nonfinite);
+        if (type == 8) {
+            for (unsigned i = 0; i < 32; ++i) out[i] = (float)(int8_t)p[2 + i] * d;
+            return 0;
+        }
+        const int affine = type == 3 || type == 7, five = type == 6 || type == 7;
+        const float mn = affine ? kq_half_to_float(rd16(p + 2)) : 0.f;
+        if (!isfinite(mn)) return fail(nonfinite);
+        const unsigned off = affine ? 4 : 2;
+        const uint32_t high = five ? rd32(p + off) : 0;
+        const uint8_t *low = p + off + (five ? 4 : 0);
+        const int bias = affine ? 0 : five ? 16 : 8;
+        for (unsigned i = 0; i < 16; ++i) {
+            const int a = (int)((low[i] & 15u) | (((high >> i) & 1u) << 4)) - bias;
+            const int b = (int)((low[i] >> 4) | (((high >> (i + 16)) & 1u) << 4)) - bias;
+            const float pa = (float)a * d, pb = (float)b * d; /* separate rounding */
+            out[i] = affine ? pa + mn : pa;
+            out[i + 16] = affine ? pb + mn : pb;
+        }
+        return 0;
+    }
     if (type == 12 || type == 13) {
         const float d = kq_half_to_float(rd16(p)), dmin = kq_half_to_float(rd16(p + 2));
         if (!isfinite(d) || !isfinite(dmin)) return fail("nonfinite weight/scale or conversion overflow");
@@ -164,13 +199,13 @@ static int write_value(uint8_t *dst, uint32_t dtype, float v) {
 
 /* Slice decode into a strided target with the reference's geometry checks:
  * decode_cpu_into gguf_decode.cpp:433-445, validate :160-183, row_into :320-367.
- * Only the K-quant block types are restated (the hot path); returns 0 or 1. */
+ * Every registered type is restated; returns 0 or 1. */
 int kq_decode(uint32_t type, const void *source, uint64_t source_bytes, uint64_t rows,
               uint64_t columns, uint64_t row_begin, uint64_t nrows, uint64_t column_begin,
               uint64_t ncolumns, uint32_t dtype, void *target, uint64_t target_bytes,
               uint64_t row_stride, uint64_t column_stride) {
     uint32_t elements, block_bytes;
-    if (kq_type_geometry(type, &elements, &block_bytes) || elements != 256)
+    if (kq_type_geometry(type, &elements, &block_bytes))
         return fail("gguf_decode: unsupported tensor type");
     if (!source || !target) return fail("null source/target storage");
     if (row_begin > rows || nrows > rows - row_begin) return fail("row slice out of bounds");
@@ -188,6 +223,22 @@ int kq_decode(uint32_t type, const void *source, uint64_t source_bytes, uint64_t
     const uint8_t *src = (const uint8_t *)source;
     uint8_t *dst = (uint8_t *)target;
     float scratch[256];
+    /* Same floating type as the target, written contiguously: a checked byte
+     * copy (row_into's copy_finite branch, gguf_decode.cpp:325-330, :136-158). */
+    const int identical = (type == 0 && dtype == KQ_F32) || (type == 1 && dtype == KQ_F16) ||
+                          (type == 30 && dtype == KQ_BF16);
+    if (identical && column_stride == block_bytes) {
+        const uint32_t mask = type == 0 ? 0x7f800000u : type == 1 ? 0x7c00u : 0x7f80u;
+        for (uint64_t r = 0; r < nrows; ++r)
+            for (uint64_t c = 0; c < ncolumns; ++c) {
+                const uint8_t *p = src + (row_begin + r) * row_bytes + (column_begin + c) * block_bytes;
+                const uint32_t bits = block_bytes == 4 ? rd32(p) : rd16(p);
+                if ((bits & mask) == mask) return fail("nonfinite source float");
+                memcpy(dst + r * row_stride + c * block_bytes, p, block_bytes);
+            }
+        kq_error[0] = 0;
+        return 0;
+    }
     for (uint64_t r = 0; r < nrows; ++r) {
         const uint64_t first = column_begin / elements, last = (column_begin + ncolumns - 1) / elements;
         for (uint64_t b = first; b <= last; ++b) {

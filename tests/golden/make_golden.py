@@ -95,6 +95,10 @@ def main():
             raw = kq_cases.extreme_case(typ, scale)
             cases["extreme"][f"{typ}/{scale!r}"] = [both(raw, typ, 2, 1024, dt) for dt in (0, 1, 2)]
 
+    cases["passthrough"] = {}
+    for name, typ, raw, rows, cols in kq_cases.passthrough_cases():
+        cases["passthrough"][name] = [both(raw, typ, rows, cols, dt) for dt in (0, 1, 2)]
+
     cases["nonfinite"] = {}
     for typ in kq_cases.K_TYPES:
         for bits, where in ((0x7C00, "d"), (0x7E00, "d"), (0x7C00, "dmin")):

@@ -47,25 +47,25 @@ def random_block(typ: int, rng: random.Random) -> bytes:
 
 
 def seed6409_cases():
-    """Yield (typ, trial, raw, rows, cols) for the K types of the seed-6409 set."""
+    """Yield (typ, trial, raw, rows, cols) for the block types of the seed-6409
+    set (Q4_0, Q4_1, Q5_0, Q5_1, Q8_0 and the K-quants)."""
     rng = random.Random(6409)
     for typ in (2, 3, 6, 7, 8, 12, 13, 14):
         elements, _ = TYPES[typ]
         for trial in range(32):
             raw = b"".join(random_block(typ, rng) for _ in range(12))
-            if typ in K_TYPES:
-                yield typ, trial, raw, 3, elements * 4
+            yield typ, trial, raw, 3, elements * 4
 
 
 def seed20260930_cases():
-    """Yield (typ, raw, rows, cols, slices) for the K types of the slice set."""
+    """Yield (typ, raw, rows, cols, slices) for every registered type of the
+    slice set (the floating-point types with 33 columns)."""
     rng = random.Random(20260930)
     for typ, (elements, _) in TYPES.items():
         columns = max(elements * 3, 33 if elements == 1 else elements * 3)
         raw = b"".join(random_block(typ, rng) for _ in range(3 * columns // elements))
-        if typ in K_TYPES:
-            slices = [(0, columns), (1, columns - 2), (elements - 1, min(elements + 2, columns - elements + 1))]
-            yield typ, raw, 3, columns, slices
+        slices = [(0, columns), (1, columns - 2), (elements - 1, min(elements + 2, columns - elements + 1))]
+        yield typ, raw, 3, columns, slices
 
 
 def f16_bits(value: float) -> int:
@@ -105,6 +105,38 @@ def extreme_case(typ: int, scale: float) -> bytes:
             p[2:4] = struct.pack("<H", f16_bits(-0.015625))
         out += p
     return bytes(out)
+
+
+def passthrough_cases():
+    """Yield (name, typ, raw, rows, cols) for the non-K types' value rules
+    (gguf_decode.cpp:56-76, 110 and the converters :389-405): nonfinite
+    inputs and scales, fp16 / bf16 overflow, subnormals and signed zeros."""
+    f32 = lambda *v: struct.pack(f"<{len(v)}f", *v)
+    f16 = lambda *v: struct.pack(f"<{len(v)}H", *v)
+    big = struct.unpack("<f", struct.pack("<I", 0x7F7FFFFF))[0]
+    yield "f32_inf", 0, f32(1.0, float("inf"), 2.0, 3.0), 1, 4
+    yield "f32_nan", 0, f32(0.5, -1.0, float("nan"), 3.0), 2, 2
+    yield "f32_max", 0, f32(big, -big, 1.0, 65504.0), 1, 4
+    yield "f32_f16_edge", 0, f32(65519.99, 65520.0, 2 ** -25, -2 ** -24), 1, 4
+    yield "f32_subnormal_zero", 0, f32(1e-40, -0.0, 2 ** -133, 7.0), 2, 2
+    yield "f16_inf", 1, f16(0x3C00, 0x7C00), 1, 2
+    yield "f16_subnormal", 1, f16(0x0001, 0x8000, 0x7BFF, 0x03FF), 2, 2
+    yield "bf16_nan", 30, f16(0x3F80, 0x7FC0), 1, 2
+    yield "bf16_max", 30, f16(0x7F7F, 0xFF7F, 0x0001, 0x477F), 1, 4
+    for typ in (2, 3, 6, 7, 8):
+        _, size = TYPES[typ]
+        for name, off, bits in (("d_inf", 0, 0x7C00), ("d_nan", 0, 0x7E00), ("m_inf", 2, 0x7C00)):
+            if name == "m_inf" and typ not in (3, 7):
+                continue
+            blk = bytearray(((i * 29 + typ) & 255) for i in range(size))
+            blk[0:2] = struct.pack("<H", 0x3C00)
+            blk[off:off + 2] = struct.pack("<H", bits)
+            yield f"{typ}_{name}", typ, bytes(blk) * 2, 2, 32
+        blk = bytearray(((i * 53 + 7 * typ) & 255) for i in range(size))
+        blk[0:2] = struct.pack("<H", 0x7BFF)   # d = 65504: products overflow fp16
+        if typ in (3, 7):
+            blk[2:4] = struct.pack("<H", 0xFBFF)
+        yield f"{typ}_d_max", typ, bytes(blk), 1, 32
 
 
 def synthetic_weight(n: int, k: int, seed: int = 0, std: float = 0.02) -> np.ndarray:

@@ -1,8 +1,9 @@
 """GPU parity of the dequantisers through the C ABI: bit-exact against the
 reference decoder (golden digests) and the oracle port.
 
-* tc_cuda_decode (raw GGUF layout, strided slices) reproduces every golden
-  case, including the reference's errors (nonfinite scale, fp16 overflow);
+* tc_cuda_decode (raw GGUF layout, strided slices, every registered type)
+  reproduces every golden case, including the reference's errors (nonfinite
+  input or scale, fp16 / bf16 overflow);
 * tc_cuda_weight_upload + tc_cuda_dequant (panel layout) is bit-exact for
   every dtype, N not a multiple of the 128-row panel, and sharded uploads.
 """
@@ -68,6 +69,16 @@ def test_decode_slices_and_strides_bit_exact(ctx, golden):
             for dt in (0, 1, 2):
                 got = _gpu_decode(ctx, raw, typ, rows, cols, dt, col_begin=b, ncols=n, column_stride=8)
                 assert got == g[str(typ)][i][dt], (typ, b, n, dt)
+
+
+def test_decode_passthrough_types(ctx, golden):
+    """F32 / F16 / BF16 and Q4_0 / Q4_1 / Q5_0 / Q5_1 / Q8_0 value rules:
+    nonfinite inputs and scales, fp16 / bf16 overflow, subnormals."""
+    g = golden["cases"]["passthrough"]
+    for name, typ, raw, rows, cols in kq_cases.passthrough_cases():
+        for dt in (0, 1, 2):
+            assert _gpu_decode(ctx, raw, typ, rows, cols, dt) == g[name][dt], (name, dt)
+    assert ctx.status() == 0
 
 
 def test_decode_pattern_extreme_nonfinite(ctx, golden):

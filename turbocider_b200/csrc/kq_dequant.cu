@@ -10,7 +10,7 @@
 namespace tc {
 namespace {
 
-enum : uint32_t { kNonfinite = 1u << 0, kF16Overflow = 1u << 1 };
+enum : uint32_t { kNonfinite = 1u << 0, kF16Overflow = 1u << 1, kBf16Overflow = 1u << 4 };
 
 __device__ __forceinline__ uint16_t ld16(const uint8_t *p) { return (uint16_t)(p[0] | (p[1] << 8)); }
 
@@ -89,6 +89,52 @@ __device__ __forceinline__ void store_value(uint8_t *p, float v, bool &ovf) {
     if (DT == 0) *reinterpret_cast<float *>(p) = v;
     else if (DT == 1) *reinterpret_cast<uint16_t *>(p) = to_f16_bits(v, ovf);
     else *reinterpret_cast<uint16_t *>(p) = to_bf16_bits(v);
+}
+// Byte-addressed store (strided targets of the raw decode need not be
+// aligned to the item size) with fp16 / bf16 overflow detection.
+template <int DT>
+__device__ __forceinline__ void store_value_bytes(uint8_t *p, float v, bool &f16_ovf, bool &bf16_ovf) {
+    uint32_t bits, n;
+    if (DT == 0) { bits = __float_as_uint(v); n = 4; }
+    else if (DT == 1) { bits = to_f16_bits(v, f16_ovf); n = 2; }
+    else { bits = to_bf16_bits(v, bf16_ovf); n = 2; }
+    for (uint32_t i = 0; i < n; ++i) p[i] = (uint8_t)(bits >> (8 * i));
+}
+__device__ __forceinline__ uint32_t ld32b(const uint8_t *p) {
+    return (uint32_t)p[0] | ((uint32_t)p[1] << 8) | ((uint32_t)p[2] << 16) | ((uint32_t)p[3] << 24);
+}
+
+// The 32 weights of one Q4_0 / Q4_1 / Q5_0 / Q5_1 / Q8_0 block
+// (gguf_decode.cpp:59-76): d (and the affine types' minimum) fp16, codes of
+// 4, 5 (fifth bits in a 32-bit word) or 8 bits.  The affine types round the
+// product and the sum separately, as the reference does.
+__device__ __forceinline__ void legacy_block(uint32_t type, const uint8_t *p, float v[32], bool &bad) {
+    const uint16_t dh = ld16(p);
+    const float d = half_bits_to_float(dh);
+    bad |= !half_bits_finite(dh);
+    if (type == 8) {
+#pragma unroll
+        for (int i = 0; i < 32; ++i) v[i] = __fmul_rn((float)(int8_t)p[2 + i], d);
+        return;
+    }
+    const bool affine = type == 3 || type == 7, five = type == 6 || type == 7;
+    float mn = 0.f;
+    if (affine) {
+        const uint16_t mh = ld16(p + 2);
+        mn = half_bits_to_float(mh);
+        bad |= !half_bits_finite(mh);
+    }
+    const uint32_t off = affine ? 4 : 2;
+    const uint32_t high = five ? ld32b(p + off) : 0u;
+    const uint8_t *low = p + off + (five ? 4 : 0);
+    const int bias = affine ? 0 : five ? 16 : 8;
+#pragma unroll
+    for (int i = 0; i < 16; ++i) {
+        const int a = (int)((low[i] & 15u) | (((high >> i) & 1u) << 4)) - bias;
+        const int b = (int)((low[i] >> 4) | (((high >> (i + 16)) & 1u) << 4)) - bias;
+        v[i] = affine ? __fadd_rn(__fmul_rn((float)a, d), mn) : __fmul_rn((float)a, d);
+        v[i + 16] = affine ? __fadd_rn(__fmul_rn((float)b, d), mn) : __fmul_rn((float)b, d);
+    }
 }
 
 // Decode the 32 weights of group G (0..7) of one super-block whose fields are
@@ -180,11 +226,41 @@ __global__ void decode_raw_kernel(uint32_t type, const uint8_t *__restrict__ src
     if (idx >= rows * groups) return;
     const uint64_t r = idx / groups;
     const uint64_t gid = first_group + idx % groups;   // global 32-group index in the row
+    const uint8_t *row = src + (row_begin + r) * row_bytes;
+    float v[32];
+    bool bad = false, ovf = false, bovf = false;
+    const uint64_t c0 = gid * 32;
+    if (type_elements(type) == 1) {
+        // F32 / F16 / BF16 (gguf_decode.cpp:56-58): every element is its own
+        // block; only the elements inside the slice are read and checked.
+        for (int j = 0; j < 32; ++j) {
+            const uint64_t c = c0 + j;
+            if (c < column_begin || c >= column_begin + columns) continue;
+            float x;
+            bool fin;
+            if (type == 0) {
+                const uint32_t b = ld32b(row + c * 4);
+                x = __uint_as_float(b);
+                fin = (b & 0x7f800000u) != 0x7f800000u;
+            } else {
+                const uint16_t h = ld16(row + c * 2);
+                x = type == 1 ? half_bits_to_float(h) : __uint_as_float((uint32_t)h << 16);
+                fin = type == 1 ? half_bits_finite(h) : (h & 0x7f80u) != 0x7f80u;
+            }
+            if (!fin) { bad = true; continue; }
+            store_value_bytes<DT>(dst + r * row_stride + (c - column_begin) * column_stride, x, ovf, bovf);
+        }
+        if (bad) atomicOr(status, kNonfinite);
+        if (ovf) atomicOr(status, kF16Overflow);
+        if (bovf) atomicOr(status, kBf16Overflow);
+        return;
+    }
+    if (type_elements(type) == 32) {
+        legacy_block(type, row + gid * type_bytes(type), v, bad);
+    } else {
     const uint64_t block = gid / 8;
     const uint32_t G = (uint32_t)(gid % 8);
-    const uint8_t *p = src + (row_begin + r) * row_bytes + block * block_bytes(type);
-    float v[32];
-    bool bad = false, ovf = false;
+    const uint8_t *p = row + block * block_bytes(type);
     if (type == 12) {
         Q4Fields f{p + 16 + (G / 2) * 32, p + 4, ld16(p), ld16(p + 2)};
         q4k_group(f, G, v, bad);
@@ -196,15 +272,16 @@ __global__ void decode_raw_kernel(uint32_t type, const uint8_t *__restrict__ src
         Q6Fields f{p + 64 * h + 32 * (g & 1), p + 128 + 32 * h, p + 192, ld16(p + 208)};
         q6k_group(f, h, g, v, bad);
     }
-    const uint64_t c0 = gid * 32;
+    }
 #pragma unroll 4
     for (int j = 0; j < 32; ++j) {
         const uint64_t c = c0 + j;
         if (c < column_begin || c >= column_begin + columns) continue;
-        store_value<DT>(dst + r * row_stride + (c - column_begin) * column_stride, v[j], ovf);
+        store_value_bytes<DT>(dst + r * row_stride + (c - column_begin) * column_stride, v[j], ovf, bovf);
     }
     if (bad) atomicOr(status, kNonfinite);
     if (ovf) atomicOr(status, kF16Overflow);
+    if (bovf) atomicOr(status, kBf16Overflow);
 }
 
 // ---------------------------------------------------- bf16 -> fp16 (staging)
@@ -257,9 +334,12 @@ cudaError_t launch_decode_raw(uint32_t type, const uint8_t *src, uint64_t row_by
                               uint64_t columns, int dtype, uint8_t *dst, uint64_t row_stride,
                               uint64_t column_stride, uint32_t *status, cudaStream_t s) {
     // Every block touched by the column range is decoded (and checked), as in
-    // the reference's row_into (gguf_decode.cpp:340-364).
-    const uint64_t first_block = column_begin / 256, last_block = (column_begin + columns - 1) / 256;
-    const uint64_t first_group = first_block * 8, groups = (last_block - first_block + 1) * 8;
+    // the reference's row_into (gguf_decode.cpp:340-364); threads work on
+    // 32-weight groups (an eighth of a K-quant super-block, one legacy block,
+    // or 32 floating-point elements).
+    const uint64_t el = type_elements(type) == 256 ? 256 : 32;
+    const uint64_t first_block = column_begin / el, last_block = (column_begin + columns - 1) / el;
+    const uint64_t first_group = first_block * (el / 32), groups = (last_block - first_block + 1) * (el / 32);
     const uint64_t total = rows * groups;
     const unsigned g = blocks_for(total, 128);
     if (dtype == 0)

@@ -64,6 +64,18 @@ __host__ __device__ constexpr uint32_t row_slot(uint32_t r) {
     return (r & ~3u) | ((r + 2u * ((r >> 2) & 1u)) & 3u);
 }
 
+// Block geometry of every GGML type the reference registers
+// (native/core/gguf_directory.hpp:21-26): weights per block, bytes per block.
+__host__ __device__ constexpr uint32_t type_elements(uint32_t t) {
+    return (t == 0 || t == 1 || t == 30) ? 1u
+           : (t == 2 || t == 3 || t == 6 || t == 7 || t == 8) ? 32u
+           : (t == 12 || t == 13 || t == 14) ? 256u : 0u;
+}
+__host__ __device__ constexpr uint32_t type_bytes(uint32_t t) {
+    return t == 0 ? 4u : (t == 1 || t == 30) ? 2u : t == 2 ? 18u : t == 3 ? 20u : t == 6 ? 22u : t == 7 ? 24u
+           : t == 8 ? 34u : t == 12 ? 144u : t == 13 ? 176u : t == 14 ? 210u : 0u;
+}
+
 __host__ __device__ constexpr uint32_t block_bytes(uint32_t type) {
     return type == 12 ? kQ4KBytes : type == 14 ? kQ6KBytes : type == 13 ? kQ5KBytes : 0u;
 }
@@ -111,6 +123,13 @@ __device__ __forceinline__ float q4k_value(float dg, float mg, uint32_t q) {
 // reported by the caller (the reference rejects |v| that rounds past 65504).
 __device__ __forceinline__ uint16_t to_bf16_bits(float v) {
     return __bfloat16_as_ushort(__float2bfloat16_rn(v));
+}
+// bf16 conversion with the reference's overflow rejection (a finite value
+// that rounds to infinity: float_to_bf16_rne, gguf_decode.cpp:389-394).
+__device__ __forceinline__ uint16_t to_bf16_bits(float v, bool &overflow) {
+    const uint16_t h = __bfloat16_as_ushort(__float2bfloat16_rn(v));
+    overflow |= (h & 0x7f80u) == 0x7f80u;
+    return h;
 }
 __device__ __forceinline__ uint16_t to_f16_bits(float v, bool &overflow) {
     const uint16_t h = __half_as_ushort(__float2half_rn(v));

@@ -291,12 +291,13 @@ int tc_cuda_decode(tc_cuda_ctx *ctx, uint32_t type, const void *source, uint64_t
                    uint64_t column_stride, void *stream) {
     if (!ctx) return fail("null context");
     if (row_begin > source_rows || rows > source_rows - row_begin) return fail("row slice out of bounds");
-    if (!supported_type(type) && type != TC_GGML_Q5_K) return fail("gguf_decode: unsupported tensor type");
+    const uint32_t elements = tc::type_elements(type);
+    if (!elements) return fail("gguf_decode: unsupported tensor type");
     if (!source || !target) return fail("null source/target storage");
-    if (!source_rows || !source_columns || source_columns % tc::kBlockWeights) return fail("invalid source geometry");
+    if (!source_rows || !source_columns || source_columns % elements) return fail("invalid source geometry");
     if (!rows || !columns || column_begin > source_columns || columns > source_columns - column_begin)
         return fail("invalid decode slice");
-    const uint64_t row_bytes = source_columns / tc::kBlockWeights * tc::block_bytes(type);
+    const uint64_t row_bytes = source_columns / elements * tc::type_bytes(type);
     if (source_rows > UINT64_MAX / row_bytes) return fail("gguf_decode: multiplication overflow");
     if (source_rows * row_bytes > source_bytes) return fail("packed source too short");
     if (dtype < 0 || dtype > 2) return fail("gguf_decode: invalid target dtype");

@@ -19,7 +19,7 @@ LIB_PATH = Path(__file__).resolve().parent / "libturbocider_cuda.so"
 Q4_K, Q5_K, Q6_K = 12, 13, 14
 F32, F16, BF16 = 0, 1, 2
 STAGE_BF16, STAGE_F16, STAGE_F16_X16 = 0, 1, 2
-STATUS_NONFINITE_SCALE, STATUS_F16_OVERFLOW, STATUS_TIMEOUT, STATUS_GEOMETRY = 1, 2, 4, 8
+STATUS_NONFINITE_SCALE, STATUS_F16_OVERFLOW, STATUS_TIMEOUT, STATUS_GEOMETRY, STATUS_BF16_OVERFLOW = 1, 2, 4, 8, 16
 EPI_BIAS, EPI_GELU_TANH, EPI_GELU_ERF, EPI_SWIGLU, EPI_GATE_RESIDUAL = 1, 2, 4, 8, 16
 BLOCK_BYTES = {Q4_K: 144, Q5_K: 176, Q6_K: 210}
 
@@ -278,9 +278,17 @@ def decode(ctx: Context, ggml_type: int, source, source_rows: int, source_column
     if check:
         bits = ctx.status(clear=True)
         if bits & STATUS_NONFINITE_SCALE:
+            # The reference's checked copy (same floating type as the target,
+            # contiguous columns) words this error differently from its
+            # decoder (gguf_decode.cpp:136-158 vs :43).
+            same = (ggml_type, dtype) in ((0, F32), (1, F16), (30, BF16))
+            if same and column_stride == (4 if dtype == F32 else 2):
+                raise DecodeError("nonfinite source float")
             raise DecodeError("nonfinite weight/scale or conversion overflow")
         if bits & STATUS_F16_OVERFLOW:
             raise DecodeError("FP16 conversion overflow")
+        if bits & STATUS_BF16_OVERFLOW:
+            raise DecodeError("BF16 conversion overflow")
 
 
 def _torch_dtype(out_dtype: int):
