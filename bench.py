@@ -385,10 +385,26 @@ def run_ours(args):
     names = [l[0] for l in layer_linears(0)]
     from turbocider_b200 import shard
     nloc = {name: shard.rows_per_rank(n, world) for name, n, _, _ in layer_linears(0)}
-    # double-buffered local outputs and gathered outputs per linear
-    y_loc = {(name, b): torch.empty(m, nloc[name], device=device, dtype=torch.bfloat16) for name in names for b in (0, 1)}
-    y_all = ({(name, b): torch.empty(world * m, nloc[name], device=device, dtype=torch.bfloat16)
-              for name in names for b in (0, 1)} if world > 1 else {})
+    fused = world > 1 and args.gather == "fused"
+    pg = None
+    if fused:
+        # All-gather fused into the GEMM epilogue: every rank's Y[M, g * N/g]
+        # lives in a buffer all ranks can store into (CUDA IPC); each GEMM
+        # writes its column shard into all of them over NVLink, then a device
+        # flag barrier marks every Y complete (turbocider_b200.peer).
+        from turbocider_b200.peer import PeerGroup
+        pg = PeerGroup(ctx, timeout_us=20_000_000)
+        y_sym = {(name, b): pg.alloc(m * world * nloc[name] * 2) for name in names for b in (0, 1)}
+        y_all = {key: buf.tensor((m, world * nloc[key[0]]), torch.bfloat16) for key, buf in y_sym.items()}
+        y_loc = {key: y_all[key][:, rank * nloc[key[0]]:rank * nloc[key[0]] + weights[0][key[0]].n]
+                 for key in y_all}
+        y_peers = {key: pg.peers_of(buf, rank * nloc[key[0]] * 2) for key, buf in y_sym.items()}
+    else:
+        # double-buffered local outputs and gathered outputs per linear
+        y_loc = {(name, b): torch.empty(m, nloc[name], device=device, dtype=torch.bfloat16)
+                 for name in names for b in (0, 1)}
+        y_all = ({(name, b): torch.empty(world * m, nloc[name], device=device, dtype=torch.bfloat16)
+                  for name in names for b in (0, 1)} if world > 1 else {})
     gathered = {(name, b): None for name in names for b in (0, 1)}
 
     def one_step(timing=None):
@@ -396,18 +412,20 @@ def run_ours(args):
             b = layer & 1
             for name in names:
                 x = x_f if name == "w2" else x_h
-                if world > 1 and gathered[(name, b)] is not None:
+                if world > 1 and not fused and gathered[(name, b)] is not None:
                     compute.wait_event(gathered[(name, b)])     # buffer reuse after its gather
                 if timing is not None:
                     e0 = torch.cuda.Event(enable_timing=True)
                     e0.record(compute)
                 tcc.qlinear(ctx, weights[layer][name], x, out=y_loc[(name, b)], stage=tcc.STAGE_F16_X16,
-                            stream=compute)
+                            stream=compute, peers=y_peers[(name, b)] if fused else None)
                 if timing is not None:
                     e1 = torch.cuda.Event(enable_timing=True)
                     e1.record(compute)
                     timing.append((e0, e1, 2.0 * m * weights[layer][name].n * weights[layer][name].k))
-                if world > 1:
+                if fused:
+                    pg.barrier(compute)
+                elif world > 1:
                     done = torch.cuda.Event()
                     done.record(compute)
                     comm.wait_event(done)
@@ -416,7 +434,7 @@ def run_ours(args):
                     ev = torch.cuda.Event()
                     ev.record(comm)
                     gathered[(name, b)] = ev
-        if world > 1:
+        if world > 1 and not fused:
             compute.wait_stream(comm)
 
     def barrier():
@@ -514,13 +532,15 @@ def run_ours(args):
                 "config": {"workload": "config5_zimage_6b_linear_stack", "layers": layers, "m_tokens": m,
                            "operands": "X fp16, W dequantised to fp16 in TMEM, fp32 accumulate, bf16 Y",
                            "hidden": HIDDEN, "ffn": FFN, "mix": "Q4_K_M (w2 Q6_K in even layers)",
-                           "parallelism": (f"N-shard x{world} + NCCL all-gather"
-                                           + (f" ({reserve} SMs left to it)" if reserve else "")
-                                           if world > 1 else "single GPU"),
+                           "parallelism": ("single GPU" if world == 1 else
+                                           f"N-shard x{world}, all-gather fused into the GEMM epilogue (NVLink "
+                                           f"peer stores) + device flag barrier per linear" if fused else
+                                           f"N-shard x{world} + NCCL all-gather"
+                                           + (f" ({reserve} SMs left to it)" if reserve else "")),
                            "l2": "inputs larger than L2 (3 GB of packed weights streamed per step)",
                            "weights": f"{layers} distinct HBM buffers per tensor, contents cycle over "
                                       f"{DISTINCT_LAYERS} seeds"},
-                "gpu_launches": len(timing) * args.steps,
+                "gpu_launches": len(timing) * args.steps * (2 if fused else 1),
                 "roofline": {"bound": "tensor", "achieved": round(achieved, 2), "peak": peak, "unit": "TFLOP/s",
                              "frac": round(achieved / peak, 4), "traffic": traffic,
                              "kernel": "pair_gemm_kernel (tcgen05 cta_group::2, A in TMEM)", "peak_source": f"{peak_src} sustained"},
@@ -537,6 +557,9 @@ def run_ours(args):
     for lw in weights:
         for wt in lw.values():
             wt.free()
+    if pg is not None:
+        del y_loc, y_all
+        pg.close()
     ctx.close()
     if world > 1:
         dist.barrier()
@@ -554,6 +577,8 @@ def main():
     ap.add_argument("--cpu-rows", type=int, default=None,
                     help="rows of X in the CPU sample (default: 2048 per reference-arm step, all rows for cpu_baseline)")
     ap.add_argument("--no-extras", action="store_true", help="skip the GEMV and CPU-baseline legs")
+    ap.add_argument("--gather", choices=["fused", "nccl"], default="fused",
+                    help="N>1: all-gather fused into the GEMM epilogue (peer stores) or NCCL after each GEMM")
     ap.add_argument("--reserve-sms", type=int, default=None,
                     help="SMs kept free of the GEMM for the all-gather (default 0: measured no gain at N=2)")
     args = ap.parse_args()

@@ -233,6 +233,38 @@ int tc_cuda_qlinear_ex(tc_cuda_ctx *ctx, const tc_cuda_weight *const *weights, u
                        const void *x, void *y, uint64_t ldy, int out_dtype, int stage,
                        const tc_epilogue *epilogue, void *stream);
 
+/* ------------------------------------------------ multi-GPU: fused all-gather
+ * N-column sharding over the GPUs of one box (one process per GPU): rank r
+ * holds output columns [c_r, c_r + n_r) of every weight (tc_cuda_weight_upload
+ * with n_begin / n_count) and every rank needs the full Y[M, N].  Instead of
+ * a separate all-gather after each linear, tc_cuda_qlinear_gather writes each
+ * output element into this rank's Y and into every peer's replica of Y over
+ * NVLink, from the GEMM's epilogue, tile by tile:
+ *   y       this rank's columns of its own Y: full_Y + c_r, row stride ldy = N;
+ *   peer_y  the same columns of the other ranks' Y buffers, as mapped in this
+ *           process (tc_cuda_peer_open), n_peer <= 7.
+ * All destinations must have identical layout.  Afterwards
+ * tc_cuda_peer_barrier(epoch) on every rank makes every rank wait (on its
+ * stream) until all ranks have finished: then every Y is complete.
+ *
+ * Buffers reachable from peers come from tc_cuda_peer_alloc (device memory
+ * plus a 64-byte CUDA IPC handle to send to the other ranks, e.g. through
+ * torch.distributed) and tc_cuda_peer_open (map another rank's handle).
+ * tc_cuda_peer_barrier: flags[r] = rank r's flag array (n_ranks uint32, zeroed,
+ * from tc_cuda_peer_alloc; flags[rank] the local one); epoch = 1, 2, ... per
+ * call; waits at most timeout_us (0: one second) and then sets
+ * TC_STATUS_TIMEOUT instead of hanging. */
+int tc_cuda_qlinear_gather(tc_cuda_ctx *ctx, const tc_cuda_weight *const *weights, uint32_t n_weights,
+                           const int32_t *seg_offsets, const int32_t *seg_weight, uint32_t n_seg,
+                           const void *x, void *y, uint64_t ldy, int out_dtype, int stage,
+                           const tc_epilogue *epilogue, void *const *peer_y, uint32_t n_peer, void *stream);
+int tc_cuda_peer_alloc(tc_cuda_ctx *ctx, uint64_t bytes, void **ptr, void *ipc_handle_64b);
+int tc_cuda_peer_open(tc_cuda_ctx *ctx, const void *ipc_handle_64b, void **ptr);
+int tc_cuda_peer_close(tc_cuda_ctx *ctx, void *ptr);
+int tc_cuda_peer_free(tc_cuda_ctx *ctx, void *ptr);
+int tc_cuda_peer_barrier(tc_cuda_ctx *ctx, uint32_t *const *flags, uint32_t n_ranks, uint32_t rank,
+                         uint32_t epoch, uint32_t timeout_us, void *stream);
+
 /* Batched small-M linear: Y_i[m, N_i] = X[m, K] * W_i^T for n_weights
  * (1..64) weights that share K and X (e.g. every block's AdaLN modulation
  * linear, which all take the timestep embedding), m = 1..16 rows of bf16 X.

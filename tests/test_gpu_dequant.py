@@ -71,6 +71,18 @@ def test_decode_slices_and_strides_bit_exact(ctx, golden):
                 assert got == g[str(typ)][i][dt], (typ, b, n, dt)
 
 
+def test_decode_unaligned_strides(ctx, golden):
+    """Odd column strides (targets not aligned to the item size) for every
+    registered type: byte-wise stores, same values as the golden digests."""
+    g = golden["cases"]["seed20260930"]
+    for typ, raw, rows, cols, slices in kq_cases.seed20260930_cases():
+        for i, (b, n) in enumerate(slices):
+            for dt in (0, 1, 2):
+                item = 4 if dt == 0 else 2
+                got = _gpu_decode(ctx, raw, typ, rows, cols, dt, col_begin=b, ncols=n, column_stride=item + 1)
+                assert got == g[str(typ)][i][dt], (typ, b, n, dt)
+
+
 def test_decode_passthrough_types(ctx, golden):
     """F32 / F16 / BF16 and Q4_0 / Q4_1 / Q5_0 / Q5_1 / Q8_0 value rules:
     nonfinite inputs and scales, fp16 / bf16 overflow, subnormals."""

@@ -1,0 +1,167 @@
+"""GPU checks of the all-gather fused into the GEMM epilogue
+(tc_cuda_qlinear_gather) and of the device flag barrier (tc_cuda_peer_barrier).
+
+On one GPU the "peer" replicas are other buffers of the same device: every
+kernel family (pair GEMM with TMA stores and with plain stores, one-CTA GEMM,
+GEMV, dense weights) must write each output into this rank's Y and into every
+replica, inside this rank's column range only.  The barrier is checked with one
+rank (it must pass) and with a flag that no rank ever raises (it must give up
+after its time limit, set TC_STATUS_TIMEOUT and return).  The two-process test
+runs the real thing across GPUs when at least two are visible.
+"""
+from __future__ import annotations
+
+import ctypes as C
+import os
+
+import numpy as np
+import pytest
+
+import kq_cases
+from oracle import oracle
+
+pytestmark = pytest.mark.gpu
+
+PATHS = {"gemv": (5, 0, "f32", 1e-5), "one_cta": (100, 3, "bf16", 1e-4), "pair": (300, 0, "bf16", 1e-4)}
+
+
+@pytest.mark.parametrize("where", list(PATHS))
+@pytest.mark.parametrize("out_dtype", [0, 2])
+@pytest.mark.parametrize("epilogue", [False, True])
+def test_replicas_receive_every_output(ctx, where, out_dtype, epilogue):
+    import torch
+    from turbocider_b200 import cuda as tcc
+    m, path, staging, f32b = PATHS[where]
+    n, k, n_total, col = 300, 768, 1024, 256          # this rank's columns [256, 556) of 1024
+    raw = tcc.quantize(12, kq_cases.synthetic_weight(n, k, seed=1))
+    w = tcc.Weight.upload(ctx, 12, n, k, raw)
+    xb = kq_cases.synthetic_x_bf16(m, k, seed=2)
+    x = torch.from_numpy(xb.view(np.int16)).view(torch.bfloat16).cuda()
+    tdt = tcc._torch_dtype(out_dtype)
+    sentinel = 7.0
+    ys = [torch.full((m, n_total), sentinel, device="cuda", dtype=tdt) for _ in range(3)]
+    item = ys[0].element_size()
+    bias = torch.randn(n, device="cuda") if epilogue else None
+    ctx.set_path(path)
+    try:
+        tcc.qlinear(ctx, w, x, out=ys[0][:, col:col + n], out_dtype=out_dtype, bias=bias,
+                    activation="gelu_tanh" if epilogue else None,
+                    peers=[ys[1].data_ptr() + col * item, ys[2].data_ptr() + col * item])
+    finally:
+        ctx.set_path(0)
+    assert ctx.status() == 0
+    ref = oracle.qlinear_ref(xb, raw, 12, n, k, staging)
+    if epilogue:
+        ref = oracle.epilogue_ref(ref, bias=bias.cpu().numpy(), activation="gelu_tanh")
+    bound = f32b if out_dtype == 0 else 3e-3
+    for y in ys:
+        h = y.float().cpu().numpy()
+        assert oracle.rel_l2(h[:, col:col + n], ref) <= bound
+        assert np.all(h[:, :col] == sentinel) and np.all(h[:, col + n:] == sentinel)
+    assert torch.equal(ys[0], ys[1]) and torch.equal(ys[0], ys[2])
+
+
+def test_dense_weight_replicas(ctx):
+    import torch
+    from turbocider_b200 import cuda as tcc
+    n, k, m = 64, 96, 40
+    w32 = np.random.default_rng(3).standard_normal((n, k)).astype(np.float32)
+    w = tcc.Weight.upload(ctx, 0, n, k, w32.tobytes())
+    x = torch.randn(m, k, device="cuda").to(torch.bfloat16)
+    ys = [torch.zeros(m, 2 * n, device="cuda", dtype=torch.bfloat16) for _ in range(2)]
+    tcc.qlinear(ctx, w, x, out=ys[0][:, n:], peers=[ys[1].data_ptr() + n * 2])
+    assert ctx.status() == 0
+    assert torch.equal(ys[0], ys[1]) and not ys[0][:, :n].any()
+
+
+def _flags(n):
+    import torch
+    return torch.zeros(n, dtype=torch.int32, device="cuda")
+
+
+def test_barrier_one_rank(ctx):
+    import torch
+    from turbocider_b200 import cuda as tcc
+    f = _flags(1)
+    arr = (C.c_void_p * 1)(f.data_ptr())
+    for epoch in (1, 2, 3):
+        tcc._check(tcc.lib().tc_cuda_peer_barrier(ctx.handle, arr, 1, 0, epoch, 100000, None))
+        torch.cuda.synchronize()
+        assert int(f[0]) == epoch
+    assert ctx.status() == 0
+
+
+def test_barrier_gives_up_on_a_missing_rank(ctx):
+    """Rank 1 never arrives: the wait ends after its limit with
+    TC_STATUS_TIMEOUT, and the device stays usable."""
+    import torch
+    from turbocider_b200 import cuda as tcc
+    mine, other = _flags(2), _flags(2)
+    arr = (C.c_void_p * 2)(mine.data_ptr(), other.data_ptr())
+    tcc._check(tcc.lib().tc_cuda_peer_barrier(ctx.handle, arr, 2, 0, 1, 20000, None))
+    torch.cuda.synchronize()
+    assert ctx.status() & tcc.STATUS_TIMEOUT
+    assert int(other[0]) == 1 and int(mine[0]) == 1 and int(mine[1]) == 0
+    assert float(torch.ones(4, device="cuda").sum()) == 4.0
+    assert ctx.status() == 0
+
+
+def _two_rank_worker(rank, world, port, q):
+    import datetime
+    import sys
+    import torch
+    import torch.distributed as dist
+    sys.path.insert(0, os.path.dirname(os.path.dirname(os.path.abspath(__file__))))
+    sys.path.insert(0, os.path.dirname(os.path.abspath(__file__)))
+    from turbocider_b200 import cuda as tcc
+    from turbocider_b200 import shard
+    from turbocider_b200.peer import PeerGroup
+    try:
+        torch.cuda.set_device(rank)
+        os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+        dist.init_process_group("nccl", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=60),
+                                device_id=torch.device("cuda", rank))
+        ctx = tcc.Context(rank)
+        n, k, m = 1024, 1024, 520
+        raw = tcc.quantize(12, kq_cases.synthetic_weight(n, k, seed=9))
+        per = shard.rows_per_rank(n, world)
+        b, rows = shard.shard_rows(n, world, rank)
+        w = tcc.Weight.upload(ctx, 12, n, k, raw, n_begin=b, n_count=rows)
+        xb = kq_cases.synthetic_x_bf16(m, k, seed=10)
+        x = torch.from_numpy(xb.view(np.int16)).view(torch.bfloat16).cuda()
+        pg = PeerGroup(ctx, timeout_us=5_000_000)
+        buf = pg.alloc(m * world * per * 2)
+        y = buf.tensor((m, world * per), torch.bfloat16)
+        for rep in range(3):
+            tcc.qlinear(ctx, w, x, out=y[:, rank * per:rank * per + rows], peers=pg.peers_of(buf, rank * per * 2))
+            pg.barrier()
+        torch.cuda.synchronize()
+        status = ctx.status()
+        got = y.float().cpu().numpy()[:, :n]
+        err = oracle.rel_l2(got, oracle.qlinear_ref(xb, raw, 12, n, k, "bf16"))
+        del y
+        pg.close()
+        ctx.close()
+        dist.destroy_process_group()
+        q.put((rank, status, err))
+    except Exception as e:  # reported to the parent
+        q.put((rank, -1, repr(e)))
+
+
+def test_two_rank_fused_gather():
+    import torch
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs two GPUs")
+    import torch.multiprocessing as mp
+    ctx_mp = mp.get_context("spawn")
+    q = ctx_mp.Queue()
+    port = 29500 + os.getpid() % 1000
+    procs = [ctx_mp.Process(target=_two_rank_worker, args=(r, 2, port, q)) for r in range(2)]
+    for p in procs:
+        p.start()
+    res = [q.get(timeout=300) for _ in procs]
+    for p in procs:
+        p.join(timeout=60)
+    for rank, status, err in res:
+        assert status == 0, (rank, err)
+        assert err <= 3e-3, (rank, err)

@@ -90,15 +90,37 @@ __device__ __forceinline__ void store_value(uint8_t *p, float v, bool &ovf) {
     else if (DT == 1) *reinterpret_cast<uint16_t *>(p) = to_f16_bits(v, ovf);
     else *reinterpret_cast<uint16_t *>(p) = to_bf16_bits(v);
 }
-// Byte-addressed store (strided targets of the raw decode need not be
-// aligned to the item size) with fp16 / bf16 overflow detection.
+// Store with fp16 / bf16 overflow detection.  Strided targets of the raw
+// decode need not be aligned to the item size: an unaligned target is
+// written with byte stores, an aligned one with one store of the item's width.
 template <int DT>
 __device__ __forceinline__ void store_value_bytes(uint8_t *p, float v, bool &f16_ovf, bool &bf16_ovf) {
-    uint32_t bits, n;
-    if (DT == 0) { bits = __float_as_uint(v); n = 4; }
-    else if (DT == 1) { bits = to_f16_bits(v, f16_ovf); n = 2; }
-    else { bits = to_bf16_bits(v, bf16_ovf); n = 2; }
-    for (uint32_t i = 0; i < n; ++i) p[i] = (uint8_t)(bits >> (8 * i));
+    if (DT == 0) {
+        const uint32_t bits = __float_as_uint(v);
+        if ((reinterpret_cast<uintptr_t>(p) & 3u) == 0) {
+            *reinterpret_cast<uint32_t *>(p) = bits;
+        } else {
+            volatile uint8_t *q = p;
+            q[0] = (uint8_t)bits;
+            q[1] = (uint8_t)(bits >> 8);
+            q[2] = (uint8_t)(bits >> 16);
+            q[3] = (uint8_t)(bits >> 24);
+        }
+        return;
+    }
+    const uint16_t h = DT == 1 ? to_f16_bits(v, f16_ovf) : to_bf16_bits(v, bf16_ovf);
+    if ((reinterpret_cast<uintptr_t>(p) & 1u) == 0) {
+        *reinterpret_cast<uint16_t *>(p) = h;
+    } else {
+        // Widen the 16-bit result with an explicit move before taking its
+        // bytes: byte stores taken straight from the conversion's 16-bit
+        // value lost the low byte on this toolchain.
+        uint32_t w;
+        asm("cvt.u32.u16 %0, %1;" : "=r"(w) : "h"(h));
+        volatile uint8_t *q = p;
+        q[0] = (uint8_t)(w & 0xffu);
+        q[1] = (uint8_t)((w >> 8) & 0xffu);
+    }
 }
 __device__ __forceinline__ uint32_t ld32b(const uint8_t *p) {
     return (uint32_t)p[0] | ((uint32_t)p[1] << 8) | ((uint32_t)p[2] << 16) | ((uint32_t)p[3] << 24);

@@ -70,6 +70,12 @@ __device__ __forceinline__ void store_out(void *p, uint64_t off, float v, bool f
     else if (f16) static_cast<__half *>(p)[off] = __float2half_rn(v);
     else static_cast<__nv_bfloat16 *>(p)[off] = __float2bfloat16_rn(v);
 }
+// Store to Y and to every peer replica of it (N-column sharding: the peers'
+// Y buffers over NVLink).
+__device__ __forceinline__ void store_out_all(const EpiView &e, void *y, uint64_t off, float v, bool f32, bool f16) {
+    store_out(y, off, v, f32, f16);
+    for (uint32_t i = 0; i < e.n_peer; ++i) store_out(e.peer[i], off, v, f32, f16);
+}
 
 // One 32-token piece of a TMEM accumulator through the fused epilogue:
 // thread = weight row n (all 32 lanes of the warp call this together, the
@@ -92,7 +98,7 @@ __device__ __forceinline__ void epi_piece(const EpiView &e, const EpiRow &r, con
         const uint32_t m = m0 + c;
         if (row_ok && r.writer && m < m_end) {
             if (gres) t = load_out(e.res, (uint64_t)m * e.ld_res + r.col, OUT_F32, f16) + r.gate * t;
-            store_out(y, (uint64_t)m * ldy + r.col, t, OUT_F32, f16);
+            store_out_all(e, y, (uint64_t)m * ldy + r.col, t, OUT_F32, f16);
         }
     }
 }

@@ -78,6 +78,10 @@ struct PairSeg {
     uint32_t m_begin, m_end, tile_begin, gate_row;
     const uint8_t *w;
 };
+// Tensor maps of the bf16 / fp16 Y tiles: this rank's Y, then its peer replicas.
+struct YMaps {
+    CUtensorMap m[kMaxPeers];
+};
 struct PairParams {
     PairSeg seg[kMaxSeg];
     uint32_t n_seg, n_tiles, kb, panels, pair_panels, n;
@@ -329,7 +333,7 @@ __device__ __forceinline__ uint16_t to16(float v, bool f16) {
 // ------------------------------------------------------------ the kernel
 template <int TYPE, bool F16, bool OUT_F32>
 __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
-    pair_gemm_kernel(const __grid_constant__ CUtensorMap xmap, const __grid_constant__ CUtensorMap ymap,
+    pair_gemm_kernel(const __grid_constant__ CUtensorMap xmap, const __grid_constant__ YMaps ymaps,
                      const __grid_constant__ PairParams p) {
     using L = PairLayout<TYPE>;
     constexpr uint32_t kChunk = chunk_bytes(TYPE);
@@ -543,7 +547,9 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
                 if (t0 >= T.m_end || n0 >= p.n) break;   // past the segment / a missing second panel
                 uint32_t v[32];
                 tmem_ld32(taddr + 32 * j, v);
-                if (!OUT_F32 && p.y_tma && t0 + 32 <= T.m_end) {
+                // TMA only for boxes wholly inside Y: past a ragged N the store
+                // would write up to the next 16-byte boundary of the row.
+                if (!OUT_F32 && p.y_tma && t0 + 32 <= T.m_end && n0 + 32 <= p.n) {
                     tma_pieces |= 1u << j;
                     uint16_t *sb = reinterpret_cast<uint16_t *>(stage + j * L::e_box) + lane;
 #pragma unroll
@@ -552,11 +558,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
 #pragma unroll
                     for (uint32_t c = 0; c < 32; ++c) {
                         const uint32_t m = t0 + c;
-                        if (m < T.m_end) {
-                            const uint64_t off = (uint64_t)m * p.ldy + n;
-                            if (OUT_F32) static_cast<float *>(p.y)[off] = __uint_as_float(v[c]);
-                            else static_cast<uint16_t *>(p.y)[off] = to16(__uint_as_float(v[c]), f16);
-                        }
+                        if (m < T.m_end)
+                            store_out_all(p.epi, p.y, (uint64_t)m * p.ldy + n, __uint_as_float(v[c]), OUT_F32, f16);
                     }
                 }
             }
@@ -569,15 +572,21 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
                 fence_proxy_async();
                 __syncwarp();
                 if (lane == 0) {
-                    for (uint32_t j = 0; j < kTileTokens / 32; ++j)
-                        if (tma_pieces & (1u << j))
-                            tma_store_2d(&ymap, su32(stage + j * L::e_box), (int)n0, (int)(T.m0 + 32 * j));
+                    // this rank's Y, then each peer replica (N-column sharding)
+                    for (uint32_t d = 0; d <= p.epi.n_peer; ++d)
+                        for (uint32_t j = 0; j < kTileTokens / 32; ++j)
+                            if (tma_pieces & (1u << j))
+                                tma_store_2d(&ymaps.m[d], su32(stage + j * L::e_box), (int)n0, (int)(T.m0 + 32 * j));
                     bulk_commit();
                 }
             }
         }
         if (lane == 0) bulk_wait_all();
         __syncwarp();
+        // Peer replicas: make this thread's stores (and, after the bulk wait,
+        // its TMA stores) visible system-wide before the kernel ends, so that
+        // a flag raised after it publishes them (tc_cuda_peer_barrier).
+        if (p.epi.n_peer) __threadfence_system();
     }
 
     tc_fence_before();
@@ -602,7 +611,7 @@ PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
 }
 
 template <int TYPE, bool F16, bool OUT_F32>
-cudaError_t launch_pair_inst(const CUtensorMap &xm, const CUtensorMap &ym, const PairParams &p, int sm_count,
+cudaError_t launch_pair_inst(const CUtensorMap &xm, const YMaps &ym, const PairParams &p, int sm_count,
                              cudaStream_t s) {
     using L = PairLayout<TYPE>;
     auto kernel = pair_gemm_kernel<TYPE, F16, OUT_F32>;
@@ -672,17 +681,22 @@ cudaError_t launch_gemm_pair(const SegmentView *segs, uint32_t n_seg, const uint
                            CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
     if (r != CUDA_SUCCESS) return cudaErrorInvalidValue;
     const int out_f32 = out_dtype == 0;
-    CUtensorMap ym;
+    YMaps ym;
     memset(&ym, 0, sizeof(ym));
-    if (!out_f32 && !p.epi.flags && (reinterpret_cast<uintptr_t>(y) & 15u) == 0 && (ldy * 2) % 16 == 0) {
+    bool aligned = (reinterpret_cast<uintptr_t>(y) & 15u) == 0 && (ldy * 2) % 16 == 0;
+    for (uint32_t d = 0; d < p.epi.n_peer; ++d) aligned &= (reinterpret_cast<uintptr_t>(p.epi.peer[d]) & 15u) == 0;
+    if (!out_f32 && !p.epi.flags && aligned) {
         const cuuint64_t ydims[2] = {p.n, m_total};
         const cuuint64_t ystrides[1] = {ldy * 2};
         const cuuint32_t ybox[2] = {32u, 32u};
-        const CUresult ry = enc(&ym, out_dtype == 1 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16,
-                                2, y, ydims, ystrides, ybox, estr,
-                                CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE,
-                                CU_TENSOR_MAP_L2_PROMOTION_NONE, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
-        p.y_tma = ry == CUDA_SUCCESS ? 1u : 0u;
+        bool ok = true;
+        for (uint32_t d = 0; d <= p.epi.n_peer && ok; ++d) {
+            void *base = d == 0 ? y : p.epi.peer[d - 1];
+            ok = enc(&ym.m[d], out_dtype == 1 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2,
+                     base, ydims, ystrides, ybox, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE,
+                     CU_TENSOR_MAP_L2_PROMOTION_NONE, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+        }
+        p.y_tma = ok ? 1u : 0u;
     }
     const uint32_t type = segs[0].w.type;
     if (type == 12) {

@@ -271,12 +271,8 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
                     for (uint32_t c = 0; c < 32; ++c) {
                         const uint32_t m = T.m0 + c0 + c;
-                        if (m < T.m_end) {
-                            const uint64_t off = (uint64_t)m * p.ldy + n;
-                            if (OUT_F32) static_cast<float *>(p.y)[off] = __uint_as_float(v[c]);
-                            else if (f16) static_cast<__half *>(p.y)[off] = __float2half_rn(__uint_as_float(v[c]));
-                            else static_cast<__nv_bfloat16 *>(p.y)[off] = __float2bfloat16_rn(__uint_as_float(v[c]));
-                        }
+                        if (m < T.m_end)
+                            store_out_all(p.epi, p.y, (uint64_t)m * p.ldy + n, __uint_as_float(v[c]), OUT_F32, f16);
                     }
                 }
             }
@@ -286,6 +282,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             acc ^= 1;
             if (acc == 0) aph ^= 1;
         }
+        if (p.epi.n_peer) __threadfence_system();   // publish peer-replica stores (see the pair kernel)
     }
 
     tc_fence_before();

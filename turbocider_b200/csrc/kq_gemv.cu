@@ -516,7 +516,7 @@ __global__ void __launch_bounds__(kWarps * 32) gemv_kernel(const __grid_constant
                         const uint64_t m = m_begin + tok;
                         if (e.flags & TC_EPI_GATE_RESIDUAL)
                             val = load_out(e.res, m * e.ld_res + er.col, DT == 0, DT == 1) + er.gate * val;
-                        store_out(y, m * ldy + er.col, val, DT == 0, DT == 1);
+                        store_out_all(e, y, m * ldy + er.col, val, DT == 0, DT == 1);
                     }
                 }
             }
@@ -532,11 +532,12 @@ __global__ void __launch_bounds__(kWarps * 32) gemv_kernel(const __grid_constant
                     const uint32_t row = row0 + g + 8 * (i >> 1);
                     if (col < TP && tok < m_count && row < w.n) {
                         const uint64_t off = (uint64_t)(m_begin + tok) * ldy + row;
-                        store_out(y, off, v[4 * nt + i], DT == 0, DT == 1);
+                        store_out_all(b.epi, y, off, v[4 * nt + i], DT == 0, DT == 1);
                     }
                 }
             }
         }
+        if (store && b.epi.n_peer) __threadfence_system();   // publish peer-replica stores
     }
 }
 

@@ -1,0 +1,142 @@
+// N-column sharding with the all-gather fused into the GEMM epilogue: buffers
+// shared between the ranks' processes (CUDA IPC) and the completion barrier.
+//
+// The reference partitions nothing (one Apple GPU).  The north star shards
+// every quantised weight by output columns over the GPUs of one box and
+// replicates the outputs with an all-gather; here each rank's GEMM writes its
+// output tiles into every rank's Y directly (tc_cuda_qlinear_gather, NVLink
+// peer stores from the epilogue), and tc_cuda_peer_barrier tells every rank
+// when all of them have finished a linear.
+//
+// The barrier is one small kernel per rank: it raises this rank's flag in
+// every rank's flag array (a system-scope release store, after a system fence
+// that publishes the preceding GEMM's peer stores) and waits, with a time
+// limit, until every rank's flag in its own array reached the epoch.  On
+// timeout it sets TC_STATUS_TIMEOUT and returns; it never traps.  The ranks are
+// separate processes on separate GPUs, so the waiting kernels run concurrently.
+#include <cstring>
+#include <string>
+
+#include "../../include/turbocider_cuda.h"
+#include "tc_internal.h"
+
+namespace tc {
+namespace {
+
+struct FlagPtrs {
+    uint32_t *p[kMaxPeers];   // flag array of rank r, as mapped in this process
+};
+
+__global__ void peer_barrier_kernel(FlagPtrs f, uint32_t n, uint32_t rank, uint32_t epoch, uint64_t timeout_ns,
+                                    uint32_t *status) {
+    const uint32_t t = threadIdx.x;
+    if (t >= n) return;
+    __threadfence_system();
+    asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(f.p[t] + rank), "r"(epoch) : "memory");
+    const uint32_t *mine = f.p[rank] + t;
+    uint64_t t0;
+    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t0));
+    for (;;) {
+        uint32_t v;
+        asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(mine) : "memory");
+        if ((int32_t)(v - epoch) >= 0) break;
+        uint64_t now;
+        asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(now));
+        if (now - t0 > timeout_ns) {
+            atomicOr(status, (uint32_t)TC_STATUS_TIMEOUT);
+            break;
+        }
+        __nanosleep(256);
+    }
+}
+
+int fail(const std::string &reason) {
+    set_last_error(reason);
+    return TC_CUDA_FAIL;
+}
+int cuda_fail(const char *what, cudaError_t e) { return fail(std::string(what) + ": " + cudaGetErrorString(e)); }
+int ok() {
+    set_last_error("");
+    return TC_CUDA_OK;
+}
+
+struct DeviceGuard {
+    int previous = -1;
+    explicit DeviceGuard(int device) {
+        if (cudaGetDevice(&previous) == cudaSuccess && previous != device) cudaSetDevice(device);
+    }
+    ~DeviceGuard() {
+        int now = -1;
+        if (previous >= 0 && cudaGetDevice(&now) == cudaSuccess && now != previous) cudaSetDevice(previous);
+    }
+};
+
+}  // namespace
+}  // namespace tc
+
+extern "C" {
+
+int tc_cuda_peer_alloc(tc_cuda_ctx *ctx, uint64_t bytes, void **ptr, void *handle) {
+    if (!ctx || !ptr || !handle || !bytes) return tc::fail("null argument or empty buffer");
+    tc::DeviceGuard guard(ctx->device);
+    *ptr = nullptr;
+    cudaError_t e = cudaMalloc(ptr, bytes);
+    if (e != cudaSuccess) return tc::cuda_fail("peer buffer allocation", e);
+    if ((e = cudaMemset(*ptr, 0, bytes)) == cudaSuccess) {
+        cudaIpcMemHandle_t h;
+        if ((e = cudaIpcGetMemHandle(&h, *ptr)) == cudaSuccess) {
+            std::memcpy(handle, &h, sizeof(h));
+            return tc::ok();
+        }
+    }
+    cudaFree(*ptr);
+    *ptr = nullptr;
+    return tc::cuda_fail("peer buffer export", e);
+}
+
+int tc_cuda_peer_open(tc_cuda_ctx *ctx, const void *handle, void **ptr) {
+    if (!ctx || !ptr || !handle) return tc::fail("null argument");
+    tc::DeviceGuard guard(ctx->device);
+    cudaIpcMemHandle_t h;
+    std::memcpy(&h, handle, sizeof(h));
+    *ptr = nullptr;
+    cudaError_t e = cudaIpcOpenMemHandle(ptr, h, cudaIpcMemLazyEnablePeerAccess);
+    if (e != cudaSuccess) return tc::cuda_fail("peer buffer import", e);
+    return tc::ok();
+}
+
+int tc_cuda_peer_close(tc_cuda_ctx *ctx, void *ptr) {
+    if (!ctx || !ptr) return tc::fail("null argument");
+    tc::DeviceGuard guard(ctx->device);
+    cudaError_t e = cudaIpcCloseMemHandle(ptr);
+    if (e != cudaSuccess) return tc::cuda_fail("peer buffer close", e);
+    return tc::ok();
+}
+
+int tc_cuda_peer_free(tc_cuda_ctx *ctx, void *ptr) {
+    if (!ctx || !ptr) return tc::fail("null argument");
+    tc::DeviceGuard guard(ctx->device);
+    cudaError_t e = cudaFree(ptr);
+    if (e != cudaSuccess) return tc::cuda_fail("peer buffer free", e);
+    return tc::ok();
+}
+
+int tc_cuda_peer_barrier(tc_cuda_ctx *ctx, uint32_t *const *flags, uint32_t n_ranks, uint32_t rank, uint32_t epoch,
+                         uint32_t timeout_us, void *stream) {
+    if (!ctx || !flags) return tc::fail("null argument");
+    if (n_ranks < 1 || n_ranks > tc::kMaxPeers || rank >= n_ranks) return tc::fail("invalid rank / rank count");
+    tc::FlagPtrs f{};
+    for (uint32_t r = 0; r < n_ranks; ++r) {
+        if (!flags[r]) return tc::fail("null flag array");
+        f.p[r] = flags[r];
+    }
+    tc::DeviceGuard guard(ctx->device);
+    const uint64_t limit = (uint64_t)(timeout_us ? timeout_us : 1000000u) * 1000u;
+    tc::peer_barrier_kernel<<<1, 32, 0, static_cast<cudaStream_t>(stream)>>>(f, n_ranks, rank, epoch, limit,
+                                                                            ctx->status);
+    cudaError_t e = cudaGetLastError();
+    if (e != cudaSuccess) return tc::cuda_fail("peer barrier launch", e);
+    return tc::ok();
+}
+
+}  // extern "C"

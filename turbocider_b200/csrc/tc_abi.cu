@@ -132,6 +132,8 @@ void tc_cuda_free(tc_cuda_ctx *ctx) {
     if (ctx->workspace) cudaFree(ctx->workspace);
     if (ctx->gemv_partials) cudaFree(ctx->gemv_partials);
     if (ctx->gemv_counters) cudaFree(ctx->gemv_counters);
+    if (ctx->dense_ws) cudaFree(ctx->dense_ws);
+    tc::dense_blas_destroy(ctx->blas);
     if (ctx->status) cudaFree(ctx->status);
     delete ctx;
 }
@@ -215,6 +217,62 @@ int upload_rows(tc_cuda_ctx *ctx, tc_cuda_weight *w, const uint8_t *const *src, 
     *out = w;
     return ok();
 }
+// Dense (passthrough) weight: raw rows [n_begin, +n_count) resident, plus bf16
+// and (when every value fits) fp16 row-major copies decoded on the device.
+int upload_dense(tc_cuda_ctx *ctx, uint32_t type, uint64_t n, uint64_t k, const void *raw_host, uint64_t raw_bytes,
+                 uint64_t n_begin, uint64_t n_count, tc_cuda_weight **out) {
+    const uint32_t el = tc::type_elements(type);
+    if (!n || !k || k % el) return fail("invalid source geometry");
+    if (n_count == 0) n_count = n - std::min(n_begin, n);
+    if (n_begin >= n || n_count > n - n_begin) return fail("row slice out of bounds");
+    if (n_count > (1ull << 31) || k > (1ull << 31)) return fail("weight shape exceeds the 2^31 limit");
+    const uint64_t row_bytes = k / el * tc::type_bytes(type);
+    if (raw_bytes / row_bytes < n) return fail("packed source too short");
+    DeviceGuard guard(ctx->device);
+    auto *w = new (std::nothrow) tc_cuda_weight;
+    if (!w) return fail("out of host memory");
+    w->device = ctx->device;
+    w->type = type;
+    w->n = n_count;
+    w->k = k;
+    w->raw_row_bytes = row_bytes;
+    const uint64_t elems = n_count * k;
+    w->bytes = n_count * row_bytes + 4 * elems;
+    cudaError_t e = cudaMalloc(&w->raw, n_count * row_bytes);
+    if (e == cudaSuccess) e = cudaMalloc(&w->dense_bf16, elems * 2);
+    if (e == cudaSuccess) e = cudaMalloc(&w->dense_f16, elems * 2);
+    if (e == cudaSuccess)
+        e = cudaMemcpy(w->raw, static_cast<const uint8_t *>(raw_host) + n_begin * row_bytes, n_count * row_bytes,
+                       cudaMemcpyHostToDevice);
+    uint32_t bits[2] = {0, 0};
+    for (int dt = 2; dt >= 1 && e == cudaSuccess; --dt) {   // bf16 first: its errors reject the weight
+        uint16_t *dst = dt == 2 ? w->dense_bf16 : w->dense_f16;
+        e = cudaMemset(ctx->status + 1, 0, sizeof(uint32_t));
+        if (e == cudaSuccess)
+            e = tc::launch_decode_raw(type, w->raw, row_bytes, 0, n_count, 0, k, dt, reinterpret_cast<uint8_t *>(dst),
+                                      k * 2, 2, ctx->status + 1, nullptr);
+        if (e == cudaSuccess) e = cudaMemcpy(&bits[dt - 1], ctx->status + 1, sizeof(uint32_t), cudaMemcpyDeviceToHost);
+    }
+    if (e != cudaSuccess) {
+        tc_cuda_weight_free(w);
+        return cuda_fail("weight upload", e);
+    }
+    if (bits[1] & TC_STATUS_NONFINITE_SCALE) {
+        tc_cuda_weight_free(w);
+        return fail("nonfinite weight/scale or conversion overflow");
+    }
+    if (bits[1] & TC_STATUS_BF16_OVERFLOW) {
+        tc_cuda_weight_free(w);
+        return fail("BF16 conversion overflow");
+    }
+    if (bits[0] & TC_STATUS_F16_OVERFLOW) {   // fp16 staging is refused for this weight
+        cudaFree(w->dense_f16);
+        w->dense_f16 = nullptr;
+    }
+    *out = w;
+    return ok();
+}
+
 }  // namespace
 
 extern "C" {
@@ -223,6 +281,7 @@ int tc_cuda_weight_upload(tc_cuda_ctx *ctx, uint32_t type, uint64_t n, uint64_t 
                           uint64_t raw_bytes, uint64_t n_begin, uint64_t n_count, tc_cuda_weight **out) {
     if (!ctx || !out || !raw_host) return fail("null context, source or out-parameter");
     *out = nullptr;
+    if (tc::dense_type(type)) return upload_dense(ctx, type, n, k, raw_host, raw_bytes, n_begin, n_count, out);
     if (!supported_type(type)) return fail("gguf_decode: unsupported tensor type");
     if (!n || !k || k % tc::kBlockWeights) return fail("invalid source geometry");
     if (n_count == 0) n_count = n - std::min(n_begin, n);
@@ -241,7 +300,7 @@ int tc_cuda_weight_upload_glu(tc_cuda_ctx *ctx, uint32_t type, uint64_t f, uint6
                               tc_cuda_weight **out) {
     if (!ctx || !out || !gate_raw || !up_raw) return fail("null context, source or out-parameter");
     *out = nullptr;
-    if (!supported_type(type)) return fail("gguf_decode: unsupported tensor type");
+    if (!supported_type(type)) return fail("SwiGLU weights take the K-quant types");
     if (!f || !k || k % tc::kBlockWeights) return fail("invalid source geometry");
     if (col_count == 0) col_count = f - std::min(col_begin, f);
     if (col_begin >= f || col_count > f - col_begin) return fail("row slice out of bounds");
@@ -261,6 +320,9 @@ void tc_cuda_weight_free(tc_cuda_weight *w) {
     if (!w) return;
     DeviceGuard guard(w->device);
     if (w->chunks) cudaFree(w->chunks);
+    if (w->raw) cudaFree(w->raw);
+    if (w->dense_bf16) cudaFree(w->dense_bf16);
+    if (w->dense_f16) cudaFree(w->dense_f16);
     delete w;
 }
 
@@ -278,6 +340,14 @@ int tc_cuda_dequant(tc_cuda_ctx *ctx, const tc_cuda_weight *w, int dtype, void *
     if (dtype < 0 || dtype > 2) return fail("gguf_decode: invalid target dtype");
     if (ld < w->k) return fail("invalid/overlapping row stride");
     DeviceGuard guard(ctx->device);
+    if (w->raw) {
+        const uint64_t item = dtype == TC_DTYPE_F32 ? 4 : 2;
+        cudaError_t e = tc::launch_decode_raw(w->type, w->raw, w->raw_row_bytes, 0, w->n, 0, w->k, dtype,
+                                              static_cast<uint8_t *>(dst), ld * item, item, ctx->status,
+                                              static_cast<cudaStream_t>(stream));
+        if (e != cudaSuccess) return cuda_fail("dequant launch", e);
+        return ok();
+    }
     cudaError_t e = tc::launch_dequant_panel(view_of(w), dtype, dst, ld, ctx->status, static_cast<cudaStream_t>(stream));
     if (e != cudaSuccess) return cuda_fail("dequant launch", e);
     return ok();
@@ -342,6 +412,7 @@ int tc_cuda_qlinear_batched(tc_cuda_ctx *ctx, const tc_cuda_weight *const *weigh
         if (w->k != k) return fail("weights of one batched call must share K");
         if (w->device != ctx->device) return fail("weight lives on another device");
         if (w->glu) return fail("a SwiGLU weight needs TC_EPI_SWIGLU (tc_cuda_qlinear_ex)");
+        if (w->raw) return fail("dense weights run through tc_cuda_qlinear");
         if (ldys && ldys[i] && ldys[i] < w->n) return fail("invalid/overlapping row stride");
     }
     DeviceGuard guard(ctx->device);
@@ -390,7 +461,19 @@ int tc_cuda_qlinear(tc_cuda_ctx *ctx, const tc_cuda_weight *const *weights, uint
 int tc_cuda_qlinear_ex(tc_cuda_ctx *ctx, const tc_cuda_weight *const *weights, uint32_t n_weights,
                        const int32_t *seg_offsets, const int32_t *seg_weight, uint32_t n_seg, const void *x, void *y,
                        uint64_t ldy, int out_dtype, int stage, const tc_epilogue *epilogue, void *stream) {
+    return tc_cuda_qlinear_gather(ctx, weights, n_weights, seg_offsets, seg_weight, n_seg, x, y, ldy, out_dtype,
+                                  stage, epilogue, nullptr, 0, stream);
+}
+
+int tc_cuda_qlinear_gather(tc_cuda_ctx *ctx, const tc_cuda_weight *const *weights, uint32_t n_weights,
+                           const int32_t *seg_offsets, const int32_t *seg_weight, uint32_t n_seg, const void *x,
+                           void *y, uint64_t ldy, int out_dtype, int stage, const tc_epilogue *epilogue,
+                           void *const *peer_y, uint32_t n_peer, void *stream) {
     if (!ctx || !weights || !n_weights || !x || !y || !seg_offsets) return fail("null argument");
+    if (n_peer > tc::kMaxPeers - 1) return fail("at most 7 peer replicas");
+    if (n_peer && !peer_y) return fail("null peer output list");
+    for (uint32_t i = 0; i < n_peer; ++i)
+        if (!peer_y[i]) return fail("null peer output");
     if (!n_seg) return fail("no segments");
     if (out_dtype < TC_DTYPE_F32 || out_dtype > TC_DTYPE_BF16) return fail("invalid output dtype");
     if (stage != TC_STAGE_BF16 && stage != TC_STAGE_F16 && stage != TC_STAGE_F16_X16)
@@ -416,6 +499,8 @@ int tc_cuda_qlinear_ex(tc_cuda_ctx *ctx, const tc_cuda_weight *const *weights, u
     if (ldy < n_out) return fail("invalid/overlapping row stride");
     tc::EpiView epi;
     epi.flags = flags;
+    epi.n_peer = n_peer;
+    for (uint32_t i = 0; i < n_peer; ++i) epi.peer[i] = peer_y[i];
     if (flags & TC_EPI_BIAS) {
         if (!epilogue->bias) return fail("TC_EPI_BIAS needs a bias vector");
         epi.bias = epilogue->bias;
@@ -451,12 +536,22 @@ int tc_cuda_qlinear_ex(tc_cuda_ctx *ctx, const tc_cuda_weight *const *weights, u
     // (one launch per weight type).
     std::vector<tc::SegmentView> gemm[3];   // Q4_K, Q6_K, Q5_K
     std::vector<tc::SegmentView> gemv;
+    struct DenseSeg { uint32_t b, e, gate_row; const tc_cuda_weight *w; };
+    std::vector<DenseSeg> dense;             // F32 / F16 / BF16 / 32-weight block types
+    uint32_t dense_rows = 0;
     for (uint32_t i = 0; i < n_seg; ++i) {
         const uint32_t b = (uint32_t)seg_offsets[i], e = (uint32_t)seg_offsets[i + 1];
         if (b == e) continue;
         const tc_cuda_weight *w = weights[seg_weight ? seg_weight[i] : 0];
         tc::SegmentView sv{b, e, view_of(w)};
         if (flags & TC_EPI_GATE_RESIDUAL) sv.gate_row = (uint32_t)(epilogue->seg_gate ? epilogue->seg_gate[i] : i);
+        if (w->raw) {
+            if (stage != TC_STAGE_BF16 && !w->dense_f16)
+                return fail("weight values exceed the fp16 range; use TC_STAGE_BF16");
+            dense.push_back({b, e, sv.gate_row, w});
+            dense_rows = std::max(dense_rows, e - b);
+            continue;
+        }
         // fp16 X (TC_STAGE_F16_X16) always takes the tensor-core GEMM: the
         // warp GEMV works in bf16 code space.
         const bool small = (e - b) <= 16 && stage != TC_STAGE_F16_X16;
@@ -468,8 +563,20 @@ int tc_cuda_qlinear_ex(tc_cuda_ctx *ctx, const tc_cuda_weight *const *weights, u
             gemm[w->type == TC_GGML_Q4_K ? 0 : w->type == TC_GGML_Q5_K ? 2 : 1].push_back(sv);
         }
     }
+    if (!dense.empty()) {
+        if (!ctx->blas && tc::dense_blas_create(&ctx->blas)) return fail("cuBLAS handle creation failed");
+        const size_t need = flags ? (size_t)dense_rows * w0->n : 0;
+        if (need > ctx->dense_ws_floats) {
+            if (ctx->dense_ws) cudaFree(ctx->dense_ws);
+            ctx->dense_ws = nullptr;
+            ctx->dense_ws_floats = 0;
+            cudaError_t e = cudaMalloc(&ctx->dense_ws, need * sizeof(float));
+            if (e != cudaSuccess) return cuda_fail("dense workspace allocation", e);
+            ctx->dense_ws_floats = need;
+        }
+    }
     const uint16_t *xg = static_cast<const uint16_t *>(x);
-    if (stage == TC_STAGE_F16 && (!gemm[0].empty() || !gemm[1].empty() || !gemm[2].empty())) {
+    if (stage == TC_STAGE_F16 && (!gemm[0].empty() || !gemm[1].empty() || !gemm[2].empty() || !dense.empty())) {
         int rc = ensure_workspace(ctx, m_total * k * 2);
         if (rc) return rc;
         cudaError_t e = tc::launch_x_to_f16(xg, static_cast<uint16_t *>(ctx->workspace), m_total * k, ctx->status, s);
@@ -498,6 +605,33 @@ int tc_cuda_qlinear_ex(tc_cuda_ctx *ctx, const tc_cuda_weight *const *weights, u
         }
         cudaError_t e = tc::launch_gemv(sv, static_cast<const uint16_t *>(x), k, y, ldy, out_dtype, sp, s, &epi);
         if (e != cudaSuccess) return cuda_fail("GEMV launch", e);
+    }
+    // Dense weights: library GEMM (fp32 accumulation), then the fused
+    // epilogue from an fp32 product when the call has one.
+    const uint64_t item = out_dtype == TC_DTYPE_F32 ? 4 : 2;
+    for (const auto &d : dense) {
+        const uint32_t rows = d.e - d.b;
+        const void *wd = stage == TC_STAGE_BF16 ? (const void *)d.w->dense_bf16 : (const void *)d.w->dense_f16;
+        const uint16_t *xd = xg + (uint64_t)d.b * k;
+        if (flags) {
+            if (tc::dense_gemm(ctx->blas, wd, xd, stage != TC_STAGE_BF16, rows, (uint32_t)d.w->n, k, ctx->dense_ws,
+                               d.w->n, TC_DTYPE_F32, s))
+                return fail("cuBLAS GEMM failed");
+            cudaError_t e = tc::launch_epi_rows(ctx->dense_ws, rows, (uint32_t)d.w->n, epi, d.gate_row, d.b, y, ldy,
+                                                out_dtype, s);
+            if (e != cudaSuccess) return cuda_fail("epilogue launch", e);
+        } else if (tc::dense_gemm(ctx->blas, wd, xd, stage != TC_STAGE_BF16, rows, (uint32_t)d.w->n, k,
+                                  static_cast<uint8_t *>(y) + (uint64_t)d.b * ldy * item, ldy, out_dtype, s)) {
+            return fail("cuBLAS GEMM failed");
+        }
+        // peer replicas of a dense segment: copy-engine copies of its rows
+        for (uint32_t i = 0; i < n_peer; ++i) {
+            const uint64_t off = (uint64_t)d.b * ldy * item;
+            cudaError_t e = cudaMemcpy2DAsync(static_cast<uint8_t *>(peer_y[i]) + off, ldy * item,
+                                              static_cast<const uint8_t *>(y) + off, ldy * item, d.w->n * item, rows,
+                                              cudaMemcpyDefault, s);
+            if (e != cudaSuccess) return cuda_fail("peer copy", e);
+        }
     }
     return ok();
 }

@@ -17,6 +17,9 @@ struct tc_cuda_ctx {
     size_t gemv_counters_n = 0;
     int path = 0;                    // 0 auto, 1 GEMV, 2 GEMM, 3 GEMM with one-CTA tiles only
     int sm_limit = 0;                // SMs the tensor-core GEMM may occupy (0 = all)
+    void *blas = nullptr;            // cuBLAS handle for dense weights (created on first use)
+    float *dense_ws = nullptr;       // fp32 product of a dense segment before its epilogue
+    size_t dense_ws_floats = 0;
 };
 
 struct tc_cuda_weight {
@@ -26,8 +29,14 @@ struct tc_cuda_weight {
     uint64_t n = 0, k = 0;
     uint32_t kb = 0;                 // super-blocks per row, K / 256
     uint32_t panels = 0;             // ceil(N / 128)
-    uint8_t *chunks = nullptr;       // panel layout, panels * kb chunks
+    uint8_t *chunks = nullptr;       // panel layout, panels * kb chunks (K-quants)
     uint64_t bytes = 0;
+    // Dense weights (F32 / F16 / BF16 / Q4_0 / Q4_1 / Q5_0 / Q5_1 / Q8_0): raw
+    // GGUF rows plus row-major bf16 and fp16 copies (fp16 null when a value
+    // does not fit fp16).
+    uint8_t *raw = nullptr;
+    uint64_t raw_row_bytes = 0;
+    uint16_t *dense_bf16 = nullptr, *dense_f16 = nullptr;
 };
 
 namespace tc {
@@ -49,6 +58,8 @@ struct SegmentView {
     uint32_t gate_row = 0;           // row of the epilogue's gate vectors
 };
 
+constexpr uint32_t kMaxPeers = 8;    // ranks of one N-sharded linear, this one included
+
 // Fused epilogue (device pointers), flags = TC_EPI_* bits; flags == 0 is a
 // plain store.  out_f16 selects fp16 over bf16 for 16-bit outputs.
 struct EpiView {
@@ -59,6 +70,11 @@ struct EpiView {
     uint64_t ld_gate = 0;
     const void *res = nullptr;       // [M][ld_res] in the output dtype
     uint64_t ld_res = 0;
+    // Output replication (N-column sharding): every value stored to Y is also
+    // stored at the same offset from each peer[i] (other ranks' Y buffers,
+    // mapped into this process), so the all-gather happens in the epilogue.
+    uint32_t n_peer = 0;
+    void *peer[kMaxPeers - 1] = {};
 };
 
 // glu_c > 0: the source holds glu_c gate rows then glu_c up rows, and panel
@@ -120,5 +136,14 @@ cudaError_t launch_gemm_pair(const SegmentView *segs, uint32_t n_seg, const uint
                              uint64_t m_total, uint64_t k, void *y, uint64_t ldy, int out_dtype,
                              int stage_f16, int sm_count, uint32_t *status, cudaStream_t s,
                              const EpiView *epi = nullptr);
+
+// Dense (passthrough) weights, dense_linear.cu.
+bool dense_type(uint32_t type);
+cudaError_t launch_epi_rows(const float *acc, uint32_t rows, uint32_t n, const EpiView &e, uint32_t gate_row,
+                            uint32_t m_begin, void *y, uint64_t ldy, int out_dtype, cudaStream_t s);
+int dense_gemm(void *blas, const void *w, const void *x, int x_f16, uint32_t rows, uint32_t n, uint64_t k, void *y,
+               uint64_t ldy, int out_dtype, cudaStream_t s);
+int dense_blas_create(void **blas);
+void dense_blas_destroy(void *blas);
 
 }  // namespace tc

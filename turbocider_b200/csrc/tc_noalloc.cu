@@ -82,6 +82,7 @@ extern "C" int tc_cuda_qlinear_small_static(const tc_cuda_weight *weight, const 
     if (out_dtype < TC_DTYPE_F32 || out_dtype > TC_DTYPE_BF16) return fail("invalid output dtype");
     if (reinterpret_cast<uintptr_t>(x) % 16) return fail("X must be 16-byte aligned");
     if (weight->glu) return fail("a SwiGLU weight needs TC_EPI_SWIGLU (tc_cuda_qlinear_ex)");
+    if (weight->raw) return fail("dense weights run through tc_cuda_qlinear");
     if (ldy == 0) ldy = weight->n;
     if (ldy < weight->n) return fail("invalid/overlapping row stride");
 

@@ -63,6 +63,14 @@ EXPORTS = {
     "tc_cuda_qlinear_ex": (C.c_int, [_vp, C.POINTER(_vp), _u32, C.POINTER(_i32), C.POINTER(_i32), _u32, _vp, _vp,
                                      _u64, C.c_int, C.c_int, C.POINTER(Epilogue), _vp]),
     "tc_cuda_weight_upload_glu": (C.c_int, [_vp, _u32, _u64, _u64, _vp, _vp, _u64, _u64, _u64, C.POINTER(_vp)]),
+    "tc_cuda_qlinear_gather": (C.c_int, [_vp, C.POINTER(_vp), _u32, C.POINTER(_i32), C.POINTER(_i32), _u32, _vp,
+                                         _vp, _u64, C.c_int, C.c_int, C.POINTER(Epilogue), C.POINTER(_vp), _u32,
+                                         _vp]),
+    "tc_cuda_peer_alloc": (C.c_int, [_vp, _u64, C.POINTER(_vp), _vp]),
+    "tc_cuda_peer_open": (C.c_int, [_vp, _vp, C.POINTER(_vp)]),
+    "tc_cuda_peer_close": (C.c_int, [_vp, _vp]),
+    "tc_cuda_peer_free": (C.c_int, [_vp, _vp]),
+    "tc_cuda_peer_barrier": (C.c_int, [_vp, C.POINTER(_vp), _u32, _u32, _u32, _u32, _vp]),
     "tc_cuda_set_path": (C.c_int, [_vp, C.c_int]),
     "tc_cuda_qlinear_batched": (C.c_int, [_vp, C.POINTER(_vp), _u32, _vp, _u32, C.POINTER(_vp), C.POINTER(_u64),
                                           C.c_int, _vp]),
@@ -298,7 +306,7 @@ def _torch_dtype(out_dtype: int):
 
 def qlinear(ctx: Context, weights, x, seg_offsets=None, seg_weight=None, out_dtype: int = BF16,
             stage: int = STAGE_BF16, out=None, stream=None, bias=None, activation: str | None = None,
-            gate=None, residual=None, seg_gate=None, bias_up_offset: int | None = None):
+            gate=None, residual=None, seg_gate=None, bias_up_offset: int | None = None, peers=None):
     """Y = X * W^T through tc_cuda_qlinear_ex.  `weights` is a Weight or a list
     of them; seg_offsets / seg_weight describe ragged request segments along M.
 
@@ -309,6 +317,8 @@ def qlinear(ctx: Context, weights, x, seg_offsets=None, seg_weight=None, out_dty
                   silu(gate) * up);
       gate, residual  y = residual + gate[seg_gate[s]] * t; gate [G, n_out]
                   f32, residual [M, n_out] in the output dtype (may be `out`).
+    peers: device addresses of replicas of `out` on other ranks (same layout;
+    tc_cuda_qlinear_gather) -- every output is also stored there.
     """
     import torch
     ws = weights if isinstance(weights, (list, tuple)) else [weights]
@@ -341,9 +351,11 @@ def qlinear(ctx: Context, weights, x, seg_offsets=None, seg_weight=None, out_dty
         epi.ld_residual = residual.stride(0) if residual is not None else 0
         if seg_gate is not None:
             epi.seg_gate = (_i32 * n_seg)(*seg_gate)
-    _check(lib().tc_cuda_qlinear_ex(ctx.handle, handles, len(ws), offs, sw, n_seg, x.data_ptr(), out.data_ptr(),
-                                    out.stride(0), out_dtype, stage, C.byref(epi) if epi.flags else None,
-                                    _stream_ptr(stream)))
+    peers = list(peers or [])
+    pv = (_vp * max(1, len(peers)))(*peers) if peers else None
+    _check(lib().tc_cuda_qlinear_gather(ctx.handle, handles, len(ws), offs, sw, n_seg, x.data_ptr(),
+                                        out.data_ptr(), out.stride(0), out_dtype, stage,
+                                        C.byref(epi) if epi.flags else None, pv, len(peers), _stream_ptr(stream)))
     return out
 
 
