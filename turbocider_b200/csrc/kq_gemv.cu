@@ -346,7 +346,10 @@ __device__ __forceinline__ void compute_stage(const uint8_t *st, const uint16_t 
     }
 }
 
-constexpr uint32_t kGemvStages = 3;
+#ifndef TC_GEMV_STAGES
+#define TC_GEMV_STAGES 3
+#endif
+constexpr uint32_t kGemvStages = TC_GEMV_STAGES;
 
 // Weights of one launch: blockIdx.x runs over the 16-row tiles of all of
 // them (entry e owns tiles [tile_begin, next entry's tile_begin)); they share
