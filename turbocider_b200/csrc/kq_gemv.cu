@@ -24,11 +24,12 @@
 // 4 warps each taking one super-block, so that thousands of short CTAs keep
 // every SM's loads in flight (the CTA count is independent of the SM count).
 // Each warp streams its super-blocks' packed fields through a 3-stage ring of
-// bulk copies.  With one token (TP = 1) the stage also carries that token's
-// 256 columns of X (512 B); with more tokens X is read straight from global
-// memory instead (at most 16 rows x K, the same for every row tile, so it
-// stays in L1 / L2): staging M rows per stage would shrink the number of
-// resident CTAs as M grows (one CTA of 4 warps per SM at M = 16).  A CTA
+// per-lane cp.async copies.  With one token (TP = 1) the stage also carries
+// that token's 256 columns of X (512 B); with more tokens X is read straight
+// from global memory instead (at most 16 rows x K, the same for every row
+// tile, so it stays in L1 / L2), all of a super-block's X fragments at once:
+// staging M rows per stage would shrink the number of resident CTAs as M
+// grows (one CTA of 4 warps per SM at M = 16).  A CTA
 // sums its warps through shared memory; with several K slices it stores the
 // 16 x M partial in the context workspace, and the last CTA of the row tile to
 // finish (per-tile arrival counter) adds the slices in slice order -- a fixed
@@ -81,72 +82,57 @@ template <> struct StageGeo<14> {
 };
 
 __device__ __forceinline__ uint32_t s_u32(const void *p) { return (uint32_t)__cvta_generic_to_shared(p); }
-__device__ __forceinline__ void mbar_init(uint32_t b, uint32_t n) {
-    asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(b), "r"(n));
+// Per-lane asynchronous copies (cp.async, 16 bytes per lane per copy, L2
+// only): the 32 lanes of a warp move a 512-byte piece with one instruction
+// each.  A stage is one commit group; cp.async.wait_group + __syncwarp make
+// it visible to the whole warp.  Unlike bulk copies these do not queue on
+// the SM's single TMA unit, which at the start of a short launch holds
+// hundreds of small requests (every warp's ring of stages) and delays the
+// first arrivals.
+__device__ __forceinline__ void cpa16(uint32_t dst, const void *src) {
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(dst), "l"(src) : "memory");
 }
-__device__ __forceinline__ void mbar_expect(uint32_t b, uint32_t bytes) {
-    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(b), "r"(bytes) : "memory");
+__device__ __forceinline__ void cpa_piece(uint32_t dst, const uint8_t *src, uint32_t bytes, uint32_t lane) {
+    for (uint32_t o = lane * 16; o < bytes; o += 512) cpa16(dst + o, src + o);
 }
-__device__ __forceinline__ void bulk_g2s(uint32_t dst, const void *src, uint32_t bytes, uint32_t b) {
-    asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];"
-                 ::"r"(dst), "l"(src), "r"(bytes), "r"(b) : "memory");
-}
-__device__ __forceinline__ bool mbar_try(uint32_t b, uint32_t parity) {
-    uint32_t ok;
-    asm volatile("{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n"
-                 " selp.u32 %0, 1, 0, p;\n}\n"
-                 : "=r"(ok) : "r"(b), "r"(parity), "r"(20000u) : "memory");
-    return ok != 0;
-}
-// Bounded wait (about one second); false on timeout, after setting the
-// timeout bit of the status word.
-__device__ __noinline__ bool mbar_wait(uint32_t b, uint32_t parity, uint32_t *status) {
-    uint64_t t0, t1;
-    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t0));
-    for (;;) {
-        if (mbar_try(b, parity)) return true;
-        asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t1));
-        if (t1 - t0 > 1000000000ull) {
-            atomicOr(status, 1u << 2);
-            return false;
-        }
-    }
-}
+__device__ __forceinline__ void cpa_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+template <int N>
+__device__ __forceinline__ void cpa_wait() { asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory"); }
 
-// Lane 0 of a warp: enqueue the weight copies of one super-block into stage
-// buffer st.
-template <int TYPE, bool STAGE_X>
-__device__ __forceinline__ void issue_w(uint8_t *st, uint32_t bar, const uint8_t *chunk, uint32_t r0) {
+// All lanes of a warp: copy the packed fields of the warp's 16 rows of one
+// super-block (panel chunk `chunk`, rows r0..r0+15) into stage buffer st.
+template <int TYPE>
+__device__ __forceinline__ void issue_w(uint8_t *st, const uint8_t *chunk, uint32_t r0, uint32_t lane) {
     using SG = StageGeo<TYPE>;
-    mbar_expect(bar, SG::w_bytes + (STAGE_X ? 512u : 0u));
     const uint32_t d = s_u32(st);
     if constexpr (TYPE == 12) {
 #pragma unroll
-        for (uint32_t q = 0; q < 4; ++q) bulk_g2s(d + SG::qs + q * 512, chunk + kQ4Qs + q * 4096 + r0 * 32, 512, bar);
-        bulk_g2s(d + SG::sc, chunk + kQ4Sc + r0 * 12, 192, bar);
-        bulk_g2s(d + SG::dm, chunk + kQ4Dm + r0 * 4, 64, bar);
+        for (uint32_t q = 0; q < 4; ++q) cpa_piece(d + SG::qs + q * 512, chunk + kQ4Qs + q * 4096 + r0 * 32, 512, lane);
+        cpa_piece(d + SG::sc, chunk + kQ4Sc + r0 * 12, 192, lane);
+        cpa_piece(d + SG::dm, chunk + kQ4Dm + r0 * 4, 64, lane);
     } else if constexpr (TYPE == 13) {
 #pragma unroll
-        for (uint32_t q = 0; q < 4; ++q) bulk_g2s(d + SG::qs + q * 512, chunk + kQ5Qs + q * 4096 + r0 * 32, 512, bar);
-        bulk_g2s(d + SG::qh, chunk + kQ5Qh + r0 * 32, 512, bar);
-        bulk_g2s(d + SG::sc, chunk + kQ5Sc + r0 * 12, 192, bar);
-        bulk_g2s(d + SG::dm, chunk + kQ5Dm + r0 * 4, 64, bar);
+        for (uint32_t q = 0; q < 4; ++q) cpa_piece(d + SG::qs + q * 512, chunk + kQ5Qs + q * 4096 + r0 * 32, 512, lane);
+        cpa_piece(d + SG::qh, chunk + kQ5Qh + r0 * 32, 512, lane);
+        cpa_piece(d + SG::sc, chunk + kQ5Sc + r0 * 12, 192, lane);
+        cpa_piece(d + SG::dm, chunk + kQ5Dm + r0 * 4, 64, lane);
     } else {
 #pragma unroll
         for (uint32_t hp = 0; hp < 4; ++hp)
-            bulk_g2s(d + SG::ql + hp * 512, chunk + kQ6Ql + (hp * kPanelRows + r0) * 32, 512, bar);
+            cpa_piece(d + SG::ql + hp * 512, chunk + kQ6Ql + (hp * kPanelRows + r0) * 32, 512, lane);
 #pragma unroll
         for (uint32_t h = 0; h < 2; ++h)
-            bulk_g2s(d + SG::qh + h * 512, chunk + kQ6Qh + (h * kPanelRows + r0) * 32, 512, bar);
-        bulk_g2s(d + SG::sc, chunk + kQ6Sc + r0 * 16, 256, bar);
-        bulk_g2s(d + SG::d, chunk + kQ6D + r0 * 2, 32, bar);
+            cpa_piece(d + SG::qh + h * 512, chunk + kQ6Qh + (h * kPanelRows + r0) * 32, 512, lane);
+        cpa_piece(d + SG::sc, chunk + kQ6Sc + r0 * 16, 256, lane);
+        cpa_piece(d + SG::d, chunk + kQ6D + r0 * 2, 32, lane);
     }
 }
-// Lane 0: the single token's 256 columns of X for super-block kb (TP = 1).
+// All lanes: the single token's 256 columns of X for super-block kb (TP = 1).
 template <int TYPE>
-__device__ __forceinline__ void issue_x1(uint8_t *st, uint32_t bar, const uint16_t *x, uint64_t k, uint32_t m,
-                                         uint32_t kb) {
-    bulk_g2s(s_u32(st) + StageGeo<TYPE>::w_bytes, x + (uint64_t)m * k + (uint64_t)kb * 256, 512, bar);
+__device__ __forceinline__ void issue_x1(uint8_t *st, const uint16_t *x, uint64_t k, uint32_t m, uint32_t kb,
+                                         uint32_t lane) {
+    cpa_piece(s_u32(st) + StageGeo<TYPE>::w_bytes,
+              reinterpret_cast<const uint8_t *>(x + (uint64_t)m * k + (uint64_t)kb * 256), 512, lane);
 }
 // Programmatic dependent launch: let the next kernel in the stream start its
 // prologue, and wait for the previous one before touching its outputs.
@@ -234,13 +220,28 @@ __device__ __forceinline__ void compute_stage(const uint8_t *st, const uint16_t 
     for (int nt = 0; nt < NT; ++nt)
         xrow[nt] = TP == 1 ? reinterpret_cast<const uint16_t *>(st + SG::w_bytes)
                            : x + (uint64_t)(m_begin + min(8 * nt + g % TP, m_count - 1)) * k + (uint64_t)kb * 256;
+    // With several tokens X is read from global memory (L1 / L2): issue all 16
+    // K16 steps' loads of this super-block up front, so that their latency is
+    // paid once per super-block instead of once per MMA step.  Step si covers
+    //   Q4_K / Q5_K: si = 4q + 2nib + sp -> columns 32(2q + nib) + 8t + 4sp;
+    //   Q6_K:        si = 8h + 4jj + grp -> columns 128h + 32grp + 16jj + 4t.
+    uint2 xs[TP > 1 ? 16 : 1][NT];
+    if constexpr (TP > 1) {
+#pragma unroll
+        for (uint32_t si = 0; si < 16; ++si) {
+            const uint32_t kl = TYPE != 14 ? 32 * (si >> 1) + 8 * t + 4 * (si & 1)
+                                           : 128 * (si >> 3) + 32 * (si & 3) + 16 * ((si >> 2) & 1) + 4 * t;
+#pragma unroll
+            for (int nt = 0; nt < NT; ++nt) xs[si][nt] = __ldg(reinterpret_cast<const uint2 *>(xrow[nt] + kl));
+        }
+    }
     const uint32_t my_j = g / TP;
     const uint32_t ones = 0x3F803F80u;
     constexpr float off = 128.f;   // Q4_K: the code-space offset of code_pair
     float cq[NT][4], c1[NT][4];
 
     // One K16 step of scale group visit v: A from code words (rows g, g+8).
-    auto step = [&](uint32_t v, uint32_t cg, uint32_t cg8, uint32_t kloc, bool chain_start) {
+    auto step = [&](uint32_t v, uint32_t si, uint32_t cg, uint32_t cg8, uint32_t kloc, bool chain_start) {
         const uint32_t j = v % S;
         if (chain_start) {
 #pragma unroll
@@ -258,8 +259,9 @@ __device__ __forceinline__ void compute_stage(const uint8_t *st, const uint16_t 
         }
 #pragma unroll
         for (int nt = 0; nt < NT; ++nt) {
-            const uint2 xv = TP == 1 ? *reinterpret_cast<const uint2 *>(xrow[nt] + kloc)
-                                     : __ldg(reinterpret_cast<const uint2 *>(xrow[nt] + kloc));
+            uint2 xv;
+            if constexpr (TP == 1) xv = *reinterpret_cast<const uint2 *>(xrow[nt] + kloc);
+            else xv = xs[si][nt];
             const bool on = my_j == j;
             const uint32_t b0 = on ? xv.x : 0u, b1 = on ? xv.y : 0u;
             mma16816(cq[nt], a0, a1, a2, a3, b0, b1, cq[nt]);
@@ -313,7 +315,7 @@ __device__ __forceinline__ void compute_stage(const uint8_t *st, const uint16_t 
                         c |= (((sp ? hq.y : hq.x) >> v) & 0x01010101u) << 4;
                         c8 |= (((sp ? hq8.y : hq8.x) >> v) & 0x01010101u) << 4;
                     }
-                    step(v, c, c8, 32 * v + 8 * t + 4 * sp, sp == 0 && v % S == 0);
+                    step(v, 2 * v + sp, c, c8, 32 * v + 8 * t + 4 * sp, sp == 0 && v % S == 0);
                 }
                 if (v % S == S - 1) close_chain(v / S);
             }
@@ -337,7 +339,7 @@ __device__ __forceinline__ void compute_stage(const uint8_t *st, const uint16_t 
 #pragma unroll
                 for (uint32_t grp = 0; grp < 4; ++grp) {
                     const uint32_t v = 8 * h + 4 * jj + grp;
-                    step(v, (lw[grp] & 0x0F0F0F0Fu) | hb[grp], (lw8[grp] & 0x0F0F0F0Fu) | hb8[grp],
+                    step(v, v, (lw[grp] & 0x0F0F0F0Fu) | hb[grp], (lw8[grp] & 0x0F0F0F0Fu) | hb8[grp],
                          128 * h + 32 * grp + 16 * jj + 4 * t, v % S == 0);
                     if (v % S == S - 1) close_chain(v / S);
                 }
@@ -365,7 +367,6 @@ __global__ void __launch_bounds__(kWarps * 32) gemv_kernel(const __grid_constant
     extern __shared__ __align__(128) uint8_t dyn[];
     __shared__ float red[kWarps][32][4 * NT];
     __shared__ __align__(16) float tab[kWarps][16 * 16];
-    __shared__ __align__(8) uint64_t bars[kWarps][kGemvStages];
     uint32_t ei = 0;
     while (ei + 1 < b.n_entries && blockIdx.x >= b.e[ei + 1].tile_begin) ++ei;
     const GemvEntry &w = b.e[ei];
@@ -380,57 +381,46 @@ __global__ void __launch_bounds__(kWarps * 32) gemv_kernel(const __grid_constant
     constexpr uint32_t stage_bytes = (SG::w_bytes + (kStageX ? 512u : 0u) + 127) / 128 * 128;
     uint8_t *mine = dyn + (size_t)warp * kGemvStages * stage_bytes;
     float *wt = tab[warp];
-    if (lane == 0)
-        for (uint32_t i = 0; i < kGemvStages; ++i) mbar_init(s_u32(&bars[warp][i]), 1);
-    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
-    __syncwarp();
 
-    // This warp's super-blocks: kb_begin + warp + kWarps * i
+    // This warp's super-blocks: kb_begin + warp + kWarps * i.  Stage i is
+    // commit group i; the weights of the first S-1 stages are issued before
+    // the wait on the previous kernel (they do not depend on it), their X
+    // after it, each as a group of its own, so that before computing stage i
+    // exactly the S-1 most recent groups may still be in flight.
     const uint32_t first = kb_begin + warp;
     const uint32_t count = first < kb_end ? (kb_end - first + kWarps - 1) / kWarps : 0;
-    // Weights do not depend on the previous kernel: prefetch them first, then
-    // wait for it (it may still be writing X, the workspace or Y).
-    if (lane == 0) {
-        for (uint32_t i = 0; i < min(count, kGemvStages - 1); ++i) {
-            const uint32_t kb = first + kWarps * i;
-            issue_w<TYPE, kStageX>(mine + i * stage_bytes, s_u32(&bars[warp][i]), pbase + (uint64_t)kb * chunk, r0);
-        }
+#pragma unroll
+    for (uint32_t i = 0; i < kGemvStages - 1; ++i) {
+        if (i < count) issue_w<TYPE>(mine + i * stage_bytes, pbase + (uint64_t)(first + kWarps * i) * chunk, r0, lane);
+        cpa_commit();
     }
     if (threadIdx.x == 0) pdl_launch_dependents();
     pdl_wait();
-    if (kStageX && lane == 0)
-        for (uint32_t i = 0; i < min(count, kGemvStages - 1); ++i)
-            issue_x1<TYPE>(mine + i * stage_bytes, s_u32(&bars[warp][i]), x, k, m_begin, first + kWarps * i);
+#pragma unroll
+    for (uint32_t i = 0; i < kGemvStages - 1; ++i) {
+        if (kStageX && i < count) issue_x1<TYPE>(mine + i * stage_bytes, x, k, m_begin, first + kWarps * i, lane);
+        cpa_commit();
+    }
     float acc[NT][4];
 #pragma unroll
     for (int nt = 0; nt < NT; ++nt)
 #pragma unroll
         for (int i = 0; i < 4; ++i) acc[nt][i] = 0.f;
-    bool ok = true;
     for (uint32_t i = 0; i < count; ++i) {
-        const uint32_t slot = i % kGemvStages, parity = (i / kGemvStages) & 1;
-        // refill the slot computed in the previous iteration (all lanes are past it)
-        if (lane == 0 && i + kGemvStages - 1 < count) {
+        // refill the slot computed in the previous iteration (every lane is
+        // past it: __syncwarp at the end of the iteration)
+        if (i + kGemvStages - 1 < count) {
             const uint32_t j = i + kGemvStages - 1, kb = first + kWarps * j;
             uint8_t *sj = mine + (j % kGemvStages) * stage_bytes;
-            const uint32_t bj = s_u32(&bars[warp][j % kGemvStages]);
-            issue_w<TYPE, kStageX>(sj, bj, pbase + (uint64_t)kb * chunk, r0);
-            if (kStageX) issue_x1<TYPE>(sj, bj, x, k, m_begin, kb);
+            issue_w<TYPE>(sj, pbase + (uint64_t)kb * chunk, r0, lane);
+            if (kStageX) issue_x1<TYPE>(sj, x, k, m_begin, kb, lane);
         }
-        if (!mbar_wait(s_u32(&bars[warp][slot]), parity, status)) { ok = false; break; }
-        compute_stage<TYPE, TP, NT>(mine + slot * stage_bytes, x, k, m_begin, first + kWarps * i, m_count, g, t,
-                                    lane, wt, acc);
+        cpa_commit();
+        cpa_wait<kGemvStages - 1>();
         __syncwarp();
-    }
-    if (!ok) {
-        // wait (bounded) for this warp's copies still in flight before exiting
-        for (uint32_t s2 = 0; s2 < kGemvStages; ++s2) {
-            // the last use of slot s2 was iteration j = largest j < count with j % S == s2
-            if (s2 < count) {
-                const uint32_t j = s2 + ((count - 1 - s2) / kGemvStages) * kGemvStages;
-                mbar_wait(s_u32(&bars[warp][s2]), (j / kGemvStages) & 1, status);
-            }
-        }
+        compute_stage<TYPE, TP, NT>(mine + (i % kGemvStages) * stage_bytes, x, k, m_begin, first + kWarps * i,
+                                    m_count, g, t, lane, wt, acc);
+        __syncwarp();
     }
     // Columns of one token are spread over the quad (TP < 8): sum them so that
     // every lane holds the full value of its (row, token) pairs.
