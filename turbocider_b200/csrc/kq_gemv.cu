@@ -178,9 +178,33 @@ __device__ __forceinline__ constexpr uint32_t group_of_visit(uint32_t v) {
     return TYPE != 14 ? v : 8 * (v >> 3) + 2 * (v & 3) + ((v >> 2) & 1);
 }
 
+// With several tokens X is read from global memory (L1 / L2) into registers:
+// the 16 K16 steps' fragments of one super-block, loaded one super-block
+// ahead of their use (one token tile) so that the load latency overlaps the
+// previous super-block's arithmetic.  Step si covers
+//   Q4_K / Q5_K: si = 4q + 2nib + sp -> columns 32(2q + nib) + 8t + 4sp;
+//   Q6_K:        si = 8h + 4jj + grp -> columns 128h + 32grp + 16jj + 4t.
+template <int TP, int NT> struct XFrags { uint2 v[16][NT]; };
+template <int NT> struct XFrags<1, NT> {};
 template <int TYPE, int TP, int NT>
-__device__ __forceinline__ void compute_stage(const uint8_t *st, const uint16_t *__restrict__ x, uint64_t k,
-                                              uint32_t m_begin, uint32_t kb, uint32_t m_count, uint32_t g,
+__device__ __forceinline__ void load_x(XFrags<TP, NT> &xs, const uint16_t *__restrict__ x, uint64_t k,
+                                       uint32_t m_begin, uint32_t kb, uint32_t m_count, uint32_t g, uint32_t t) {
+    if constexpr (TP > 1) {
+#pragma unroll
+        for (int nt = 0; nt < NT; ++nt) {
+            const uint16_t *xr = x + (uint64_t)(m_begin + min(8 * nt + g % TP, m_count - 1)) * k + (uint64_t)kb * 256;
+#pragma unroll
+            for (uint32_t si = 0; si < 16; ++si) {
+                const uint32_t kl = TYPE != 14 ? 32 * (si >> 1) + 8 * t + 4 * (si & 1)
+                                               : 128 * (si >> 3) + 32 * (si & 3) + 16 * ((si >> 2) & 1) + 4 * t;
+                xs.v[si][nt] = __ldg(reinterpret_cast<const uint2 *>(xr + kl));
+            }
+        }
+    }
+}
+
+template <int TYPE, int TP, int NT>
+__device__ __forceinline__ void compute_stage(const uint8_t *st, const XFrags<TP, NT> &xs, uint32_t g,
                                               uint32_t t, uint32_t lane, float *wt, float (&acc)[NT][4]) {
     using SG = StageGeo<TYPE>;
     constexpr uint32_t S = 8 / TP;
@@ -215,26 +239,8 @@ __device__ __forceinline__ void compute_stage(const uint8_t *st, const uint16_t 
         o[1] = make_float4(d * (b[0] - 128.f), d * (b[1] - 128.f), d * (b[2] - 128.f), d * (b[3] - 128.f));
     }
     __syncwarp();
-    const uint16_t *xrow[NT];   // this thread's tokens, columns of this super-block
-#pragma unroll
-    for (int nt = 0; nt < NT; ++nt)
-        xrow[nt] = TP == 1 ? reinterpret_cast<const uint16_t *>(st + SG::w_bytes)
-                           : x + (uint64_t)(m_begin + min(8 * nt + g % TP, m_count - 1)) * k + (uint64_t)kb * 256;
-    // With several tokens X is read from global memory (L1 / L2): issue all 16
-    // K16 steps' loads of this super-block up front, so that their latency is
-    // paid once per super-block instead of once per MMA step.  Step si covers
-    //   Q4_K / Q5_K: si = 4q + 2nib + sp -> columns 32(2q + nib) + 8t + 4sp;
-    //   Q6_K:        si = 8h + 4jj + grp -> columns 128h + 32grp + 16jj + 4t.
-    uint2 xs[TP > 1 ? 16 : 1][NT];
-    if constexpr (TP > 1) {
-#pragma unroll
-        for (uint32_t si = 0; si < 16; ++si) {
-            const uint32_t kl = TYPE != 14 ? 32 * (si >> 1) + 8 * t + 4 * (si & 1)
-                                           : 128 * (si >> 3) + 32 * (si & 3) + 16 * ((si >> 2) & 1) + 4 * t;
-#pragma unroll
-            for (int nt = 0; nt < NT; ++nt) xs[si][nt] = __ldg(reinterpret_cast<const uint2 *>(xrow[nt] + kl));
-        }
-    }
+    // one token: its 256 columns of X are part of the stage
+    const uint16_t *x1 = reinterpret_cast<const uint16_t *>(st + SG::w_bytes);
     const uint32_t my_j = g / TP;
     const uint32_t ones = 0x3F803F80u;
     constexpr float off = 128.f;   // Q4_K: the code-space offset of code_pair
@@ -260,8 +266,8 @@ __device__ __forceinline__ void compute_stage(const uint8_t *st, const uint16_t 
 #pragma unroll
         for (int nt = 0; nt < NT; ++nt) {
             uint2 xv;
-            if constexpr (TP == 1) xv = *reinterpret_cast<const uint2 *>(xrow[nt] + kloc);
-            else xv = xs[si][nt];
+            if constexpr (TP == 1) xv = *reinterpret_cast<const uint2 *>(x1 + kloc);
+            else xv = xs.v[si][nt];
             const bool on = my_j == j;
             const uint32_t b0 = on ? xv.x : 0u, b1 = on ? xv.y : 0u;
             mma16816(cq[nt], a0, a1, a2, a3, b0, b1, cq[nt]);
@@ -357,7 +363,7 @@ constexpr uint32_t kGemvStages = TC_GEMV_STAGES;
 // them (entry e owns tiles [tile_begin, next entry's tile_begin)); they share
 // K, type and X, each has its own Y.
 template <int TYPE, int TP, int NT, int DT>
-__global__ void __launch_bounds__(kWarps * 32) gemv_kernel(const __grid_constant__ GemvBatch b,
+__global__ void __launch_bounds__(kWarps * 32, 4) gemv_kernel(const __grid_constant__ GemvBatch b,
                                                            const uint16_t *__restrict__ x, uint32_t m_begin,
                                                            uint32_t m_count, uint64_t k, uint32_t kb_per_slice,
                                                            float *__restrict__ partials,
@@ -406,9 +412,14 @@ __global__ void __launch_bounds__(kWarps * 32) gemv_kernel(const __grid_constant
     for (int nt = 0; nt < NT; ++nt)
 #pragma unroll
         for (int i = 0; i < 4; ++i) acc[nt][i] = 0.f;
-    for (uint32_t i = 0; i < count; ++i) {
-        // refill the slot computed in the previous iteration (every lane is
-        // past it: __syncwarp at the end of the iteration)
+    // One super-block: refill the slot computed in the previous iteration
+    // (every lane is past it: __syncwarp at the end of the iteration), wait
+    // for this one's stage, load the next super-block's X fragments, compute.
+    // With two token tiles (NT = 2) a second fragment set would halve the
+    // resident CTAs (registers): there X is loaded at the start of its own
+    // super-block instead.
+    constexpr bool kAhead = NT == 1;
+    auto iteration = [&](uint32_t i, XFrags<TP, NT> &xs_cur, XFrags<TP, NT> &xs_next) {
         if (i + kGemvStages - 1 < count) {
             const uint32_t j = i + kGemvStages - 1, kb = first + kWarps * j;
             uint8_t *sj = mine + (j % kGemvStages) * stage_bytes;
@@ -418,9 +429,19 @@ __global__ void __launch_bounds__(kWarps * 32) gemv_kernel(const __grid_constant
         cpa_commit();
         cpa_wait<kGemvStages - 1>();
         __syncwarp();
-        compute_stage<TYPE, TP, NT>(mine + (i % kGemvStages) * stage_bytes, x, k, m_begin, first + kWarps * i,
-                                    m_count, g, t, lane, wt, acc);
+        if constexpr (kAhead) {
+            if (i + 1 < count) load_x<TYPE, TP, NT>(xs_next, x, k, m_begin, first + kWarps * (i + 1), m_count, g, t);
+        } else {
+            load_x<TYPE, TP, NT>(xs_cur, x, k, m_begin, first + kWarps * i, m_count, g, t);
+        }
+        compute_stage<TYPE, TP, NT>(mine + (i % kGemvStages) * stage_bytes, xs_cur, g, t, lane, wt, acc);
         __syncwarp();
+    };
+    XFrags<TP, NT> xa, xb;
+    if (kAhead && count) load_x<TYPE, TP, NT>(xa, x, k, m_begin, first, m_count, g, t);
+    for (uint32_t i = 0; i < count; i += 2) {
+        iteration(i, xa, xb);
+        if (i + 1 < count) iteration(i + 1, xb, xa);
     }
     // Columns of one token are spread over the quad (TP < 8): sum them so that
     // every lane holds the full value of its (row, token) pairs.
