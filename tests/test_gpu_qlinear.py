@@ -128,6 +128,23 @@ def test_gemv_config2_shape(ctx, typ, m):
     assert oracle.rel_l2(yb, oracle.qlinear_ref(xb, raw, typ, n, k, "f32")) <= 3e-3
 
 
+@pytest.mark.parametrize("typ", [12, 13, 14])
+@pytest.mark.parametrize("m", [1, 5, 16])
+@pytest.mark.parametrize("n,k", [(64, 12288), (16, 12288), (1000, 2048), (48, 3072), (16, 4096)])
+def test_gemv_k_split_reductions(ctx, typ, m, n, k):
+    """The GEMV's K-slice sums through the workspace and the last-arriving CTA
+    of each row tile: 12 slices (n=64 and n=16 at k=12288), 2 (n=1000), 3
+    (n=48), 4 (n=16 at k=4096).  Each runs twice, so a tile counter not left
+    at zero by the first call would break the second."""
+    from turbocider_b200 import cuda as tcc
+    raw, w, xb, x = _setup(ctx, typ, n, k, m, wseed=n + m)
+    ref = oracle.qlinear_ref(xb, raw, typ, n, k, "f32")
+    for _ in range(2):
+        y = _run(ctx, w, x, tcc.F32)
+        assert oracle.rel_l2(y, ref) <= 1e-5
+    assert ctx.status() == 0
+
+
 def test_forced_paths_agree(ctx):
     """M=40 through the GEMV (forced) and through the GEMM."""
     from turbocider_b200 import cuda as tcc

@@ -139,6 +139,13 @@ __device__ __forceinline__ void issue_x1(uint8_t *st, const uint16_t *x, uint64_
 __device__ __forceinline__ void pdl_launch_dependents() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
 __device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
 
+// Tile arrival counter: atomic add with acquire-release semantics at GPU scope.
+__device__ __forceinline__ uint32_t arrive_acq_rel(uint32_t *counter) {
+    uint32_t old;
+    asm volatile("atom.add.acq_rel.gpu.u32 %0, [%1], 1;" : "=r"(old) : "l"(counter) : "memory");
+    return old;
+}
+
 __device__ __forceinline__ uint32_t lds32(const uint8_t *p) { return *reinterpret_cast<const uint32_t *>(p); }
 
 // Four bytes of a word as exact small-integer floats (byte = 0..255):
@@ -492,12 +499,15 @@ __global__ void __launch_bounds__(kWarps * 32, 4) gemv_kernel(const __grid_const
             float *dst = partials + (((uint64_t)blockIdx.y * gridDim.x + blockIdx.x) * 32 + lane) * (4 * NT);
 #pragma unroll
             for (int j = 0; j < 4 * NT; ++j) __stcg(dst + j, v[j]);
-            __threadfence();
+            // The warp barrier orders every lane's partial stores before lane
+            // 0's arrival; the arrival is one acquire-release atomic: release
+            // publishes this slice's partial, acquire (for the last slice to
+            // arrive) makes the other slices' partials visible -- one round
+            // trip to L2 instead of fence + atomic + fence.
             __syncwarp();
-            if (lane == 0) last = (atomicAdd(counters + blockIdx.x, 1u) + 1 == n_slices) ? 1u : 0u;
+            if (lane == 0) last = (arrive_acq_rel(counters + blockIdx.x) + 1 == n_slices) ? 1u : 0u;
             __syncwarp();
             if (last) {
-                __threadfence();
 #pragma unroll
                 for (int j = 0; j < 4 * NT; ++j) v[j] = 0.f;
                 for (uint32_t sl = 0; sl < n_slices; ++sl) {
