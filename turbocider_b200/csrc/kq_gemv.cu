@@ -185,34 +185,46 @@ __device__ __forceinline__ constexpr uint32_t group_of_visit(uint32_t v) {
     return TYPE != 14 ? v : 8 * (v >> 3) + 2 * (v & 3) + ((v >> 2) & 1);
 }
 
-// With several tokens X is read from global memory (L1 / L2) into registers:
-// the 16 K16 steps' fragments of one super-block, loaded one super-block
-// ahead of their use (one token tile) so that the load latency overlaps the
-// previous super-block's arithmetic.  Step si covers
-//   Q4_K / Q5_K: si = 4q + 2nib + sp -> columns 32(2q + nib) + 8t + 4sp;
-//   Q6_K:        si = 8h + 4jj + grp -> columns 128h + 32grp + 16jj + 4t.
-template <int TP, int NT> struct XFrags { uint2 v[16][NT]; };
-template <int NT> struct XFrags<1, NT> {};
+// B operand: in the K16 step of scale-group visit v the MMA column slot is
+// j = v % S, and only the quad whose token column g / TP equals j supplies X
+// (every other thread supplies zeros).  So a thread needs X on 2 TP of the 16
+// steps of a super-block -- its "own" steps, visits v = g / TP + S c -- and
+// keeps just those fragments; on every step it supplies own[c] * bmask[j]
+// with bmask[j] = 1 for its own slot and 0 otherwise (an integer multiply:
+// exact, and off the integer / logic pipe that unpacks the codes).
+//   Q6_K:        own step c = visit my_j + S c (one K16 step per visit);
+//   Q4_K / Q5_K: own step c = sub-block my_j + S (c / 2), K16 half c % 2.
+// With one token the fragments come from the stage in shared memory; with
+// several from global memory (L1 / L2), loaded one super-block ahead of their
+// use (one token tile) so that the load latency overlaps the previous
+// super-block's arithmetic.
+template <int TYPE, int TP>
+__device__ __forceinline__ uint32_t own_col(uint32_t c, uint32_t my_j, uint32_t t) {
+    constexpr uint32_t S = 8 / TP;
+    if constexpr (TYPE == 14) {
+        const uint32_t v = my_j + S * c;
+        return 128 * (v >> 3) + 32 * (v & 3) + 16 * ((v >> 2) & 1) + 4 * t;
+    } else {
+        return 32 * (my_j + S * (c >> 1)) + 8 * t + 4 * (c & 1);
+    }
+}
+template <int TP, int NT> struct XFrags { uint2 v[2 * TP][NT]; };
 template <int TYPE, int TP, int NT>
 __device__ __forceinline__ void load_x(XFrags<TP, NT> &xs, const uint16_t *__restrict__ x, uint64_t k,
                                        uint32_t m_begin, uint32_t kb, uint32_t m_count, uint32_t g, uint32_t t) {
-    if constexpr (TP > 1) {
 #pragma unroll
-        for (int nt = 0; nt < NT; ++nt) {
-            const uint16_t *xr = x + (uint64_t)(m_begin + min(8 * nt + g % TP, m_count - 1)) * k + (uint64_t)kb * 256;
+    for (int nt = 0; nt < NT; ++nt) {
+        const uint16_t *xr = x + (uint64_t)(m_begin + min(8 * nt + g % TP, m_count - 1)) * k + (uint64_t)kb * 256;
 #pragma unroll
-            for (uint32_t si = 0; si < 16; ++si) {
-                const uint32_t kl = TYPE != 14 ? 32 * (si >> 1) + 8 * t + 4 * (si & 1)
-                                               : 128 * (si >> 3) + 32 * (si & 3) + 16 * ((si >> 2) & 1) + 4 * t;
-                xs.v[si][nt] = __ldg(reinterpret_cast<const uint2 *>(xr + kl));
-            }
-        }
+        for (uint32_t c = 0; c < 2 * TP; ++c)
+            xs.v[c][nt] = __ldg(reinterpret_cast<const uint2 *>(xr + own_col<TYPE, TP>(c, g / TP, t)));
     }
 }
 
 template <int TYPE, int TP, int NT>
-__device__ __forceinline__ void compute_stage(const uint8_t *st, const XFrags<TP, NT> &xs, uint32_t g,
-                                              uint32_t t, uint32_t lane, float *wt, float (&acc)[NT][4]) {
+__device__ __forceinline__ void compute_stage(const uint8_t *st, const XFrags<TP, NT> &xs_global, uint32_t g,
+                                              uint32_t t, uint32_t lane, const uint32_t (&bmask)[8 / TP],
+                                              float *wt, float (&acc)[NT][4]) {
     using SG = StageGeo<TYPE>;
     constexpr uint32_t S = 8 / TP;
     const uint32_t rg = row_slot(g), rg8 = row_slot(g + 8);   // slots inside the 16-row piece
@@ -246,15 +258,23 @@ __device__ __forceinline__ void compute_stage(const uint8_t *st, const XFrags<TP
         o[1] = make_float4(d * (b[0] - 128.f), d * (b[1] - 128.f), d * (b[2] - 128.f), d * (b[3] - 128.f));
     }
     __syncwarp();
-    // one token: its 256 columns of X are part of the stage
-    const uint16_t *x1 = reinterpret_cast<const uint16_t *>(st + SG::w_bytes);
     const uint32_t my_j = g / TP;
+    // one token: its 256 columns of X are part of the stage; read the own steps'
+    XFrags<TP, NT> xs_stage;
+    if constexpr (TP == 1) {
+        const uint16_t *x1 = reinterpret_cast<const uint16_t *>(st + SG::w_bytes);
+#pragma unroll
+        for (uint32_t c = 0; c < 2; ++c)
+            xs_stage.v[c][0] = *reinterpret_cast<const uint2 *>(x1 + own_col<TYPE, TP>(c, my_j, t));
+    }
+    const XFrags<TP, NT> &xs = TP == 1 ? xs_stage : xs_global;
     const uint32_t ones = 0x3F803F80u;
     constexpr float off = 128.f;   // Q4_K: the code-space offset of code_pair
     float cq[NT][4], c1[NT][4];
 
     // One K16 step of scale group visit v: A from code words (rows g, g+8).
-    auto step = [&](uint32_t v, uint32_t si, uint32_t cg, uint32_t cg8, uint32_t kloc, bool chain_start) {
+    // c = this step's own-step index (see own_col)
+    auto step = [&](uint32_t v, uint32_t c, uint32_t cg, uint32_t cg8, bool chain_start) {
         const uint32_t j = v % S;
         if (chain_start) {
 #pragma unroll
@@ -272,11 +292,8 @@ __device__ __forceinline__ void compute_stage(const uint8_t *st, const XFrags<TP
         }
 #pragma unroll
         for (int nt = 0; nt < NT; ++nt) {
-            uint2 xv;
-            if constexpr (TP == 1) xv = *reinterpret_cast<const uint2 *>(x1 + kloc);
-            else xv = xs.v[si][nt];
-            const bool on = my_j == j;
-            const uint32_t b0 = on ? xv.x : 0u, b1 = on ? xv.y : 0u;
+            const uint2 xv = xs.v[c][nt];
+            const uint32_t b0 = xv.x * bmask[j], b1 = xv.y * bmask[j];
             mma16816(cq[nt], a0, a1, a2, a3, b0, b1, cq[nt]);
             if constexpr (TYPE != 14) mma16816(c1[nt], ones, ones, ones, ones, b0, b1, c1[nt]);
         }
@@ -328,7 +345,7 @@ __device__ __forceinline__ void compute_stage(const uint8_t *st, const XFrags<TP
                         c |= (((sp ? hq.y : hq.x) >> v) & 0x01010101u) << 4;
                         c8 |= (((sp ? hq8.y : hq8.x) >> v) & 0x01010101u) << 4;
                     }
-                    step(v, 2 * v + sp, c, c8, 32 * v + 8 * t + 4 * sp, sp == 0 && v % S == 0);
+                    step(v, 2 * (v / S) + sp, c, c8, sp == 0 && v % S == 0);
                 }
                 if (v % S == S - 1) close_chain(v / S);
             }
@@ -352,8 +369,8 @@ __device__ __forceinline__ void compute_stage(const uint8_t *st, const XFrags<TP
 #pragma unroll
                 for (uint32_t grp = 0; grp < 4; ++grp) {
                     const uint32_t v = 8 * h + 4 * jj + grp;
-                    step(v, v, (lw[grp] & 0x0F0F0F0Fu) | hb[grp], (lw8[grp] & 0x0F0F0F0Fu) | hb8[grp],
-                         128 * h + 32 * grp + 16 * jj + 4 * t, v % S == 0);
+                    step(v, v / S, (lw[grp] & 0x0F0F0F0Fu) | hb[grp], (lw8[grp] & 0x0F0F0F0Fu) | hb8[grp],
+                         v % S == 0);
                     if (v % S == S - 1) close_chain(v / S);
                 }
             }
@@ -426,6 +443,9 @@ __global__ void __launch_bounds__(kWarps * 32, 4) gemv_kernel(const __grid_const
     // resident CTAs (registers): there X is loaded at the start of its own
     // super-block instead.
     constexpr bool kAhead = NT == 1;
+    uint32_t bmask[8 / TP];
+#pragma unroll
+    for (uint32_t j = 0; j < 8 / TP; ++j) bmask[j] = g / TP == j ? 1u : 0u;
     auto iteration = [&](uint32_t i, XFrags<TP, NT> &xs_cur, XFrags<TP, NT> &xs_next) {
         if (i + kGemvStages - 1 < count) {
             const uint32_t j = i + kGemvStages - 1, kb = first + kWarps * j;
@@ -436,16 +456,17 @@ __global__ void __launch_bounds__(kWarps * 32, 4) gemv_kernel(const __grid_const
         cpa_commit();
         cpa_wait<kGemvStages - 1>();
         __syncwarp();
-        if constexpr (kAhead) {
+        if constexpr (TP == 1) {
+        } else if constexpr (kAhead) {
             if (i + 1 < count) load_x<TYPE, TP, NT>(xs_next, x, k, m_begin, first + kWarps * (i + 1), m_count, g, t);
         } else {
             load_x<TYPE, TP, NT>(xs_cur, x, k, m_begin, first + kWarps * i, m_count, g, t);
         }
-        compute_stage<TYPE, TP, NT>(mine + (i % kGemvStages) * stage_bytes, xs_cur, g, t, lane, wt, acc);
+        compute_stage<TYPE, TP, NT>(mine + (i % kGemvStages) * stage_bytes, xs_cur, g, t, lane, bmask, wt, acc);
         __syncwarp();
     };
     XFrags<TP, NT> xa, xb;
-    if (kAhead && count) load_x<TYPE, TP, NT>(xa, x, k, m_begin, first, m_count, g, t);
+    if (TP > 1 && kAhead && count) load_x<TYPE, TP, NT>(xa, x, k, m_begin, first, m_count, g, t);
     for (uint32_t i = 0; i < count; i += 2) {
         iteration(i, xa, xb);
         if (i + 1 < count) iteration(i + 1, xb, xa);
