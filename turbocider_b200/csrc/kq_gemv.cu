@@ -208,21 +208,28 @@ __device__ __forceinline__ uint32_t own_col(uint32_t c, uint32_t my_j, uint32_t 
         return 32 * (my_j + S * (c >> 1)) + 8 * t + 4 * (c & 1);
     }
 }
-template <int TP, int NT> struct XFrags { uint2 v[2 * TP][NT]; };
-template <int TYPE, int TP, int NT>
-__device__ __forceinline__ void load_x(XFrags<TP, NT> &xs, const uint16_t *__restrict__ x, uint64_t k,
-                                       uint32_t m_begin, uint32_t kb, uint32_t m_count, uint32_t g, uint32_t t) {
+// N own steps' fragments (N = 2 TP: a whole super-block; 8: half of one).
+template <int N, int NT> struct XFrags { uint2 v[N][NT]; };
+template <int TYPE, int TP, int NT, int N>
+__device__ __forceinline__ void load_x(XFrags<N, NT> &xs, const uint16_t *__restrict__ x, uint64_t k,
+                                       uint32_t m_begin, uint32_t kb, uint32_t m_count, uint32_t g, uint32_t t,
+                                       uint32_t c_begin) {
 #pragma unroll
     for (int nt = 0; nt < NT; ++nt) {
         const uint16_t *xr = x + (uint64_t)(m_begin + min(8 * nt + g % TP, m_count - 1)) * k + (uint64_t)kb * 256;
 #pragma unroll
-        for (uint32_t c = 0; c < 2 * TP; ++c)
-            xs.v[c][nt] = __ldg(reinterpret_cast<const uint2 *>(xr + own_col<TYPE, TP>(c, g / TP, t)));
+        for (uint32_t c = 0; c < (uint32_t)N; ++c)
+            xs.v[c][nt] = __ldg(reinterpret_cast<const uint2 *>(xr + own_col<TYPE, TP>(c_begin + c, g / TP, t)));
     }
 }
 
-template <int TYPE, int TP, int NT>
-__device__ __forceinline__ void compute_stage(const uint8_t *st, const XFrags<TP, NT> &xs_global, uint32_t g,
+// Halves [H0, H1) of one super-block (weights 128 H0 .. 128 H1 - 1 of its
+// rows); the scale table is built with half 0.  The own-step fragments in
+// xs_global start at own step C0 (0, or 8 for a second-half call; halves are
+// only computed separately with 8 tokens per tile, where every chain is
+// within a half).
+template <int TYPE, int TP, int NT, int N, uint32_t H0 = 0, uint32_t H1 = 2, uint32_t C0 = 0>
+__device__ __forceinline__ void compute_stage(const uint8_t *st, const XFrags<N, NT> &xs_global, uint32_t g,
                                               uint32_t t, uint32_t lane, const uint32_t (&bmask)[8 / TP],
                                               float *wt, float (&acc)[NT][4]) {
     using SG = StageGeo<TYPE>;
@@ -231,6 +238,7 @@ __device__ __forceinline__ void compute_stage(const uint8_t *st, const XFrags<TP
     const uint32_t half = lane & 1, rr = lane >> 1;
     // Scale table, written by all lanes: row rr, half `half` of its groups.
     //   Q4_K: float2 (d*sc_g, dmin*m_g) [16][8];  Q6_K: float d*sc_i [16][16].
+    if constexpr (H0 == 0) {
     __syncwarp();
     if constexpr (TYPE != 14) {
         const uint32_t dm = lds32(st + SG::dm + rr * 4);
@@ -258,16 +266,17 @@ __device__ __forceinline__ void compute_stage(const uint8_t *st, const XFrags<TP
         o[1] = make_float4(d * (b[0] - 128.f), d * (b[1] - 128.f), d * (b[2] - 128.f), d * (b[3] - 128.f));
     }
     __syncwarp();
+    }
     const uint32_t my_j = g / TP;
     // one token: its 256 columns of X are part of the stage; read the own steps'
-    XFrags<TP, NT> xs_stage;
+    XFrags<N, NT> xs_stage;
     if constexpr (TP == 1) {
         const uint16_t *x1 = reinterpret_cast<const uint16_t *>(st + SG::w_bytes);
 #pragma unroll
         for (uint32_t c = 0; c < 2; ++c)
             xs_stage.v[c][0] = *reinterpret_cast<const uint2 *>(x1 + own_col<TYPE, TP>(c, my_j, t));
     }
-    const XFrags<TP, NT> &xs = TP == 1 ? xs_stage : xs_global;
+    const XFrags<N, NT> &xs = TP == 1 ? xs_stage : xs_global;
     const uint32_t ones = 0x3F803F80u;
     constexpr float off = 128.f;   // Q4_K: the code-space offset of code_pair
     float cq[NT][4], c1[NT][4];
@@ -292,7 +301,7 @@ __device__ __forceinline__ void compute_stage(const uint8_t *st, const XFrags<TP
         }
 #pragma unroll
         for (int nt = 0; nt < NT; ++nt) {
-            const uint2 xv = xs.v[c][nt];
+            const uint2 xv = xs.v[c - C0][nt];
             const uint32_t b0 = xv.x * bmask[j], b1 = xv.y * bmask[j];
             mma16816(cq[nt], a0, a1, a2, a3, b0, b1, cq[nt]);
             if constexpr (TYPE != 14) mma16816(c1[nt], ones, ones, ones, ones, b0, b1, c1[nt]);
@@ -331,7 +340,7 @@ __device__ __forceinline__ void compute_stage(const uint8_t *st, const XFrags<TP
             hq8 = *reinterpret_cast<const uint2 *>(st + StageGeo<13>::qh + rg8 * 32 + 8 * t);
         }
 #pragma unroll
-        for (uint32_t q = 0; q < 4; ++q) {
+        for (uint32_t q = 2 * H0; q < 2 * H1; ++q) {
             const uint2 wg = *reinterpret_cast<const uint2 *>(st + SG::qs + q * 512 + rg * 32 + 8 * t);
             const uint2 wg8 = *reinterpret_cast<const uint2 *>(st + SG::qs + q * 512 + rg8 * 32 + 8 * t);
 #pragma unroll
@@ -352,7 +361,7 @@ __device__ __forceinline__ void compute_stage(const uint8_t *st, const XFrags<TP
         }
     } else {
 #pragma unroll
-        for (uint32_t h = 0; h < 2; ++h) {
+        for (uint32_t h = H0; h < H1; ++h) {
 #pragma unroll
             for (uint32_t jj = 0; jj < 2; ++jj) {
                 const uint32_t o0 = SG::ql + (h * 2) * 512 + 16 * jj + 4 * t;
@@ -446,7 +455,7 @@ __global__ void __launch_bounds__(kWarps * 32, 4) gemv_kernel(const __grid_const
     uint32_t bmask[8 / TP];
 #pragma unroll
     for (uint32_t j = 0; j < 8 / TP; ++j) bmask[j] = g / TP == j ? 1u : 0u;
-    auto iteration = [&](uint32_t i, XFrags<TP, NT> &xs_cur, XFrags<TP, NT> &xs_next) {
+    auto refill_and_wait = [&](uint32_t i) {
         if (i + kGemvStages - 1 < count) {
             const uint32_t j = i + kGemvStages - 1, kb = first + kWarps * j;
             uint8_t *sj = mine + (j % kGemvStages) * stage_bytes;
@@ -456,20 +465,45 @@ __global__ void __launch_bounds__(kWarps * 32, 4) gemv_kernel(const __grid_const
         cpa_commit();
         cpa_wait<kGemvStages - 1>();
         __syncwarp();
-        if constexpr (TP == 1) {
-        } else if constexpr (kAhead) {
-            if (i + 1 < count) load_x<TYPE, TP, NT>(xs_next, x, k, m_begin, first + kWarps * (i + 1), m_count, g, t);
-        } else {
-            load_x<TYPE, TP, NT>(xs_cur, x, k, m_begin, first + kWarps * i, m_count, g, t);
-        }
-        compute_stage<TYPE, TP, NT>(mine + (i % kGemvStages) * stage_bytes, xs_cur, g, t, lane, bmask, wt, acc);
-        __syncwarp();
     };
-    XFrags<TP, NT> xa, xb;
-    if (TP > 1 && kAhead && count) load_x<TYPE, TP, NT>(xa, x, k, m_begin, first, m_count, g, t);
-    for (uint32_t i = 0; i < count; i += 2) {
-        iteration(i, xa, xb);
-        if (i + 1 < count) iteration(i + 1, xb, xa);
+    if constexpr (kAhead) {
+        // One super-block per iteration: refill the slot computed in the
+        // previous iteration (every lane is past it: __syncwarp at the end of
+        // the iteration), wait for this one's stage, load the next
+        // super-block's X fragments (several tokens), compute.
+        using XF = XFrags<2 * TP, NT>;
+        auto iteration = [&](uint32_t i, XF &xs_cur, XF &xs_next) {
+            refill_and_wait(i);
+            if constexpr (TP > 1)
+                if (i + 1 < count)
+                    load_x<TYPE, TP, NT>(xs_next, x, k, m_begin, first + kWarps * (i + 1), m_count, g, t, 0);
+            compute_stage<TYPE, TP, NT>(mine + (i % kGemvStages) * stage_bytes, xs_cur, g, t, lane, bmask, wt, acc);
+            __syncwarp();
+        };
+        XF xa, xb;
+        if (TP > 1 && count) load_x<TYPE, TP, NT>(xa, x, k, m_begin, first, m_count, g, t, 0);
+        for (uint32_t i = 0; i < count; i += 2) {
+            iteration(i, xa, xb);
+            if (i + 1 < count) iteration(i + 1, xb, xa);
+        }
+    } else {
+        // Two token tiles (8 tokens each): a second whole-super-block fragment
+        // set would cost resident CTAs (registers), so X runs half a
+        // super-block ahead instead -- half 1's fragments load while half 0
+        // computes, the next super-block's half 0 while half 1 computes.
+        using XF = XFrags<8, NT>;
+        XF xa, xb;
+        if (count) load_x<TYPE, TP, NT>(xa, x, k, m_begin, first, m_count, g, t, 0);
+        for (uint32_t i = 0; i < count; ++i) {
+            refill_and_wait(i);
+            const uint8_t *st = mine + (i % kGemvStages) * stage_bytes;
+            const uint32_t kb = first + kWarps * i;
+            load_x<TYPE, TP, NT>(xb, x, k, m_begin, kb, m_count, g, t, 8);
+            compute_stage<TYPE, TP, NT, 8, 0, 1, 0>(st, xa, g, t, lane, bmask, wt, acc);
+            if (i + 1 < count) load_x<TYPE, TP, NT>(xa, x, k, m_begin, kb + kWarps, m_count, g, t, 0);
+            compute_stage<TYPE, TP, NT, 8, 1, 2, 8>(st, xb, g, t, lane, bmask, wt, acc);
+            __syncwarp();
+        }
     }
     // Columns of one token are spread over the quad (TP < 8): sum them so that
     // every lane holds the full value of its (row, token) pairs.
