@@ -23,8 +23,8 @@
 // Work split: CTA (x, y) = (16 weight rows, one K slice of 4 super-blocks),
 // 4 warps each taking one super-block, so that thousands of short CTAs keep
 // every SM's loads in flight (the CTA count is independent of the SM count).
-// Each warp streams its super-blocks' packed fields through a 3-stage ring of
-// per-lane cp.async copies.  With one token (TP = 1) the stage also carries
+// Each warp streams its super-blocks' packed fields through a ring of 3 (2
+// with more than 8 tokens) stages of per-lane cp.async copies.  With one token (TP = 1) the stage also carries
 // that token's 256 columns of X (512 B); with more tokens X is read straight
 // from global memory instead (at most 16 rows x K, the same for every row
 // tile, so it stays in L1 / L2), all of a super-block's X fragments at once:
@@ -387,10 +387,11 @@ __device__ __forceinline__ void compute_stage(const uint8_t *st, const XFrags<N,
     }
 }
 
-#ifndef TC_GEMV_STAGES
-#define TC_GEMV_STAGES 3
-#endif
-constexpr uint32_t kGemvStages = TC_GEMV_STAGES;
+// Depth of each warp's stage ring: 3 stages, except with two token tiles
+// (M > 8), where 2 stages leave room for more resident CTAs (measured: per
+// call at M = 16, 19.0 -> 18.0 us; at M = 1 a 2-stage ring is slower).
+template <int NT>
+constexpr uint32_t gemv_stages() { return NT == 2 ? 2u : 3u; }
 
 // Weights of one launch: blockIdx.x runs over the 16-row tiles of all of
 // them (entry e owns tiles [tile_begin, next entry's tile_begin)); they share
@@ -418,6 +419,7 @@ __global__ void __launch_bounds__(kWarps * 32, 4) gemv_kernel(const __grid_const
     const uint8_t *pbase = w.chunks + (uint64_t)panel * b.kb * chunk;
     constexpr bool kStageX = TP == 1;
     constexpr uint32_t stage_bytes = (SG::w_bytes + (kStageX ? 512u : 0u) + 127) / 128 * 128;
+    constexpr uint32_t kGemvStages = gemv_stages<NT>();
     uint8_t *mine = dyn + (size_t)warp * kGemvStages * stage_bytes;
     float *wt = tab[warp];
 
@@ -625,13 +627,13 @@ cudaError_t launch_typed(const GemvBatch &bt, uint32_t tiles, uint32_t m_begin, 
                          uint64_t k, int out_dtype, const GemvSplit &sp, cudaStream_t s) {
     const dim3 grid(tiles, sp.n_slices);
     const size_t stage = (StageGeo<TYPE>::w_bytes + (TP == 1 ? 512u : 0u) + 127) / 128 * 128;
-    const size_t smem = stage * kGemvStages * kWarps;
+    const size_t smem = stage * gemv_stages<NT>() * kWarps;
     auto kern = out_dtype == 0 ? gemv_kernel<TYPE, TP, NT, 0>
                 : out_dtype == 1 ? gemv_kernel<TYPE, TP, NT, 1> : gemv_kernel<TYPE, TP, NT, 2>;
-    // Opt in once per instantiation to the largest stage set (16 tokens).
+    // Opt in once per instantiation to its shared-memory size.
     static bool configured[3] = {false, false, false};
     if (!configured[out_dtype]) {
-        const int most = (int)((StageGeo<TYPE>::w_bytes + (TP == 1 ? 512u : 0u) + 127) / 128 * 128 * kGemvStages * kWarps);
+        const int most = (int)smem;
         cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, most);
         if (e != cudaSuccess) return e;
         configured[out_dtype] = true;
