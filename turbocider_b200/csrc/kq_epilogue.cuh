@@ -23,12 +23,19 @@ namespace tc {
 
 __device__ __forceinline__ uint32_t glu_column(uint32_t n) { return (n >> 4) * 8 + (n & 7); }
 
+// t * logistic(z) = t / (1 + e^-z), with the fast exponential and division:
+// relative error ~1e-6 (the exponent's rounding, scaled by |z| <~ 20 where it
+// matters), far below every output dtype's rounding.  For very negative z the
+// denominator overflows to +inf and the quotient is 0, the limit.
+__device__ __forceinline__ float times_logistic(float t, float z) { return __fdividef(t, 1.f + __expf(-z)); }
+// tanh-form GELU, 0.5 t (1 + tanh(u)) with u = sqrt(2/pi) (t + 0.044715 t^3),
+// written as t * logistic(2u) (1 + tanh(u) = 2 logistic(2u)).
 __device__ __forceinline__ float gelu_tanh(float t) {
     const float u = 0.7978845608028654f * (t + 0.044715f * t * t * t);   // sqrt(2/pi)
-    return 0.5f * t * (1.f + tanhf(u));
+    return times_logistic(t, 2.f * u);
 }
 __device__ __forceinline__ float gelu_erf(float t) { return 0.5f * t * (1.f + erff(t * 0.7071067811865476f)); }
-__device__ __forceinline__ float silu(float t) { return t / (1.f + expf(-t)); }
+__device__ __forceinline__ float silu(float t) { return times_logistic(t, t); }
 
 // Per output row (weight row n of the tile) state of the fused epilogue.
 struct EpiRow {

@@ -529,18 +529,15 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
             const uint32_t taddr = tmem + ((quad * 32) << 16);
             uint32_t tma_pieces = 0;   // bit j: piece j goes out by TMA
             const bool f16 = p.epi.out_f16;
-            if (p.epi.flags) {
-                // fused epilogue: direct stores (SwiGLU halves the columns)
-                const EpiRow er = epi_row(p.epi, min(n, p.n - 1), T.gate_row);
-#pragma unroll 1
-                for (uint32_t j = 0; j < kTileTokens / 32; ++j) {
-                    const uint32_t t0 = T.m0 + 32 * j;
-                    if (t0 >= T.m_end || n0 >= p.n) break;
-                    uint32_t v[32];
-                    tmem_ld32(taddr + 32 * j, v);
-                    epi_piece<OUT_F32>(p.epi, er, v, n < p.n, t0, T.m_end, p.y, p.ldy);
-                }
-            } else {
+            // Fused epilogue (p.epi.flags): bias / GELU / SwiGLU are applied on
+            // the way into the staging box, so the accumulator is held no
+            // longer than for a plain store; a SwiGLU box is 32 tokens x the
+            // warp's 16 outputs (its gate rows).  Pieces that cannot go out by
+            // TMA (ragged ends, f32 output, gated residual: the host leaves
+            // y_tma 0) take the direct per-element path.
+            const uint32_t fl = p.epi.flags;
+            const bool glu = fl & TC_EPI_SWIGLU;
+            const EpiRow er = fl ? epi_row(p.epi, min(n, p.n - 1), T.gate_row) : EpiRow{0.f, 0.f, n, true};
 #pragma unroll 1
             for (uint32_t j = 0; j < kTileTokens / 32; ++j) {
                 const uint32_t t0 = T.m0 + 32 * j;
@@ -551,9 +548,37 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
                 // would write up to the next 16-byte boundary of the row.
                 if (!OUT_F32 && p.y_tma && t0 + 32 <= T.m_end && n0 + 32 <= p.n) {
                     tma_pieces |= 1u << j;
-                    uint16_t *sb = reinterpret_cast<uint16_t *>(stage + j * L::e_box) + lane;
+                    if (!fl) {
+                        uint16_t *sb = reinterpret_cast<uint16_t *>(stage + j * L::e_box) + lane;
 #pragma unroll
-                    for (uint32_t c = 0; c < 32; ++c) sb[c * 32] = to16(__uint_as_float(v[c]), f16);
+                        for (uint32_t c = 0; c < 32; ++c) sb[c * 32] = to16(__uint_as_float(v[c]), f16);
+                    } else if (glu) {
+                        // gate lane L (L & 8 == 0) pairs with up lane L + 8
+                        uint16_t *sb = reinterpret_cast<uint16_t *>(stage + j * L::e_box) + (lane >> 4) * 8 + (lane & 7);
+#pragma unroll
+                        for (uint32_t c = 0; c < 32; ++c) {
+                            const float t = __uint_as_float(v[c]) + er.bias;
+                            const float up = __shfl_down_sync(0xffffffffu, t, 8);
+                            if (er.writer) sb[c * 16] = to16(silu(t) * up, f16);
+                        }
+                    } else {
+                        uint16_t *sb = reinterpret_cast<uint16_t *>(stage + j * L::e_box) + lane;
+                        if (fl & TC_EPI_GELU_TANH) {
+#pragma unroll
+                            for (uint32_t c = 0; c < 32; ++c)
+                                sb[c * 32] = to16(gelu_tanh(__uint_as_float(v[c]) + er.bias), f16);
+                        } else if (fl & TC_EPI_GELU_ERF) {
+#pragma unroll
+                            for (uint32_t c = 0; c < 32; ++c)
+                                sb[c * 32] = to16(gelu_erf(__uint_as_float(v[c]) + er.bias), f16);
+                        } else {
+#pragma unroll
+                            for (uint32_t c = 0; c < 32; ++c) sb[c * 32] = to16(__uint_as_float(v[c]) + er.bias, f16);
+                        }
+                    }
+                } else if (fl) {
+                    // all lanes: the SwiGLU pairing shuffles
+                    epi_piece<OUT_F32>(p.epi, er, v, n < p.n, t0, T.m_end, p.y, p.ldy);
                 } else if (n < p.n) {
 #pragma unroll
                     for (uint32_t c = 0; c < 32; ++c) {
@@ -562,7 +587,6 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
                             store_out_all(p.epi, p.y, (uint64_t)m * p.ldy + n, __uint_as_float(v[c]), OUT_F32, f16);
                     }
                 }
-            }
             }
             // Every TMEM load has completed (tcgen05.ld waits): hand D back.
             tc_fence_before();
@@ -576,7 +600,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
                     for (uint32_t d = 0; d <= p.epi.n_peer; ++d)
                         for (uint32_t j = 0; j < kTileTokens / 32; ++j)
                             if (tma_pieces & (1u << j))
-                                tma_store_2d(&ymaps.m[d], su32(stage + j * L::e_box), (int)n0, (int)(T.m0 + 32 * j));
+                                tma_store_2d(&ymaps.m[d], su32(stage + j * L::e_box), (int)(glu ? n0 / 2 : n0),
+                                             (int)(T.m0 + 32 * j));
                     bulk_commit();
                 }
             }
@@ -685,10 +710,13 @@ cudaError_t launch_gemm_pair(const SegmentView *segs, uint32_t n_seg, const uint
     memset(&ym, 0, sizeof(ym));
     bool aligned = (reinterpret_cast<uintptr_t>(y) & 15u) == 0 && (ldy * 2) % 16 == 0;
     for (uint32_t d = 0; d < p.epi.n_peer; ++d) aligned &= (reinterpret_cast<uintptr_t>(p.epi.peer[d]) & 15u) == 0;
-    if (!out_f32 && !p.epi.flags && aligned) {
-        const cuuint64_t ydims[2] = {p.n, m_total};
+    if (!out_f32 && !(p.epi.flags & TC_EPI_GATE_RESIDUAL) && aligned) {
+        // SwiGLU: Y has one column per gate / up row pair, and a warp's box is
+        // its 16 outputs wide
+        const bool glu = p.epi.flags & TC_EPI_SWIGLU;
+        const cuuint64_t ydims[2] = {glu ? p.n / 2 : p.n, m_total};
         const cuuint64_t ystrides[1] = {ldy * 2};
-        const cuuint32_t ybox[2] = {32u, 32u};
+        const cuuint32_t ybox[2] = {glu ? 16u : 32u, 32u};
         bool ok = true;
         for (uint32_t d = 0; d <= p.epi.n_peer && ok; ++d) {
             void *base = d == 0 ? y : p.epi.peer[d - 1];
