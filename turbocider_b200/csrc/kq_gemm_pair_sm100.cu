@@ -553,13 +553,17 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
 #pragma unroll
                         for (uint32_t c = 0; c < 32; ++c) sb[c * 32] = to16(__uint_as_float(v[c]), f16);
                     } else if (glu) {
-                        // gate lane L (L & 8 == 0) pairs with up lane L + 8
+                        // gate lane L (L & 8 == 0) pairs with up lane L + 8.
+                        // Every lane computes (no divergent branch in the
+                        // loop); only the gate lanes' stores take effect.
                         uint16_t *sb = reinterpret_cast<uint16_t *>(stage + j * L::e_box) + (lane >> 4) * 8 + (lane & 7);
+                        const bool wr = er.writer;
 #pragma unroll
                         for (uint32_t c = 0; c < 32; ++c) {
                             const float t = __uint_as_float(v[c]) + er.bias;
                             const float up = __shfl_down_sync(0xffffffffu, t, 8);
-                            if (er.writer) sb[c * 16] = to16(silu(t) * up, f16);
+                            const uint16_t o = to16(silu(t) * up, f16);
+                            if (wr) sb[c * 16] = o;
                         }
                     } else {
                         uint16_t *sb = reinterpret_cast<uint16_t *>(stage + j * L::e_box) + lane;
