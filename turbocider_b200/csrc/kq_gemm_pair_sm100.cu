@@ -553,17 +553,22 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
 #pragma unroll
                         for (uint32_t c = 0; c < 32; ++c) sb[c * 32] = to16(__uint_as_float(v[c]), f16);
                     } else if (glu) {
-                        // gate lane L (L & 8 == 0) pairs with up lane L + 8.
-                        // Every lane computes (no divergent branch in the
-                        // loop); only the gate lanes' stores take effect.
-                        uint16_t *sb = reinterpret_cast<uint16_t *>(stage + j * L::e_box) + (lane >> 4) * 8 + (lane & 7);
-                        const bool wr = er.writer;
+                        // Gate lane L (L & 8 == 0) and up lane L + 8 share
+                        // output column (L >> 4) * 8 + (L & 7): the gate lane
+                        // produces tokens 0-15 of the piece, the up lane 16-31,
+                        // each fetching the partner's value with one shuffle.
+                        // No divergent branch in the loop.
+                        const bool gate_lane = er.writer;
+                        uint16_t *sb = reinterpret_cast<uint16_t *>(stage + j * L::e_box) + (lane >> 4) * 8 + (lane & 7) +
+                                       (gate_lane ? 0 : 16 * 16);
 #pragma unroll
-                        for (uint32_t c = 0; c < 32; ++c) {
-                            const float t = __uint_as_float(v[c]) + er.bias;
-                            const float up = __shfl_down_sync(0xffffffffu, t, 8);
-                            const uint16_t o = to16(silu(t) * up, f16);
-                            if (wr) sb[c * 16] = o;
+                        for (uint32_t c = 0; c < 16; ++c) {
+                            const float lo = __uint_as_float(v[c]) + er.bias;        // token c
+                            const float hi = __uint_as_float(v[c + 16]) + er.bias;   // token c + 16
+                            const float up_lo = __shfl_down_sync(0xffffffffu, lo, 8);    // to the gate lane
+                            const float gate_hi = __shfl_up_sync(0xffffffffu, hi, 8);    // to the up lane
+                            const float g = gate_lane ? lo : gate_hi, u = gate_lane ? up_lo : hi;
+                            sb[c * 16] = to16(silu(g) * u, f16);
                         }
                     } else {
                         uint16_t *sb = reinterpret_cast<uint16_t *>(stage + j * L::e_box) + lane;
