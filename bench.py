@@ -162,8 +162,10 @@ def run_reference(args):
 
 
 # ---------------------------------------------------------------- GPU arm
-def build_weights(ctx, rank, world, layers, device):
-    """Upload every layer's weight shard (turbocider_b200.shard.shard_rows) to HBM."""
+def build_weights(ctx, rank, world, layers, device, ffn: str = "separate"):
+    """Upload every layer's weight shard (turbocider_b200.shard.shard_rows) to HBM.
+    ffn "swiglu": w1 and w3 go up as one interleaved weight "w13" whose GEMM
+    epilogue computes silu(w1 x) * w3 x (tc_cuda_weight_upload_glu)."""
     import torch
     from turbocider_b200 import cuda as tcc
     from turbocider_b200 import shard
@@ -182,6 +184,11 @@ def build_weights(ctx, rank, world, layers, device):
         for name, n, k, typ in layer_linears(layer):
             raw, rows, kk, t = raw_cache[(layer % DISTINCT_LAYERS, name)]
             assert t == typ
+            if ffn == "swiglu" and name in ("w1", "w3"):
+                if name == "w1":
+                    up = raw_cache[(layer % DISTINCT_LAYERS, "w3")]
+                    lw["w13"] = tcc.Weight.upload_glu(ctx, typ, rows, kk, raw, up[0])
+                continue
             lw[name] = tcc.Weight.upload(ctx, typ, rows, kk, raw)
         weights.append(lw)
     return weights
@@ -349,6 +356,53 @@ def config4_stream(ctx, device, passes: int = 2):
             "passes": passes}
 
 
+def epilogue_measure(ctx, device):
+    """Fused epilogues on config-5 shapes (M = 8448, K = 3840, fp16 activations
+    and staging, bf16 out): the qkv weight plain, with a bias, with bias + GELU;
+    a 20480-row weight plain and as the SwiGLU pair w1 / w3 (one output per
+    gate / up row pair).  Each timed over 10 calls with CUDA events."""
+    import torch
+    from turbocider_b200 import cuda as tcc
+    threads = os.cpu_count() or 1
+    m = M_TOKENS
+
+    def raw(n, seed):
+        g = torch.Generator(device=device).manual_seed(seed)
+        w = torch.randn(n, HIDDEN, generator=g, device=device).mul_(0.02)
+        return tcc.quantize(Q4_K, w.cpu().numpy(), threads=threads)
+    w_qkv = tcc.Weight.upload(ctx, Q4_K, 3 * HIDDEN, HIDDEN, raw(3 * HIDDEN, 71))
+    r1, r3 = raw(FFN, 72), raw(FFN, 73)
+    w_glu = tcc.Weight.upload_glu(ctx, Q4_K, FFN, HIDDEN, r1, r3)
+    w_2f = tcc.Weight.upload(ctx, Q4_K, 2 * FFN, HIDDEN, raw(2 * FFN, 74))
+    g = torch.Generator(device=device).manual_seed(75)
+    x = torch.randn(m, HIDDEN, generator=g, device=device).to(torch.float16)
+    b_qkv = torch.randn(3 * HIDDEN, generator=g, device=device) * 0.1
+    b_glu = torch.randn(2 * FFN, generator=g, device=device) * 0.1
+    s = torch.cuda.Stream(device)
+
+    def tflops(w, **kw):
+        out = torch.empty(m, w.n_out, dtype=torch.bfloat16, device=device)
+        call = lambda: tcc.qlinear(ctx, w, x, out=out, stage=tcc.STAGE_F16_X16, stream=s, **kw)
+        with torch.cuda.stream(s):
+            for _ in range(3):
+                call()
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record(s)
+            for _ in range(10):
+                call()
+            e1.record(s)
+            e1.synchronize()
+        return round(2.0 * m * w.n * w.k * 10 / (e0.elapsed_time(e1) / 1e3) / 1e12, 1)
+    res = {"config": "config-5 shapes, M = 8448, K = 3840, X fp16, bf16 out; TFLOP/s of 2 M N K",
+           "qkv_plain": tflops(w_qkv), "qkv_bias": tflops(w_qkv, bias=b_qkv),
+           "qkv_bias_gelu_tanh": tflops(w_qkv, bias=b_qkv, activation="gelu_tanh"),
+           "rows20480_plain": tflops(w_2f), "w1_w3_swiglu_bias": tflops(w_glu, bias=b_glu)}
+    assert ctx.status() == 0
+    for w in (w_qkv, w_glu, w_2f):
+        w.free()
+    return res
+
+
 def run_ours(args):
     import torch
     import torch.distributed as dist
@@ -371,7 +425,7 @@ def run_ours(args):
     if reserve:
         # leave SMs free for the NCCL all-gather that runs beside each GEMM
         ctx.set_sm_limit(torch.cuda.get_device_properties(device).multi_processor_count - reserve)
-    weights = build_weights(ctx, rank, world, layers, device)
+    weights = build_weights(ctx, rank, world, layers, device, args.ffn)
 
     m = M_TOKENS
     g = torch.Generator(device=device).manual_seed(7)
@@ -383,8 +437,11 @@ def run_ours(args):
     compute = torch.cuda.Stream(device)
     comm = torch.cuda.Stream(device)
     names = [l[0] for l in layer_linears(0)]
+    if args.ffn == "swiglu":
+        names = ["w13" if nm == "w1" else nm for nm in names if nm != "w3"]
     from turbocider_b200 import shard
     nloc = {name: shard.rows_per_rank(n, world) for name, n, _, _ in layer_linears(0)}
+    nloc["w13"] = nloc["w1"]   # SwiGLU: one output column per gate / up row pair
     fused = world > 1 and args.gather == "fused"
     pg = None
     if fused:
@@ -396,7 +453,7 @@ def run_ours(args):
         pg = PeerGroup(ctx, timeout_us=20_000_000)
         y_sym = {(name, b): pg.alloc(m * world * nloc[name] * 2) for name in names for b in (0, 1)}
         y_all = {key: buf.tensor((m, world * nloc[key[0]]), torch.bfloat16) for key, buf in y_sym.items()}
-        y_loc = {key: y_all[key][:, rank * nloc[key[0]]:rank * nloc[key[0]] + weights[0][key[0]].n]
+        y_loc = {key: y_all[key][:, rank * nloc[key[0]]:rank * nloc[key[0]] + weights[0][key[0]].n_out]
                  for key in y_all}
         y_peers = {key: pg.peers_of(buf, rank * nloc[key[0]] * 2) for key, buf in y_sym.items()}
     else:
@@ -500,10 +557,12 @@ def run_ours(args):
 
     gemv = None
     streamed = None
+    epilogues = None
     cpu = None
     if rank == 0 and world == 1 and not args.no_extras:
         gemv = gemv_measure(ctx, device, hbm_peak)
         streamed = config4_stream(ctx, device)
+        epilogues = epilogue_measure(ctx, device)
         # bounded CPU sample: layer 0 at cpu_rows rows, repeated until >= 10 s of work
         linears, threads = make_cpu_linears(0), os.cpu_count() or 1
         cpu_rows = args.cpu_rows or M_TOKENS
@@ -532,6 +591,8 @@ def run_ours(args):
                 "config": {"workload": "config5_zimage_6b_linear_stack", "layers": layers, "m_tokens": m,
                            "operands": "X fp16, W dequantised to fp16 in TMEM, fp32 accumulate, bf16 Y",
                            "hidden": HIDDEN, "ffn": FFN, "mix": "Q4_K_M (w2 Q6_K in even layers)",
+                           "ffn_form": ("SwiGLU: w1 / w3 as one weight, silu(w1 x) * w3 x in the GEMM epilogue"
+                                        if args.ffn == "swiglu" else "w1, w3 as separate linears (no SwiGLU op)"),
                            "parallelism": ("single GPU" if world == 1 else
                                            f"N-shard x{world}, all-gather fused into the GEMM epilogue (NVLink "
                                            f"peer stores) + device flag barrier per linear" if fused else
@@ -553,6 +614,7 @@ def run_ours(args):
         if gemv:
             line["gemv"] = gemv
             line["config4_streamed"] = streamed
+            line["epilogues"] = epilogues
         print(json.dumps(line), flush=True)
     for lw in weights:
         for wt in lw.values():
@@ -579,6 +641,8 @@ def main():
     ap.add_argument("--no-extras", action="store_true", help="skip the GEMV and CPU-baseline legs")
     ap.add_argument("--gather", choices=["fused", "nccl"], default="fused",
                     help="N>1: all-gather fused into the GEMM epilogue (peer stores) or NCCL after each GEMM")
+    ap.add_argument("--ffn", choices=["swiglu", "separate"], default="separate",
+                    help="FFN input projections: one SwiGLU-fused weight (silu(w1 x) * w3 x) or two plain linears")
     ap.add_argument("--reserve-sms", type=int, default=None,
                     help="SMs kept free of the GEMM for the all-gather (default 0: measured no gain at N=2)")
     args = ap.parse_args()
