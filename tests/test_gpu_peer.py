@@ -61,6 +61,45 @@ def test_replicas_receive_every_output(ctx, where, out_dtype, epilogue):
     assert torch.equal(ys[0], ys[1]) and torch.equal(ys[0], ys[2])
 
 
+@pytest.mark.parametrize("where", list(PATHS))
+@pytest.mark.parametrize("out_dtype", [0, 2])
+def test_swiglu_replicas_receive_every_output(ctx, where, out_dtype):
+    """A SwiGLU weight (one output per gate / up row pair) with N-column
+    replicas: this rank's 320 outputs [256, 576) of 1024 land in Y and in both
+    replicas, nothing outside that range is touched (the pair kernel's
+    16-output TMA boxes included)."""
+    import torch
+    from turbocider_b200 import cuda as tcc
+    m, path, staging, f32b = PATHS[where]
+    f, k, n_total, col = 320, 768, 1024, 256
+    rg = tcc.quantize(12, kq_cases.synthetic_weight(f, k, seed=31))
+    ru = tcc.quantize(12, kq_cases.synthetic_weight(f, k, seed=32))
+    w = tcc.Weight.upload_glu(ctx, 12, f, k, rg, ru)
+    xb = kq_cases.synthetic_x_bf16(m, k, seed=33)
+    x = torch.from_numpy(xb.view(np.int16)).view(torch.bfloat16).cuda()
+    tdt = tcc._torch_dtype(out_dtype)
+    sentinel = 7.0
+    ys = [torch.full((m, n_total), sentinel, device="cuda", dtype=tdt) for _ in range(3)]
+    item = ys[0].element_size()
+    bias = np.random.default_rng(34).standard_normal(2 * f).astype(np.float32) * 0.5
+    ctx.set_path(path)
+    try:
+        tcc.qlinear(ctx, w, x, out=ys[0][:, col:col + f], out_dtype=out_dtype, bias=torch.from_numpy(bias).cuda(),
+                    peers=[ys[1].data_ptr() + col * item, ys[2].data_ptr() + col * item])
+    finally:
+        ctx.set_path(0)
+    assert ctx.status() == 0
+    acc = np.concatenate([oracle.qlinear_ref(xb, rg, 12, f, k, staging), oracle.qlinear_ref(xb, ru, 12, f, k, staging)],
+                         axis=1)
+    ref = oracle.epilogue_ref(acc, bias=bias, glu=True)
+    bound = f32b if out_dtype == 0 else 3e-3
+    for y in ys:
+        h = y.float().cpu().numpy()
+        assert oracle.rel_l2(h[:, col:col + f], ref) <= bound
+        assert np.all(h[:, :col] == sentinel) and np.all(h[:, col + f:] == sentinel)
+    assert torch.equal(ys[0], ys[1]) and torch.equal(ys[0], ys[2])
+
+
 def test_dense_weight_replicas(ctx):
     import torch
     from turbocider_b200 import cuda as tcc
