@@ -9,10 +9,14 @@ tokens (1024x1024 image: 4096 image + 128 text tokens, CFG 2).  Q4_K_M mix:
 every tensor Q4_K except w2 (ffn_down), which is Q6_K in even layers.
 Weights ~ N(0, 0.02), activations ~ N(0, 1) bf16, all synthetic.
 
-A step is one pass of the hot path over the batch: 150 quantised linears.
-With --gpus N each weight is N-column sharded across the ranks (one process
-per GPU) and every linear's bf16 output is all-gathered over NVLink with NCCL,
-overlapped with the next linear's GEMM.  Prints one JSON line (rank 0).
+A step is one pass of the hot path over the batch: every layer's qkv, out,
+w1 / w3 and w2 projections (the FLOPs of 150 quantised linears).  By default
+(--ffn swiglu) w1 and w3 run as one interleaved weight whose GEMM epilogue
+computes the FFN's silu(w1 x) * w3 x, as the model does; --ffn separate runs
+them as two plain linears without the SwiGLU.  With --gpus N each weight is
+N-column sharded across the ranks (one process per GPU) and every output is
+all-gathered over NVLink, by default inside the GEMM epilogue (peer stores),
+with --gather nccl by NCCL after each GEMM.  Prints one JSON line (rank 0).
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
 """
@@ -641,7 +645,7 @@ def main():
     ap.add_argument("--no-extras", action="store_true", help="skip the GEMV and CPU-baseline legs")
     ap.add_argument("--gather", choices=["fused", "nccl"], default="fused",
                     help="N>1: all-gather fused into the GEMM epilogue (peer stores) or NCCL after each GEMM")
-    ap.add_argument("--ffn", choices=["swiglu", "separate"], default="separate",
+    ap.add_argument("--ffn", choices=["swiglu", "separate"], default="swiglu",
                     help="FFN input projections: one SwiGLU-fused weight (silu(w1 x) * w3 x) or two plain linears")
     ap.add_argument("--reserve-sms", type=int, default=None,
                     help="SMs kept free of the GEMM for the all-gather (default 0: measured no gain at N=2)")
