@@ -447,8 +447,21 @@ def run_ours(args):
     nloc = {name: shard.rows_per_rank(n, world) for name, n, _, _ in layer_linears(0)}
     nloc["w13"] = nloc["w1"]   # SwiGLU: one output column per gate / up row pair
     fused = world > 1 and args.gather == "fused"
+    ce = world > 1 and args.gather == "copy"
     pg = None
-    if fused:
+    if ce:
+        # All-gather by the copy engines: every rank's gathered Y is
+        # shard-major [g, M, N/g] (an NCCL all-gather's layout) in a buffer all
+        # ranks can write (CUDA IPC).  The GEMM stores only this rank's slot;
+        # a side stream then pushes the slot into every peer's buffer
+        # (tc_cuda_peer_push) while the next linear runs, and one device flag
+        # barrier per layer on that stream marks every rank's Y complete.
+        from turbocider_b200.peer import PeerGroup
+        pg = PeerGroup(ctx, timeout_us=20_000_000)
+        y_sym = {(name, b): pg.alloc(world * m * nloc[name] * 2) for name in names for b in (0, 1)}
+        y_all = {key: buf.tensor((world, m, nloc[key[0]]), torch.bfloat16) for key, buf in y_sym.items()}
+        y_loc = {key: y_all[key][rank][:, :weights[0][key[0]].n_out] for key in y_all}
+    elif fused:
         # All-gather fused into the GEMM epilogue: every rank's Y[M, g * N/g]
         # lives in a buffer all ranks can store into (CUDA IPC); each GEMM
         # writes its column shard into all of them over NVLink, then a device
@@ -474,7 +487,7 @@ def run_ours(args):
             for name in names:
                 x = x_f if name == "w2" else x_h
                 if world > 1 and not fused and gathered[(name, b)] is not None:
-                    compute.wait_event(gathered[(name, b)])     # buffer reuse after its gather
+                    compute.wait_event(gathered[(name, b)])     # buffer reuse after its gather / push
                 if timing is not None:
                     e0 = torch.cuda.Event(enable_timing=True)
                     e0.record(compute)
@@ -486,6 +499,15 @@ def run_ours(args):
                     timing.append((e0, e1, 2.0 * m * weights[layer][name].n * weights[layer][name].k))
                 if fused:
                     pg.barrier(compute)
+                elif ce:
+                    done = torch.cuda.Event()
+                    done.record(compute)
+                    comm.wait_event(done)
+                    nb = m * nloc[name] * 2
+                    pg.push(y_sym[(name, b)], rank * nb, nb, stream=comm)
+                    ev = torch.cuda.Event()
+                    ev.record(comm)
+                    gathered[(name, b)] = ev
                 elif world > 1:
                     done = torch.cuda.Event()
                     done.record(compute)
@@ -495,6 +517,8 @@ def run_ours(args):
                     ev = torch.cuda.Event()
                     ev.record(comm)
                     gathered[(name, b)] = ev
+            if ce:
+                pg.barrier(comm)        # every rank's outputs of this layer complete
         if world > 1 and not fused:
             compute.wait_stream(comm)
 
@@ -600,12 +624,14 @@ def run_ours(args):
                            "parallelism": ("single GPU" if world == 1 else
                                            f"N-shard x{world}, all-gather fused into the GEMM epilogue (NVLink "
                                            f"peer stores) + device flag barrier per linear" if fused else
+                                           f"N-shard x{world}, all-gather by copy-engine peer pushes on a side "
+                                           f"stream (shard-major Y) + device flag barrier per layer" if ce else
                                            f"N-shard x{world} + NCCL all-gather"
                                            + (f" ({reserve} SMs left to it)" if reserve else "")),
                            "l2": "inputs larger than L2 (3 GB of packed weights streamed per step)",
                            "weights": f"{layers} distinct HBM buffers per tensor, contents cycle over "
                                       f"{DISTINCT_LAYERS} seeds"},
-                "gpu_launches": len(timing) * args.steps * (2 if fused else 1),
+                "gpu_launches": (len(timing) * (2 if fused else 1) + (layers if ce else 0)) * args.steps,
                 "roofline": {"bound": "tensor", "achieved": round(achieved, 2), "peak": peak, "unit": "TFLOP/s",
                              "frac": round(achieved / peak, 4), "traffic": traffic,
                              "kernel": "pair_gemm_kernel (tcgen05 cta_group::2, A in TMEM)", "peak_source": f"{peak_src} sustained"},
@@ -643,8 +669,9 @@ def main():
     ap.add_argument("--cpu-rows", type=int, default=None,
                     help="rows of X in the CPU sample (default: 2048 per reference-arm step, all rows for cpu_baseline)")
     ap.add_argument("--no-extras", action="store_true", help="skip the GEMV and CPU-baseline legs")
-    ap.add_argument("--gather", choices=["fused", "nccl"], default="fused",
-                    help="N>1: all-gather fused into the GEMM epilogue (peer stores) or NCCL after each GEMM")
+    ap.add_argument("--gather", choices=["fused", "copy", "nccl"], default="fused",
+                    help="N>1: all-gather fused into the GEMM epilogue (peer stores), pushed by the copy "
+                         "engines beside the next GEMM, or NCCL after each GEMM")
     ap.add_argument("--ffn", choices=["swiglu", "separate"], default="swiglu",
                     help="FFN input projections: one SwiGLU-fused weight (silu(w1 x) * w3 x) or two plain linears")
     ap.add_argument("--reserve-sms", type=int, default=None,

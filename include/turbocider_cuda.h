@@ -265,6 +265,19 @@ int tc_cuda_peer_free(tc_cuda_ctx *ctx, void *ptr);
 int tc_cuda_peer_barrier(tc_cuda_ctx *ctx, uint32_t *const *flags, uint32_t n_ranks, uint32_t rank,
                          uint32_t epoch, uint32_t timeout_us, void *stream);
 
+/* All-gather by the copy engines instead of the GEMM epilogue: after a plain
+ * tc_cuda_qlinear has written this rank's shard (e.g. its slot of a
+ * shard-major Y[g][M][N/g], the layout of an NCCL all-gather), push the shard
+ * into the same place of every peer's buffer with peer copies enqueued on
+ * `stream` (a side stream, so the transfer overlaps the next linear and takes
+ * no SMs).  rows x width_bytes region, row pitches src_pitch / dst_pitch
+ * (ignored for rows == 1; equal to the width: one linear copy per peer).
+ * Completion on every rank: tc_cuda_peer_barrier on the same stream.  Like
+ * the fused gather, this replaces the ncclAllGather that follows each
+ * N-sharded linear; the reference runs on one device and has no counterpart. */
+int tc_cuda_peer_push(tc_cuda_ctx *ctx, const void *src, void *const *dst, uint32_t n_dst, uint64_t width_bytes,
+                      uint64_t rows, uint64_t src_pitch, uint64_t dst_pitch, void *stream);
+
 /* Batched small-M linear: Y_i[m, N_i] = X[m, K] * W_i^T for n_weights
  * (1..64) weights that share K and X (e.g. every block's AdaLN modulation
  * linear, which all take the timestep embedding), m = 1..16 rows of bf16 X.

@@ -113,6 +113,41 @@ def test_dense_weight_replicas(ctx):
     assert torch.equal(ys[0], ys[1]) and not ys[0][:, :n].any()
 
 
+@pytest.mark.parametrize("layout", ["shard_major", "strided"])
+def test_copy_engine_push_fills_every_replica(ctx, layout):
+    """tc_cuda_peer_push: this rank's shard of a GEMM output reaches the same
+    place in every replica (linear copies for a shard-major Y[g][M][N/g], 2-D
+    copies for column shards of Y[M, N]); nothing outside the shard is written."""
+    import torch
+    from turbocider_b200 import cuda as tcc
+    n, k, m, world, rank = 256, 512, 300, 3, 1
+    raw = tcc.quantize(12, kq_cases.synthetic_weight(n, k, seed=4))
+    w = tcc.Weight.upload(ctx, 12, n, k, raw)
+    x = torch.randn(m, k, device="cuda").to(torch.bfloat16)
+    if layout == "shard_major":
+        ys = [torch.zeros(world, m, n, device="cuda", dtype=torch.bfloat16) for _ in range(world)]
+        shard = ys[0][rank]
+        src, width, rows, pitch = shard.data_ptr(), m * n * 2, 1, m * n * 2
+        offset = rank * m * n * 2
+    else:
+        ys = [torch.zeros(m, world * n, device="cuda", dtype=torch.bfloat16) for _ in range(world)]
+        shard = ys[0][:, rank * n:(rank + 1) * n]
+        src, width, rows, pitch = shard.data_ptr(), n * 2, m, world * n * 2
+        offset = rank * n * 2
+    tcc.qlinear(ctx, w, x, out=shard)
+    dst = (C.c_void_p * (world - 1))(*[ys[i].data_ptr() + offset for i in range(1, world)])
+    for _ in range(2):
+        tcc._check(tcc.lib().tc_cuda_peer_push(ctx.handle, C.c_void_p(src), dst, world - 1, width, rows, pitch,
+                                               pitch, None))
+    torch.cuda.synchronize()
+    assert ctx.status() == 0
+    assert shard.abs().sum() > 0
+    for y in ys[1:]:
+        assert torch.equal(y, ys[0])
+    total = sum(int((y != 0).sum()) for y in ys)
+    assert total == world * int((shard != 0).sum())
+
+
 def _flags(n):
     import torch
     return torch.zeros(n, dtype=torch.int32, device="cuda")

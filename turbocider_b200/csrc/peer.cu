@@ -121,6 +121,28 @@ int tc_cuda_peer_free(tc_cuda_ctx *ctx, void *ptr) {
     return tc::ok();
 }
 
+int tc_cuda_peer_push(tc_cuda_ctx *ctx, const void *src, void *const *dst, uint32_t n_dst, uint64_t width_bytes,
+                      uint64_t rows, uint64_t src_pitch, uint64_t dst_pitch, void *stream) {
+    if (!ctx || !src || (n_dst && !dst)) return tc::fail("null argument");
+    if (n_dst > tc::kMaxPeers) return tc::fail("more destinations than ranks");
+    if (!width_bytes || !rows) return tc::ok();
+    if (rows > 1 && (src_pitch < width_bytes || dst_pitch < width_bytes))
+        return tc::fail("row pitch smaller than the row width");
+    for (uint32_t i = 0; i < n_dst; ++i)
+        if (!dst[i]) return tc::fail("null destination");
+    tc::DeviceGuard guard(ctx->device);
+    const cudaStream_t s = static_cast<cudaStream_t>(stream);
+    // Contiguous regions go as one linear copy (the copy engines' fastest form).
+    const bool linear = rows == 1 || (src_pitch == width_bytes && dst_pitch == width_bytes);
+    for (uint32_t i = 0; i < n_dst; ++i) {
+        cudaError_t e = linear ? cudaMemcpyAsync(dst[i], src, width_bytes * rows, cudaMemcpyDeviceToDevice, s)
+                               : cudaMemcpy2DAsync(dst[i], dst_pitch, src, src_pitch, width_bytes, rows,
+                                                   cudaMemcpyDeviceToDevice, s);
+        if (e != cudaSuccess) return tc::cuda_fail("peer push", e);
+    }
+    return tc::ok();
+}
+
 int tc_cuda_peer_barrier(tc_cuda_ctx *ctx, uint32_t *const *flags, uint32_t n_ranks, uint32_t rank, uint32_t epoch,
                          uint32_t timeout_us, void *stream) {
     if (!ctx || !flags) return tc::fail("null argument");

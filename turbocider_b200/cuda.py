@@ -71,6 +71,7 @@ EXPORTS = {
     "tc_cuda_peer_close": (C.c_int, [_vp, _vp]),
     "tc_cuda_peer_free": (C.c_int, [_vp, _vp]),
     "tc_cuda_peer_barrier": (C.c_int, [_vp, C.POINTER(_vp), _u32, _u32, _u32, _u32, _vp]),
+    "tc_cuda_peer_push": (C.c_int, [_vp, _vp, C.POINTER(_vp), _u32, _u64, _u64, _u64, _u64, _vp]),
     "tc_cuda_set_path": (C.c_int, [_vp, C.c_int]),
     "tc_cuda_qlinear_batched": (C.c_int, [_vp, C.POINTER(_vp), _u32, _vp, _u32, C.POINTER(_vp), C.POINTER(_u64),
                                           C.c_int, _vp]),

@@ -100,6 +100,17 @@ class PeerGroup:
         """The other ranks' copies of `buf` (+ byte_offset), for qlinear(peers=...)."""
         return [p + byte_offset for r, p in enumerate(buf.ptrs) if r != self.rank]
 
+    def push(self, buf: SymmetricBuffer, byte_offset: int, nbytes: int, stream=None):
+        """Copy-engine all-gather step: copy bytes [byte_offset, +nbytes) of this
+        rank's `buf` into the same bytes of every other rank's `buf`
+        (tc_cuda_peer_push, enqueued on `stream`).  Rank r sends to r+1, r+2, ...
+        in turn, so at any moment every rank receives from a different sender.
+        Completion on every rank: `barrier` on the same stream."""
+        order = [(self.rank + i) % self.world for i in range(1, self.world)]
+        dst = (C.c_void_p * max(1, len(order)))(*[buf.ptrs[r] + byte_offset for r in order])
+        tcc._check(tcc.lib().tc_cuda_peer_push(self.ctx.handle, C.c_void_p(buf.local + byte_offset), dst, len(order),
+                                               nbytes, 1, nbytes, nbytes, tcc._stream_ptr(stream)))
+
     def barrier(self, stream=None):
         """Every rank's `stream` waits until all ranks reached this barrier."""
         self.epoch += 1
