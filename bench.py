@@ -15,8 +15,10 @@ w1 / w3 and w2 projections (the FLOPs of 150 quantised linears).  By default
 computes the FFN's silu(w1 x) * w3 x, as the model does; --ffn separate runs
 them as two plain linears without the SwiGLU.  With --gpus N each weight is
 N-column sharded across the ranks (one process per GPU) and every output is
-all-gathered over NVLink, by default inside the GEMM epilogue (peer stores),
-with --gather nccl by NCCL after each GEMM.  Prints one JSON line (rank 0).
+all-gathered over NVLink, by default by copy-engine peer pushes on a side
+stream beside the next GEMM (--gather copy), with --gather fused inside the
+GEMM epilogue (peer stores), with --gather nccl by NCCL after each GEMM.
+Prints one JSON line (rank 0).
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
 """
@@ -669,7 +671,7 @@ def main():
     ap.add_argument("--cpu-rows", type=int, default=None,
                     help="rows of X in the CPU sample (default: 2048 per reference-arm step, all rows for cpu_baseline)")
     ap.add_argument("--no-extras", action="store_true", help="skip the GEMV and CPU-baseline legs")
-    ap.add_argument("--gather", choices=["fused", "copy", "nccl"], default="fused",
+    ap.add_argument("--gather", choices=["fused", "copy", "nccl"], default="copy",
                     help="N>1: all-gather fused into the GEMM epilogue (peer stores), pushed by the copy "
                          "engines beside the next GEMM, or NCCL after each GEMM")
     ap.add_argument("--ffn", choices=["swiglu", "separate"], default="swiglu",
