@@ -10,7 +10,9 @@ every tensor Q4_K except w2 (ffn_down), which is Q6_K in even layers.
 Weights ~ N(0, 0.02), activations ~ N(0, 1) bf16, all synthetic.
 
 A step is one pass of the hot path over the batch: every layer's qkv, out,
-w1 / w3 and w2 projections (the FLOPs of 150 quantised linears).  By default
+w1 / w3 and w2 projections (the FLOPs of 150 quantised linears), fp16
+activations in and fp16 outputs out (the reference's GGUF execution runs fp16
+activations, and its projection returns X's dtype).  By default
 (--ffn swiglu) w1 and w3 run as one interleaved weight whose GEMM epilogue
 computes the FFN's silu(w1 x) * w3 x, as the model does; --ffn separate runs
 them as two plain linears without the SwiGLU.  With --gpus N each weight is
@@ -18,6 +20,9 @@ N-column sharded across the ranks (one process per GPU) and every output is
 all-gathered over NVLink, by default by copy-engine peer pushes on a side
 stream beside the next GEMM (--gather copy), with --gather fused inside the
 GEMM epilogue (peer stores), with --gather nccl by NCCL after each GEMM.
+After timing, sampled rows of the last outputs are checked against the CPU
+oracle (dequant + fp64 matmul) on every rank, and at N > 1 every rank's
+gathered Y is checked to equal the shards the other ranks computed.
 Prints one JSON line (rank 0).
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
@@ -107,61 +112,86 @@ class ClockSampler:
 
 
 # ---------------------------------------------------------------- CPU path
-def cpu_reference_sample(m_sample: int, linears, threads: int):
+def cpu_model() -> str:
+    try:
+        for line in Path("/proc/cpuinfo").read_text().splitlines():
+            if line.startswith("model name"):
+                return line.split(":", 1)[1].strip()
+    except OSError:
+        pass
+    import platform
+    return platform.processor() or "unknown"
+
+
+def workload_config(layers: int) -> dict:
+    """The workload both arms measure."""
+    return {"workload": "config5_zimage_6b_linear_stack", "layers": layers, "m_tokens": M_TOKENS,
+            "hidden": HIDDEN, "ffn": FFN, "mix": "Q4_K_M (w2 Q6_K in even layers)",
+            "weights": "N(0, 0.02) quantised to the mix; X ~ N(0, 1)"}
+
+
+def cpu_reference_sample(m_sample: int, linears, threads: int, x=None):
     """The reference's CPU path on a bounded sample: decode_cpu_into -> f32
-    (row-split over `threads`, as RowDecodePool) then an fp32 matmul with
-    torch on `threads` host threads.  Returns (seconds, flops, kind)."""
+    (the reference decoder built from its sources, row-split over `threads`
+    as its RowDecodePool does, native/runtime/streaming/gguf_packed_bank.cpp:48-100)
+    then an fp32 matmul with torch on `threads` host threads (the reference
+    has no CPU GEMM).  Returns (seconds, flops, kind)."""
     import torch
-    sys.path.insert(0, str(ROOT / "tests"))
     from oracle import oracle
     kind = "reference" if oracle.ref() is not None else "port"
     torch.set_num_threads(threads)
-    x = torch.randn(m_sample, FFN, generator=torch.Generator().manual_seed(5))
+    if x is None:
+        x = torch.randn(m_sample, FFN, generator=torch.Generator().manual_seed(5))
     t0 = time.perf_counter()
     flops = 0.0
     for name, n, k, typ, raw in linears:
         w = oracle.decode_parallel(raw, typ, n, k, 0, which="ref" if kind == "reference" else "port", threads=threads)
-        y = x[:, :k] @ torch.from_numpy(w).T
+        y = x[:m_sample, :k] @ torch.from_numpy(w).T
         flops += 2.0 * m_sample * n * k
         del y, w
     return time.perf_counter() - t0, flops, kind
 
 
 def make_cpu_linears(layer: int = 0):
-    """Raw GGUF blocks of one layer's linears (same seeds as the GPU arm)."""
-    from turbocider_b200 import cuda as tcc
+    """Raw GGUF blocks of one layer's linears, quantised by the numpy
+    restatement of the backend's quantiser (oracle/kq_quantize.py, same bytes
+    as tc_quantize), so the CPU arm never loads the backend library."""
+    from oracle import kq_quantize
     out = []
     for i, (name, n, k, typ) in enumerate(layer_linears(layer)):
         w = (np.random.default_rng(1000 * layer + i).standard_normal((n, k), dtype=np.float32) * np.float32(0.02))
-        out.append((name, n, k, typ, tcc.quantize(typ, w)))
+        out.append((name, n, k, typ, kq_quantize.quantize(typ, w)))
     return out
 
 
 def run_reference(args):
+    """The reference arm: the reference's own CPU path for the workload (its
+    decoder from oracle/_ref, all host threads) on rank 0; other ranks exit."""
     rank = int(os.environ.get("RANK", "0"))
     if rank != 0:
         return 0
+    import torch
     threads = os.cpu_count() or 1
     linears = make_cpu_linears(0)
-    m_sample = args.cpu_rows or 2048
+    m_sample = args.cpu_rows or M_TOKENS
+    x = torch.randn(m_sample, FFN, generator=torch.Generator().manual_seed(5))
     for _ in range(args.warmup):
-        cpu_reference_sample(m_sample, linears, threads)
+        cpu_reference_sample(m_sample, linears, threads, x)
     times, flops, kind = [], 0.0, "port"
     for _ in range(args.steps):
-        t, flops, kind = cpu_reference_sample(m_sample, linears, threads)
+        t, flops, kind = cpu_reference_sample(m_sample, linears, threads, x)
         times.append(t)
     total = sum(times)
     value = flops * args.steps / total / 1e12
-    sample = (f"layer 0 of the config-5 stack (qkv, out, w1, w3, w2 Q6_K): decode_cpu_into->f32 of the 5 weights "
-              f"+ fp32 matmul at {m_sample} of {M_TOKENS} rows, per step")
+    sample = (f"layer 0 of the stack (qkv, out, w1, w3, w2 Q6_K) per step: the reference's decode_cpu_into -> f32 "
+              f"of the 5 weights + fp32 matmul at {m_sample} of {M_TOKENS} rows")
     line = {"impl": "reference", "metric": METRIC, "value": round(value, 4), "unit": "TFLOPS",
             "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
             "ms_per_step": round(1e3 * total / args.steps, 3), "higher_is_better": True, "scaling": "strong",
-            "vs_baseline": None, "dtype": "f32", "data": "synthetic",
-            "config": {"workload": "config5_zimage_6b_linear_stack", "layers": LAYERS, "m_tokens": M_TOKENS,
-                       "hidden": HIDDEN, "ffn": FFN, "mix": "Q4_K_M", "cpu_sample_rows": m_sample},
-            "cpu_baseline": {"value": round(value, 4), "unit": "TFLOPS", "cores": threads, "kind": kind,
-                             "sample": sample},
+            "vs_baseline": None, "dtype": "f32", "data": "synthetic", "config": workload_config(args.layers),
+            "parallelism": "CPU, rank 0 only",
+            "cpu_baseline": {"value": round(value, 4), "unit": "TFLOPS", "cores": threads, "cpu": cpu_model(),
+                             "kind": kind, "sample": sample},
             "e2e": {"value": round(value, 4), "unit": "TFLOPS", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
     print(json.dumps(line), flush=True)
     return 0
@@ -171,7 +201,8 @@ def run_reference(args):
 def build_weights(ctx, rank, world, layers, device, ffn: str = "separate"):
     """Upload every layer's weight shard (turbocider_b200.shard.shard_rows) to HBM.
     ffn "swiglu": w1 and w3 go up as one interleaved weight "w13" whose GEMM
-    epilogue computes silu(w1 x) * w3 x (tc_cuda_weight_upload_glu)."""
+    epilogue computes silu(w1 x) * w3 x (tc_cuda_weight_upload_glu).
+    Returns (weights per layer, {(seed layer, name): (raw shard, rows, K, type)})."""
     import torch
     from turbocider_b200 import cuda as tcc
     from turbocider_b200 import shard
@@ -197,7 +228,7 @@ def build_weights(ctx, rank, world, layers, device, ffn: str = "separate"):
                 continue
             lw[name] = tcc.Weight.upload(ctx, typ, rows, kk, raw)
         weights.append(lw)
-    return weights
+    return weights, raw_cache
 
 
 def gemv_measure(ctx, device, hbm_peak):
@@ -386,9 +417,10 @@ def epilogue_measure(ctx, device):
     b_glu = torch.randn(2 * FFN, generator=g, device=device) * 0.1
     s = torch.cuda.Stream(device)
 
-    def tflops(w, **kw):
+    def tflops(w, xin=None, stage=tcc.STAGE_F16_X16, **kw):
         out = torch.empty(m, w.n_out, dtype=torch.bfloat16, device=device)
-        call = lambda: tcc.qlinear(ctx, w, x, out=out, stage=tcc.STAGE_F16_X16, stream=s, **kw)
+        xx = x if xin is None else xin
+        call = lambda: tcc.qlinear(ctx, w, xx, out=out, stage=stage, stream=s, **kw)
         with torch.cuda.stream(s):
             for _ in range(3):
                 call()
@@ -399,14 +431,285 @@ def epilogue_measure(ctx, device):
             e1.record(s)
             e1.synchronize()
         return round(2.0 * m * w.n * w.k * 10 / (e0.elapsed_time(e1) / 1e3) / 1e12, 1)
+    x_b = x.to(torch.bfloat16)
     res = {"config": "config-5 shapes, M = 8448, K = 3840, X fp16, bf16 out; TFLOP/s of 2 M N K",
            "qkv_plain": tflops(w_qkv), "qkv_bias": tflops(w_qkv, bias=b_qkv),
+           "qkv_bf16_x_stage_f16": tflops(w_qkv, xin=x_b, stage=tcc.STAGE_F16),
+           "qkv_bf16_x_stage_bf16": tflops(w_qkv, xin=x_b, stage=tcc.STAGE_BF16),
            "qkv_bias_gelu_tanh": tflops(w_qkv, bias=b_qkv, activation="gelu_tanh"),
            "rows20480_plain": tflops(w_2f), "w1_w3_swiglu_bias": tflops(w_glu, bias=b_glu)}
     assert ctx.status() == 0
     for w in (w_qkv, w_glu, w_2f):
         w.free()
     return res
+
+
+# ---------------------------------------------------------------- configs 1 and 3
+def config1_measure(ctx, device, tc_burst):
+    """BASELINE configs[0] on the GPU: one Q4_K linear, W [3072, 3072], X bf16
+    [256, 3072] (converted to fp16 for fp16 staging, TC_STAGE_F16), bf16 out.
+    32 weight copies (170 MB > L2) cycled inside a CUDA graph of 64 calls."""
+    import torch
+    from turbocider_b200 import cuda as tcc
+    n = k = 3072
+    m, copies, calls, reps = 256, 32, 64, 10
+    g = torch.Generator(device=device).manual_seed(11)
+    raw = tcc.quantize(Q4_K, (torch.randn(n, k, generator=g, device=device) * 0.02).cpu().numpy())
+    ws = [tcc.Weight.upload(ctx, Q4_K, n, k, raw) for _ in range(copies)]
+    x = torch.randn(m, k, generator=g, device=device).to(torch.bfloat16)
+    y = torch.empty(m, n, device=device, dtype=torch.bfloat16)
+    stream = torch.cuda.Stream(device)
+    res = {"config": "configs[0]: Q4_K W[3072, 3072], X bf16 [256, 3072] -> fp16 staging (TC_STAGE_F16, "
+                     "conversion included), bf16 Y; 32 weight copies cycled (> L2), 64 calls per CUDA graph"}
+    with torch.cuda.stream(stream):
+        for i in range(copies):
+            tcc.qlinear(ctx, ws[i], x, out=y, stage=tcc.STAGE_F16, stream=stream)
+        stream.synchronize()
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph, stream=stream):
+            for i in range(calls):
+                tcc.qlinear(ctx, ws[i % copies], x, out=y, stage=tcc.STAGE_F16, stream=stream)
+        for _ in range(3):
+            graph.replay()
+        stream.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        for _ in range(reps):
+            graph.replay()
+        e1.record(stream)
+        e1.synchronize()
+    sec = e0.elapsed_time(e1) / 1e3 / (reps * calls)
+    tflops = 2.0 * m * n * k / sec / 1e12
+    res.update({"us_per_call": round(sec * 1e6, 2), "tflops": round(tflops, 1),
+                "frac": round(tflops / tc_burst, 4), "peak": "measured burst bf16",
+                "tiles": "12 pair tiles (256 weight rows x 256 tokens) of 4.8 GFLOP in total"})
+    del graph
+    assert ctx.status() == 0
+    for w in ws:
+        w.free()
+    return res
+
+
+C3_HIDDEN, C3_FFN, C3_IMG, C3_TXT = 3072, 12288, 2048, 512
+
+
+def config3_linears(block: int):
+    """(name, N, K, type, activation) of one Qwen-Image-style dual-stream
+    MMDiT block, per stream (reference call sites
+    native/models/qwen21/transformer.cpp:857-859 to_q/k/v, :953 to_out,
+    :971-978 the FFN): q, k, out, ffn_up Q4_K; v Q6_K; ffn_down Q6_K in even
+    blocks and Q4_K in odd ones; ffn_up carries the GELU (tanh form)."""
+    h, f = C3_HIDDEN, C3_FFN
+    return [("q", h, h, Q4_K, None), ("k", h, h, Q4_K, None), ("v", h, h, Q6_K, None),
+            ("out", h, h, Q4_K, None), ("up", f, h, Q4_K, "gelu_tanh"),
+            ("down", h, f, Q6_K if block % 2 == 0 else Q4_K, None)]
+
+
+def config3_measure(ctx, device, tc_sustained):
+    """one dual-stream MMDiT block's linears, image stream
+    M = 2048 and text stream M = 512 packed as two ragged segments of one call
+    per projection (separate image / text weights), X bf16 -> fp16 staging,
+    bf16 out, GELU fused into ffn_up; plus the AdaLN modulation linears
+    [6 * 3072, 3072] of both streams at M = 2 (the CFG pair's timestep
+    embedding, reference transformer.cpp:368-369, :420-421) in one batched
+    GEMV.  Two blocks per iteration (ffn_down Q6_K, then Q4_K)."""
+    import torch
+    from turbocider_b200 import cuda as tcc
+    threads = os.cpu_count() or 1
+    h, f, m = C3_HIDDEN, C3_FFN, C3_IMG + C3_TXT
+    seg, sw = [0, C3_IMG, m], [0, 1]
+    blocks = []
+    seed = 300
+    for b in range(2):
+        lw = {}
+        for name, n, k, typ, act in config3_linears(b):
+            pair = []
+            for stream_id in range(2):
+                seed += 1
+                g = torch.Generator(device=device).manual_seed(seed)
+                raw = tcc.quantize(typ, (torch.randn(n, k, generator=g, device=device) * 0.02).cpu().numpy(),
+                                   threads=threads)
+                pair.append(tcc.Weight.upload(ctx, typ, n, k, raw))
+            lw[name] = pair
+        mods = []
+        for stream_id in range(2):
+            seed += 1
+            g = torch.Generator(device=device).manual_seed(seed)
+            raw = tcc.quantize(Q4_K, (torch.randn(6 * h, h, generator=g, device=device) * 0.02).cpu().numpy(),
+                               threads=threads)
+            mods.append(tcc.Weight.upload(ctx, Q4_K, 6 * h, h, raw))
+        lw["mod"] = mods
+        blocks.append(lw)
+    g = torch.Generator(device=device).manual_seed(399)
+    x_h = torch.randn(m, h, generator=g, device=device).to(torch.bfloat16)
+    x_f = torch.randn(m, f, generator=g, device=device).to(torch.bfloat16)
+    temb = torch.randn(2, h, generator=g, device=device).to(torch.bfloat16)
+    y_h = torch.empty(m, h, device=device, dtype=torch.bfloat16)
+    y_f = torch.empty(m, f, device=device, dtype=torch.bfloat16)
+    y_mod = [torch.empty(2, 6 * h, device=device, dtype=torch.bfloat16) for _ in range(2)]
+    stream = torch.cuda.Stream(device)
+    flops = 0.0
+
+    def one_iter():
+        nonlocal flops
+        flops = 0.0
+        for b, lw in enumerate(blocks):
+            tcc.qlinear_batched(ctx, lw["mod"], temb, outs=y_mod, stream=stream)
+            flops += 2 * 2.0 * 2 * 6 * h * h
+            for name, n, k, typ, act in config3_linears(b):
+                x = x_f if name == "down" else x_h
+                out = y_f if n == f else y_h
+                tcc.qlinear(ctx, lw[name], x, seg_offsets=seg, seg_weight=sw, out=out, stage=tcc.STAGE_F16,
+                            activation=act, stream=stream)
+                flops += 2.0 * m * n * k
+
+    reps = 10
+    with torch.cuda.stream(stream):
+        for _ in range(3):
+            one_iter()
+        stream.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        for _ in range(reps):
+            one_iter()
+        e1.record(stream)
+        e1.synchronize()
+    sec = e0.elapsed_time(e1) / 1e3 / reps
+    tflops = flops / sec / 1e12
+    assert ctx.status() == 0
+    for lw in blocks:
+        for pair in lw.values():
+            for w in pair:
+                w.free()
+    return {"config": "configs[2]: 2 dual-stream MMDiT blocks (hidden 3072, FFN 12288 GELU; ffn_down Q6_K then "
+                      "Q4_K), image M = 2048 + text M = 512 as two ragged segments per call, X bf16 -> fp16 "
+                      "staging, bf16 Y, + AdaLN modulation [18432, 3072] x 2 streams at M = 2 (batched GEMV)",
+            "ms_per_block": round(sec * 1e3 / 2, 3), "gflop_per_block": round(flops / 2 / 1e9, 2),
+            "tflops": round(tflops, 1), "frac": round(tflops / tc_sustained, 4), "peak": "measured sustained bf16"}
+
+
+# ---------------------------------------------------------------- multi-GPU
+def gather_measure(ctx, device, world, rank, m, width):
+    """The all-gather alone (no GEMM running): one rank's shard of `m` rows x
+    `width` fp16 columns goes to every other rank, by copy-engine pushes fanned
+    out over one side stream per peer, by the same pushes back to back on one
+    stream, and by NCCL all_gather_into_tensor.  GB/s = bytes each GPU
+    receives ((world - 1) shards) / time, max over ranks."""
+    import torch
+    import torch.distributed as dist
+    from turbocider_b200.peer import PeerGroup
+    pg = PeerGroup(ctx, timeout_us=20_000_000)
+    shard = m * width * 2
+    buf = pg.alloc(world * shard)
+    s = torch.cuda.Stream(device)
+    out = {"shard_mb": round(shard / 1e6, 2)}
+
+    def timed(fn, reps=5):
+        for _ in range(2):
+            fn()
+        torch.cuda.synchronize(device)
+        dist.barrier()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(s)
+        for _ in range(reps):
+            fn()
+        e1.record(s)
+        e1.synchronize()
+        t = torch.tensor([e0.elapsed_time(e1) / 1e3 / reps], device=device, dtype=torch.float64)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t.item())
+
+    def push():
+        pg.push(buf, rank * shard, shard, stream=s)
+        pg.barrier(s)
+
+    for mode, serial in (("push_fanout", False), ("push_serial", True)):
+        ctx.set_push_serial(serial)
+        t = timed(push)
+        out[mode] = {"ms": round(t * 1e3, 3), "gbs_in_per_gpu": round((world - 1) * shard / t / 1e9, 1)}
+    ctx.set_push_serial(False)
+    src = torch.zeros(m, width, device=device, dtype=torch.float16)
+    dst = torch.empty(world * m, width, device=device, dtype=torch.float16)
+
+    def nccl():
+        with torch.cuda.stream(s):
+            dist.all_gather_into_tensor(dst, src)
+
+    t = timed(nccl)
+    out["nccl_all_gather"] = {"ms": round(t * 1e3, 3), "gbs_in_per_gpu": round((world - 1) * shard / t / 1e9, 1),
+                              "bus_gbs": round((world - 1) * shard / t / 1e9, 1)}
+    assert ctx.status() == 0
+    del src, dst
+    pg.close()
+    return out
+
+
+def parity_check(raw_cache, names, layers, y_loc, y_all, x_h, x_f, world, rank, nloc, mode, n_out):
+    """Sampled rows of the last outputs against the CPU oracle, and the
+    gathered Y of every rank against the shards the ranks computed.
+
+    Oracle: the reference's decode (decode_cpu_into to f32, oracle/ port) and
+    an fp64 matmul of the same fp16 X rows (oracle.qlinear_ref), with the
+    SwiGLU silu(w1 x) * w3 x applied in fp64 (oracle.epilogue_ref); bar
+    rel-L2 <= 1e-3 on the fp16 outputs.  Both buffers of each linear are
+    checked: they hold the last two layers (w2 Q6_K and Q4_K).
+    Gather: every rank checksums each rank-slot of its gathered buffers; all
+    ranks must agree, i.e. each rank's copy of slot r equals what rank r
+    wrote (its own slot, whose rows were checked against the oracle)."""
+    import torch
+    import torch.distributed as dist
+    from oracle import oracle
+    rows = np.sort(np.random.default_rng(123).choice(M_TOKENS, 16, replace=False))
+    idx = torch.from_numpy(rows).to(x_h.device)
+    xs = {"h": x_h.index_select(0, idx).view(torch.int16).cpu().numpy().view(np.uint16),
+          "f": x_f.index_select(0, idx).view(torch.int16).cpu().numpy().view(np.uint16)}
+    worst, checked = 0.0, []
+    for b in (0, 1):
+        layer = layers - 1 if ((layers - 1) & 1) == b else layers - 2
+        if layer < 0:
+            continue
+        d = layer % DISTINCT_LAYERS
+        for name in names:
+            raw, cols, k, typ = raw_cache[(d, "w1" if name == "w13" else name)]
+            if not cols:
+                continue   # this rank holds no columns of the weight
+            got = y_loc[(name, b)].index_select(0, idx).float().cpu().numpy().astype(np.float64)
+            x = xs["f"] if name == "w2" else xs["h"]
+            if name == "w13":
+                u_raw = raw_cache[(d, "w3")][0]
+                acc = np.concatenate([oracle.qlinear_ref(x, raw, typ, cols, k, "f32", x_dtype="f16"),
+                                      oracle.qlinear_ref(x, u_raw, typ, cols, k, "f32", x_dtype="f16")], axis=1)
+                ref = oracle.epilogue_ref(acc, glu=True)
+            else:
+                ref = oracle.qlinear_ref(x, raw, typ, cols, k, "f32", x_dtype="f16")
+            err = oracle.rel_l2(got[:, :ref.shape[1]], ref)
+            worst = max(worst, err)
+            checked.append(f"layer{layer}.{name}")
+    consistent = None
+    if world > 1:
+        sums = []
+        for key in sorted(y_all):
+            name = key[0]
+            buf = y_all[key]
+            if mode == "fused":
+                slots = [buf[:, r * nloc[name]:(r + 1) * nloc[name]] for r in range(world)]
+            else:
+                slots = list(buf.reshape(world, M_TOKENS, nloc[name]).unbind(0))
+            for sl in slots:
+                v = sl.contiguous().view(torch.int16).to(torch.int64).flatten()
+                w = torch.arange(v.numel(), device=v.device, dtype=torch.int64) % 65521 + 1
+                sums.append((v * w).sum())
+        mine = torch.stack(sums)
+        every = [torch.empty_like(mine) for _ in range(world)]
+        dist.all_gather(every, mine)
+        consistent = all(bool(torch.equal(e, every[0])) for e in every)
+        t = torch.tensor([worst, 0.0 if consistent else 1.0], device=x_h.device, dtype=torch.float64)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        worst, consistent = float(t[0]), float(t[1]) == 0.0
+    return {"rel_l2_max": float(f"{worst:.3e}"), "bar": 1e-3, "ok": bool(worst <= 1e-3 and consistent is not False),
+            "rows_sampled": int(len(rows)), "linears_checked_per_rank": len(checked),
+            "oracle": "decode_cpu_into(f32) + fp64 matmul of the same fp16 X rows; SwiGLU in fp64",
+            "gathered_y_consistent_on_all_ranks": consistent}
 
 
 def run_ours(args):
@@ -431,13 +734,13 @@ def run_ours(args):
     if reserve:
         # leave SMs free for the NCCL all-gather that runs beside each GEMM
         ctx.set_sm_limit(torch.cuda.get_device_properties(device).multi_processor_count - reserve)
-    weights = build_weights(ctx, rank, world, layers, device, args.ffn)
+    weights, raw_cache = build_weights(ctx, rank, world, layers, device, args.ffn)
 
     m = M_TOKENS
     g = torch.Generator(device=device).manual_seed(7)
-    # fp16 activations, W staged fp16 (TC_STAGE_F16_X16): the precision that
-    # meets rel-L2 <= 1e-3 against dequant + fp32 matmul, and the activation
-    # type of the reference's own GGUF execution.
+    # fp16 activations, W staged fp16 (TC_STAGE_F16_X16), fp16 outputs: the
+    # precision that meets rel-L2 <= 1e-3 against dequant + fp32 matmul, and
+    # the activation type of the reference's own GGUF execution.
     x_h = torch.randn(m, HIDDEN, generator=g, device=device).to(torch.float16)
     x_f = torch.randn(m, FFN, generator=g, device=device).to(torch.float16)
     compute = torch.cuda.Stream(device)
@@ -451,6 +754,7 @@ def run_ours(args):
     fused = world > 1 and args.gather == "fused"
     ce = world > 1 and args.gather == "copy"
     pg = None
+    f16 = torch.float16
     if ce:
         # All-gather by the copy engines: every rank's gathered Y is
         # shard-major [g, M, N/g] (an NCCL all-gather's layout) in a buffer all
@@ -461,7 +765,7 @@ def run_ours(args):
         from turbocider_b200.peer import PeerGroup
         pg = PeerGroup(ctx, timeout_us=20_000_000)
         y_sym = {(name, b): pg.alloc(world * m * nloc[name] * 2) for name in names for b in (0, 1)}
-        y_all = {key: buf.tensor((world, m, nloc[key[0]]), torch.bfloat16) for key, buf in y_sym.items()}
+        y_all = {key: buf.tensor((world, m, nloc[key[0]]), f16) for key, buf in y_sym.items()}
         y_loc = {key: y_all[key][rank][:, :weights[0][key[0]].n_out] for key in y_all}
     elif fused:
         # All-gather fused into the GEMM epilogue: every rank's Y[M, g * N/g]
@@ -471,30 +775,36 @@ def run_ours(args):
         from turbocider_b200.peer import PeerGroup
         pg = PeerGroup(ctx, timeout_us=20_000_000)
         y_sym = {(name, b): pg.alloc(m * world * nloc[name] * 2) for name in names for b in (0, 1)}
-        y_all = {key: buf.tensor((m, world * nloc[key[0]]), torch.bfloat16) for key, buf in y_sym.items()}
+        y_all = {key: buf.tensor((m, world * nloc[key[0]]), f16) for key, buf in y_sym.items()}
         y_loc = {key: y_all[key][:, rank * nloc[key[0]]:rank * nloc[key[0]] + weights[0][key[0]].n_out]
                  for key in y_all}
         y_peers = {key: pg.peers_of(buf, rank * nloc[key[0]] * 2) for key, buf in y_sym.items()}
     else:
         # double-buffered local outputs and gathered outputs per linear
-        y_loc = {(name, b): torch.empty(m, nloc[name], device=device, dtype=torch.bfloat16)
+        y_loc = {(name, b): torch.empty(m, nloc[name], device=device, dtype=f16)
                  for name in names for b in (0, 1)}
-        y_all = ({(name, b): torch.empty(world * m, nloc[name], device=device, dtype=torch.bfloat16)
+        y_all = ({(name, b): torch.empty(world * m, nloc[name], device=device, dtype=f16)
                   for name in names for b in (0, 1)} if world > 1 else {})
     gathered = {(name, b): None for name in names for b in (0, 1)}
 
-    def one_step(timing=None):
+    def one_step(timing=None, dependent=False):
+        """One pass of the stack.  dependent=True: every linear waits (on the
+        compute stream) until the previous linear's output has been gathered
+        on every rank, as a chain of layers that consume the gathered Y must."""
+        prev = None
         for layer in range(layers):
             b = layer & 1
             for name in names:
                 x = x_f if name == "w2" else x_h
                 if world > 1 and not fused and gathered[(name, b)] is not None:
                     compute.wait_event(gathered[(name, b)])     # buffer reuse after its gather / push
+                if dependent and prev is not None:
+                    compute.wait_event(prev)
                 if timing is not None:
                     e0 = torch.cuda.Event(enable_timing=True)
                     e0.record(compute)
-                tcc.qlinear(ctx, weights[layer][name], x, out=y_loc[(name, b)], stage=tcc.STAGE_F16_X16,
-                            stream=compute, peers=y_peers[(name, b)] if fused else None)
+                tcc.qlinear(ctx, weights[layer][name], x, out=y_loc[(name, b)], out_dtype=tcc.F16,
+                            stage=tcc.STAGE_F16_X16, stream=compute, peers=y_peers[(name, b)] if fused else None)
                 if timing is not None:
                     e1 = torch.cuda.Event(enable_timing=True)
                     e1.record(compute)
@@ -507,9 +817,12 @@ def run_ours(args):
                     comm.wait_event(done)
                     nb = m * nloc[name] * 2
                     pg.push(y_sym[(name, b)], rank * nb, nb, stream=comm)
+                    if dependent:
+                        pg.barrier(comm)    # this linear's Y complete on every rank
                     ev = torch.cuda.Event()
                     ev.record(comm)
                     gathered[(name, b)] = ev
+                    prev = ev
                 elif world > 1:
                     done = torch.cuda.Event()
                     done.record(compute)
@@ -519,7 +832,8 @@ def run_ours(args):
                     ev = torch.cuda.Event()
                     ev.record(comm)
                     gathered[(name, b)] = ev
-            if ce:
+                    prev = ev
+            if ce and not dependent:
                 pg.barrier(comm)        # every rank's outputs of this layer complete
         if world > 1 and not fused:
             compute.wait_stream(comm)
@@ -528,6 +842,13 @@ def run_ours(args):
         if world > 1:
             dist.barrier()
         torch.cuda.synchronize(device)
+
+    def max_over_ranks(sec):
+        if world == 1:
+            return sec
+        tt = torch.tensor([sec], device=device, dtype=torch.float64)
+        dist.all_reduce(tt, op=dist.ReduceOp.MAX)
+        return float(tt.item())
 
     with torch.cuda.stream(compute):
         for _ in range(args.warmup):
@@ -549,17 +870,34 @@ def run_ours(args):
     t1.record(compute)
     barrier()
     clock_info = clocks.stop()
-    elapsed = t0.elapsed_time(t1) / 1e3
-    if world > 1:
-        tt = torch.tensor([elapsed], device=device, dtype=torch.float64)
-        dist.all_reduce(tt, op=dist.ReduceOp.MAX)
-        elapsed = float(tt.item())
+    elapsed = max_over_ranks(t0.elapsed_time(t1) / 1e3)
     flops = step_flops(layers) * args.steps
     value = flops / elapsed / 1e12
     gemm_time = sum(a.elapsed_time(b) for a, b, _ in timing) / 1e3
     gemm_flops = sum(f for _, _, f in timing)
     achieved = gemm_flops / gemm_time / 1e12
     status = ctx.status(clear=True)
+
+    # the same stack as a dependent chain (N > 1: each linear waits for the
+    # previous linear's gathered output)
+    dependent = None
+    if world > 1:
+        dep_steps = max(1, min(args.steps, 3))
+        with torch.cuda.stream(compute):
+            one_step(dependent=True)
+        barrier()
+        d0, d1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        d0.record(compute)
+        with torch.cuda.stream(compute):
+            for _ in range(dep_steps):
+                one_step(dependent=True)
+        d1.record(compute)
+        barrier()
+        dsec = max_over_ranks(d0.elapsed_time(d1) / 1e3)
+        dependent = {"value": round(step_flops(layers) * dep_steps / dsec / 1e12, 2), "unit": "TFLOPS",
+                     "ms_per_step": round(1e3 * dsec / dep_steps, 3), "steps": dep_steps,
+                     "note": "every linear waits until the previous linear's output is gathered on every rank "
+                             "(no overlap of a transfer with the next linear)"}
 
     # end to end: pinned host inputs -> HBM, the stack, result -> pinned host
     h_xh = x_h.cpu().pin_memory()
@@ -578,21 +916,24 @@ def run_ours(args):
             h_y.copy_(last, non_blocking=True)
     s1.record(compute)
     barrier()
-    e2e_sec = s0.elapsed_time(s1) / 1e3
-    if world > 1:
-        tt = torch.tensor([e2e_sec], device=device, dtype=torch.float64)
-        dist.all_reduce(tt, op=dist.ReduceOp.MAX)
-        e2e_sec = float(tt.item())
+    e2e_sec = max_over_ranks(s0.elapsed_time(s1) / 1e3)
     e2e_value = step_flops(layers) * e2e_steps / e2e_sec / 1e12
 
-    gemv = None
-    streamed = None
-    epilogues = None
+    parity = parity_check(raw_cache, names, layers, y_loc, y_all, x_h, x_f, world, rank, nloc,
+                          "fused" if fused else "copy" if ce else "nccl", None)
+
+    gather = None
+    if world > 1 and not args.no_extras:
+        gather = gather_measure(ctx, device, world, rank, m, nloc["w13"])
+
+    extras = {}
     cpu = None
     if rank == 0 and world == 1 and not args.no_extras:
-        gemv = gemv_measure(ctx, device, hbm_peak)
-        streamed = config4_stream(ctx, device)
-        epilogues = epilogue_measure(ctx, device)
+        extras["gemv"] = gemv_measure(ctx, device, hbm_peak)
+        extras["config1"] = config1_measure(ctx, device, tc_burst)
+        extras["config3"] = config3_measure(ctx, device, tc_sustained)
+        extras["config4_streamed"] = config4_stream(ctx, device)
+        extras["epilogues"] = epilogue_measure(ctx, device)
         # bounded CPU sample: layer 0 at cpu_rows rows, repeated until >= 10 s of work
         linears, threads = make_cpu_linears(0), os.cpu_count() or 1
         cpu_rows = args.cpu_rows or M_TOKENS
@@ -601,9 +942,10 @@ def run_ours(args):
         while t < 10.0 and reps < 20:
             dt, df, kind = cpu_reference_sample(cpu_rows, linears, threads)
             t, f, reps = t + dt, f + df, reps + 1
-        cpu = {"value": round(f / t / 1e12, 4), "unit": "TFLOPS", "cores": threads, "kind": kind,
-               "sample": f"layer 0 of the stack (5 linears): decode_cpu_into->f32 + fp32 torch matmul at "
-                         f"{cpu_rows} of {M_TOKENS} rows, {reps} repetitions, {t:.1f} s"}
+        cpu = {"value": round(f / t / 1e12, 4), "unit": "TFLOPS", "cores": threads, "cpu": cpu_model(),
+               "kind": kind,
+               "sample": f"layer 0 of the stack (5 linears): the reference's decode_cpu_into->f32 + fp32 torch "
+                         f"matmul at {cpu_rows} of {M_TOKENS} rows, {reps} repetitions, {t:.1f} s"}
 
     # DRAM bytes per GEMM launch from the committed ncu summary (mean over one layer)
     traffic = None
@@ -614,39 +956,43 @@ def run_ours(args):
         traffic = int(mt.group(1)) if mt else None
     if rank == 0:
         peak = tc_sustained
+        parallelism = ("single GPU" if world == 1 else
+                       f"N-shard x{world}, all-gather fused into the GEMM epilogue (NVLink peer stores) + device "
+                       f"flag barrier per linear" if fused else
+                       f"N-shard x{world}, all-gather by copy-engine peer pushes (one side stream per peer, "
+                       f"shard-major Y) beside the next GEMM + device flag barrier per layer" if ce else
+                       f"N-shard x{world} + NCCL all-gather" + (f" ({reserve} SMs left to it)" if reserve else ""))
+        cfg = workload_config(layers)
+        cfg.update({"operands": "X fp16, W dequantised to fp16 in TMEM, fp32 accumulate, fp16 Y",
+                    "ffn_form": ("SwiGLU: w1 / w3 as one weight, silu(w1 x) * w3 x in the GEMM epilogue"
+                                 if args.ffn == "swiglu" else "w1, w3 as separate linears (no SwiGLU op)"),
+                    "l2": "inputs larger than L2 (3 GB of packed weights streamed per step)",
+                    "weight_buffers": f"{layers} distinct HBM buffers per tensor, contents cycle over "
+                                      f"{DISTINCT_LAYERS} seeds"})
         line = {"metric": METRIC, "value": round(value, 2), "unit": "TFLOPS", "n_gpus": world, "steps": args.steps,
                 "warmup": args.warmup, "ms_per_step": round(1e3 * elapsed / args.steps, 3),
                 "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
-                "dtype": "f16", "data": "synthetic",
-                "config": {"workload": "config5_zimage_6b_linear_stack", "layers": layers, "m_tokens": m,
-                           "operands": "X fp16, W dequantised to fp16 in TMEM, fp32 accumulate, bf16 Y",
-                           "hidden": HIDDEN, "ffn": FFN, "mix": "Q4_K_M (w2 Q6_K in even layers)",
-                           "ffn_form": ("SwiGLU: w1 / w3 as one weight, silu(w1 x) * w3 x in the GEMM epilogue"
-                                        if args.ffn == "swiglu" else "w1, w3 as separate linears (no SwiGLU op)"),
-                           "parallelism": ("single GPU" if world == 1 else
-                                           f"N-shard x{world}, all-gather fused into the GEMM epilogue (NVLink "
-                                           f"peer stores) + device flag barrier per linear" if fused else
-                                           f"N-shard x{world}, all-gather by copy-engine peer pushes on a side "
-                                           f"stream (shard-major Y) + device flag barrier per layer" if ce else
-                                           f"N-shard x{world} + NCCL all-gather"
-                                           + (f" ({reserve} SMs left to it)" if reserve else "")),
-                           "l2": "inputs larger than L2 (3 GB of packed weights streamed per step)",
-                           "weights": f"{layers} distinct HBM buffers per tensor, contents cycle over "
-                                      f"{DISTINCT_LAYERS} seeds"},
+                "dtype": "f16", "data": "synthetic", "config": cfg, "parallelism": parallelism,
+                "headline_form": ("independent linears: each output's transfer overlaps the next linear"
+                                  if world > 1 else "single GPU"),
                 "gpu_launches": (len(timing) * (2 if fused else 1) + (layers if ce else 0)) * args.steps,
                 "roofline": {"bound": "tensor", "achieved": round(achieved, 2), "peak": peak, "unit": "TFLOP/s",
                              "frac": round(achieved / peak, 4), "traffic": traffic,
-                             "kernel": "pair_gemm_kernel (tcgen05 cta_group::2, A in TMEM)", "peak_source": f"{peak_src} sustained"},
+                             "traffic_source": "ncu dram bytes per launch, mean over one layer's linears, from "
+                                               "the committed capture profiles/gemm_pair_config5_layer.md",
+                             "kernel": "pair_gemm_kernel (tcgen05 cta_group::2, A in TMEM)",
+                             "peak_source": f"{peak_src} sustained"},
                 "e2e": {"value": round(e2e_value, 2), "unit": "TFLOPS",
                         "h2d_bytes_per_step": int(h_xh.numel() * 2 + h_xf.numel() * 2),
                         "d2h_bytes_per_step": int(h_y.numel() * 2), "steps": e2e_steps},
-                "clocks": clock_info, "status_word": status}
+                "parity": parity, "clocks": clock_info, "status_word": status}
+        if dependent:
+            line["dependent_chain"] = dependent
+        if gather:
+            line["gather_alone"] = gather
         if cpu:
             line["cpu_baseline"] = cpu
-        if gemv:
-            line["gemv"] = gemv
-            line["config4_streamed"] = streamed
-            line["epilogues"] = epilogues
+        line.update(extras)
         print(json.dumps(line), flush=True)
     for lw in weights:
         for wt in lw.values():

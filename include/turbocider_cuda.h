@@ -78,8 +78,9 @@ uint32_t tc_cuda_abi_version(void);
  * (cf. tc_gguf_test_error, gguf_core_probe.cpp:31). */
 const char *tc_cuda_last_error(void);
 
-/* Create a context on `device`.  The context owns the device status word and
- * reusable split-K workspace; it does not own streams. */
+/* Create a context on `device`.  The context owns the device status word,
+ * reusable workspaces (split-K partials, fp16 staging of X) and the side
+ * streams of tc_cuda_peer_push; it never takes over the caller's streams. */
 int tc_cuda_init(int device, tc_cuda_ctx **ctx);
 void tc_cuda_free(tc_cuda_ctx *ctx);
 
@@ -274,9 +275,16 @@ int tc_cuda_peer_barrier(tc_cuda_ctx *ctx, uint32_t *const *flags, uint32_t n_ra
  * (ignored for rows == 1; equal to the width: one linear copy per peer).
  * Completion on every rank: tc_cuda_peer_barrier on the same stream.  Like
  * the fused gather, this replaces the ncclAllGather that follows each
- * N-sharded linear; the reference runs on one device and has no counterpart. */
+ * N-sharded linear; the reference runs on one device and has no counterpart.
+ * The copies to different destinations run concurrently: each goes on its
+ * own side stream owned by the context (created by the first push), forked
+ * from `stream` and joined back into it, so that several copy engines share
+ * the transfer; to `stream` the push still looks like one ordered step. */
 int tc_cuda_peer_push(tc_cuda_ctx *ctx, const void *src, void *const *dst, uint32_t n_dst, uint64_t width_bytes,
                       uint64_t rows, uint64_t src_pitch, uint64_t dst_pitch, void *stream);
+/* serial != 0: tc_cuda_peer_push issues its copies back to back on `stream`
+ * (one copy engine at a time) instead of fanning them out; for comparison. */
+int tc_cuda_set_push_serial(tc_cuda_ctx *ctx, int serial);
 
 /* Batched small-M linear: Y_i[m, N_i] = X[m, K] * W_i^T for n_weights
  * (1..64) weights that share K and X (e.g. every block's AdaLN modulation
@@ -309,13 +317,20 @@ int tc_cuda_set_sm_limit(tc_cuda_ctx *ctx, int sms);
  * word) here lives in a 4 MiB file-scope device array instead of a cudaMalloc'd
  * context workspace.  No context argument; X bf16 [m, K] (16-byte aligned), Y
  * f32, f16 or bf16 with row stride ldy (0 = N), all device memory, enqueued on
- * `stream`.  The first call on a device looks up the array's address (make it
- * before any stream capture); the K-split rule keeps every shape's scratch
- * under about 0.9 MiB, and a size check rejects anything over 4 MiB;
- * every call shares the array, so calls that may overlap on the GPU must be
- * serialised by the caller.  Allocates nothing. */
+ * `stream`.  The first call on a device looks up the array's address and
+ * clears its status word, synchronously (make it before any stream capture);
+ * the K-split rule keeps every shape's scratch under about 0.9 MiB, and a
+ * size check rejects anything over 4 MiB; every call shares the array, so
+ * calls that may overlap on the GPU must be serialised by the caller.
+ * Device-side errors (TC_STATUS_* bits) accumulate in the array's status word
+ * until read with tc_cuda_small_static_status.  Allocates nothing. */
 int tc_cuda_qlinear_small_static(const tc_cuda_weight *weight, const void *x, uint32_t m, void *y, uint64_t ldy,
                                  int out_dtype, void *stream);
+/* Status word of tc_cuda_qlinear_small_static on `device` (the counterpart of
+ * tc_cuda_status for that entry point, which has no context): synchronises
+ * the device, returns the accumulated TC_STATUS_* bits and, if clear != 0,
+ * resets them.  No counterpart in the reference.  Allocates nothing. */
+int tc_cuda_small_static_status(int device, uint32_t *bits, int clear);
 
 /* ---------------------------------------------------------------- GGUF files
  * Directory parser and payload reader for GGUF v2/v3 containers, with the

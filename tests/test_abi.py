@@ -109,3 +109,24 @@ def test_quantiser_rejects_bad_input():
         tcc.quantize(14, bad)
     with pytest.raises(KeyError):
         tcc.quantize(10, np.zeros((1, 256), np.float32))
+
+
+@pytest.mark.parametrize("typ", [12, 13, 14])
+def test_numpy_quantiser_matches_tc_quantize(typ):
+    """oracle/kq_quantize.py (used where the backend library must not be
+    loaded: the CPU reference arm of bench.py) produces the same bytes as
+    tc_quantize, including all-zero sub-blocks, an all-zero row and large
+    and tiny scales."""
+    from oracle import kq_quantize
+    from turbocider_b200 import cuda as tcc
+    rng = np.random.default_rng(typ)
+    w = (rng.standard_normal((40, 1024)) * 0.02).astype(np.float32)
+    w[3] = 0.0
+    w[5, :40] = 0.0
+    w[7] *= 3000.0
+    w[9] *= 1e-6
+    w[11] = np.abs(w[11])
+    w[13] = -np.abs(w[13])
+    assert np.array_equal(kq_quantize.quantize(typ, w, threads=3), tcc.quantize(typ, w))
+    big = kq_cases.synthetic_weight(300, 2048, seed=typ)
+    assert np.array_equal(kq_quantize.quantize(typ, big), tcc.quantize(typ, big))

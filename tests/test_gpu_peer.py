@@ -180,7 +180,7 @@ def test_barrier_gives_up_on_a_missing_rank(ctx):
     assert ctx.status() == 0
 
 
-def _two_rank_worker(rank, world, port, q):
+def _two_rank_worker(rank, world, port, q, mode="fused"):
     import datetime
     import sys
     import torch
@@ -205,13 +205,31 @@ def _two_rank_worker(rank, world, port, q):
         x = torch.from_numpy(xb.view(np.int16)).view(torch.bfloat16).cuda()
         pg = PeerGroup(ctx, timeout_us=5_000_000)
         buf = pg.alloc(m * world * per * 2)
-        y = buf.tensor((m, world * per), torch.bfloat16)
-        for rep in range(3):
-            tcc.qlinear(ctx, w, x, out=y[:, rank * per:rank * per + rows], peers=pg.peers_of(buf, rank * per * 2))
-            pg.barrier()
-        torch.cuda.synchronize()
+        if mode == "fused":
+            y = buf.tensor((m, world * per), torch.bfloat16)
+            for rep in range(3):
+                tcc.qlinear(ctx, w, x, out=y[:, rank * per:rank * per + rows], peers=pg.peers_of(buf, rank * per * 2))
+                pg.barrier()
+            torch.cuda.synchronize()
+            got = y.float().cpu().numpy()[:, :n]
+        else:
+            # copy-engine gather (bench.py's default): the GEMM writes this
+            # rank's slot of a shard-major Y[world][M][per]; a side stream
+            # pushes the slot to every peer, then the flag barrier
+            y = buf.tensor((world, m, per), torch.bfloat16)
+            side = torch.cuda.Stream()
+            for rep in range(3):
+                y[rank].zero_()
+                tcc.qlinear(ctx, w, x, out=y[rank][:, :rows])
+                done = torch.cuda.Event()
+                done.record()
+                side.wait_event(done)
+                pg.push(buf, rank * m * per * 2, m * per * 2, stream=side)
+                pg.barrier(side)
+                torch.cuda.current_stream().wait_stream(side)
+            torch.cuda.synchronize()
+            got = shard.assemble(y.float().cpu().numpy(), n)
         status = ctx.status()
-        got = y.float().cpu().numpy()[:, :n]
         err = oracle.rel_l2(got, oracle.qlinear_ref(xb, raw, 12, n, k, "bf16"))
         del y
         pg.close()
@@ -222,15 +240,19 @@ def _two_rank_worker(rank, world, port, q):
         q.put((rank, -1, repr(e)))
 
 
-def test_two_rank_fused_gather():
+@pytest.mark.parametrize("mode", ["fused", "copy"])
+def test_two_rank_gather(mode):
+    """Two ranks on two GPUs: each computes its column shard and the full Y on
+    each rank matches the oracle, with the all-gather fused into the GEMM
+    epilogue or pushed by the copy engines (fanned out over side streams)."""
     import torch
     if torch.cuda.device_count() < 2:
         pytest.skip("needs two GPUs")
     import torch.multiprocessing as mp
     ctx_mp = mp.get_context("spawn")
     q = ctx_mp.Queue()
-    port = 29500 + os.getpid() % 1000
-    procs = [ctx_mp.Process(target=_two_rank_worker, args=(r, 2, port, q)) for r in range(2)]
+    port = 29500 + os.getpid() % 1000 + (7 if mode == "copy" else 0)
+    procs = [ctx_mp.Process(target=_two_rank_worker, args=(r, 2, port, q, mode)) for r in range(2)]
     for p in procs:
         p.start()
     res = [q.get(timeout=300) for _ in procs]

@@ -3,10 +3,12 @@
 It serves callers that cannot allocate device memory while running a linear
 (pre-sized memory arenas, allocator callbacks, loops that cannot absorb
 cudaMalloc's synchronisation): the split-K GEMV runs with its scratch in a
-fixed static device array.  Its output must match the existing entry point
+fixed static device array.  Its output must match the fp32-decode oracle
+(decode_cpu_into(f32) + an fp64 matmul) and the existing entry point
 (tc_cuda_qlinear, same kernel with a cudaMalloc'd workspace) within the GEMV
 tolerance used elsewhere (rel-L2 <= 1e-5), on two calls in a row -- the second
-call sees the array as the first one left it.  This file is collected last.
+call sees the array as the first one left it -- and its status word, read with
+tc_cuda_small_static_status, must stay clear.  This file is collected last.
 """
 from __future__ import annotations
 
@@ -29,15 +31,20 @@ def test_static_scratch_matches_qlinear_twice(ctx, typ, n, k, m):
     xb = kq_cases.synthetic_x_bf16(m, k, seed=m + 3)
     x = torch.from_numpy(xb.view(np.int16)).view(torch.bfloat16).cuda()
     ref = tcc.qlinear(ctx, w, x, out_dtype=tcc.F32).cpu().numpy()
+    want = oracle.qlinear_ref(xb, raw, typ, n, k, "f32")
+    assert oracle.rel_l2(ref, want) <= 1e-5
     for _ in range(2):
         y = torch.full((m, n), float("nan"), device="cuda", dtype=torch.float32)
         tcc.qlinear_small_static(w, x, out_dtype=tcc.F32, out=y)
         torch.cuda.synchronize()
         got = y.cpu().numpy()
         assert np.isfinite(got).all()
+        assert oracle.rel_l2(got, want) <= 1e-5
         assert oracle.rel_l2(got, ref) <= 1e-5
+        assert tcc.small_static_status(0) == 0
     yb = tcc.qlinear_small_static(w, x, out_dtype=tcc.BF16)
-    assert oracle.rel_l2(yb.float().cpu().numpy(), ref) <= 3e-3
+    assert oracle.rel_l2(yb.float().cpu().numpy(), want) <= 3e-3
+    assert tcc.small_static_status(0) == 0
     assert ctx.status() == 0
 
 
@@ -56,6 +63,10 @@ def test_static_scratch_covers_large_shapes_and_rejects_bad_rows(ctx):
     ref = tcc.qlinear(ctx, w, x, out_dtype=tcc.F32).cpu().numpy()
     got = tcc.qlinear_small_static(w, x, out_dtype=tcc.F32).cpu().numpy()
     assert oracle.rel_l2(got, ref) <= 1e-5
+    xb = x.view(torch.int16).cpu().numpy().view(np.uint16)
+    rows = np.arange(0, n, 7)   # every 7th output column against the fp32-decode oracle
+    sub = raw.reshape(n, -1)[rows]
+    assert oracle.rel_l2(got[:, rows], oracle.qlinear_ref(xb, sub, 12, len(rows), k, "f32")) <= 1e-5
     for n2, k2 in ((3072, 12288), (128, 256), (9000, 1024)):
         w2 = tcc.Weight.upload(ctx, 14, n2, k2, tcc.quantize(14, kq_cases.synthetic_weight(n2, k2, seed=n2)))
         x2 = torch.randn(16, k2, device="cuda").to(torch.bfloat16)
@@ -65,3 +76,4 @@ def test_static_scratch_covers_large_shapes_and_rejects_bad_rows(ctx):
     x17 = torch.zeros(17, k, device="cuda", dtype=torch.bfloat16)
     with pytest.raises(tcc.BackendError, match="1..16 rows"):
         tcc.qlinear_small_static(w, x17)
+    assert tcc.small_static_status(0) == 0

@@ -633,14 +633,16 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
 
 // ------------------------------------------------------------ host side
 PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
-    static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
-    if (!fn) {
+    // The driver entry point is process-wide; a function-local static is
+    // initialised once, thread-safely.
+    static const PFN_cuTensorMapEncodeTiled_v12000 fn = [] {
         void *ptr = nullptr;
         cudaDriverEntryPointQueryResult q;
         if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &ptr, cudaEnableDefault, &q) == cudaSuccess &&
             q == cudaDriverEntryPointSuccess)
-            fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(ptr);
-    }
+            return reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(ptr);
+        return static_cast<PFN_cuTensorMapEncodeTiled_v12000>(nullptr);
+    }();
     return fn;
 }
 
@@ -649,18 +651,20 @@ cudaError_t launch_pair_inst(const CUtensorMap &xm, const YMaps &ym, const PairP
                              cudaStream_t s) {
     using L = PairLayout<TYPE>;
     auto kernel = pair_gemm_kernel<TYPE, F16, OUT_F32>;
-    static int max_clusters = 0;   // co-resident 2-CTA clusters on this GPU
-    if (!max_clusters) {
-        cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)L::bytes);
-        if (e != cudaSuccess) return e;
+    // Shared-memory opt-in and co-resident 2-CTA clusters, per device.
+    static DeviceCache cache;
+    int max_clusters = 0;
+    cudaError_t e = per_device(cache, max_clusters, [&](int &v) {
+        cudaError_t r = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)L::bytes);
+        if (r != cudaSuccess) return r;
         cudaLaunchConfig_t q = {};
         q.gridDim = dim3(2);
         q.blockDim = dim3(kThreads);
         q.dynamicSmemBytes = L::bytes;
-        e = cudaOccupancyMaxActiveClusters(&max_clusters, kernel, &q);
-        if (e != cudaSuccess) return e;
-        if (max_clusters < 1) return cudaErrorInvalidConfiguration;
-    }
+        if ((r = cudaOccupancyMaxActiveClusters(&v, kernel, &q)) != cudaSuccess) return r;
+        return v < 1 ? cudaErrorInvalidConfiguration : cudaSuccess;
+    });
+    if (e != cudaSuccess) return e;
     uint32_t pairs = p.n_tiles < (uint32_t)max_clusters ? p.n_tiles : (uint32_t)max_clusters;
     if (sm_count >= 2 && pairs > (uint32_t)sm_count / 2) pairs = (uint32_t)sm_count / 2;
     cudaLaunchConfig_t cfg = {};

@@ -295,14 +295,14 @@ __global__ void __launch_bounds__(kThreads, 1)
 
 // ------------------------------------------------------------ host side
 PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
-    static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
-    if (!fn) {
+    static const PFN_cuTensorMapEncodeTiled_v12000 fn = [] {
         void *ptr = nullptr;
         cudaDriverEntryPointQueryResult q;
         if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &ptr, cudaEnableDefault, &q) == cudaSuccess &&
             q == cudaDriverEntryPointSuccess)
-            fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(ptr);
-    }
+            return reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(ptr);
+        return static_cast<PFN_cuTensorMapEncodeTiled_v12000>(nullptr);
+    }();
     return fn;
 }
 
@@ -310,12 +310,12 @@ template <int TYPE, int BN, bool F16, bool OUT_F32>
 cudaError_t launch_inst(const CUtensorMap &map, const GemmParams &p, int sm_count, cudaStream_t s) {
     using L = Layout<TYPE, BN>;
     auto kernel = gemm_kernel<TYPE, BN, F16, OUT_F32>;
-    static bool configured = false;
-    if (!configured) {
-        cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)L::bytes);
-        if (e != cudaSuccess) return e;
-        configured = true;
-    }
+    static DeviceCache cache;   // shared-memory opt-in, per device
+    int unused = 0;
+    cudaError_t e = per_device(cache, unused, [&](int &) {
+        return cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)L::bytes);
+    });
+    if (e != cudaSuccess) return e;
     const unsigned grid = p.n_tiles < (uint32_t)sm_count ? p.n_tiles : (unsigned)sm_count;
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(grid);

@@ -630,14 +630,13 @@ cudaError_t launch_typed(const GemvBatch &bt, uint32_t tiles, uint32_t m_begin, 
     const size_t smem = stage * gemv_stages<NT>() * kWarps;
     auto kern = out_dtype == 0 ? gemv_kernel<TYPE, TP, NT, 0>
                 : out_dtype == 1 ? gemv_kernel<TYPE, TP, NT, 1> : gemv_kernel<TYPE, TP, NT, 2>;
-    // Opt in once per instantiation to its shared-memory size.
-    static bool configured[3] = {false, false, false};
-    if (!configured[out_dtype]) {
-        const int most = (int)smem;
-        cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, most);
-        if (e != cudaSuccess) return e;
-        configured[out_dtype] = true;
-    }
+    // Opt in once per instantiation and device to its shared-memory size.
+    static DeviceCache cache[3];
+    int unused = 0;
+    cudaError_t e = per_device(cache[out_dtype], unused, [&](int &) {
+        return cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    });
+    if (e != cudaSuccess) return e;
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = grid;
     cfg.blockDim = dim3(kWarps * 32);

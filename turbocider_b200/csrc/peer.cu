@@ -134,12 +134,44 @@ int tc_cuda_peer_push(tc_cuda_ctx *ctx, const void *src, void *const *dst, uint3
     const cudaStream_t s = static_cast<cudaStream_t>(stream);
     // Contiguous regions go as one linear copy (the copy engines' fastest form).
     const bool linear = rows == 1 || (src_pitch == width_bytes && dst_pitch == width_bytes);
-    for (uint32_t i = 0; i < n_dst; ++i) {
-        cudaError_t e = linear ? cudaMemcpyAsync(dst[i], src, width_bytes * rows, cudaMemcpyDeviceToDevice, s)
-                               : cudaMemcpy2DAsync(dst[i], dst_pitch, src, src_pitch, width_bytes, rows,
-                                                   cudaMemcpyDeviceToDevice, s);
-        if (e != cudaSuccess) return tc::cuda_fail("peer push", e);
+    auto copy = [&](uint32_t i, cudaStream_t on) {
+        return linear ? cudaMemcpyAsync(dst[i], src, width_bytes * rows, cudaMemcpyDeviceToDevice, on)
+                      : cudaMemcpy2DAsync(dst[i], dst_pitch, src, src_pitch, width_bytes, rows,
+                                          cudaMemcpyDeviceToDevice, on);
+    };
+    if (ctx->push_serial || n_dst < 2) {
+        for (uint32_t i = 0; i < n_dst; ++i) {
+            cudaError_t e = copy(i, s);
+            if (e != cudaSuccess) return tc::cuda_fail("peer push", e);
+        }
+        return tc::ok();
     }
+    // Fan out: every destination's copy on its own side stream (the driver
+    // spreads streams over the copy engines), ordered after the work already
+    // on `stream`, and `stream` continues only after all of them.
+    cudaError_t e = cudaSuccess;
+    if (!ctx->push_fork) {
+        e = cudaEventCreateWithFlags(&ctx->push_fork, cudaEventDisableTiming);
+        for (uint32_t i = 0; i < tc::kMaxPeers && e == cudaSuccess; ++i) {
+            e = cudaStreamCreateWithFlags(&ctx->push_stream[i], cudaStreamNonBlocking);
+            if (e == cudaSuccess) e = cudaEventCreateWithFlags(&ctx->push_join[i], cudaEventDisableTiming);
+        }
+        if (e != cudaSuccess) return tc::cuda_fail("push stream creation", e);
+    }
+    if ((e = cudaEventRecord(ctx->push_fork, s)) != cudaSuccess) return tc::cuda_fail("peer push", e);
+    for (uint32_t i = 0; i < n_dst; ++i) {
+        const cudaStream_t side = ctx->push_stream[i];
+        if ((e = cudaStreamWaitEvent(side, ctx->push_fork, 0)) != cudaSuccess ||
+            (e = copy(i, side)) != cudaSuccess || (e = cudaEventRecord(ctx->push_join[i], side)) != cudaSuccess ||
+            (e = cudaStreamWaitEvent(s, ctx->push_join[i], 0)) != cudaSuccess)
+            return tc::cuda_fail("peer push", e);
+    }
+    return tc::ok();
+}
+
+int tc_cuda_set_push_serial(tc_cuda_ctx *ctx, int serial) {
+    if (!ctx) return tc::fail("null context");
+    ctx->push_serial = serial ? 1 : 0;
     return tc::ok();
 }
 

@@ -133,6 +133,12 @@ void tc_cuda_free(tc_cuda_ctx *ctx) {
     if (ctx->gemv_partials) cudaFree(ctx->gemv_partials);
     if (ctx->gemv_counters) cudaFree(ctx->gemv_counters);
     if (ctx->dense_ws) cudaFree(ctx->dense_ws);
+    if (ctx->split_ws) cudaFree(ctx->split_ws);
+    for (int i = 0; i < 8; ++i) {
+        if (ctx->push_stream[i]) cudaStreamDestroy(ctx->push_stream[i]);
+        if (ctx->push_join[i]) cudaEventDestroy(ctx->push_join[i]);
+    }
+    if (ctx->push_fork) cudaEventDestroy(ctx->push_fork);
     tc::dense_blas_destroy(ctx->blas);
     if (ctx->status) cudaFree(ctx->status);
     delete ctx;

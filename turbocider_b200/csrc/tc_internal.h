@@ -2,6 +2,7 @@
 // launchers.  Nothing here crosses the public ABI.
 #pragma once
 #include <cstdint>
+#include <mutex>
 #include <string>
 #include <cuda_runtime.h>
 
@@ -20,6 +21,16 @@ struct tc_cuda_ctx {
     void *blas = nullptr;            // cuBLAS handle for dense weights (created on first use)
     float *dense_ws = nullptr;       // fp32 product of a dense segment before its epilogue
     size_t dense_ws_floats = 0;
+    // Copy-engine all-gather (tc_cuda_peer_push): one side stream per
+    // destination, forked from and joined back into the caller's stream, so
+    // the copies to different peers run on several copy engines at once.
+    // Created on the first push; push_serial = 1 issues them back to back on
+    // the caller's stream instead.
+    int push_serial = 0;
+    cudaStream_t push_stream[8] = {};
+    cudaEvent_t push_fork = nullptr, push_join[8] = {};
+    float *split_ws = nullptr;       // split-K partial products of the tensor-core GEMM
+    size_t split_ws_floats = 0;
 };
 
 struct tc_cuda_weight {
@@ -43,6 +54,35 @@ namespace tc {
 
 // Sets the thread-local message returned by tc_cuda_last_error().
 void set_last_error(const std::string &reason);
+
+// Per-device launch set-up (a kernel's shared-memory opt-in, its occupancy):
+// cudaFuncSetAttribute acts on the current device only, so the result is
+// cached per device ordinal, and the cache is shared by concurrent callers.
+// Each instantiation of a launch template owns one cache.
+constexpr int kMaxDevices = 64;
+struct DeviceCache {
+    std::mutex mu;
+    bool done[kMaxDevices] = {};
+    int value[kMaxDevices] = {};
+};
+// Runs setup(int &value) once per device (the current one) and returns the
+// cached value in `out`; a failed set-up is retried on the next call.
+template <class F>
+cudaError_t per_device(DeviceCache &c, int &out, F &&setup) {
+    int dev = -1;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e != cudaSuccess) return e;
+    if (dev < 0 || dev >= kMaxDevices) return cudaErrorInvalidDevice;
+    std::lock_guard<std::mutex> lock(c.mu);
+    if (!c.done[dev]) {
+        int v = 0;
+        if ((e = setup(v)) != cudaSuccess) return e;
+        c.value[dev] = v;
+        c.done[dev] = true;
+    }
+    out = c.value[dev];
+    return cudaSuccess;
+}
 
 // Geometry handed to the kernels for one weight.
 struct WeightView {

@@ -18,12 +18,16 @@
 // and passed to the kernel as an argument.
 //
 // Contract:
-//   * the first call on a device fetches that address (one-time set-up); make
-//     that first call before capturing any stream;
+//   * the first call on a device fetches that address and clears the status
+//     word (one-time set-up, synchronous); make that first call before
+//     capturing any stream;
 //   * every call shares the one array, which keeps the previous call's
-//     contents: the counters and the status word are cleared on the call's
-//     stream before the kernel runs; the partials are fully written before
-//     they are read;
+//     contents: the per-tile counters are cleared on the call's stream before
+//     the kernel runs, and the partials are fully written before they are
+//     read;
+//   * the status word (TC_STATUS_* bits: nonfinite scale, timeout) is sticky
+//     across calls, like a context's: tc_cuda_small_static_status reads it
+//     (and optionally clears it) after synchronising the device;
 //   * calls whose kernels may overlap on the GPU (different streams, or
 //     different host threads) race on the array -- serialise them;
 //   * sizes whose scratch exceeds kScratchBytes are rejected with an error
@@ -62,11 +66,13 @@ int scratch_address(int device, void **out) {
         if (cudaGetDevice(&previous) != cudaSuccess) return fail("cudaGetDevice failed");
         if (previous != device && cudaSetDevice(device) != cudaSuccess) return fail("cudaSetDevice failed");
         void *ptr = nullptr;
-        const cudaError_t e = cudaGetSymbolAddress(&ptr, g_gemv_scratch);
+        cudaError_t e = cudaGetSymbolAddress(&ptr, g_gemv_scratch);
+        // the status word starts at zero (it is only cleared on request later)
+        if (e == cudaSuccess) e = cudaMemset(ptr, 0, kStatusBytes);
+        if (e == cudaSuccess) e = cudaDeviceSynchronize();
         if (previous != device) cudaSetDevice(previous);
         if (e != cudaSuccess)
-            return fail(std::string("cudaGetSymbolAddress of the static GEMV scratch failed: ") +
-                        cudaGetErrorString(e));
+            return fail(std::string("set-up of the static GEMV scratch failed: ") + cudaGetErrorString(e));
         g_scratch_ptr[device] = ptr;
     }
     *out = g_scratch_ptr[device];
@@ -109,14 +115,31 @@ extern "C" int tc_cuda_qlinear_small_static(const tc_cuda_weight *weight, const 
     sp.counters = reinterpret_cast<uint32_t *>(bytes + kStatusBytes);
     sp.partials = reinterpret_cast<float *>(bytes + kStatusBytes + counter_bytes);
     cudaStream_t s = static_cast<cudaStream_t>(stream);
-    // the status word and the counters must start at zero
-    cudaError_t e = cudaMemsetAsync(bytes, 0, kStatusBytes + counter_bytes, s);
+    // the per-tile counters must start at zero; the status word is sticky
+    cudaError_t e = cudaMemsetAsync(bytes + kStatusBytes, 0, counter_bytes, s);
     if (e == cudaSuccess) {
         const tc::SegmentView seg{0u, m, view};
         e = tc::launch_gemv(seg, static_cast<const uint16_t *>(x), weight->k, y, ldy, out_dtype, sp, s);
     }
     if (previous != weight->device) cudaSetDevice(previous);
     if (e != cudaSuccess) return fail(std::string("static-scratch GEMV launch: ") + cudaGetErrorString(e));
+    tc::set_last_error("");
+    return TC_CUDA_OK;
+}
+
+extern "C" int tc_cuda_small_static_status(int device, uint32_t *bits, int clear) {
+    if (!bits) return fail("null out-parameter");
+    void *base = nullptr;
+    int rc = scratch_address(device, &base);
+    if (rc) return rc;
+    int previous = -1;
+    if (cudaGetDevice(&previous) != cudaSuccess) return fail("cudaGetDevice failed");
+    if (previous != device && cudaSetDevice(device) != cudaSuccess) return fail("cudaSetDevice failed");
+    cudaError_t e = cudaDeviceSynchronize();
+    if (e == cudaSuccess) e = cudaMemcpy(bits, base, sizeof(uint32_t), cudaMemcpyDeviceToHost);
+    if (e == cudaSuccess && clear) e = cudaMemset(base, 0, sizeof(uint32_t));
+    if (previous != device) cudaSetDevice(previous);
+    if (e != cudaSuccess) return fail(std::string("static GEMV status read: ") + cudaGetErrorString(e));
     tc::set_last_error("");
     return TC_CUDA_OK;
 }

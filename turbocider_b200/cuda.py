@@ -72,12 +72,14 @@ EXPORTS = {
     "tc_cuda_peer_free": (C.c_int, [_vp, _vp]),
     "tc_cuda_peer_barrier": (C.c_int, [_vp, C.POINTER(_vp), _u32, _u32, _u32, _u32, _vp]),
     "tc_cuda_peer_push": (C.c_int, [_vp, _vp, C.POINTER(_vp), _u32, _u64, _u64, _u64, _u64, _vp]),
+    "tc_cuda_set_push_serial": (C.c_int, [_vp, C.c_int]),
     "tc_cuda_set_path": (C.c_int, [_vp, C.c_int]),
     "tc_cuda_qlinear_batched": (C.c_int, [_vp, C.POINTER(_vp), _u32, _vp, _u32, C.POINTER(_vp), C.POINTER(_u64),
                                           C.c_int, _vp]),
     "tc_cuda_set_sm_limit": (C.c_int, [_vp, C.c_int]),
     "tc_quantize": (C.c_int, [_u32, _vp, _u64, _u64, _vp, _u64, C.c_int]),
     "tc_cuda_qlinear_small_static": (C.c_int, [_vp, _vp, _u32, _vp, _u64, C.c_int, _vp]),
+    "tc_cuda_small_static_status": (C.c_int, [C.c_int, C.POINTER(_u32), C.c_int]),
     "tc_panel_bytes": (_u64, [_u32, _u64, _u64]),
     "tc_relayout_host": (C.c_int, [_u32, _vp, _u64, _u64, _u64, _u64, _u64, _vp, _u64, C.c_int]),
     "tc_cuda_weight_copy_panels": (C.c_int, [_vp, _vp, _vp, _u64, _vp]),
@@ -180,6 +182,11 @@ class Context:
     def set_sm_limit(self, sms: int):
         """SMs the tensor-core GEMM may occupy (0 = all)."""
         _check(lib().tc_cuda_set_sm_limit(self._h, sms))
+
+    def set_push_serial(self, serial: bool):
+        """Peer pushes back to back on the caller's stream (True) or fanned out
+        over one side stream per destination (False, the default)."""
+        _check(lib().tc_cuda_set_push_serial(self._h, int(serial)))
 
     def close(self):
         if self._h:
@@ -383,6 +390,14 @@ def qlinear_small_static(weight: Weight, x, out_dtype: int = BF16, out=None, str
     _check(lib().tc_cuda_qlinear_small_static(weight.handle, x.data_ptr(), x.shape[0], out.data_ptr(),
                                               out.stride(0), out_dtype, _stream_ptr(stream)))
     return out
+
+
+def small_static_status(device: int = 0, clear: bool = True) -> int:
+    """TC_STATUS_* bits accumulated by qlinear_small_static on `device`
+    (synchronises the device; clear resets them)."""
+    bits = _u32()
+    _check(lib().tc_cuda_small_static_status(device, C.byref(bits), int(clear)))
+    return bits.value
 
 
 class GGUFError(BackendError):
