@@ -302,6 +302,16 @@ int tc_cuda_qlinear_batched(tc_cuda_ctx *ctx, const tc_cuda_weight *const *weigh
  *   3 tensor-core GEMM with one-CTA tiles only (no 2-CTA pairs). */
 int tc_cuda_set_path(tc_cuda_ctx *ctx, int path);
 
+/* Which kernel family a one-segment call with m rows of X on `weight` takes
+ * under the context's current settings, and for the 2-CTA GEMM into how many
+ * K shares each tile is split (1: none; more when the call has too few tiles
+ * to occupy the GPU's SM pairs: each share's fp32 partial product goes to the
+ * context workspace and a reduce kernel adds them in order).  No launch; for
+ * tests and for sizing work.  No counterpart in the reference. */
+enum { TC_KERNEL_GEMV = 1, TC_KERNEL_GEMM_PAIR = 2, TC_KERNEL_GEMM_1CTA = 3, TC_KERNEL_DENSE = 4 };
+int tc_cuda_qlinear_plan(tc_cuda_ctx *ctx, const tc_cuda_weight *weight, uint32_t m, int stage, uint32_t *kernel,
+                         uint32_t *ksplit);
+
 /* Cap the SMs the tensor-core GEMM's persistent grid may occupy (0 = all, the
  * default).  The GEMM holds one CTA per SM for its whole run; with N-column
  * sharding a communication kernel (the all-gather of the previous linear's

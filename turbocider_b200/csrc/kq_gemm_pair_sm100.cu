@@ -85,6 +85,12 @@ struct YMaps {
 struct PairParams {
     PairSeg seg[kMaxSeg];
     uint32_t n_seg, n_tiles, kb, panels, pair_panels, n;
+    // Work units: unit u is tile u / ksplit over super-block columns
+    // [(u % ksplit) * kbu, +kbu).  ksplit > 1 (few tiles, split-K): each unit
+    // stores its fp32 partial product at y + (u % ksplit) * split_stride and a
+    // reduce kernel adds the splits in order; ksplit = 1: kbu = kb.
+    uint32_t ksplit, kbu, n_units;
+    uint64_t split_stride;
     void *y;
     uint64_t ldy;
     uint32_t *status;
@@ -199,6 +205,11 @@ __device__ __forceinline__ void tmem_st_wait() { asm volatile("tcgen05.wait::st.
 __device__ __forceinline__ void tma_store_2d(const CUtensorMap *map, uint32_t src, int x, int y) {
     asm volatile("cp.async.bulk.tensor.2d.global.shared::cta.bulk_group [%0, {%2, %3}], [%1];"
                  ::"l"(reinterpret_cast<uint64_t>(map)), "r"(src), "r"(x), "r"(y) : "memory");
+}
+// fp32 box (x = output columns, y = tokens, z = split-K share) of a 3-D map.
+__device__ __forceinline__ void tma_store_3d(const CUtensorMap *map, uint32_t src, int x, int y, int z) {
+    asm volatile("cp.async.bulk.tensor.3d.global.shared::cta.bulk_group [%0, {%2, %3, %4}], [%1];"
+                 ::"l"(reinterpret_cast<uint64_t>(map)), "r"(src), "r"(x), "r"(y), "r"(z) : "memory");
 }
 __device__ __forceinline__ void bulk_commit() { asm volatile("cp.async.bulk.commit_group;" ::: "memory"); }
 __device__ __forceinline__ void bulk_wait_read0() { asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory"); }
@@ -355,9 +366,9 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
     const uint32_t acc_empty = acc_full + 8, fin = acc_full + 16;
     uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(smem + L::misc_off);
     volatile uint32_t *abort_flag = tmem_slot + 1;
-    // Tiles of this pair: pair, pair + n_pairs, ...; 4 stages per packed chunk.
-    const uint32_t my_tiles = p.n_tiles > pair ? (p.n_tiles - pair + n_pairs - 1) / n_pairs : 0;
-    const uint32_t n_chunks = my_tiles * p.kb;
+    // Units of this pair: pair, pair + n_pairs, ...; 4 stages per packed chunk.
+    const uint32_t my_units = p.n_units > pair ? (p.n_units - pair + n_pairs - 1) / n_pairs : 0;
+    const uint32_t n_chunks = my_units * p.kbu;
 
     if (threadIdx.x == 0) {
         for (int i = 0; i < kStages; ++i) {
@@ -398,13 +409,15 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
             bool x_used[kStages] = {};
             bool ok = true;
             uint32_t i = 0;   // stage counter
-            for (uint32_t t = pair; ok && t < p.n_tiles; t += n_pairs) {
-                const int my_m = (int)(pair_tile(p, t).m0 + rank * kHalf);
-                for (uint32_t s = 0; ok && s < 4 * p.kb; ++s, ++i) {
+            for (uint32_t u = pair; ok && u < p.n_units; u += n_pairs) {
+                const int my_m = (int)(pair_tile(p, u / p.ksplit).m0 + rank * kHalf);
+                const uint32_t s0 = 4 * (u % p.ksplit) * p.kbu;   // first 64-K stage of the unit
+                for (uint32_t s = 0; ok && s < 4 * p.kbu; ++s, ++i) {
                     const uint32_t st = i % kStages, ph = (i / kStages) & 1;
                     if (!(ok = pwait(st_empty(st), ph ^ 1, ab))) break;
                     bar_expect_tx(x_full(st), L::x_stage);
-                    tma_load_2d(su32(smem + L::x_off + st * L::x_stage), &xmap, x_full(st), (int)(s * 64), my_m);
+                    tma_load_2d(su32(smem + L::x_off + st * L::x_stage), &xmap, x_full(st), (int)((s0 + s) * 64),
+                                my_m);
                     x_last[st] = ph; x_used[st] = true;
                 }
             }
@@ -420,14 +433,16 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
             uint32_t w_last[kWStages];
             bool w_used[kWStages] = {};
             bool ok = true;
-            // Chunk c of this pair's sequence: tile c / kb, K block c % kb.
-            // A missing second panel (odd panel count) re-reads the last
-            // panel; its outputs fall past N and are never stored.
+            // Chunk c of this pair's sequence: unit c / kbu, K block
+            // (unit % ksplit) * kbu + c % kbu.  A missing second panel (odd
+            // panel count) re-reads the last panel; its outputs fall past N
+            // and are never stored.
             auto chunk_src = [&](uint32_t c) -> const uint8_t * {
-                const PairTile T = pair_tile(p, pair + (c / p.kb) * n_pairs);
+                const uint32_t u = pair + (c / p.kbu) * n_pairs;
+                const PairTile T = pair_tile(p, u / p.ksplit);
                 uint32_t panel = 2 * T.pp + rank;
                 if (panel >= p.panels) panel = p.panels - 1;
-                return T.w + ((uint64_t)panel * p.kb + c % p.kb) * kChunk;
+                return T.w + ((uint64_t)panel * p.kb + (u % p.ksplit) * p.kbu + c % p.kbu) * kChunk;
             };
             for (uint32_t c = 0; c < kWStages && c < n_chunks; ++c) l2_prefetch(chunk_src(c), kChunk);
             for (uint32_t c = 0; ok && c < n_chunks; ++c) {
@@ -448,10 +463,10 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
             constexpr uint32_t idesc = pair_idesc<F16>();
             bool ok = true;
             uint32_t i = 0;   // stage counter
-            for (uint32_t tt = 0; ok && tt < my_tiles; ++tt) {
+            for (uint32_t tt = 0; ok && tt < my_units; ++tt) {
                 if (!(ok = pwait(acc_empty, (tt & 1) ^ 1, ab))) break;
                 tc_fence_after();
-                for (uint32_t s = 0; ok && s < 4 * p.kb; ++s, ++i) {
+                for (uint32_t s = 0; ok && s < 4 * p.kbu; ++s, ++i) {
                     const uint32_t st = i % kStages, ph = (i / kStages) & 1;
                     if (!(ok = pwait(x_full(st), ph, ab))) break;
                     if (!(ok = pwait(a_full(st), ph, ab))) break;
@@ -517,16 +532,72 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
         // stores are issued.
         const uint32_t quad = warp & 3;   // TMEM lanes 32*quad .. +31
         uint8_t *stage = smem + L::e_off + quad * L::e_warp;
-        for (uint32_t tt = 0; tt < my_tiles; ++tt) {
-            const PairTile T = pair_tile(p, pair + tt * n_pairs);
+        for (uint32_t tt = 0; tt < my_units; ++tt) {
+            const uint32_t u = pair + tt * n_pairs;
+            const PairTile T = pair_tile(p, u / p.ksplit);
+            const uint64_t yoff = (uint64_t)(u % p.ksplit) * p.split_stride;   // split-K partial slice
             const uint32_t n0 = (2 * T.pp + rank) * 128 + quad * 32, n = n0 + lane;
             if (!__all_sync(0xffffffffu, pwait(acc_full, tt & 1, ab))) break;
             tc_fence_after();
-            if (!OUT_F32 && p.y_tma) {
+            if (p.y_tma) {
                 if (lane == 0) bulk_wait_read0();   // the last tile's stores have read the staging area
                 __syncwarp();
             }
             const uint32_t taddr = tmem + ((quad * 32) << 16);
+            if (OUT_F32 && p.y_tma) {
+                // Plain fp32 tile (also every split-K partial): 32-token x
+                // 32-output fp32 boxes (4 KB) staged in shared memory and
+                // written by TMA stores -- per-element stores from the four
+                // epilogue warps measured several times slower.  The warp's
+                // 16 KB staging area holds four boxes, so the eight pieces go
+                // out in two rounds; TMEM is released after the second
+                // round's loads.  Ragged pieces are stored directly.
+                const uint32_t split = u % p.ksplit;
+#pragma unroll 1
+                for (uint32_t half = 0; half < 2; ++half) {
+                    if (half) {
+                        if (lane == 0) bulk_wait_read0();   // round 0 has left the staging area
+                        __syncwarp();
+                    }
+                    uint32_t boxes = 0;
+#pragma unroll 1
+                    for (uint32_t jj = 0; jj < 4; ++jj) {
+                        const uint32_t j = 4 * half + jj, t0 = T.m0 + 32 * j;
+                        if (t0 >= T.m_end || n0 >= p.n) break;
+                        uint32_t v[32];
+                        tmem_ld32(taddr + 32 * j, v);
+                        if (t0 + 32 <= T.m_end && n0 + 32 <= p.n) {
+                            float *sb = reinterpret_cast<float *>(stage + jj * 4096) + lane;
+#pragma unroll
+                            for (uint32_t c = 0; c < 32; ++c) sb[c * 32] = __uint_as_float(v[c]);
+                            boxes |= 1u << jj;
+                        } else if (n < p.n) {
+#pragma unroll
+                            for (uint32_t c = 0; c < 32; ++c)
+                                if (t0 + c < T.m_end)
+                                    static_cast<float *>(p.y)[yoff + (uint64_t)(t0 + c) * p.ldy + n] =
+                                        __uint_as_float(v[c]);
+                        }
+                    }
+                    if (half) {   // every TMEM load of the tile is done: hand D back
+                        tc_fence_before();
+                        __syncwarp();
+                        if (lane == 0) bar_arrive_cluster(cluster_addr(acc_empty, 0));
+                    }
+                    if (boxes) {
+                        fence_proxy_async();
+                        __syncwarp();
+                        if (lane == 0) {
+                            for (uint32_t jj = 0; jj < 4; ++jj)
+                                if (boxes & (1u << jj))
+                                    tma_store_3d(&ymaps.m[0], su32(stage + jj * 4096), (int)n0,
+                                                 (int)(T.m0 + 32 * (4 * half + jj)), (int)split);
+                            bulk_commit();
+                        }
+                    }
+                }
+                continue;
+            }
             uint32_t tma_pieces = 0;   // bit j: piece j goes out by TMA
             const bool f16 = p.epi.out_f16;
             // Fused epilogue (p.epi.flags): bias / GELU / SwiGLU are applied on
@@ -593,7 +664,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
                     for (uint32_t c = 0; c < 32; ++c) {
                         const uint32_t m = t0 + c;
                         if (m < T.m_end)
-                            store_out_all(p.epi, p.y, (uint64_t)m * p.ldy + n, __uint_as_float(v[c]), OUT_F32, f16);
+                            store_out_all(p.epi, p.y, yoff + (uint64_t)m * p.ldy + n, __uint_as_float(v[c]), OUT_F32,
+                                          f16);
                     }
                 }
             }
@@ -665,7 +737,7 @@ cudaError_t launch_pair_inst(const CUtensorMap &xm, const YMaps &ym, const PairP
         return v < 1 ? cudaErrorInvalidConfiguration : cudaSuccess;
     });
     if (e != cudaSuccess) return e;
-    uint32_t pairs = p.n_tiles < (uint32_t)max_clusters ? p.n_tiles : (uint32_t)max_clusters;
+    uint32_t pairs = p.n_units < (uint32_t)max_clusters ? p.n_units : (uint32_t)max_clusters;
     if (sm_count >= 2 && pairs > (uint32_t)sm_count / 2) pairs = (uint32_t)sm_count / 2;
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(2 * pairs);
@@ -680,11 +752,58 @@ cudaError_t launch_pair_inst(const CUtensorMap &xm, const YMaps &ym, const PairP
     return cudaLaunchKernelEx(&cfg, kernel, xm, ym, p);
 }
 
+// fp32 Y (or split-K partials) as a 3-D tensor map: x = output columns (n),
+// y = tokens (m_total, row pitch ld), z = split-K share (pitch `plane`
+// elements); 32 x 32 x 1 boxes.  Base and pitches must be 16-byte aligned.
+bool encode_f32_map(PFN_cuTensorMapEncodeTiled_v12000 enc, CUtensorMap *map, void *base, uint32_t n,
+                    uint64_t m_total, uint64_t ld, uint32_t planes, uint64_t plane) {
+    if ((reinterpret_cast<uintptr_t>(base) & 15u) || (ld * 4) % 16 || (plane * 4) % 16) return false;
+    const cuuint64_t dims[3] = {n, m_total, planes};
+    const cuuint64_t strides[2] = {ld * 4, plane * 4};
+    const cuuint32_t box[3] = {32u, 32u, 1u};
+    const cuuint32_t estr[3] = {1u, 1u, 1u};
+    return enc(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 3, base, dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+               CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_NONE,
+               CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+uint32_t pair_tiles(const SegmentView *segs, uint32_t n_seg) {
+    const uint32_t pair_panels = (segs[0].w.panels + 1) / 2;
+    uint32_t tiles = 0;
+    for (uint32_t i = 0; i < n_seg; ++i)
+        tiles += (segs[i].m_end - segs[i].m_begin + kTileTokens - 1) / kTileTokens * pair_panels;
+    return tiles;
+}
+
+}  // namespace
+
+uint32_t pair_ksplit(const SegmentView *segs, uint32_t n_seg, int sm_count) {
+    if (!n_seg) return 1;
+    const uint32_t tiles = pair_tiles(segs, n_seg), clusters = (uint32_t)max(sm_count, 2) / 2, kb = segs[0].w.kb;
+    if (!tiles || 2 * tiles >= clusters) return 1;   // at least half the pairs busy without a split
+    // The divisor of kb (at most 16 shares, the reduce kernel's limit) that
+    // fills the most pairs in one wave.
+    uint32_t best = 1;
+    for (uint32_t d = 2; d <= kb && d <= 16 && d * tiles <= clusters; ++d)
+        if (kb % d == 0) best = d;
+    return best;
+}
+
+cudaError_t launch_split_reduce(const float *part, uint32_t ksplit, uint64_t stride, uint32_t n_w, uint32_t m_begin,
+                                uint32_t rows, const EpiView &e, uint32_t gate_row, void *y, uint64_t ldy,
+                                int out_dtype, cudaStream_t s);
+
+namespace {
+
+cudaError_t launch_pair_split(const CUtensorMap &xm, const YMaps &ym, PairParams p, const SegmentView *segs,
+                              uint32_t n_seg, const SplitK &sk, void *y, uint64_t ldy, int out_dtype, int stage_f16,
+                              uint64_t m_total, int sm_count, cudaStream_t s);
+
 }  // namespace
 
 cudaError_t launch_gemm_pair(const SegmentView *segs, uint32_t n_seg, const uint16_t *x, uint64_t m_total,
                              uint64_t k, void *y, uint64_t ldy, int out_dtype, int stage_f16, int sm_count,
-                             uint32_t *status, cudaStream_t s, const EpiView *epi) {
+                             uint32_t *status, cudaStream_t s, const EpiView *epi, const SplitK *split) {
     if (n_seg == 0) return cudaSuccess;
     if (n_seg > (uint32_t)kMaxSeg) return cudaErrorInvalidValue;
     PairParams p{};
@@ -705,6 +824,10 @@ cudaError_t launch_gemm_pair(const SegmentView *segs, uint32_t n_seg, const uint
     }
     p.n_tiles = tiles;
     if (!tiles) return cudaSuccess;
+    p.ksplit = 1;
+    p.kbu = p.kb;
+    p.n_units = tiles;
+    p.split_stride = 0;
 
     auto enc = encode_fn();
     if (!enc) return cudaErrorNotSupported;
@@ -738,6 +861,13 @@ cudaError_t launch_gemm_pair(const SegmentView *segs, uint32_t n_seg, const uint
                      CU_TENSOR_MAP_L2_PROMOTION_NONE, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
         }
         p.y_tma = ok ? 1u : 0u;
+    } else if (out_f32 && !p.epi.flags && !p.epi.n_peer && (reinterpret_cast<uintptr_t>(y) & 15u) == 0 &&
+               (ldy * 4) % 16 == 0) {
+        p.y_tma = encode_f32_map(enc, &ym.m[0], y, p.n, m_total, ldy, 1, m_total * ldy) ? 1u : 0u;
+    }
+    if (split && split->ksplit > 1) {
+        if (!split->ws || p.kb % split->ksplit) return cudaErrorInvalidValue;
+        return launch_pair_split(xm, ym, p, segs, n_seg, *split, y, ldy, out_dtype, stage_f16, m_total, sm_count, s);
     }
     const uint32_t type = segs[0].w.type;
     if (type == 12) {
@@ -751,5 +881,38 @@ cudaError_t launch_gemm_pair(const SegmentView *segs, uint32_t n_seg, const uint
     if (stage_f16) return out_f32 ? launch_pair_inst<14, true, true>(xm, ym, p, sm_count, s) : launch_pair_inst<14, true, false>(xm, ym, p, sm_count, s);
     return out_f32 ? launch_pair_inst<14, false, true>(xm, ym, p, sm_count, s) : launch_pair_inst<14, false, false>(xm, ym, p, sm_count, s);
 }
+
+namespace {
+// Split-K launch: the units store fp32 partials (plain stores, no epilogue,
+// no peers) into sk.ws; one reduce per segment adds them in split order and
+// writes Y (with the call's epilogue and peer replicas).
+cudaError_t launch_pair_split(const CUtensorMap &xm, const YMaps &ym, PairParams p, const SegmentView *segs,
+                              uint32_t n_seg, const SplitK &sk, void *y, uint64_t ldy, int out_dtype, int stage_f16,
+                              uint64_t m_total, int sm_count, cudaStream_t s) {
+    const EpiView epi = p.epi;
+    p.ksplit = sk.ksplit;
+    p.kbu = p.kb / sk.ksplit;
+    p.n_units = p.n_tiles * sk.ksplit;
+    p.split_stride = m_total * p.n;
+    p.y = sk.ws;
+    p.ldy = p.n;
+    p.epi = EpiView{};
+    YMaps pm;
+    memset(&pm, 0, sizeof(pm));
+    p.y_tma = encode_f32_map(encode_fn(), &pm.m[0], sk.ws, p.n, m_total, p.n, sk.ksplit, p.split_stride) ? 1u : 0u;
+    cudaError_t e;
+    const uint32_t type = segs[0].w.type;
+    if (type == 12) e = stage_f16 ? launch_pair_inst<12, true, true>(xm, pm, p, sm_count, s)
+                                  : launch_pair_inst<12, false, true>(xm, pm, p, sm_count, s);
+    else if (type == 13) e = stage_f16 ? launch_pair_inst<13, true, true>(xm, pm, p, sm_count, s)
+                                       : launch_pair_inst<13, false, true>(xm, pm, p, sm_count, s);
+    else e = stage_f16 ? launch_pair_inst<14, true, true>(xm, pm, p, sm_count, s)
+                       : launch_pair_inst<14, false, true>(xm, pm, p, sm_count, s);
+    for (uint32_t i = 0; i < n_seg && e == cudaSuccess; ++i)
+        e = launch_split_reduce(sk.ws, sk.ksplit, p.split_stride, p.n, segs[i].m_begin, segs[i].m_end - segs[i].m_begin,
+                                epi, segs[i].gate_row, y, ldy, out_dtype, s);
+    return e;
+}
+}  // namespace
 
 }  // namespace tc

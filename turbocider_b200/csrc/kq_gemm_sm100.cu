@@ -340,14 +340,15 @@ cudaError_t launch_bn(const CUtensorMap &map, const GemmParams &p, int f16, int 
 
 cudaError_t launch_gemm(const SegmentView *segs, uint32_t n_seg, const uint16_t *x, uint64_t m_total, uint64_t k,
                         void *y, uint64_t ldy, int out_dtype, int stage_f16, int sm_count, uint32_t *status,
-                        int allow_pair, cudaStream_t s, const EpiView *epi) {
+                        int allow_pair, cudaStream_t s, const EpiView *epi, const SplitK *split) {
     if (n_seg == 0) return cudaSuccess;
     if (n_seg > (uint32_t)kMaxSeg) return cudaErrorInvalidValue;
     uint32_t max_rows = 0;
     for (uint32_t i = 0; i < n_seg; ++i) max_rows = max(max_rows, segs[i].m_end - segs[i].m_begin);
     const int bn = max_rows <= 64 ? 64 : max_rows <= 128 ? 128 : 256;
     if (bn == 256 && allow_pair)
-        return launch_gemm_pair(segs, n_seg, x, m_total, k, y, ldy, out_dtype, stage_f16, sm_count, status, s, epi);
+        return launch_gemm_pair(segs, n_seg, x, m_total, k, y, ldy, out_dtype, stage_f16, sm_count, status, s, epi,
+                                split);
     GemmParams p{};
     p.n_seg = n_seg;
     p.kb = segs[0].w.kb;

@@ -450,6 +450,32 @@ int tc_cuda_qlinear_batched(tc_cuda_ctx *ctx, const tc_cuda_weight *const *weigh
     return ok();
 }
 
+int tc_cuda_qlinear_plan(tc_cuda_ctx *ctx, const tc_cuda_weight *w, uint32_t m, int stage, uint32_t *kernel,
+                         uint32_t *ksplit) {
+    if (!ctx || !w || !kernel || !ksplit) return fail("null argument");
+    if (stage != TC_STAGE_BF16 && stage != TC_STAGE_F16 && stage != TC_STAGE_F16_X16)
+        return fail("invalid staging precision");
+    *ksplit = 1;
+    if (w->raw) {
+        *kernel = TC_KERNEL_DENSE;
+        return ok();
+    }
+    const bool small = m <= 16 && stage != TC_STAGE_F16_X16;
+    if ((small && ctx->path < 2) || ctx->path == 1) {
+        *kernel = TC_KERNEL_GEMV;
+        return ok();
+    }
+    if (m <= 128 || ctx->path == 3) {
+        *kernel = TC_KERNEL_GEMM_1CTA;
+        return ok();
+    }
+    *kernel = TC_KERNEL_GEMM_PAIR;
+    const tc::SegmentView sv{0u, m, view_of(w)};
+    const int sms = ctx->sm_limit > 0 ? std::min(ctx->sm_limit, ctx->sm_count) : ctx->sm_count;
+    if (!(w->glu && w->n % 16)) *ksplit = tc::pair_ksplit(&sv, 1, sms);
+    return ok();
+}
+
 int tc_cuda_set_sm_limit(tc_cuda_ctx *ctx, int sms) {
     if (!ctx) return fail("null context");
     if (sms < 0) return fail("negative SM limit");
@@ -589,14 +615,33 @@ int tc_cuda_qlinear_gather(tc_cuda_ctx *ctx, const tc_cuda_weight *const *weight
         if (e != cudaSuccess) return cuda_fail("fp16 staging launch", e);
         xg = static_cast<const uint16_t *>(ctx->workspace);
     }
+    const int gemm_sms = ctx->sm_limit > 0 ? std::min(ctx->sm_limit, ctx->sm_count) : ctx->sm_count;
     for (int t = 0; t < 3; ++t) {
         for (size_t i = 0; i < gemm[t].size(); i += 32) {
             const uint32_t cnt = (uint32_t)std::min<size_t>(32, gemm[t].size() - i);
-            cudaError_t e = tc::launch_gemm(gemm[t].data() + i, cnt, xg, m_total, k, y, ldy, out_dtype,
-                                            stage != TC_STAGE_BF16,
-                                            ctx->sm_limit > 0 ? std::min(ctx->sm_limit, ctx->sm_count) : ctx->sm_count,
-                                            ctx->status,
-                                            ctx->path != 3, s, &epi);
+            const tc::SegmentView *sv = gemm[t].data() + i;
+            // Split-K for the 2-CTA path when its tiles cannot fill the SM
+            // pairs (SwiGLU weights only with whole 16-row gate / up groups).
+            tc::SplitK sk;
+            uint32_t max_rows = 0;
+            for (uint32_t j = 0; j < cnt; ++j) max_rows = std::max(max_rows, sv[j].m_end - sv[j].m_begin);
+            if (ctx->path != 3 && max_rows > 128 && !(w0->glu && w0->n % 16)) {
+                sk.ksplit = tc::pair_ksplit(sv, cnt, gemm_sms);
+                if (sk.ksplit > 1) {
+                    const size_t need = tc::pair_split_floats(sk.ksplit, m_total, (uint32_t)w0->n);
+                    if (need > ctx->split_ws_floats) {
+                        if (ctx->split_ws) cudaFree(ctx->split_ws);
+                        ctx->split_ws = nullptr;
+                        ctx->split_ws_floats = 0;
+                        cudaError_t e = cudaMalloc(&ctx->split_ws, need * sizeof(float));
+                        if (e != cudaSuccess) return cuda_fail("split-K workspace allocation", e);
+                        ctx->split_ws_floats = need;
+                    }
+                    sk.ws = ctx->split_ws;
+                }
+            }
+            cudaError_t e = tc::launch_gemm(sv, cnt, xg, m_total, k, y, ldy, out_dtype, stage != TC_STAGE_BF16,
+                                            gemm_sms, ctx->status, ctx->path != 3, s, &epi, &sk);
             if (e != cudaSuccess) return cuda_fail("GEMM launch", e);
         }
     }

@@ -165,17 +165,38 @@ cudaError_t launch_gemv(const SegmentView &seg, const uint16_t *x, uint64_t k, v
                         const EpiView *epi = nullptr);
 cudaError_t launch_x_to_f16(const uint16_t *x, uint16_t *x16, uint64_t count, uint32_t *status,
                             cudaStream_t s);
+// Split-K of the 2-CTA GEMM when a call has too few 256 x 256 tiles to fill
+// the GPU (e.g. 256 tokens x 3072 rows: 12 tiles for 74 SM pairs): each tile
+// becomes ksplit work units over equal shares of the super-block columns,
+// each unit stores its fp32 partial product in `ws` ([ksplit][m_total][n]),
+// and a reduce kernel adds the shares in split order (deterministic) and
+// applies the fused epilogue.
+struct SplitK {
+    uint32_t ksplit = 1;
+    float *ws = nullptr;
+};
+// ksplit for these segments on `sm_count` SMs (1: no split); the 2-CTA path
+// only (a segment longer than 128 rows).
+uint32_t pair_ksplit(const SegmentView *segs, uint32_t n_seg, int sm_count);
+inline size_t pair_split_floats(uint32_t ksplit, uint64_t m_total, uint32_t n) {
+    return ksplit > 1 ? (size_t)ksplit * m_total * n : 0;
+}
 // Tensor-core GEMM over a list of segments that share type, N and K.  Uses
 // 2-CTA (cta_group::2) 256 x 256 tiles when a segment has more than 128 rows
 // and allow_pair is set, one-CTA 128 x {64, 128, 256} tiles otherwise.
 cudaError_t launch_gemm(const SegmentView *segs, uint32_t n_seg, const uint16_t *x,
                         uint64_t m_total, uint64_t k, void *y, uint64_t ldy, int out_dtype,
                         int stage_f16, int sm_count, uint32_t *status, int allow_pair, cudaStream_t s,
-                        const EpiView *epi = nullptr);
+                        const EpiView *epi = nullptr, const SplitK *split = nullptr);
 cudaError_t launch_gemm_pair(const SegmentView *segs, uint32_t n_seg, const uint16_t *x,
                              uint64_t m_total, uint64_t k, void *y, uint64_t ldy, int out_dtype,
                              int stage_f16, int sm_count, uint32_t *status, cudaStream_t s,
-                             const EpiView *epi = nullptr);
+                             const EpiView *epi = nullptr, const SplitK *split = nullptr);
+// Y rows [m_begin, +rows) = epilogue(sum over s < ksplit of part[s][m][.]) in
+// split order; n_w = the weight's rows (SwiGLU: gate / up interleaved).
+cudaError_t launch_split_reduce(const float *part, uint32_t ksplit, uint64_t stride, uint32_t n_w, uint32_t m_begin,
+                                uint32_t rows, const EpiView &e, uint32_t gate_row, void *y, uint64_t ldy,
+                                int out_dtype, cudaStream_t s);
 
 // Dense (passthrough) weights, dense_linear.cu.
 bool dense_type(uint32_t type);

@@ -77,6 +77,7 @@ EXPORTS = {
     "tc_cuda_qlinear_batched": (C.c_int, [_vp, C.POINTER(_vp), _u32, _vp, _u32, C.POINTER(_vp), C.POINTER(_u64),
                                           C.c_int, _vp]),
     "tc_cuda_set_sm_limit": (C.c_int, [_vp, C.c_int]),
+    "tc_cuda_qlinear_plan": (C.c_int, [_vp, _vp, _u32, C.c_int, C.POINTER(_u32), C.POINTER(_u32)]),
     "tc_quantize": (C.c_int, [_u32, _vp, _u64, _u64, _vp, _u64, C.c_int]),
     "tc_cuda_qlinear_small_static": (C.c_int, [_vp, _vp, _u32, _vp, _u64, C.c_int, _vp]),
     "tc_cuda_small_static_status": (C.c_int, [C.c_int, C.POINTER(_u32), C.c_int]),
@@ -182,6 +183,13 @@ class Context:
     def set_sm_limit(self, sms: int):
         """SMs the tensor-core GEMM may occupy (0 = all)."""
         _check(lib().tc_cuda_set_sm_limit(self._h, sms))
+
+    def plan(self, weight, m: int, stage: int = STAGE_BF16) -> tuple[int, int]:
+        """(kernel family, K splits) a one-segment call with m rows would use:
+        kernel 1 GEMV, 2 2-CTA GEMM, 3 one-CTA GEMM, 4 dense."""
+        kern, split = _u32(), _u32()
+        _check(lib().tc_cuda_qlinear_plan(self._h, weight.handle, m, stage, C.byref(kern), C.byref(split)))
+        return kern.value, split.value
 
     def set_push_serial(self, serial: bool):
         """Peer pushes back to back on the caller's stream (True) or fanned out
