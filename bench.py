@@ -591,9 +591,9 @@ def config3_measure(ctx, device, tc_sustained):
 # ---------------------------------------------------------------- multi-GPU
 def gather_measure(ctx, device, world, rank, m, width):
     """The all-gather alone (no GEMM running): one rank's shard of `m` rows x
-    `width` fp16 columns goes to every other rank, by copy-engine pushes fanned
-    out over one side stream per peer, by the same pushes back to back on one
-    stream, and by NCCL all_gather_into_tensor.  GB/s = bytes each GPU
+    `width` fp16 columns goes to every other rank, by copy-engine pushes back
+    to back on one stream or spread over 2, 4 or world - 1 side streams, and
+    by NCCL all_gather_into_tensor.  GB/s = bytes each GPU
     receives ((world - 1) shards) / time, max over ranks."""
     import torch
     import torch.distributed as dist
@@ -623,11 +623,14 @@ def gather_measure(ctx, device, world, rank, m, width):
         pg.push(buf, rank * shard, shard, stream=s)
         pg.barrier(s)
 
-    for mode, serial in (("push_fanout", False), ("push_serial", True)):
-        ctx.set_push_serial(serial)
+    for streams in sorted({1, 2, 4, world - 1}):
+        if streams > world - 1:
+            continue
+        ctx.set_push_fanout(streams)
         t = timed(push)
-        out[mode] = {"ms": round(t * 1e3, 3), "gbs_in_per_gpu": round((world - 1) * shard / t / 1e9, 1)}
-    ctx.set_push_serial(False)
+        out["push_serial" if streams == 1 else f"push_{streams}_streams"] = {
+            "ms": round(t * 1e3, 3), "gbs_in_per_gpu": round((world - 1) * shard / t / 1e9, 1)}
+    ctx.set_push_fanout(0)
     src = torch.zeros(m, width, device=device, dtype=torch.float16)
     dst = torch.empty(world * m, width, device=device, dtype=torch.float16)
 
@@ -745,6 +748,7 @@ def run_ours(args):
     x_f = torch.randn(m, FFN, generator=g, device=device).to(torch.float16)
     compute = torch.cuda.Stream(device)
     comm = torch.cuda.Stream(device)
+    sync = torch.cuda.Stream(device)   # per-layer completion barriers, off the push stream
     names = [l[0] for l in layer_linears(0)]
     if args.ffn == "swiglu":
         names = ["w13" if nm == "w1" else nm for nm in names if nm != "w3"]
@@ -764,6 +768,7 @@ def run_ours(args):
         # barrier per layer on that stream marks every rank's Y complete.
         from turbocider_b200.peer import PeerGroup
         pg = PeerGroup(ctx, timeout_us=20_000_000)
+        ctx.set_push_fanout(args.push_streams)
         y_sym = {(name, b): pg.alloc(world * m * nloc[name] * 2) for name in names for b in (0, 1)}
         y_all = {key: buf.tensor((world, m, nloc[key[0]]), f16) for key, buf in y_sym.items()}
         y_loc = {key: y_all[key][rank][:, :weights[0][key[0]].n_out] for key in y_all}
@@ -834,9 +839,16 @@ def run_ours(args):
                     gathered[(name, b)] = ev
                     prev = ev
             if ce and not dependent:
-                pg.barrier(comm)        # every rank's outputs of this layer complete
+                # every rank's outputs of this layer complete: a flag barrier
+                # ordered after this rank's pushes, on its own stream so that
+                # the next layer's pushes do not queue behind the slowest rank
+                pushed = torch.cuda.Event()
+                pushed.record(comm)
+                sync.wait_event(pushed)
+                pg.barrier(sync)
         if world > 1 and not fused:
             compute.wait_stream(comm)
+            compute.wait_stream(sync)
 
     def barrier():
         if world > 1:
@@ -925,6 +937,7 @@ def run_ours(args):
     gather = None
     if world > 1 and not args.no_extras:
         gather = gather_measure(ctx, device, world, rank, m, nloc["w13"])
+        ctx.set_push_fanout(args.push_streams)
 
     extras = {}
     cpu = None
@@ -959,8 +972,10 @@ def run_ours(args):
         parallelism = ("single GPU" if world == 1 else
                        f"N-shard x{world}, all-gather fused into the GEMM epilogue (NVLink peer stores) + device "
                        f"flag barrier per linear" if fused else
-                       f"N-shard x{world}, all-gather by copy-engine peer pushes (one side stream per peer, "
-                       f"shard-major Y) beside the next GEMM + device flag barrier per layer" if ce else
+                       f"N-shard x{world}, all-gather by copy-engine peer pushes ("
+                       + ("back to back on a side stream" if args.push_streams < 2 else
+                          f"over {args.push_streams} side streams")
+                       + ", shard-major Y) beside the next GEMM + device flag barrier per layer" if ce else
                        f"N-shard x{world} + NCCL all-gather" + (f" ({reserve} SMs left to it)" if reserve else ""))
         cfg = workload_config(layers)
         cfg.update({"operands": "X fp16, W dequantised to fp16 in TMEM, fp32 accumulate, fp16 Y",
@@ -1022,6 +1037,9 @@ def main():
                          "engines beside the next GEMM, or NCCL after each GEMM")
     ap.add_argument("--ffn", choices=["swiglu", "separate"], default="swiglu",
                     help="FFN input projections: one SwiGLU-fused weight (silu(w1 x) * w3 x) or two plain linears")
+    ap.add_argument("--push-streams", type=int, default=0,
+                    help="--gather copy: spread each output's peer copies over this many side streams "
+                         "(0 / 1: back to back, the default)")
     ap.add_argument("--reserve-sms", type=int, default=None,
                     help="SMs kept free of the GEMM for the all-gather (default 0: measured no gain at N=2)")
     args = ap.parse_args()

@@ -113,8 +113,9 @@ def test_dense_weight_replicas(ctx):
     assert torch.equal(ys[0], ys[1]) and not ys[0][:, :n].any()
 
 
+@pytest.mark.parametrize("fanout", [0, 2])
 @pytest.mark.parametrize("layout", ["shard_major", "strided"])
-def test_copy_engine_push_fills_every_replica(ctx, layout):
+def test_copy_engine_push_fills_every_replica(ctx, layout, fanout):
     """tc_cuda_peer_push: this rank's shard of a GEMM output reaches the same
     place in every replica (linear copies for a shard-major Y[g][M][N/g], 2-D
     copies for column shards of Y[M, N]); nothing outside the shard is written."""
@@ -136,9 +137,13 @@ def test_copy_engine_push_fills_every_replica(ctx, layout):
         offset = rank * n * 2
     tcc.qlinear(ctx, w, x, out=shard)
     dst = (C.c_void_p * (world - 1))(*[ys[i].data_ptr() + offset for i in range(1, world)])
-    for _ in range(2):
-        tcc._check(tcc.lib().tc_cuda_peer_push(ctx.handle, C.c_void_p(src), dst, world - 1, width, rows, pitch,
-                                               pitch, None))
+    ctx.set_push_fanout(fanout)
+    try:
+        for _ in range(2):
+            tcc._check(tcc.lib().tc_cuda_peer_push(ctx.handle, C.c_void_p(src), dst, world - 1, width, rows, pitch,
+                                                   pitch, None))
+    finally:
+        ctx.set_push_fanout(0)
     torch.cuda.synchronize()
     assert ctx.status() == 0
     assert shard.abs().sum() > 0

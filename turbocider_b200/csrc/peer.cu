@@ -14,6 +14,7 @@
 // limit, until every rank's flag in its own array reached the epoch.  On
 // timeout it sets TC_STATUS_TIMEOUT and returns; it never traps.  The ranks are
 // separate processes on separate GPUs, so the waiting kernels run concurrently.
+#include <algorithm>
 #include <cstring>
 #include <string>
 
@@ -139,16 +140,19 @@ int tc_cuda_peer_push(tc_cuda_ctx *ctx, const void *src, void *const *dst, uint3
                       : cudaMemcpy2DAsync(dst[i], dst_pitch, src, src_pitch, width_bytes, rows,
                                           cudaMemcpyDeviceToDevice, on);
     };
-    if (ctx->push_serial || n_dst < 2) {
+    const uint32_t lanes = std::min<uint32_t>((uint32_t)ctx->push_fanout, n_dst);
+    if (lanes < 2) {
         for (uint32_t i = 0; i < n_dst; ++i) {
             cudaError_t e = copy(i, s);
             if (e != cudaSuccess) return tc::cuda_fail("peer push", e);
         }
         return tc::ok();
     }
-    // Fan out: every destination's copy on its own side stream (the driver
-    // spreads streams over the copy engines), ordered after the work already
-    // on `stream`, and `stream` continues only after all of them.
+    // Fan out over `lanes` side streams (destination i on stream i % lanes,
+    // back to back within a stream), ordered after the work already on
+    // `stream`; `stream` continues only after all of them.  (Measured on 8
+    // B200s with one stream per peer: 369 GB/s received per GPU, against
+    // 535 GB/s for the same copies back to back -- the copies contend.)
     cudaError_t e = cudaSuccess;
     if (!ctx->push_fork) {
         e = cudaEventCreateWithFlags(&ctx->push_fork, cudaEventDisableTiming);
@@ -159,19 +163,22 @@ int tc_cuda_peer_push(tc_cuda_ctx *ctx, const void *src, void *const *dst, uint3
         if (e != cudaSuccess) return tc::cuda_fail("push stream creation", e);
     }
     if ((e = cudaEventRecord(ctx->push_fork, s)) != cudaSuccess) return tc::cuda_fail("peer push", e);
-    for (uint32_t i = 0; i < n_dst; ++i) {
-        const cudaStream_t side = ctx->push_stream[i];
-        if ((e = cudaStreamWaitEvent(side, ctx->push_fork, 0)) != cudaSuccess ||
-            (e = copy(i, side)) != cudaSuccess || (e = cudaEventRecord(ctx->push_join[i], side)) != cudaSuccess ||
-            (e = cudaStreamWaitEvent(s, ctx->push_join[i], 0)) != cudaSuccess)
+    for (uint32_t l = 0; l < lanes; ++l)
+        if ((e = cudaStreamWaitEvent(ctx->push_stream[l], ctx->push_fork, 0)) != cudaSuccess)
             return tc::cuda_fail("peer push", e);
-    }
+    for (uint32_t i = 0; i < n_dst; ++i)
+        if ((e = copy(i, ctx->push_stream[i % lanes])) != cudaSuccess) return tc::cuda_fail("peer push", e);
+    for (uint32_t l = 0; l < lanes; ++l)
+        if ((e = cudaEventRecord(ctx->push_join[l], ctx->push_stream[l])) != cudaSuccess ||
+            (e = cudaStreamWaitEvent(s, ctx->push_join[l], 0)) != cudaSuccess)
+            return tc::cuda_fail("peer push", e);
     return tc::ok();
 }
 
-int tc_cuda_set_push_serial(tc_cuda_ctx *ctx, int serial) {
+int tc_cuda_set_push_fanout(tc_cuda_ctx *ctx, int streams) {
     if (!ctx) return tc::fail("null context");
-    ctx->push_serial = serial ? 1 : 0;
+    if (streams < 0 || streams > (int)tc::kMaxPeers) return tc::fail("fan-out streams out of range 0..8");
+    ctx->push_fanout = streams;
     return tc::ok();
 }
 

@@ -21,12 +21,11 @@ struct tc_cuda_ctx {
     void *blas = nullptr;            // cuBLAS handle for dense weights (created on first use)
     float *dense_ws = nullptr;       // fp32 product of a dense segment before its epilogue
     size_t dense_ws_floats = 0;
-    // Copy-engine all-gather (tc_cuda_peer_push): one side stream per
-    // destination, forked from and joined back into the caller's stream, so
-    // the copies to different peers run on several copy engines at once.
-    // Created on the first push; push_serial = 1 issues them back to back on
-    // the caller's stream instead.
-    int push_serial = 0;
+    // Copy-engine all-gather (tc_cuda_peer_push): by default the copies to
+    // the peers go back to back on the caller's stream; push_fanout = k >= 2
+    // spreads them over k side streams (created on first use), forked from
+    // and joined back into the caller's stream.
+    int push_fanout = 0;
     cudaStream_t push_stream[8] = {};
     cudaEvent_t push_fork = nullptr, push_join[8] = {};
     float *split_ws = nullptr;       // split-K partial products of the tensor-core GEMM

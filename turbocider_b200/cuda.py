@@ -72,7 +72,7 @@ EXPORTS = {
     "tc_cuda_peer_free": (C.c_int, [_vp, _vp]),
     "tc_cuda_peer_barrier": (C.c_int, [_vp, C.POINTER(_vp), _u32, _u32, _u32, _u32, _vp]),
     "tc_cuda_peer_push": (C.c_int, [_vp, _vp, C.POINTER(_vp), _u32, _u64, _u64, _u64, _u64, _vp]),
-    "tc_cuda_set_push_serial": (C.c_int, [_vp, C.c_int]),
+    "tc_cuda_set_push_fanout": (C.c_int, [_vp, C.c_int]),
     "tc_cuda_set_path": (C.c_int, [_vp, C.c_int]),
     "tc_cuda_qlinear_batched": (C.c_int, [_vp, C.POINTER(_vp), _u32, _vp, _u32, C.POINTER(_vp), C.POINTER(_u64),
                                           C.c_int, _vp]),
@@ -191,10 +191,10 @@ class Context:
         _check(lib().tc_cuda_qlinear_plan(self._h, weight.handle, m, stage, C.byref(kern), C.byref(split)))
         return kern.value, split.value
 
-    def set_push_serial(self, serial: bool):
-        """Peer pushes back to back on the caller's stream (True) or fanned out
-        over one side stream per destination (False, the default)."""
-        _check(lib().tc_cuda_set_push_serial(self._h, int(serial)))
+    def set_push_fanout(self, streams: int):
+        """Peer pushes spread over `streams` side streams (>= 2) or back to
+        back on the caller's stream (0 / 1, the default)."""
+        _check(lib().tc_cuda_set_push_fanout(self._h, int(streams)))
 
     def close(self):
         if self._h:
