@@ -153,9 +153,86 @@ def f32_to_bf16_bits(x: np.ndarray) -> np.ndarray:
     return ((b + 0x7FFF + ((b >> 16) & 1)) >> 16).astype(np.uint16)
 
 
+def kquant_fields(raw, ggml_type: int, n: int, k: int):
+    """Per-weight fields of a raw K-quant matrix [n, k], restating the block
+    layouts of reference native/core/gguf_decode.cpp:48-54 (scale_min), :77-90
+    (Q4_K / Q5_K) and :91-105 (Q6_K).  Returns (code, scale, min, sub) as
+    [n, k] arrays: code the integer code (Q6_K: 0..63 with its +32 bias),
+    scale = fp32 d * sc, min = fp32 dmin * m (0 for Q6_K), sub = the weight's
+    sub-block index inside its super-block (Q4_K / Q5_K: 0..7)."""
+    b = _as_u8(raw).reshape(n * (k // 256), BLOCK_BYTES[ggml_type])
+    nb = b.shape[0]
+    half = lambda lo: b[:, lo:lo + 2].copy().view(np.float16).astype(np.float32).reshape(nb)
+    if ggml_type in (12, 13):
+        d, dmin = half(0), half(2)
+        s6 = b[:, 4:16].astype(np.uint32)
+        sc = np.empty((nb, 8), np.uint32)
+        mn = np.empty((nb, 8), np.uint32)
+        for g in range(8):
+            if g < 4:
+                sc[:, g], mn[:, g] = s6[:, g] & 63, s6[:, g + 4] & 63
+            else:
+                sc[:, g] = (s6[:, g + 4] & 0xF) | ((s6[:, g - 4] >> 6) << 4)
+                mn[:, g] = (s6[:, g + 4] >> 4) | ((s6[:, g] >> 6) << 4)
+        qs = b[:, 16:144] if ggml_type == 12 else b[:, 48:176]
+        code = np.empty((nb, 8, 32), np.uint32)
+        for g in range(8):
+            code[:, g, :] = (qs[:, (g // 2) * 32:(g // 2) * 32 + 32] >> (4 * (g & 1))) & 0xF
+            if ggml_type == 13:
+                code[:, g, :] |= ((b[:, 16:48] >> g) & 1).astype(np.uint32) << 4
+        scale = np.repeat(d[:, None] * sc.astype(np.float32), 32, axis=1)
+        mins = np.repeat(dmin[:, None] * mn.astype(np.float32), 32, axis=1)
+        sub = np.tile(np.repeat(np.arange(8), 32), (nb, 1))
+        return (code.reshape(n, k), scale.reshape(n, k), mins.reshape(n, k), sub.reshape(n, k))
+    ql, qh = b[:, 0:128].astype(np.uint32), b[:, 128:192].astype(np.uint32)
+    sc8 = b[:, 192:208].copy().view(np.int8).astype(np.float32)
+    d = half(208)
+    code = np.empty((nb, 256), np.uint32)
+    scale = np.empty((nb, 256), np.float32)
+    for h in range(2):
+        for g in range(4):
+            j = np.arange(32)
+            lo = (ql[:, 64 * h + 32 * (g & 1) + j] >> (4 if g >= 2 else 0)) & 0xF
+            code[:, 128 * h + 32 * g + j] = lo | (((qh[:, 32 * h + j] >> (2 * g)) & 3) << 4)
+            scale[:, 128 * h + 32 * g + j] = d[:, None] * sc8[:, 8 * h + j // 16 + 2 * g]
+    return code.reshape(n, k), scale.reshape(n, k), np.zeros((n, k), np.float32), None
+
+
+def f16_staged_weight(raw, ggml_type: int, n: int, k: int) -> np.ndarray:
+    """The tensor-core GEMMs' fp16 staging (TC_STAGE_F16 / TC_STAGE_F16_X16):
+    fp16(code * s_h - m_h) with one rounding of the exact value
+    (fma.rn.f16x2), where s_h = fp16(d sc) (Q4_K's odd sub-blocks, high
+    nibbles read in place as 16 code: fp16(d sc / 16)) and m_h = fp16(m')
+    with the compensated min m' = m + (m / s) (s_h - s) = m s_h / s while s_h
+    is a normal fp16 number (plain m otherwise); Q6_K: fp16((code - 32) * s_h).
+    The kernel forms 1 / s with an approximate reciprocal, which can move m_h
+    by one fp16 step in rare ties.  Widened exactly to float64."""
+    code, scale, mins, sub = kquant_fields(raw, ggml_type, n, k)
+    if ggml_type == 14:
+        v = (code.astype(np.float64) - 32.0) * scale.astype(np.float16).astype(np.float64)
+    else:
+        q = code.astype(np.float64)
+        s32 = scale.astype(np.float32)
+        if ggml_type == 12:
+            odd = (sub & 1) == 1
+            q = np.where(odd, 16.0 * q, q)
+            s32 = np.where(odd, s32 * np.float32(0.0625), s32).astype(np.float32)
+        sh = s32.astype(np.float16).astype(np.float64)
+        s64, m64 = s32.astype(np.float64), mins.astype(np.float64)
+        comp = sh >= 2.0 ** -14
+        with np.errstate(divide="ignore", invalid="ignore"):
+            mc = np.where(comp, m64 + (m64 / np.where(comp, s64, 1.0)) * (sh - s64), m64)
+        mh = mc.astype(np.float32).astype(np.float16).astype(np.float64)
+        v = q * sh - mh
+    return v.astype(np.float16).astype(np.float64)
+
+
 def staged_weight(raw, ggml_type: int, n: int, k: int, staging: str, which: str = "port") -> np.ndarray:
     """The weight as the kernel sees it: decode to the staging dtype
-    (bf16 / f16 / f32) and widen exactly to float64."""
+    (bf16 / f16 / f32: the reference decoder's values) or "f16k" (the
+    tensor-core GEMMs' fp16 staging arithmetic), widened exactly to float64."""
+    if staging == "f16k":
+        return f16_staged_weight(raw, ggml_type, n, k)
     if staging == "f32":
         return decode_checked(raw, ggml_type, n, k, F32, which).astype(np.float64)
     if staging == "bf16":
@@ -173,7 +250,7 @@ def qlinear_ref(x_bits: np.ndarray, raw, ggml_type: int, n: int, k: int, staging
         x = np.asarray(x_bits, dtype=np.uint16).view(np.float16)
     else:
         x = bf16_bits_to_f32(x_bits)
-        if staging == "f16":
+        if staging in ("f16", "f16k"):
             x = x.astype(np.float16)
     w = staged_weight(raw, ggml_type, n, k, staging, which)
     return x.astype(np.float64) @ w.T

@@ -258,34 +258,36 @@ __device__ __forceinline__ void unpack_row(const uint8_t *wc, uint32_t q, uint32
         uint32_t w[8], hb[8];
         load_row32(wc + kQs + q * 4096 + slot * 32, slot, w);
         if (kQ5) load_row32(wc + kQ5Qh + slot * 32, slot, hb);
+        // Scales in the form the staging needs (f32x2 exact, or f16x2).
         const uint64_t off2 = f2splat(-8388608.0f);
-        {
-            const uint64_t sc2 = f2splat(a0), mn2 = f2splat(-b0);
+        uint64_t sc2 = f2splat(a0), mn2 = f2splat(-b0);
+        uint32_t sch = 0, mnh = 0;
+        if (F16) { sch = h2splat(a0); mnh = h2splat(-min_compensated(a0, b0)); }
 #pragma unroll
-            for (int i = 0; i < 8; ++i) {
-                const uint32_t c = kQ5 ? (w[i] & 0x0F0F0F0Fu) | (((hb[i] >> (2 * q)) & 0x01010101u) << 4)
-                                       : w[i] & 0x0F0F0F0Fu;
-                const uint2 v = four_values<TYPE, F16>(c, sc2, off2, mn2);
-                out[2 * i] = v.x;
-                out[2 * i + 1] = v.y;
-            }
-            tmem_st16(ta, out);
+        for (int i = 0; i < 8; ++i) {
+            const uint32_t c = kQ5 ? (w[i] & 0x0F0F0F0Fu) | (((hb[i] >> (2 * q)) & 0x01010101u) << 4)
+                                   : w[i] & 0x0F0F0F0Fu;
+            const uint2 v = F16 ? four_values_h<TYPE>(c, sch, mnh) : four_values<TYPE, F16>(c, sc2, off2, mn2);
+            out[2 * i] = v.x;
+            out[2 * i + 1] = v.y;
         }
-        {
-            // Q4_K high nibbles are read in place (16 q) with the scale
-            // pre-divided by 16, a power of two, so every product stays exact;
-            // Q5_K's 5-bit codes are shifted down instead.
-            const uint64_t sc2 = f2splat(kQ5 ? a1 : a1 * 0.0625f), mn2 = f2splat(-b1);
+        tmem_st16(ta, out);
+        // Q4_K high nibbles are read in place (16 q) with the scale
+        // pre-divided by 16, a power of two, so every product stays exact;
+        // Q5_K's 5-bit codes are shifted down instead.
+        const float a1s = kQ5 ? a1 : a1 * 0.0625f;
+        sc2 = f2splat(a1s);
+        mn2 = f2splat(-b1);
+        if (F16) { sch = h2splat(a1s); mnh = h2splat(-min_compensated(a1s, b1)); }
 #pragma unroll
-            for (int i = 0; i < 8; ++i) {
-                const uint32_t c = kQ5 ? ((w[i] >> 4) & 0x0F0F0F0Fu) | (((hb[i] >> (2 * q + 1)) & 0x01010101u) << 4)
-                                       : w[i] & 0xF0F0F0F0u;
-                const uint2 v = four_values<TYPE, F16>(c, sc2, off2, mn2);
-                out[2 * i] = v.x;
-                out[2 * i + 1] = v.y;
-            }
-            tmem_st16(ta + 16, out);
+        for (int i = 0; i < 8; ++i) {
+            const uint32_t c = kQ5 ? ((w[i] >> 4) & 0x0F0F0F0Fu) | (((hb[i] >> (2 * q + 1)) & 0x01010101u) << 4)
+                                   : w[i] & 0xF0F0F0F0u;
+            const uint2 v = F16 ? four_values_h<TYPE>(c, sch, mnh) : four_values<TYPE, F16>(c, sc2, off2, mn2);
+            out[2 * i] = v.x;
+            out[2 * i + 1] = v.y;
         }
+        tmem_st16(ta + 16, out);
     } else {
         const uint32_t h = q >> 1, shift = (q & 1) * 4, g0 = 2 * (q & 1);
         const float d = half_bits_to_float(*reinterpret_cast<const uint16_t *>(wc + kQ6D + r * 2));
@@ -300,10 +302,12 @@ __device__ __forceinline__ void unpack_row(const uint8_t *wc, uint32_t q, uint32
         load_row32(wc + kQ6Ql + ((h * 2 + 0) * kPanelRows + slot) * 32, slot, l);
         {
             const uint64_t s0 = f2splat(sa0), s1 = f2splat(sa1);
+            const uint32_t h0 = F16 ? h2splat(sa0) : 0u, h1 = F16 ? h2splat(sa1) : 0u;
 #pragma unroll
             for (int i = 0; i < 8; ++i) {
                 const uint32_t c = ((l[i] >> shift) & 0x0F0F0F0Fu) | (((qh[i] >> (2 * g0)) & 0x03030303u) << 4);
-                const uint2 v = four_values<14, F16>(c, i < 4 ? s0 : s1, off2, 0);
+                const uint2 v = F16 ? four_values_h<14>(c, i < 4 ? h0 : h1, 0u)
+                                    : four_values<14, F16>(c, i < 4 ? s0 : s1, off2, 0);
                 out[2 * i] = v.x;
                 out[2 * i + 1] = v.y;
             }
@@ -312,10 +316,12 @@ __device__ __forceinline__ void unpack_row(const uint8_t *wc, uint32_t q, uint32
         load_row32(wc + kQ6Ql + ((h * 2 + 1) * kPanelRows + slot) * 32, slot, l);
         {
             const uint64_t s0 = f2splat(sb0), s1 = f2splat(sb1);
+            const uint32_t h0 = F16 ? h2splat(sb0) : 0u, h1 = F16 ? h2splat(sb1) : 0u;
 #pragma unroll
             for (int i = 0; i < 8; ++i) {
                 const uint32_t c = ((l[i] >> shift) & 0x0F0F0F0Fu) | (((qh[i] >> (2 * g0 + 2)) & 0x03030303u) << 4);
-                const uint2 v = four_values<14, F16>(c, i < 4 ? s0 : s1, off2, 0);
+                const uint2 v = F16 ? four_values_h<14>(c, i < 4 ? h0 : h1, 0u)
+                                    : four_values<14, F16>(c, i < 4 ? s0 : s1, off2, 0);
                 out[2 * i] = v.x;
                 out[2 * i + 1] = v.y;
             }

@@ -142,6 +142,16 @@ __device__ __forceinline__ uint64_t f2fma(uint64_t a, uint64_t b, uint64_t c) {
     return r;
 }
 __device__ __forceinline__ uint64_t f2splat(float v) { return f2pack(__float_as_uint(v), __float_as_uint(v)); }
+// fp16 staging's compensated min (see four_values_h): m * fp16(s) / s, formed
+// as m + (m / s) (fp16(s) - s), while fp16(s) is a normal fp16 number.
+__device__ __forceinline__ float min_compensated(float s, float m) {
+    const float sh = __half2float(__float2half_rn(s));
+    if (!(sh >= 6.103515625e-05f)) return m;   // fp16(s) subnormal or zero: plain min
+    float r;
+    asm("rcp.approx.ftz.f32 %0, %1;" : "=f"(r) : "f"(s));
+    return fmaf(m * r, sh - s, m);
+}
+
 // Byte i of w as the float 2^23 + byte (exact): the byte goes into the low
 // mantissa bits under the exponent of 2^23.
 __device__ __forceinline__ uint32_t magic_byte(uint32_t w, uint32_t i) {
@@ -186,6 +196,8 @@ __device__ __forceinline__ void build_table(const uint8_t *wc, float *tab, uint3
             const float a1 = d * (float)s1;
             ovf |= fmaxf(fabsf(v.y), fabsf(fmaf(v.x, kQMax, -v.y))) >= kF16Inf ||
                    fmaxf(fabsf(v.w), fabsf(fmaf(a1, kQMax, -v.w))) >= kF16Inf;
+            v.y = min_compensated(v.x, v.y);   // fp16 staging: see four_values_h
+            v.w = min_compensated(v.z, v.w);
         }
     } else {
         const float d = half_bits_to_float(*reinterpret_cast<const uint16_t *>(wc + kQ6D + r * 2));
@@ -224,6 +236,64 @@ __device__ __forceinline__ uint2 four_values(uint32_t codes, uint64_t scale2, ui
     return make_uint2(pack_pair<F16>(v0), pack_pair<F16>(v1));
 }
 
+// ---- fp16 staging (TC_STAGE_F16 / TC_STAGE_F16_X16): packed f16x2 arithmetic.
+// The GEMM's output bar is rel-L2 <= 1e-3 against dequant + fp32 matmul, not
+// bit-exact staging (the dequantise hooks, tc_cuda_dequant / tc_cuda_decode,
+// stay bit-exact), so fp16 staging computes each weight as
+//     Q4_K / Q5_K: fp16(code * fp16(d sc) - fp16(dmin m))   one fma.rn.f16x2
+//     Q6_K:        fp16((code - 32) * fp16(d sc))           one mul.rn.f16x2
+// with the per-sub-block scale rounded to fp16 once (Q4_K high nibbles, read
+// in place as 16 code, use fp16(d sc / 16)) and the min compensated for that
+// rounding: m' = m * fp16(s) / s (min_compensated), so the sub-block's zero
+// point m / s is kept and the scale's rounding error scales with the weight
+// rather than with the code; only the min's own fp16 rounding remains.
+// Compensation applies while fp16(s) is a normal fp16 number (>= 2^-14).
+// Per 4 weights: 2
+// prmt (each code byte under the fp16 exponent of 1024: 0x64cc = 1024 + code),
+// 2 exact f16x2 subtracts, 2 f16x2 FMAs -- against 4 prmt, 2 f32x2 adds, 2
+// f32x2 FMAs and 2 conversions for the exact form.
+__device__ __forceinline__ uint32_t h2splat(float v) {
+    const __half2 h = __floats2half2_rn(v, v);
+    return *reinterpret_cast<const uint32_t *>(&h);
+}
+__device__ __forceinline__ uint32_t h2_code(uint32_t codes, uint32_t sel) {
+    uint32_t r;
+    asm("prmt.b32 %0, %1, %2, %3;" : "=r"(r) : "r"(codes), "r"(0x64646464u), "r"(sel));
+    return r;
+}
+__device__ __forceinline__ uint32_t h2_sub(uint32_t a, uint32_t b) {
+    uint32_t r;
+    asm("sub.rn.f16x2 %0, %1, %2;" : "=r"(r) : "r"(a), "r"(b));
+    return r;
+}
+__device__ __forceinline__ uint32_t h2_fma(uint32_t a, uint32_t b, uint32_t c) {
+    uint32_t r;
+    asm("fma.rn.f16x2 %0, %1, %2, %3;" : "=r"(r) : "r"(a), "r"(b), "r"(c));
+    return r;
+}
+__device__ __forceinline__ uint32_t h2_mul(uint32_t a, uint32_t b) {
+    uint32_t r;
+    asm("mul.rn.f16x2 %0, %1, %2;" : "=r"(r) : "r"(a), "r"(b));
+    return r;
+}
+// Four weights from the four code bytes (Q4_K / Q5_K: 0..255 as read, Q6_K:
+// 0..63 with the +32 bias), scale / min as fp16 pairs (min negated).
+template <int TYPE>
+__device__ __forceinline__ uint2 four_values_h(uint32_t codes, uint32_t scale_h2, uint32_t min_h2) {
+    constexpr uint32_t kOff = TYPE == 14 ? 0x64206420u : 0x64006400u;   // 1024 + 32 / 1024
+    const uint32_t p0 = h2_sub(h2_code(codes, 0x4140u), kOff), p1 = h2_sub(h2_code(codes, 0x4342u), kOff);
+    if (affine_type(TYPE)) return make_uint2(h2_fma(p0, scale_h2, min_h2), h2_fma(p1, scale_h2, min_h2));
+    return make_uint2(h2_mul(p0, scale_h2), h2_mul(p1, scale_h2));
+}
+// The task's four-weight groups: the exact form for bf16 staging, the f16x2
+// form for fp16 staging (scale / min given in fp32, converted here).
+template <int TYPE, bool F16>
+__device__ __forceinline__ uint2 four_any(uint32_t codes, float scale, float min_neg) {
+    if constexpr (F16) return four_values_h<TYPE>(codes, h2splat(scale), h2splat(min_neg));
+    return four_values<TYPE, F16>(codes, f2splat(scale), f2splat(TYPE == 14 ? -8388640.0f : -8388608.0f),
+                                  f2splat(min_neg));
+}
+
 // One task: weight row r, bytes 8t..8t+7 of the 64-weight slice q.  Writes
 // two 16-byte chunks (slice K 8t..8t+7 and 32+8t..32+8t+7) of the swizzled
 // A tile.  Q4_K: low nibbles = sub-block 2q, high nibbles = sub-block 2q+1.
@@ -237,42 +307,36 @@ __device__ __forceinline__ void dequant_task(const uint8_t *wc, const float *tab
     if (TYPE == 12) {
         const uint2 b = *reinterpret_cast<const uint2 *>(wc + kQ4Qs + q * 4096 + slot * 32 + t * 8);
         const float4 s = *reinterpret_cast<const float4 *>(trow + 16 * q);
-        const uint64_t off2 = f2splat(-8388608.0f);
-        const uint64_t dl = f2splat(s.x), ml = f2splat(-s.y), dh = f2splat(s.z), mh = f2splat(-s.w);
-        lo0 = four_values<12, F16>(b.x & 0x0F0F0F0Fu, dl, off2, ml);
-        lo1 = four_values<12, F16>(b.y & 0x0F0F0F0Fu, dl, off2, ml);
-        hi0 = four_values<12, F16>(b.x & 0xF0F0F0F0u, dh, off2, mh);
-        hi1 = four_values<12, F16>(b.y & 0xF0F0F0F0u, dh, off2, mh);
+        lo0 = four_any<12, F16>(b.x & 0x0F0F0F0Fu, s.x, -s.y);
+        lo1 = four_any<12, F16>(b.y & 0x0F0F0F0Fu, s.x, -s.y);
+        hi0 = four_any<12, F16>(b.x & 0xF0F0F0F0u, s.z, -s.w);
+        hi1 = four_any<12, F16>(b.y & 0xF0F0F0F0u, s.z, -s.w);
     } else if (TYPE == 13) {
         // Q5_K: low nibble | fifth bit (bit 2q of qh) for sub-block 2q, high
         // nibble shifted down | bit 2q+1 for sub-block 2q+1 (codes 0..31).
         const uint2 b = *reinterpret_cast<const uint2 *>(wc + kQ5Qs + q * 4096 + slot * 32 + t * 8);
         const uint2 hb = *reinterpret_cast<const uint2 *>(wc + kQ5Qh + slot * 32 + t * 8);
         const float4 s = *reinterpret_cast<const float4 *>(trow + 16 * q);
-        const uint64_t off2 = f2splat(-8388608.0f);
-        const uint64_t dl = f2splat(s.x), ml = f2splat(-s.y), dh = f2splat(s.z), mh = f2splat(-s.w);
         const uint32_t bl = 2 * q, bh = 2 * q + 1;
-        lo0 = four_values<13, F16>((b.x & 0x0F0F0F0Fu) | (((hb.x >> bl) & 0x01010101u) << 4), dl, off2, ml);
-        lo1 = four_values<13, F16>((b.y & 0x0F0F0F0Fu) | (((hb.y >> bl) & 0x01010101u) << 4), dl, off2, ml);
-        hi0 = four_values<13, F16>(((b.x >> 4) & 0x0F0F0F0Fu) | (((hb.x >> bh) & 0x01010101u) << 4), dh, off2, mh);
-        hi1 = four_values<13, F16>(((b.y >> 4) & 0x0F0F0F0Fu) | (((hb.y >> bh) & 0x01010101u) << 4), dh, off2, mh);
+        lo0 = four_any<13, F16>((b.x & 0x0F0F0F0Fu) | (((hb.x >> bl) & 0x01010101u) << 4), s.x, -s.y);
+        lo1 = four_any<13, F16>((b.y & 0x0F0F0F0Fu) | (((hb.y >> bl) & 0x01010101u) << 4), s.x, -s.y);
+        hi0 = four_any<13, F16>(((b.x >> 4) & 0x0F0F0F0Fu) | (((hb.x >> bh) & 0x01010101u) << 4), s.z, -s.w);
+        hi1 = four_any<13, F16>(((b.y >> 4) & 0x0F0F0F0Fu) | (((hb.y >> bh) & 0x01010101u) << 4), s.z, -s.w);
     } else {
         const uint32_t h = q >> 1, shift = (q & 1) * 4, g0 = 2 * (q & 1);
         const uint2 la = *reinterpret_cast<const uint2 *>(wc + kQ6Ql + ((h * 2 + 0) * kPanelRows + slot) * 32 + t * 8);
         const uint2 lb = *reinterpret_cast<const uint2 *>(wc + kQ6Ql + ((h * 2 + 1) * kPanelRows + slot) * 32 + t * 8);
         const uint2 qh = *reinterpret_cast<const uint2 *>(wc + kQ6Qh + (h * kPanelRows + slot) * 32 + t * 8);
         const float *tf = reinterpret_cast<const float *>(trow);
-        const uint64_t da = f2splat(tf[8 * h + (t >> 1) + 2 * g0]);
-        const uint64_t db = f2splat(tf[8 * h + (t >> 1) + 2 * g0 + 2]);
-        const uint64_t off2 = f2splat(-8388640.0f);  // -(2^23 + 32)
+        const float da = tf[8 * h + (t >> 1) + 2 * g0], db = tf[8 * h + (t >> 1) + 2 * g0 + 2];
         const uint32_t ca0 = ((la.x >> shift) & 0x0F0F0F0Fu) | (((qh.x >> (2 * g0)) & 0x03030303u) << 4);
         const uint32_t ca1 = ((la.y >> shift) & 0x0F0F0F0Fu) | (((qh.y >> (2 * g0)) & 0x03030303u) << 4);
         const uint32_t cb0 = ((lb.x >> shift) & 0x0F0F0F0Fu) | (((qh.x >> (2 * g0 + 2)) & 0x03030303u) << 4);
         const uint32_t cb1 = ((lb.y >> shift) & 0x0F0F0F0Fu) | (((qh.y >> (2 * g0 + 2)) & 0x03030303u) << 4);
-        lo0 = four_values<14, F16>(ca0, da, off2, 0);
-        lo1 = four_values<14, F16>(ca1, da, off2, 0);
-        hi0 = four_values<14, F16>(cb0, db, off2, 0);
-        hi1 = four_values<14, F16>(cb1, db, off2, 0);
+        lo0 = four_any<14, F16>(ca0, da, 0.f);
+        lo1 = four_any<14, F16>(ca1, da, 0.f);
+        hi0 = four_any<14, F16>(cb0, db, 0.f);
+        hi1 = four_any<14, F16>(cb1, db, 0.f);
     }
     uint8_t *row = a + (r >> 3) * 1024 + (r & 7) * 128;
     *reinterpret_cast<uint4 *>(row + ((t ^ (r & 7)) << 4)) = make_uint4(lo0.x, lo0.y, lo1.x, lo1.y);
