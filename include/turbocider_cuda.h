@@ -33,7 +33,7 @@
 extern "C" {
 #endif
 
-#define TC_CUDA_ABI_VERSION 1u
+#define TC_CUDA_ABI_VERSION 2u
 
 enum { TC_CUDA_OK = 0, TC_CUDA_FAIL = 1, TC_CUDA_CANCELLED = 2 };
 
@@ -132,13 +132,18 @@ void tc_cuda_weight_free(tc_cuda_weight *weight);
  * tc_relayout_host re-lays rows [n_begin, n_begin + n_count) (0 = to the end)
  * of a raw GGUF matrix [n, k] into the panel layout of an n_count-row weight,
  * on `threads` CPU threads, checking every d/dmin is finite; tc_panel_bytes
- * is the size of that layout.  tc_cuda_weight_copy_panels then copies panel
+ * is the size of that layout.  `cancel` (NULL: not cancellable) is a
+ * caller-owned flag polled once per panel chunk: nonzero stops the work and
+ * the call returns TC_CUDA_CANCELLED ("generation cancelled"; the panels are
+ * then incomplete), as the reference polls its cancel flag once per block
+ * (gguf_decode.cpp:44-47, :344).  tc_cuda_weight_copy_panels then copies panel
  * bytes (pinned host or device memory, exactly weight_info's device_bytes)
  * into a weight made by tc_cuda_weight_create, asynchronously on `stream`,
  * with no kernel (so it overlaps a running GEMM). */
 uint64_t tc_panel_bytes(uint32_t ggml_type, uint64_t n, uint64_t k);
 int tc_relayout_host(uint32_t ggml_type, const void *raw, uint64_t raw_bytes, uint64_t n, uint64_t k,
-                     uint64_t n_begin, uint64_t n_count, void *panels, uint64_t panel_bytes, int threads);
+                     uint64_t n_begin, uint64_t n_count, void *panels, uint64_t panel_bytes, int threads,
+                     const volatile int32_t *cancel);
 int tc_cuda_weight_copy_panels(tc_cuda_ctx *ctx, tc_cuda_weight *weight, const void *panels, uint64_t bytes,
                                void *stream);
 
@@ -165,6 +170,21 @@ int tc_cuda_decode(tc_cuda_ctx *ctx, uint32_t ggml_type, const void *source, uin
                    uint64_t rows, uint64_t column_begin, uint64_t columns, int dtype,
                    void *target, uint64_t target_bytes, uint64_t row_stride,
                    uint64_t column_stride, void *stream);
+
+/* Device mirror of decode_cpu_gather (gguf_decode.cpp:446-465, declared at
+ * gguf_decode.hpp:60-62; the probe ABI's gather mode, gguf_core_probe.cpp:44):
+ * bounded row gather for embedding-style lookups -- target row r is source row
+ * row_indices[r] (device array of n_indices uint64, duplicates and order
+ * kept), columns [column_begin, +columns), any registered type, strided
+ * target as tc_cuda_decode.  Host checks: the reference's validate() rules
+ * with one row per index, then "gather indices overlap target".  Each index
+ * is checked on the device: one past source_rows sets TC_STATUS_GEOMETRY
+ * (reported as "gather row out of bounds") and its target row is not
+ * written. */
+int tc_cuda_decode_gather(tc_cuda_ctx *ctx, uint32_t ggml_type, const void *source, uint64_t source_bytes,
+                          uint64_t source_rows, uint64_t source_columns, const uint64_t *row_indices,
+                          uint64_t n_indices, uint64_t column_begin, uint64_t columns, int dtype, void *target,
+                          uint64_t target_bytes, uint64_t row_stride, uint64_t column_stride, void *stream);
 
 /* Quantised linear Y[M, N] = X[M, K] * W^T (fp32 accumulate) -- the operator
  * behind Weights::project (reference native/backends/mlx.cpp:668-679).
@@ -371,9 +391,34 @@ int tc_gguf_meta(const tc_gguf *file, const char *key, uint32_t *type, uint64_t 
                  char *text, uint64_t text_cap, uint64_t *array_count);
 /* Read rows [row_begin, row_begin + rows) of a tensor's payload (raw GGUF
  * blocks, row pitch dims[0] / block_elements * block_bytes) into host memory
- * (pinned memory lets the following upload run at full PCIe rate). */
+ * (pinned memory lets the following upload run at full PCIe rate), in preads
+ * of at most 8 MiB; `cancel` (NULL: not cancellable) is polled before each:
+ * nonzero returns TC_CUDA_CANCELLED ("generation cancelled"). */
 int tc_gguf_read(const tc_gguf *file, uint64_t index, uint64_t row_begin, uint64_t rows, void *dst,
-                 uint64_t dst_bytes);
+                 uint64_t dst_bytes, const volatile int32_t *cancel);
+
+/* Streaming load of a K-quant tensor (rows [n_begin, +n_count), 0 = to the
+ * end: an N-column shard) from the file into a new weight in HBM, replacing
+ * GgufPackedBank::load_candidate's read / decode / publish loop
+ * (native/runtime/streaming/gguf_packed_bank.cpp:393-452) and its read-ahead
+ * worker (native/runtime/streaming/read_ahead_worker.hpp:21-70).  Chunks of
+ * whole 128-row panels, about chunk_bytes each (0: 8 MiB), flow through two
+ * pinned host slots and two device slots: a worker thread preads chunk i + 1
+ * while chunk i is copied to HBM and re-laid into the weight's panels on the
+ * GPU.  `cancel` (NULL: not cancellable) is polled before every chunk and
+ * between preads.  Synchronous; every d/dmin is checked finite.  On failure
+ * or cancellation (TC_CUDA_CANCELLED) no weight is returned (the one being
+ * filled is freed).  The staging slots are the context's, allocated by the
+ * first load and reused.  stats (may be NULL): bytes loaded, chunks, wall
+ * seconds, seconds spent in pread, seconds the loading thread waited for
+ * reads. */
+typedef struct tc_gguf_load_stats {
+    uint64_t bytes, chunks;
+    double seconds, read_seconds, wait_seconds;
+} tc_gguf_load_stats;
+int tc_cuda_weight_load_gguf(tc_cuda_ctx *ctx, const tc_gguf *file, uint64_t index, uint64_t n_begin,
+                             uint64_t n_count, uint64_t chunk_bytes, const volatile int32_t *cancel,
+                             tc_cuda_weight **weight, tc_gguf_load_stats *stats);
 /* Validate a split set (validate_split_set, gguf_directory.hpp:273-304). */
 int tc_gguf_validate_split(const tc_gguf *const *shards, uint32_t n);
 

@@ -103,6 +103,42 @@ def decode(raw, ggml_type: int, rows: int, cols: int, dtype: int = F32, which: s
     return rc, (out if rc == 0 else None), err
 
 
+def decode_gather(raw, ggml_type: int, rows: int, cols: int, indices, dtype: int = F32, which: str = "port",
+                  col_begin: int = 0, ncols: int | None = None):
+    """decode_cpu_gather (gguf_decode.cpp:446-465): row r of the result is
+    source row indices[r].  "ref" runs the reference decoder's own gather
+    (its probe's gather mode); "port" decodes the rows one by one with the C
+    port and applies the reference's index check.  Returns (status, array,
+    error) like decode()."""
+    src = _as_u8(raw)
+    idx = np.ascontiguousarray(indices, dtype=np.uint64)
+    ncols = cols - col_begin if ncols is None else ncols
+    item = 4 if dtype == F32 else 2
+    out = np.zeros((max(len(idx), 1), max(ncols, 1)), dtype=np.float32 if dtype == F32 else np.uint16)
+    if which == "ref":
+        lib = ref()
+        if lib is None:
+            raise RuntimeError("reference decoder not built (oracle/_ref)")
+        stats = (C.c_uint64 * 4)()
+        rc = lib.tc_gguf_test_decode(ggml_type, src.ctypes.data, src.nbytes, rows, cols, 0, 0, col_begin, ncols,
+                                     dtype, out.ctypes.data, out.nbytes, ncols * item, item,
+                                     idx.ctypes.data_as(C.POINTER(C.c_uint64)), len(idx), 0, stats)
+        err = lib.tc_gguf_test_error().decode()
+        return rc, (out if rc == 0 else None), err
+    if len(idx) == 0:
+        return 1, None, "invalid decode slice"
+    for r in idx:
+        if int(r) >= rows:
+            return 1, None, "gather row out of bounds"
+    for i, r in enumerate(idx):
+        rc, row, err = decode(raw, ggml_type, rows, cols, dtype, "port", row_begin=int(r), nrows=1,
+                              col_begin=col_begin, ncols=ncols)
+        if rc:
+            return rc, None, err
+        out[i] = row[0]
+    return 0, out, ""
+
+
 def decode_checked(raw, ggml_type: int, rows: int, cols: int, dtype: int = F32, which: str = "port") -> np.ndarray:
     rc, out, err = decode(raw, ggml_type, rows, cols, dtype, which)
     if rc:

@@ -36,7 +36,7 @@ def test_library_exports_every_declared_symbol():
 
 
 def test_abi_version():
-    assert tcc.lib().tc_cuda_abi_version() == 1
+    assert tcc.lib().tc_cuda_abi_version() == 2
 
 
 def test_init_fails_loudly_without_b200():

@@ -184,3 +184,63 @@ def test_panel_dequant_f16_overflow_sets_status(ctx):
     assert ctx.status() & tcc.STATUS_F16_OVERFLOW
     tcc.dequant(ctx, w, 2)
     assert ctx.status() == 0
+
+
+def _gpu_gather(ctx, raw, typ, rows, cols, idx, dtype, col_begin=0, ncols=None):
+    """Device gather into a guarded target with an odd row pitch; returns the
+    values (uint8 bytes of each target row) or 'error: msg'."""
+    import torch
+    from turbocider_b200 import cuda as tcc
+    ncols = cols - col_begin if ncols is None else ncols
+    item = 4 if dtype == 0 else 2
+    rs = ncols * item + 6
+    size = (len(idx) - 1) * rs + ncols * item + 16
+    target = torch.full((size,), GUARD, dtype=torch.uint8, device="cuda")
+    ind = torch.tensor(np.asarray(idx, dtype=np.int64), device="cuda")
+    try:
+        tcc.decode_gather(ctx, typ, _dev(raw), rows, cols, ind, col_begin, ncols, dtype, target, rs, item)
+    except tcc.DecodeError as e:
+        return "error: " + str(e)
+    host = target.cpu().numpy()
+    out = np.stack([host[r * rs:r * rs + ncols * item] for r in range(len(idx))])
+    touched = np.zeros(size, dtype=bool)
+    for r in range(len(idx)):
+        touched[r * rs:r * rs + ncols * item] = True
+    assert np.all(host[~touched] == GUARD), "guard bytes overwritten"
+    return out
+
+
+def test_decode_gather_bit_exact(ctx):
+    """tc_cuda_decode_gather against the reference's own decode_cpu_gather
+    (its probe's gather mode; the C port where the reference was not built)
+    on the seed-20260930 blocks of every registered type: duplicated and
+    reordered rows, a column slice, all three target dtypes."""
+    which = "ref" if oracle.ref() is not None else "port"
+    for typ, raw, rows, cols, slices in kq_cases.seed20260930_cases():
+        for idx in ([2, 0, 2, 1], [1], [0, 0, 0]):
+            for cb, nc in slices[:2]:
+                for dt in (0, 1, 2):
+                    rc, want, err = oracle.decode_gather(raw, typ, rows, cols, idx, dt, which, col_begin=cb, ncols=nc)
+                    got = _gpu_gather(ctx, raw, typ, rows, cols, idx, dt, cb, nc)
+                    if rc:
+                        assert got == "error: " + err, (typ, idx, dt, got, err)
+                    else:
+                        assert not isinstance(got, str), (typ, idx, dt, got)
+                        assert np.array_equal(got.view(np.uint8).reshape(len(idx), -1),
+                                              want.view(np.uint8).reshape(len(idx), -1)), (typ, idx, dt)
+
+
+def test_decode_gather_errors(ctx):
+    """The reference's gather rejections: an index past the matrix, indices
+    overlapping the target, an empty index list (validate's slice check)."""
+    import torch
+    from turbocider_b200 import cuda as tcc
+    raw = kq_cases.pattern_case(12, 4, 512)
+    assert _gpu_gather(ctx, raw, 12, 4, 512, [1, 4], 0) == "error: gather row out of bounds"
+    assert oracle.decode_gather(raw, 12, 4, 512, [1, 4], 0, "port")[2] == "gather row out of bounds"
+    buf = torch.zeros(4096, dtype=torch.int64, device="cuda")
+    with pytest.raises(tcc.DecodeError, match="gather indices overlap target"):
+        tcc.decode_gather(ctx, 12, _dev(raw), 4, 512, buf[:2], 0, 8, 0, buf, 64, 4)
+    with pytest.raises(tcc.DecodeError, match="invalid decode slice"):
+        tcc.decode_gather(ctx, 12, _dev(raw), 4, 512, buf[:0], 0, 8, 0, buf[64:], 64, 4)
+    assert ctx.status() == 0

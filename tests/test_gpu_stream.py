@@ -92,3 +92,90 @@ def test_gguf_file_to_hbm(ctx, tmp_path):
     assert ctx.status() == 0
     assert oracle.rel_l2(y, oracle.qlinear_ref(xb, raw, 12, n, k, "bf16")) <= 1e-4
     f.close()
+
+
+def _gguf_file(tmp_path, typ, n, k, seed):
+    gguf = pytest.importorskip("gguf")
+    from turbocider_b200 import cuda as tcc
+    raw = tcc.quantize(typ, kq_cases.synthetic_weight(n, k, seed=seed))
+    path = tmp_path / f"w{typ}.gguf"
+    wr = gguf.GGUFWriter(str(path), "test")
+    wr.add_tensor("w", raw.reshape(n, -1), raw_dtype=gguf.GGMLQuantizationType(typ))
+    wr.write_header_to_file()
+    wr.write_kv_data_to_file()
+    wr.write_tensors_to_file()
+    wr.close()
+    return raw, tcc.GGUFFile(path)
+
+
+@pytest.mark.parametrize("typ", [12, 13, 14])
+def test_streaming_loader_equals_upload(ctx, tmp_path, typ):
+    """tc_cuda_weight_load_gguf (read-ahead: pread of chunk i + 1 beside the
+    copy and device re-layout of chunk i) gives the same panels as the
+    synchronous upload, for the whole tensor and for a row shard, with
+    chunks of 128 rows (many chunks, ragged last one)."""
+    import torch
+    from turbocider_b200 import cuda as tcc
+    n, k = 1000, 2048
+    raw, f = _gguf_file(tmp_path, typ, n, k, seed=typ + 40)
+    for n_begin, n_count in ((0, 0), (256, 500)):
+        w, stats = tcc.Weight.load_gguf(ctx, f, "w", n_begin, n_count, chunk_bytes=1)
+        rows = n_count or n
+        ref = tcc.Weight.upload(ctx, typ, n, k, raw, n_begin=n_begin, n_count=n_count)
+        a = tcc.dequant(ctx, w, tcc.F32)
+        b = tcc.dequant(ctx, ref, tcc.F32)
+        assert torch.equal(a, b)
+        want = oracle.decode_checked(raw.reshape(n, -1)[n_begin:n_begin + rows], typ, rows, k, oracle.F32)
+        assert np.array_equal(a.cpu().numpy(), want)
+        assert stats["bytes"] == rows * (k // 256) * {12: 144, 13: 176, 14: 210}[typ]
+        assert stats["chunks"] == -(-rows // 128)
+        w.free()
+        ref.free()
+    assert ctx.status() == 0
+    f.close()
+
+
+def test_streaming_loader_cancel_and_errors(ctx, tmp_path):
+    """A set cancel flag returns Cancelled and publishes nothing; a row range
+    past the tensor is rejected; the context stays usable."""
+    from turbocider_b200 import cuda as tcc
+    raw, f = _gguf_file(tmp_path, 12, 512, 1024, seed=3)
+    flag = tcc.CancelFlag()
+    flag.set()
+    with pytest.raises(tcc.Cancelled):
+        tcc.Weight.load_gguf(ctx, f, "w", cancel=flag)
+    with pytest.raises(tcc.DecodeError, match="out of bounds"):
+        tcc.Weight.load_gguf(ctx, f, "w", 500, 20)
+    flag.clear()
+    w, _ = tcc.Weight.load_gguf(ctx, f, "w", cancel=flag)
+    assert np.array_equal(tcc.dequant(ctx, w, tcc.F32).cpu().numpy(),
+                          oracle.decode_checked(raw, 12, 512, 1024, oracle.F32))
+    w.free()
+    assert ctx.status() == 0
+    f.close()
+
+
+def test_layer_stream_cancel(ctx):
+    """LayerStream raises Cancelled at the next prefetch / acquire once its
+    flag is set; the layers already acquired stay valid."""
+    import torch
+    from turbocider_b200 import cuda as tcc
+    from turbocider_b200.stream import LayerStream
+    n, k = 256, 512
+    raw = tcc.quantize(12, kq_cases.synthetic_weight(n, k, seed=8))
+    flag = tcc.CancelFlag()
+    st = LayerStream(ctx, [{"w": (12, n, k, raw)} for _ in range(4)], "cuda:0", cancel=flag)
+    compute = torch.cuda.Stream()
+    st.begin(compute)
+    w0 = st.acquire(0, compute)["w"]
+    flag.set()
+    with pytest.raises(tcc.Cancelled):
+        st.acquire(1, compute)
+    with pytest.raises(tcc.Cancelled):
+        st.release(0, compute)    # would prefetch layer 2
+    compute.synchronize()
+    assert np.array_equal(tcc.dequant(ctx, w0, tcc.F32).cpu().numpy(),
+                          oracle.decode_checked(raw, 12, n, k, oracle.F32))
+    st.close()
+    with pytest.raises(tcc.Cancelled):
+        LayerStream(ctx, [{"w": (12, n, k, raw)}], "cuda:0", cancel=flag)

@@ -392,7 +392,8 @@ int tc_gguf_meta(const tc_gguf *g, const char *key, uint32_t *type, uint64_t *u,
     return ok();
 }
 
-int tc_gguf_read(const tc_gguf *g, uint64_t index, uint64_t row_begin, uint64_t rows, void *dst, uint64_t dst_bytes) {
+int tc_gguf_read(const tc_gguf *g, uint64_t index, uint64_t row_begin, uint64_t rows, void *dst, uint64_t dst_bytes,
+                 const volatile int32_t *cancel) {
     if (!g || (!dst && rows)) return fail_msg("null argument");
     if (index >= g->tensors.size()) return fail_msg("tensor index out of range");
     const Tensor &t = g->tensors[size_t(index)];
@@ -406,6 +407,11 @@ int tc_gguf_read(const tc_gguf *g, uint64_t index, uint64_t row_begin, uint64_t 
     uint64_t got = 0;
     const uint64_t at = t.offset + row_begin * row_bytes;
     while (got < n) {
+        // the caller's cancel flag is polled between reads of at most 8 MiB
+        if (cancel && *cancel) {
+            tc::set_last_error("generation cancelled");
+            return TC_CUDA_CANCELLED;
+        }
         const ssize_t r = ::pread(g->fd, out + got, size_t(std::min<uint64_t>(n - got, 8ull << 20)), off_t(at + got));
         if (r < 0 && errno == EINTR) continue;
         if (r <= 0) return fail_msg("gguf_invalid: payload read failed or source changed");

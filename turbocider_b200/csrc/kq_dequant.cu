@@ -2,6 +2,7 @@
 // kernels (panel layout and raw GGUF layout) and the bf16 -> fp16 activation
 // conversion used by fp16 staging.  All of these are HBM-bound byte work: one
 // thread per 32-weight group, coalesced along the fastest-varying index.
+#include "../../include/turbocider_cuda.h"
 #include "kq_format.cuh"
 #include "tc_internal.h"
 
@@ -243,12 +244,22 @@ __global__ void decode_raw_kernel(uint32_t type, const uint8_t *__restrict__ src
                                   uint64_t row_begin, uint64_t rows, uint64_t column_begin,
                                   uint64_t columns, uint8_t *__restrict__ dst, uint64_t row_stride,
                                   uint64_t column_stride, uint64_t first_group, uint64_t groups,
-                                  uint32_t *status) {
+                                  uint32_t *status, const uint64_t *__restrict__ gather, uint64_t source_rows) {
     const uint64_t idx = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x;
     if (idx >= rows * groups) return;
     const uint64_t r = idx / groups;
     const uint64_t gid = first_group + idx % groups;   // global 32-group index in the row
-    const uint8_t *row = src + (row_begin + r) * row_bytes;
+    // Gather (decode_cpu_gather, gguf_decode.cpp:446-465): target row r takes
+    // source row gather[r]; an index past the matrix is reported, never read.
+    uint64_t src_row = row_begin + r;
+    if (gather) {
+        src_row = __ldg(gather + r);
+        if (src_row >= source_rows) {
+            atomicOr(status, (uint32_t)TC_STATUS_GEOMETRY);
+            return;
+        }
+    }
+    const uint8_t *row = src + src_row * row_bytes;
     float v[32];
     bool bad = false, ovf = false, bovf = false;
     const uint64_t c0 = gid * 32;
@@ -354,7 +365,8 @@ cudaError_t launch_dequant_panel(const WeightView &w, int dtype, void *dst, uint
 cudaError_t launch_decode_raw(uint32_t type, const uint8_t *src, uint64_t row_bytes,
                               uint64_t row_begin, uint64_t rows, uint64_t column_begin,
                               uint64_t columns, int dtype, uint8_t *dst, uint64_t row_stride,
-                              uint64_t column_stride, uint32_t *status, cudaStream_t s) {
+                              uint64_t column_stride, uint32_t *status, cudaStream_t s, const uint64_t *gather,
+                              uint64_t source_rows) {
     // Every block touched by the column range is decoded (and checked), as in
     // the reference's row_into (gguf_decode.cpp:340-364); threads work on
     // 32-weight groups (an eighth of a K-quant super-block, one legacy block,
@@ -366,13 +378,16 @@ cudaError_t launch_decode_raw(uint32_t type, const uint8_t *src, uint64_t row_by
     const unsigned g = blocks_for(total, 128);
     if (dtype == 0)
         decode_raw_kernel<0><<<g, 128, 0, s>>>(type, src, row_bytes, row_begin, rows, column_begin, columns,
-                                               dst, row_stride, column_stride, first_group, groups, status);
+                                               dst, row_stride, column_stride, first_group, groups, status, gather,
+                                               source_rows);
     else if (dtype == 1)
         decode_raw_kernel<1><<<g, 128, 0, s>>>(type, src, row_bytes, row_begin, rows, column_begin, columns,
-                                               dst, row_stride, column_stride, first_group, groups, status);
+                                               dst, row_stride, column_stride, first_group, groups, status, gather,
+                                               source_rows);
     else
         decode_raw_kernel<2><<<g, 128, 0, s>>>(type, src, row_bytes, row_begin, rows, column_begin, columns,
-                                               dst, row_stride, column_stride, first_group, groups, status);
+                                               dst, row_stride, column_stride, first_group, groups, status, gather,
+                                               source_rows);
     return cudaGetLastError();
 }
 

@@ -75,7 +75,8 @@ uint64_t tc_panel_bytes(uint32_t ggml_type, uint64_t n, uint64_t k) {
 }
 
 int tc_relayout_host(uint32_t ggml_type, const void *raw, uint64_t raw_bytes, uint64_t n, uint64_t k,
-                     uint64_t n_begin, uint64_t n_count, void *panels, uint64_t panel_bytes, int threads) {
+                     uint64_t n_begin, uint64_t n_count, void *panels, uint64_t panel_bytes, int threads,
+                     const volatile int32_t *cancel) {
     if (!raw || !panels) {
         tc::set_last_error("null argument");
         return TC_CUDA_FAIL;
@@ -101,18 +102,28 @@ int tc_relayout_host(uint32_t ggml_type, const void *raw, uint64_t raw_bytes, ui
     const uint64_t n_panels = (n_count + tc::kPanelRows - 1) / tc::kPanelRows;
     const uint64_t total = n_panels * kb;
     std::atomic<uint64_t> next{0};
-    std::atomic<bool> finite{true};
+    std::atomic<bool> finite{true}, stopped{false};
     auto work = [&]() {
-        for (uint64_t pc; (pc = next.fetch_add(1)) < total;)
+        for (uint64_t pc; (pc = next.fetch_add(1)) < total;) {
+            // the caller's cancel flag is polled once per chunk (128 rows x 256 K)
+            if (cancel && *cancel) {
+                stopped = true;
+                return;
+            }
             if (!chunk_host(ggml_type, rows, n_count, kb, pc / kb, (uint32_t)(pc % kb),
                             out + pc * tc::chunk_bytes(ggml_type)))
                 finite = false;
+        }
     };
     const int t = std::max(1, std::min(threads, 64));
     std::vector<std::thread> pool;
     for (int i = 1; i < t; ++i) pool.emplace_back(work);
     work();
     for (auto &th : pool) th.join();
+    if (stopped) {
+        tc::set_last_error("generation cancelled");
+        return TC_CUDA_CANCELLED;
+    }
     if (!finite) {
         tc::set_last_error("nonfinite d/dmin in a K-quant block");
         return TC_CUDA_FAIL;

@@ -139,6 +139,12 @@ void tc_cuda_free(tc_cuda_ctx *ctx) {
         if (ctx->push_join[i]) cudaEventDestroy(ctx->push_join[i]);
     }
     if (ctx->push_fork) cudaEventDestroy(ctx->push_fork);
+    for (int i = 0; i < 2; ++i) {
+        if (ctx->load_host[i]) cudaFreeHost(ctx->load_host[i]);
+        if (ctx->load_dev[i]) cudaFree(ctx->load_dev[i]);
+        if (ctx->load_freed[i]) cudaEventDestroy(ctx->load_freed[i]);
+    }
+    if (ctx->load_stream) cudaStreamDestroy(ctx->load_stream);
     tc::dense_blas_destroy(ctx->blas);
     if (ctx->status) cudaFree(ctx->status);
     delete ctx;
@@ -359,14 +365,16 @@ int tc_cuda_dequant(tc_cuda_ctx *ctx, const tc_cuda_weight *w, int dtype, void *
     return ok();
 }
 
-// Geometry rules and messages of the reference's validate() and
-// decode_cpu_into() (native/core/gguf_decode.cpp:160-183, :433-438).
-int tc_cuda_decode(tc_cuda_ctx *ctx, uint32_t type, const void *source, uint64_t source_bytes, uint64_t source_rows,
-                   uint64_t source_columns, uint64_t row_begin, uint64_t rows, uint64_t column_begin,
-                   uint64_t columns, int dtype, void *target, uint64_t target_bytes, uint64_t row_stride,
-                   uint64_t column_stride, void *stream) {
-    if (!ctx) return fail("null context");
-    if (row_begin > source_rows || rows > source_rows - row_begin) return fail("row slice out of bounds");
+}  // extern "C"
+
+namespace {
+// The reference's validate() (native/core/gguf_decode.cpp:160-183): source and
+// target geometry for `rows` decoded rows, same checks, order and messages.
+// Returns 0 and the source row pitch / target extent, or fails.
+int validate_decode(uint32_t type, const void *source, uint64_t source_bytes, uint64_t source_rows,
+                    uint64_t source_columns, uint64_t rows, uint64_t column_begin, uint64_t columns, int dtype,
+                    const void *target, uint64_t target_bytes, uint64_t row_stride, uint64_t column_stride,
+                    uint64_t *row_bytes_out, uint64_t *extent_out) {
     const uint32_t elements = tc::type_elements(type);
     if (!elements) return fail("gguf_decode: unsupported tensor type");
     if (!source || !target) return fail("null source/target storage");
@@ -388,11 +396,61 @@ int tc_cuda_decode(tc_cuda_ctx *ctx, uint32_t type, const void *source, uint64_t
     const uintptr_t s0 = reinterpret_cast<uintptr_t>(source), t0 = reinterpret_cast<uintptr_t>(target);
     const uint64_t source_extent = source_rows * row_bytes;
     if (!(s0 + source_extent <= t0 || t0 + extent <= s0)) return fail("packed source overlaps target");
+    *row_bytes_out = row_bytes;
+    *extent_out = extent;
+    return TC_CUDA_OK;
+}
+}  // namespace
+
+extern "C" {
+
+// Geometry rules and messages of the reference's validate() and
+// decode_cpu_into() (native/core/gguf_decode.cpp:160-183, :433-438).
+int tc_cuda_decode(tc_cuda_ctx *ctx, uint32_t type, const void *source, uint64_t source_bytes, uint64_t source_rows,
+                   uint64_t source_columns, uint64_t row_begin, uint64_t rows, uint64_t column_begin,
+                   uint64_t columns, int dtype, void *target, uint64_t target_bytes, uint64_t row_stride,
+                   uint64_t column_stride, void *stream) {
+    if (!ctx) return fail("null context");
+    if (row_begin > source_rows || rows > source_rows - row_begin) return fail("row slice out of bounds");
+    uint64_t row_bytes = 0, extent = 0;
+    int rc = validate_decode(type, source, source_bytes, source_rows, source_columns, rows, column_begin, columns,
+                             dtype, target, target_bytes, row_stride, column_stride, &row_bytes, &extent);
+    if (rc) return rc;
     DeviceGuard guard(ctx->device);
     cudaError_t e = tc::launch_decode_raw(type, static_cast<const uint8_t *>(source), row_bytes, row_begin, rows,
                                           column_begin, columns, dtype, static_cast<uint8_t *>(target), row_stride,
                                           column_stride, ctx->status, static_cast<cudaStream_t>(stream));
     if (e != cudaSuccess) return cuda_fail("decode launch", e);
+    return ok();
+}
+
+// decode_cpu_gather (native/core/gguf_decode.cpp:446-465): validate() with
+// one row per index, then the indices must not overlap the target; every
+// index is checked on the device (an index past the matrix sets
+// TC_STATUS_GEOMETRY and its row is not written -- the reference rejects the
+// call before decoding; its contract already has callers discard a target
+// that a failed call touched).
+int tc_cuda_decode_gather(tc_cuda_ctx *ctx, uint32_t type, const void *source, uint64_t source_bytes,
+                          uint64_t source_rows, uint64_t source_columns, const uint64_t *row_indices,
+                          uint64_t n_indices, uint64_t column_begin, uint64_t columns, int dtype, void *target,
+                          uint64_t target_bytes, uint64_t row_stride, uint64_t column_stride, void *stream) {
+    if (!ctx) return fail("null context");
+    uint64_t row_bytes = 0, extent = 0;
+    int rc = validate_decode(type, source, source_bytes, source_rows, source_columns, n_indices, column_begin, columns,
+                             dtype, target, target_bytes, row_stride, column_stride, &row_bytes, &extent);
+    if (rc) return rc;
+    if (!row_indices) return fail("null gather indices");
+    const uintptr_t i0 = reinterpret_cast<uintptr_t>(row_indices), t0 = reinterpret_cast<uintptr_t>(target);
+    if (n_indices > UINT64_MAX / sizeof(uint64_t)) return fail("gguf_decode: multiplication overflow");
+    const uint64_t index_bytes = n_indices * sizeof(uint64_t);
+    if (!(index_bytes <= UINTPTR_MAX - i0 && (i0 + index_bytes <= t0 || t0 + extent <= i0)))
+        return fail("gather indices overlap target");
+    DeviceGuard guard(ctx->device);
+    cudaError_t e = tc::launch_decode_raw(type, static_cast<const uint8_t *>(source), row_bytes, 0, n_indices,
+                                          column_begin, columns, dtype, static_cast<uint8_t *>(target), row_stride,
+                                          column_stride, ctx->status, static_cast<cudaStream_t>(stream), row_indices,
+                                          source_rows);
+    if (e != cudaSuccess) return cuda_fail("gather launch", e);
     return ok();
 }
 

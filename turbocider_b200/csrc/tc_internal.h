@@ -30,6 +30,12 @@ struct tc_cuda_ctx {
     cudaEvent_t push_fork = nullptr, push_join[8] = {};
     float *split_ws = nullptr;       // split-K partial products of the tensor-core GEMM
     size_t split_ws_floats = 0;
+    // Streaming GGUF loader (tc_cuda_weight_load_gguf): two pinned host and
+    // two device staging slots (grow-only), its stream and per-slot events.
+    void *load_host[2] = {}, *load_dev[2] = {};
+    size_t load_slot_bytes = 0;
+    cudaStream_t load_stream = nullptr;
+    cudaEvent_t load_freed[2] = {};
 };
 
 struct tc_cuda_weight {
@@ -123,10 +129,13 @@ cudaError_t launch_relayout(uint32_t type, const uint8_t *raw, uint64_t n, uint3
                             uint64_t glu_c = 0);
 cudaError_t launch_dequant_panel(const WeightView &w, int dtype, void *dst, uint64_t ld,
                                  uint32_t *status, cudaStream_t s);
+// gather != nullptr: target row r decodes source row gather[r] (device array,
+// checked against source_rows; TC_STATUS_GEOMETRY for an index past it).
 cudaError_t launch_decode_raw(uint32_t type, const uint8_t *src, uint64_t row_bytes,
                               uint64_t row_begin, uint64_t rows, uint64_t column_begin,
                               uint64_t columns, int dtype, uint8_t *dst, uint64_t row_stride,
-                              uint64_t column_stride, uint32_t *status, cudaStream_t s);
+                              uint64_t column_stride, uint32_t *status, cudaStream_t s,
+                              const uint64_t *gather = nullptr, uint64_t source_rows = 0);
 // Small-M GEMV K split: n_slices CTAs per 16-row tile.  With n_slices > 1
 // the kernel needs `partials` (gemv_workspace_floats floats) and one zeroed
 // uint32 counter per 16-row tile; both are left as found (counters back to 0).

@@ -34,6 +34,45 @@ class DecodeError(BackendError):
     """Mirror of tc::gguf::DecodeError (reference native/core/gguf_decode.hpp:10-16)."""
 
 
+class Cancelled(BackendError):
+    """A call stopped by its cancel flag (status TC_CUDA_CANCELLED = 2; the
+    reference's tc::Cancelled, native/core/common.hpp:19-21)."""
+
+
+class CancelFlag:
+    """A caller-owned cancel flag (int32, nonzero = cancel) for the calls that
+    take one: tc_gguf_read, tc_relayout_host, tc_cuda_weight_load_gguf and
+    LayerStream.  Thread-safe to set from another thread while a call runs
+    (the reference's std::atomic<bool> cancel, gguf_decode.cpp:44-47)."""
+
+    def __init__(self):
+        self._v = C.c_int32(0)
+
+    def set(self):
+        self._v.value = 1
+
+    def clear(self):
+        self._v.value = 0
+
+    @property
+    def is_set(self) -> bool:
+        return self._v.value != 0
+
+    @property
+    def pointer(self):
+        return C.byref(self._v)
+
+
+def _cancel_ptr(cancel):
+    return cancel.pointer if cancel is not None else None
+
+
+class LoadStats(C.Structure):
+    """struct tc_gguf_load_stats."""
+    _fields_ = [("bytes", C.c_uint64), ("chunks", C.c_uint64), ("seconds", C.c_double),
+                ("read_seconds", C.c_double), ("wait_seconds", C.c_double)]
+
+
 _vp, _u32, _u64, _i32 = C.c_void_p, C.c_uint32, C.c_uint64, C.c_int32
 
 
@@ -58,6 +97,8 @@ EXPORTS = {
     "tc_cuda_dequant": (C.c_int, [_vp, _vp, C.c_int, _vp, _u64, _vp]),
     "tc_cuda_decode": (C.c_int, [_vp, _u32, _vp, _u64, _u64, _u64, _u64, _u64, _u64, _u64, C.c_int, _vp, _u64,
                                  _u64, _u64, _vp]),
+    "tc_cuda_decode_gather": (C.c_int, [_vp, _u32, _vp, _u64, _u64, _u64, _vp, _u64, _u64, _u64, C.c_int, _vp,
+                                        _u64, _u64, _u64, _vp]),
     "tc_cuda_qlinear": (C.c_int, [_vp, C.POINTER(_vp), _u32, C.POINTER(_i32), C.POINTER(_i32), _u32, _vp, _vp,
                                   _u64, C.c_int, C.c_int, _vp]),
     "tc_cuda_qlinear_ex": (C.c_int, [_vp, C.POINTER(_vp), _u32, C.POINTER(_i32), C.POINTER(_i32), _u32, _vp, _vp,
@@ -82,7 +123,7 @@ EXPORTS = {
     "tc_cuda_qlinear_small_static": (C.c_int, [_vp, _vp, _u32, _vp, _u64, C.c_int, _vp]),
     "tc_cuda_small_static_status": (C.c_int, [C.c_int, C.POINTER(_u32), C.c_int]),
     "tc_panel_bytes": (_u64, [_u32, _u64, _u64]),
-    "tc_relayout_host": (C.c_int, [_u32, _vp, _u64, _u64, _u64, _u64, _u64, _vp, _u64, C.c_int]),
+    "tc_relayout_host": (C.c_int, [_u32, _vp, _u64, _u64, _u64, _u64, _u64, _vp, _u64, C.c_int, _vp]),
     "tc_cuda_weight_copy_panels": (C.c_int, [_vp, _vp, _vp, _u64, _vp]),
     "tc_gguf_open": (C.c_int, [C.c_char_p, C.c_char_p, C.POINTER(_vp)]),
     "tc_gguf_close": (None, [_vp]),
@@ -93,7 +134,9 @@ EXPORTS = {
     "tc_gguf_find": (C.c_int, [_vp, C.c_char_p, C.POINTER(_u64)]),
     "tc_gguf_meta": (C.c_int, [_vp, C.c_char_p, C.POINTER(_u32), C.POINTER(_u64), C.POINTER(C.c_int64),
                                C.POINTER(C.c_double), C.c_char_p, _u64, C.POINTER(_u64)]),
-    "tc_gguf_read": (C.c_int, [_vp, _u64, _u64, _u64, _vp, _u64]),
+    "tc_gguf_read": (C.c_int, [_vp, _u64, _u64, _u64, _vp, _u64, _vp]),
+    "tc_cuda_weight_load_gguf": (C.c_int, [_vp, _vp, _u64, _u64, _u64, _u64, _vp, C.POINTER(_vp),
+                                           C.POINTER(LoadStats)]),
     "tc_gguf_validate_split": (C.c_int, [C.POINTER(_vp), _u32]),
 }
 
@@ -115,6 +158,8 @@ def lib() -> C.CDLL:
 
 
 def _check(rc: int, cls=BackendError):
+    if rc == 2:
+        raise Cancelled(lib().tc_cuda_last_error().decode())
     if rc != 0:
         raise cls(lib().tc_cuda_last_error().decode())
 
@@ -144,9 +189,10 @@ def panel_bytes(ggml_type: int, n: int, k: int) -> int:
 
 
 def relayout_host(ggml_type: int, raw, n: int, k: int, n_begin: int = 0, n_count: int = 0, out=None,
-                  threads: int | None = None):
+                  threads: int | None = None, cancel: CancelFlag | None = None):
     """Panel layout of rows [n_begin, +n_count) of a raw GGUF matrix, built on
-    the CPU (uint8 numpy array in, uint8 numpy array or pinned torch tensor out)."""
+    the CPU (uint8 numpy array in, uint8 numpy array or pinned torch tensor
+    out).  Raises Cancelled when `cancel` is set while it runs."""
     raw = np.ascontiguousarray(np.frombuffer(raw, dtype=np.uint8) if isinstance(raw, (bytes, bytearray))
                                else raw).view(np.uint8).reshape(-1)
     rows = n_count or (n - n_begin)
@@ -156,7 +202,7 @@ def relayout_host(ggml_type: int, raw, n: int, k: int, n_begin: int = 0, n_count
     ptr = out.data_ptr() if hasattr(out, "data_ptr") else out.ctypes.data
     cap = out.numel() if hasattr(out, "numel") else out.nbytes
     _check(lib().tc_relayout_host(ggml_type, raw.ctypes.data, raw.nbytes, n, k, n_begin, n_count, ptr, cap,
-                                  threads or os.cpu_count() or 1), DecodeError)
+                                  threads or os.cpu_count() or 1, _cancel_ptr(cancel)), DecodeError)
     return out
 
 
@@ -244,6 +290,20 @@ class Weight:
         return cls(ctx, h)
 
     @classmethod
+    def load_gguf(cls, ctx: Context, file: "GGUFFile", name_or_index, n_begin: int = 0, n_count: int = 0,
+                  chunk_bytes: int = 0, cancel: CancelFlag | None = None):
+        """Stream a K-quant tensor (or a row shard of it) from a GGUF file into
+        HBM with read-ahead (tc_cuda_weight_load_gguf).  Returns (Weight,
+        stats dict); raises Cancelled when `cancel` is set while it runs."""
+        idx = name_or_index if isinstance(name_or_index, int) else file.tensor(name_or_index)["index"]
+        h = _vp()
+        st = LoadStats()
+        _check(lib().tc_cuda_weight_load_gguf(ctx.handle, file._h, idx, n_begin, n_count, chunk_bytes,
+                                              _cancel_ptr(cancel), C.byref(h), C.byref(st)), DecodeError)
+        stats = {f: getattr(st, f) for f, _ in LoadStats._fields_}
+        return cls(ctx, h), stats
+
+    @classmethod
     def create(cls, ctx: Context, ggml_type: int, n: int, k: int):
         h = _vp()
         _check(lib().tc_cuda_weight_create(ctx.handle, ggml_type, n, k, C.byref(h)))
@@ -308,6 +368,30 @@ def decode(ctx: Context, ggml_type: int, source, source_rows: int, source_column
             same = (ggml_type, dtype) in ((0, F32), (1, F16), (30, BF16))
             if same and column_stride == (4 if dtype == F32 else 2):
                 raise DecodeError("nonfinite source float")
+            raise DecodeError("nonfinite weight/scale or conversion overflow")
+        if bits & STATUS_F16_OVERFLOW:
+            raise DecodeError("FP16 conversion overflow")
+        if bits & STATUS_BF16_OVERFLOW:
+            raise DecodeError("BF16 conversion overflow")
+
+
+def decode_gather(ctx: Context, ggml_type: int, source, source_rows: int, source_columns: int, indices,
+                  column_begin: int, columns: int, dtype: int, target, row_stride: int, column_stride: int,
+                  stream=None, check: bool = True):
+    """Device mirror of decode_cpu_gather: target row r = source row
+    indices[r] (device int64 / uint64 tensor).  Raises DecodeError with the
+    reference's messages; with check=True (synchronises) also for an index
+    past the matrix and for value errors detected by the kernel."""
+    _check(lib().tc_cuda_decode_gather(ctx.handle, ggml_type, source.data_ptr(),
+                                       source.numel() * source.element_size(), source_rows, source_columns,
+                                       indices.data_ptr(), indices.numel(), column_begin, columns, dtype,
+                                       target.data_ptr(), target.numel() * target.element_size(), row_stride,
+                                       column_stride, _stream_ptr(stream)), DecodeError)
+    if check:
+        bits = ctx.status(clear=True)
+        if bits & STATUS_GEOMETRY:
+            raise DecodeError("gather row out of bounds")
+        if bits & STATUS_NONFINITE_SCALE:
             raise DecodeError("nonfinite weight/scale or conversion overflow")
         if bits & STATUS_F16_OVERFLOW:
             raise DecodeError("FP16 conversion overflow")
@@ -460,9 +544,11 @@ class GGUFFile:
             return i.value
         return u.value
 
-    def read(self, name_or_index, row_begin: int = 0, rows: int | None = None, out=None) -> np.ndarray:
+    def read(self, name_or_index, row_begin: int = 0, rows: int | None = None, out=None,
+             cancel: CancelFlag | None = None) -> np.ndarray:
         """Raw block bytes of rows [row_begin, +rows) into `out` (a uint8
-        numpy array or a pinned torch uint8 tensor; allocated if None)."""
+        numpy array or a pinned torch uint8 tensor; allocated if None).
+        Raises Cancelled when `cancel` is set while it reads."""
         info = self.tensors[name_or_index] if isinstance(name_or_index, int) else self.tensor(name_or_index)
         idx = name_or_index if isinstance(name_or_index, int) else info["index"]
         rows = info["rows"] - row_begin if rows is None else rows
@@ -471,7 +557,7 @@ class GGUFFile:
             out = np.empty(nbytes, dtype=np.uint8)
         ptr = out.data_ptr() if hasattr(out, "data_ptr") else out.ctypes.data
         size = out.numel() if hasattr(out, "numel") else out.nbytes
-        _check(lib().tc_gguf_read(self._h, idx, row_begin, rows, ptr, size), GGUFError)
+        _check(lib().tc_gguf_read(self._h, idx, row_begin, rows, ptr, size, _cancel_ptr(cancel)), GGUFError)
         return out
 
     @staticmethod

@@ -34,9 +34,16 @@ class LayerStream:
     GGUF rows of each weight (or of this rank's N-shard).  Panels are built
     once into pinned host memory; two device slots are cycled."""
 
-    def __init__(self, ctx: tcc.Context, layers, device, threads: int | None = None, pinned_cache: dict | None = None):
+    def __init__(self, ctx: tcc.Context, layers, device, threads: int | None = None, pinned_cache: dict | None = None,
+                 cancel: tcc.CancelFlag | None = None):
+        """cancel: a CancelFlag polled while the panels are built (once per
+        panel chunk, tc_relayout_host) and before every layer is prefetched or
+        acquired, as the reference's pager and bank poll their cancel flag
+        (native/runtime/streaming/gguf_weight_pager.cpp,
+        gguf_packed_bank.cpp:393-452); a set flag raises tcc.Cancelled, with
+        no copy or compute enqueued for the layer."""
         import torch
-        self.ctx, self.device = ctx, device
+        self.ctx, self.device, self.cancel = ctx, device, cancel
         self.n_layers = len(layers)
         threads = threads or os.cpu_count() or 1
         # Pinned panel buffers per layer (layers that share raw bytes share buffers
@@ -49,7 +56,7 @@ class LayerStream:
                 key = (id(raw), typ, n, k)
                 if key not in cache:
                     buf = torch.empty(tcc.panel_bytes(typ, n, k), dtype=torch.uint8, pin_memory=True)
-                    tcc.relayout_host(typ, raw, n, k, out=buf, threads=threads)
+                    tcc.relayout_host(typ, raw, n, k, out=buf, threads=threads, cancel=cancel)
                     cache[key] = (raw, buf)   # keep raw alive so its id stays unique
                 lay[name] = (typ, n, k, cache[key][1])
             self.host.append(lay)
@@ -67,9 +74,13 @@ class LayerStream:
             self.slots[slot][key] = w
         return w
 
+    def _check_cancel(self):
+        if self.cancel is not None and self.cancel.is_set:
+            raise tcc.Cancelled("generation cancelled")
+
     def prefetch(self, layer: int):
         """Enqueue layer's panel copies into slot layer % 2 on the copy stream."""
-        import torch
+        self._check_cancel()
         slot = layer % 2
         if self.free[slot] is not None:
             self.copy.wait_event(self.free[slot])
@@ -89,6 +100,7 @@ class LayerStream:
             self.prefetch(layer)
 
     def acquire(self, layer: int, compute) -> dict:
+        self._check_cancel()
         slot = layer % 2
         compute.wait_event(self.ready[slot])
         return {name: self._weight(slot, name, typ, n, k) for name, (typ, n, k, _) in self.host[layer].items()}
