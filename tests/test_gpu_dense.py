@@ -135,3 +135,23 @@ def test_dense_fp16_range_and_errors(ctx):
     with pytest.raises(tcc.BackendError, match="dense weights"):
         tcc.qlinear_batched(ctx, [wt], x)
     assert ctx.status() == 0
+
+
+@pytest.mark.parametrize("typ,n,k,m", [(0, 40, 33, 5), (1, 130, 100, 300), (30, 96, 7, 129),
+                                       (8, 3072, 4096, 700), (2, 1000, 2048, 64)])
+def test_dense_tensor_core_gemm_shapes(ctx, typ, n, k, m):
+    """The dense GEMM (TMA-fed tcgen05, no library GEMM): K not a multiple of
+    8 (X copied to a 16-byte row pitch, boxes past K zero-filled), N not a
+    multiple of 128, several token tiles, a realistic Q8_0 size."""
+    import torch
+    from turbocider_b200 import cuda as tcc
+    raw = dense_raw(typ, n, k, seed=n + k)
+    w = tcc.Weight.upload(ctx, typ, n, k, raw)
+    xb = kq_cases.synthetic_x_bf16(m, k, seed=k)
+    x = torch.from_numpy(xb.view(np.int16)).view(torch.bfloat16).cuda()
+    y = tcc.qlinear(ctx, w, x, out_dtype=tcc.F32).cpu().numpy()
+    assert ctx.status() == 0
+    assert oracle.rel_l2(y, oracle.qlinear_ref(xb, raw, typ, n, k, "bf16")) <= TIGHT
+    y16 = tcc.qlinear(ctx, w, x, out_dtype=tcc.F16, stage=tcc.STAGE_F16).float().cpu().numpy()
+    assert oracle.rel_l2(y16, oracle.qlinear_ref(xb, raw, typ, n, k, "f16")) <= 1e-3
+    w.free()

@@ -57,7 +57,7 @@ def build(verbose: bool = False) -> Path:
         objs = list(pool.map(lambda s: _compile(s, verbose), srcs))
     if OUT.exists() and OUT.stat().st_mtime >= max(o.stat().st_mtime for o in objs):
         return OUT
-    cmd = [nvcc(), *ARCH, "-shared", "-o", str(OUT), *map(str, objs), "-lcublas", "-lpthread"]
+    cmd = [nvcc(), *ARCH, "-shared", "-o", str(OUT), *map(str, objs), "-lpthread"]
     res = subprocess.run(cmd, capture_output=True, text=True)
     if res.returncode != 0:
         raise RuntimeError(f"link failed:\n{res.stderr}")

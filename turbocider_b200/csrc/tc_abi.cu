@@ -132,7 +132,7 @@ void tc_cuda_free(tc_cuda_ctx *ctx) {
     if (ctx->workspace) cudaFree(ctx->workspace);
     if (ctx->gemv_partials) cudaFree(ctx->gemv_partials);
     if (ctx->gemv_counters) cudaFree(ctx->gemv_counters);
-    if (ctx->dense_ws) cudaFree(ctx->dense_ws);
+    if (ctx->dense_x) cudaFree(ctx->dense_x);
     if (ctx->split_ws) cudaFree(ctx->split_ws);
     for (int i = 0; i < 8; ++i) {
         if (ctx->push_stream[i]) cudaStreamDestroy(ctx->push_stream[i]);
@@ -145,7 +145,6 @@ void tc_cuda_free(tc_cuda_ctx *ctx) {
         if (ctx->load_freed[i]) cudaEventDestroy(ctx->load_freed[i]);
     }
     if (ctx->load_stream) cudaStreamDestroy(ctx->load_stream);
-    tc::dense_blas_destroy(ctx->blas);
     if (ctx->status) cudaFree(ctx->status);
     delete ctx;
 }
@@ -248,11 +247,14 @@ int upload_dense(tc_cuda_ctx *ctx, uint32_t type, uint64_t n, uint64_t k, const 
     w->n = n_count;
     w->k = k;
     w->raw_row_bytes = row_bytes;
-    const uint64_t elems = n_count * k;
+    w->dense_ld = (k + 7) / 8 * 8;   // 16-byte row pitch for TMA
+    const uint64_t elems = n_count * w->dense_ld;
     w->bytes = n_count * row_bytes + 4 * elems;
     cudaError_t e = cudaMalloc(&w->raw, n_count * row_bytes);
     if (e == cudaSuccess) e = cudaMalloc(&w->dense_bf16, elems * 2);
     if (e == cudaSuccess) e = cudaMalloc(&w->dense_f16, elems * 2);
+    if (e == cudaSuccess) e = cudaMemset(w->dense_bf16, 0, elems * 2);   // pad columns stay zero
+    if (e == cudaSuccess) e = cudaMemset(w->dense_f16, 0, elems * 2);
     if (e == cudaSuccess)
         e = cudaMemcpy(w->raw, static_cast<const uint8_t *>(raw_host) + n_begin * row_bytes, n_count * row_bytes,
                        cudaMemcpyHostToDevice);
@@ -262,7 +264,7 @@ int upload_dense(tc_cuda_ctx *ctx, uint32_t type, uint64_t n, uint64_t k, const 
         e = cudaMemset(ctx->status + 1, 0, sizeof(uint32_t));
         if (e == cudaSuccess)
             e = tc::launch_decode_raw(type, w->raw, row_bytes, 0, n_count, 0, k, dt, reinterpret_cast<uint8_t *>(dst),
-                                      k * 2, 2, ctx->status + 1, nullptr);
+                                      w->dense_ld * 2, 2, ctx->status + 1, nullptr);
         if (e == cudaSuccess) e = cudaMemcpy(&bits[dt - 1], ctx->status + 1, sizeof(uint32_t), cudaMemcpyDeviceToHost);
     }
     if (e != cudaSuccess) {
@@ -628,7 +630,6 @@ int tc_cuda_qlinear_gather(tc_cuda_ctx *ctx, const tc_cuda_weight *const *weight
     std::vector<tc::SegmentView> gemv;
     struct DenseSeg { uint32_t b, e, gate_row; const tc_cuda_weight *w; };
     std::vector<DenseSeg> dense;             // F32 / F16 / BF16 / 32-weight block types
-    uint32_t dense_rows = 0;
     for (uint32_t i = 0; i < n_seg; ++i) {
         const uint32_t b = (uint32_t)seg_offsets[i], e = (uint32_t)seg_offsets[i + 1];
         if (b == e) continue;
@@ -639,7 +640,6 @@ int tc_cuda_qlinear_gather(tc_cuda_ctx *ctx, const tc_cuda_weight *const *weight
             if (stage != TC_STAGE_BF16 && !w->dense_f16)
                 return fail("weight values exceed the fp16 range; use TC_STAGE_BF16");
             dense.push_back({b, e, sv.gate_row, w});
-            dense_rows = std::max(dense_rows, e - b);
             continue;
         }
         // fp16 X (TC_STAGE_F16_X16) always takes the tensor-core GEMM: the
@@ -651,18 +651,6 @@ int tc_cuda_qlinear_gather(tc_cuda_ctx *ctx, const tc_cuda_weight *const *weight
             for (uint32_t m = b; m < e; m += 16) gemv.push_back({m, std::min(e, m + 16), sv.w, sv.gate_row});
         } else {
             gemm[w->type == TC_GGML_Q4_K ? 0 : w->type == TC_GGML_Q5_K ? 2 : 1].push_back(sv);
-        }
-    }
-    if (!dense.empty()) {
-        if (!ctx->blas && tc::dense_blas_create(&ctx->blas)) return fail("cuBLAS handle creation failed");
-        const size_t need = flags ? (size_t)dense_rows * w0->n : 0;
-        if (need > ctx->dense_ws_floats) {
-            if (ctx->dense_ws) cudaFree(ctx->dense_ws);
-            ctx->dense_ws = nullptr;
-            ctx->dense_ws_floats = 0;
-            cudaError_t e = cudaMalloc(&ctx->dense_ws, need * sizeof(float));
-            if (e != cudaSuccess) return cuda_fail("dense workspace allocation", e);
-            ctx->dense_ws_floats = need;
         }
     }
     const uint16_t *xg = static_cast<const uint16_t *>(x);
@@ -715,31 +703,33 @@ int tc_cuda_qlinear_gather(tc_cuda_ctx *ctx, const tc_cuda_weight *const *weight
         cudaError_t e = tc::launch_gemv(sv, static_cast<const uint16_t *>(x), k, y, ldy, out_dtype, sp, s, &epi);
         if (e != cudaSuccess) return cuda_fail("GEMV launch", e);
     }
-    // Dense weights: library GEMM (fp32 accumulation), then the fused
-    // epilogue from an fp32 product when the call has one.
-    const uint64_t item = out_dtype == TC_DTYPE_F32 ? 4 : 2;
-    for (const auto &d : dense) {
-        const uint32_t rows = d.e - d.b;
-        const void *wd = stage == TC_STAGE_BF16 ? (const void *)d.w->dense_bf16 : (const void *)d.w->dense_f16;
-        const uint16_t *xd = xg + (uint64_t)d.b * k;
-        if (flags) {
-            if (tc::dense_gemm(ctx->blas, wd, xd, stage != TC_STAGE_BF16, rows, (uint32_t)d.w->n, k, ctx->dense_ws,
-                               d.w->n, TC_DTYPE_F32, s))
-                return fail("cuBLAS GEMM failed");
-            cudaError_t e = tc::launch_epi_rows(ctx->dense_ws, rows, (uint32_t)d.w->n, epi, d.gate_row, d.b, y, ldy,
-                                                out_dtype, s);
-            if (e != cudaSuccess) return cuda_fail("epilogue launch", e);
-        } else if (tc::dense_gemm(ctx->blas, wd, xd, stage != TC_STAGE_BF16, rows, (uint32_t)d.w->n, k,
-                                  static_cast<uint8_t *>(y) + (uint64_t)d.b * ldy * item, ldy, out_dtype, s)) {
-            return fail("cuBLAS GEMM failed");
+    // Dense weights: the dense tensor-core GEMM on the bf16 or fp16 copy, with
+    // the fused epilogue and peer stores in its epilogue.  X needs a 16-byte
+    // row pitch: with K not a multiple of 8 it is copied (zero-padded) first.
+    if (!dense.empty()) {
+        const uint16_t *xd = xg;
+        uint64_t ldx = k;
+        if (k % 8) {
+            ldx = (k + 7) / 8 * 8;
+            const size_t need = m_total * ldx * 2;
+            if (need > ctx->dense_x_bytes) {
+                if (ctx->dense_x) cudaFree(ctx->dense_x);
+                ctx->dense_x = nullptr;
+                ctx->dense_x_bytes = 0;
+                cudaError_t e = cudaMalloc(&ctx->dense_x, need);
+                if (e != cudaSuccess) return cuda_fail("dense X workspace allocation", e);
+                ctx->dense_x_bytes = need;
+            }
+            cudaError_t e = tc::launch_pad_rows(xg, ctx->dense_x, m_total, k, ldx, s);
+            if (e != cudaSuccess) return cuda_fail("X pitch copy", e);
+            xd = ctx->dense_x;
         }
-        // peer replicas of a dense segment: copy-engine copies of its rows
-        for (uint32_t i = 0; i < n_peer; ++i) {
-            const uint64_t off = (uint64_t)d.b * ldy * item;
-            cudaError_t e = cudaMemcpy2DAsync(static_cast<uint8_t *>(peer_y[i]) + off, ldy * item,
-                                              static_cast<const uint8_t *>(y) + off, ldy * item, d.w->n * item, rows,
-                                              cudaMemcpyDefault, s);
-            if (e != cudaSuccess) return cuda_fail("peer copy", e);
+        for (const auto &d : dense) {
+            const bool f16 = stage != TC_STAGE_BF16;
+            cudaError_t e = tc::launch_dense_gemm(f16 ? d.w->dense_f16 : d.w->dense_bf16, d.w->dense_ld,
+                                                  (uint32_t)d.w->n, xd, ldx, m_total, k, d.b, d.e, d.gate_row, y, ldy,
+                                                  out_dtype, f16, gemm_sms, ctx->status, &epi, s);
+            if (e != cudaSuccess) return cuda_fail("dense GEMM launch", e);
         }
     }
     return ok();

@@ -18,9 +18,8 @@ struct tc_cuda_ctx {
     size_t gemv_counters_n = 0;
     int path = 0;                    // 0 auto, 1 GEMV, 2 GEMM, 3 GEMM with one-CTA tiles only
     int sm_limit = 0;                // SMs the tensor-core GEMM may occupy (0 = all)
-    void *blas = nullptr;            // cuBLAS handle for dense weights (created on first use)
-    float *dense_ws = nullptr;       // fp32 product of a dense segment before its epilogue
-    size_t dense_ws_floats = 0;
+    uint16_t *dense_x = nullptr;     // X with a 16-byte row pitch for the dense GEMM (grows on demand)
+    size_t dense_x_bytes = 0;
     // Copy-engine all-gather (tc_cuda_peer_push): by default the copies to
     // the peers go back to back on the caller's stream; push_fanout = k >= 2
     // spreads them over k side streams (created on first use), forked from
@@ -53,6 +52,7 @@ struct tc_cuda_weight {
     uint8_t *raw = nullptr;
     uint64_t raw_row_bytes = 0;
     uint16_t *dense_bf16 = nullptr, *dense_f16 = nullptr;
+    uint64_t dense_ld = 0;           // row pitch (elements) of the dense copies: K rounded up to 8
 };
 
 namespace tc {
@@ -208,11 +208,15 @@ cudaError_t launch_split_reduce(const float *part, uint32_t ksplit, uint64_t str
 
 // Dense (passthrough) weights, dense_linear.cu.
 bool dense_type(uint32_t type);
-cudaError_t launch_epi_rows(const float *acc, uint32_t rows, uint32_t n, const EpiView &e, uint32_t gate_row,
-                            uint32_t m_begin, void *y, uint64_t ldy, int out_dtype, cudaStream_t s);
-int dense_gemm(void *blas, const void *w, const void *x, int x_f16, uint32_t rows, uint32_t n, uint64_t k, void *y,
-               uint64_t ldy, int out_dtype, cudaStream_t s);
-int dense_blas_create(void **blas);
-void dense_blas_destroy(void *blas);
+// Y rows [m_begin, m_end) = X * W^T on the tensor cores (dense_gemm_sm100.cu):
+// W [n, k] 16-bit, row pitch ldw; X [m_total, k] 16-bit, row pitch ldx (both
+// pitches multiples of 8 elements, bases 16-byte aligned); f16: fp16
+// operands, else bf16; fused epilogue and peer stores as the K-quant GEMMs.
+cudaError_t launch_dense_gemm(const uint16_t *w, uint64_t ldw, uint32_t n, const uint16_t *x, uint64_t ldx,
+                              uint64_t m_total, uint64_t k, uint32_t m_begin, uint32_t m_end, uint32_t gate_row,
+                              void *y, uint64_t ldy, int out_dtype, int f16, int sm_count, uint32_t *status,
+                              const EpiView *epi, cudaStream_t s);
+// Copy X [m, k] (row pitch k) into out [m, ld] (ld >= k, zeros past k).
+cudaError_t launch_pad_rows(const uint16_t *x, uint16_t *out, uint64_t m, uint64_t k, uint64_t ld, cudaStream_t s);
 
 }  // namespace tc
