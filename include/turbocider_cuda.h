@@ -65,7 +65,9 @@ enum {
     TC_STATUS_F16_OVERFLOW    = 1u << 1, /* a value does not fit fp16          */
     TC_STATUS_TIMEOUT         = 1u << 2, /* a bounded pipeline wait gave up    */
     TC_STATUS_GEOMETRY        = 1u << 3, /* a kernel saw an impossible tile    */
-    TC_STATUS_BF16_OVERFLOW   = 1u << 4  /* a value rounds past the bf16 range */
+    TC_STATUS_BF16_OVERFLOW   = 1u << 4, /* a value rounds past the bf16 range */
+    TC_STATUS_BOUNDS          = 1u << 5  /* bounds-checked build only: an index
+                                            outside its buffer (access skipped) */
 };
 
 typedef struct tc_cuda_ctx tc_cuda_ctx;

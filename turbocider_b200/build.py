@@ -17,7 +17,11 @@ from pathlib import Path
 HERE = Path(__file__).resolve().parent
 CSRC = HERE / "csrc"
 OUT = HERE / "libturbocider_cuda.so"
-OBJ = HERE / "_build"
+# The bounds-checked variant (-DTC_BOUNDS_CHECK): every output store, weight
+# chunk address and decode target offset is checked, an index outside sets
+# TC_STATUS_BOUNDS instead of faulting.  The substitute for compute-sanitizer
+# in the GPU tests; loaded when TURBOCIDER_CHECKED=1.
+OUT_CHECKED = HERE / "libturbocider_cuda_checked.so"
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 COMMON = ["-std=c++17", "-O3", "-lineinfo", "-Xcompiler", "-fPIC", "-Xcompiler", "-Wall",
           "--expt-relaxed-constexpr", "-I", str(HERE.parent / "include")]
@@ -34,12 +38,12 @@ def sources() -> list[Path]:
     return sorted(p for p in CSRC.iterdir() if p.suffix in (".cu", ".cpp"))
 
 
-def _compile(src: Path, verbose: bool) -> Path:
-    obj = OBJ / (src.stem + ".o")
+def _compile(src: Path, obj_dir: Path, defines: list[str], verbose: bool) -> Path:
+    obj = obj_dir / (src.stem + ".o")
     deps = [src] + list(CSRC.glob("*.cuh")) + list(CSRC.glob("*.h")) + list((HERE.parent / "include").glob("*.h"))
     if obj.exists() and obj.stat().st_mtime >= max(d.stat().st_mtime for d in deps):
         return obj
-    cmd = [nvcc(), *ARCH, *COMMON, "-c", str(src), "-o", str(obj)]
+    cmd = [nvcc(), *ARCH, *COMMON, *defines, "-c", str(src), "-o", str(obj)]
     if src.suffix == ".cu" and verbose:
         cmd += ["-Xptxas", "-v"]
     res = subprocess.run(cmd, capture_output=True, text=True)
@@ -50,18 +54,29 @@ def _compile(src: Path, verbose: bool) -> Path:
     return obj
 
 
-def build(verbose: bool = False) -> Path:
-    OBJ.mkdir(exist_ok=True)
+def build(verbose: bool = False, checked: bool | None = None) -> Path:
+    """Build the library (and, unless checked is False, its bounds-checked
+    variant); returns the path of the normal library (checked=True: of the
+    checked one only)."""
+    variants = [(OUT, HERE / "_build", [])] if checked is not True else []
+    if checked is not False:
+        variants.append((OUT_CHECKED, HERE / "_build_checked", ["-DTC_BOUNDS_CHECK"]))
     srcs = sources()
+    jobs = []
+    for out, obj_dir, defines in variants:
+        obj_dir.mkdir(exist_ok=True)
+        jobs += [(src, obj_dir, defines) for src in srcs]
     with cf.ThreadPoolExecutor(max_workers=min(8, os.cpu_count() or 1)) as pool:
-        objs = list(pool.map(lambda s: _compile(s, verbose), srcs))
-    if OUT.exists() and OUT.stat().st_mtime >= max(o.stat().st_mtime for o in objs):
-        return OUT
-    cmd = [nvcc(), *ARCH, "-shared", "-o", str(OUT), *map(str, objs), "-lpthread"]
-    res = subprocess.run(cmd, capture_output=True, text=True)
-    if res.returncode != 0:
-        raise RuntimeError(f"link failed:\n{res.stderr}")
-    return OUT
+        objs = list(pool.map(lambda j: _compile(j[0], j[1], j[2], verbose), jobs))
+    for i, (out, obj_dir, defines) in enumerate(variants):
+        mine = objs[i * len(srcs):(i + 1) * len(srcs)]
+        if out.exists() and out.stat().st_mtime >= max(o.stat().st_mtime for o in mine):
+            continue
+        cmd = [nvcc(), *ARCH, "-shared", "-o", str(out), *map(str, mine), "-lpthread"]
+        res = subprocess.run(cmd, capture_output=True, text=True)
+        if res.returncode != 0:
+            raise RuntimeError(f"link failed:\n{res.stderr}")
+    return variants[0][0]
 
 
 if __name__ == "__main__":

@@ -244,7 +244,8 @@ __global__ void decode_raw_kernel(uint32_t type, const uint8_t *__restrict__ src
                                   uint64_t row_begin, uint64_t rows, uint64_t column_begin,
                                   uint64_t columns, uint8_t *__restrict__ dst, uint64_t row_stride,
                                   uint64_t column_stride, uint64_t first_group, uint64_t groups,
-                                  uint32_t *status, const uint64_t *__restrict__ gather, uint64_t source_rows) {
+                                  uint32_t *status, const uint64_t *__restrict__ gather, uint64_t source_rows,
+                                  uint64_t dst_bytes) {
     const uint64_t idx = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x;
     if (idx >= rows * groups) return;
     const uint64_t r = idx / groups;
@@ -310,7 +311,9 @@ __global__ void decode_raw_kernel(uint32_t type, const uint8_t *__restrict__ src
     for (int j = 0; j < 32; ++j) {
         const uint64_t c = c0 + j;
         if (c < column_begin || c >= column_begin + columns) continue;
-        store_value_bytes<DT>(dst + r * row_stride + (c - column_begin) * column_stride, v[j], ovf, bovf);
+        const uint64_t at = r * row_stride + (c - column_begin) * column_stride;
+        if (!tc_in_bounds(!dst_bytes || at + (DT == 0 ? 4 : 2) <= dst_bytes, status)) continue;
+        store_value_bytes<DT>(dst + at, v[j], ovf, bovf);
     }
     if (bad) atomicOr(status, kNonfinite);
     if (ovf) atomicOr(status, kF16Overflow);
@@ -366,7 +369,7 @@ cudaError_t launch_decode_raw(uint32_t type, const uint8_t *src, uint64_t row_by
                               uint64_t row_begin, uint64_t rows, uint64_t column_begin,
                               uint64_t columns, int dtype, uint8_t *dst, uint64_t row_stride,
                               uint64_t column_stride, uint32_t *status, cudaStream_t s, const uint64_t *gather,
-                              uint64_t source_rows) {
+                              uint64_t source_rows, uint64_t dst_bytes) {
     // Every block touched by the column range is decoded (and checked), as in
     // the reference's row_into (gguf_decode.cpp:340-364); threads work on
     // 32-weight groups (an eighth of a K-quant super-block, one legacy block,
@@ -379,15 +382,15 @@ cudaError_t launch_decode_raw(uint32_t type, const uint8_t *src, uint64_t row_by
     if (dtype == 0)
         decode_raw_kernel<0><<<g, 128, 0, s>>>(type, src, row_bytes, row_begin, rows, column_begin, columns,
                                                dst, row_stride, column_stride, first_group, groups, status, gather,
-                                               source_rows);
+                                               source_rows, dst_bytes);
     else if (dtype == 1)
         decode_raw_kernel<1><<<g, 128, 0, s>>>(type, src, row_bytes, row_begin, rows, column_begin, columns,
                                                dst, row_stride, column_stride, first_group, groups, status, gather,
-                                               source_rows);
+                                               source_rows, dst_bytes);
     else
         decode_raw_kernel<2><<<g, 128, 0, s>>>(type, src, row_bytes, row_begin, rows, column_begin, columns,
                                                dst, row_stride, column_stride, first_group, groups, status, gather,
-                                               source_rows);
+                                               source_rows, dst_bytes);
     return cudaGetLastError();
 }
 

@@ -80,6 +80,7 @@ __device__ __forceinline__ void store_out(void *p, uint64_t off, float v, bool f
 // Store to Y and to every peer replica of it (N-column sharding: the peers'
 // Y buffers over NVLink).
 __device__ __forceinline__ void store_out_all(const EpiView &e, void *y, uint64_t off, float v, bool f32, bool f16) {
+    if (!tc_in_bounds(!e.y_limit || off < e.y_limit, e.status)) return;
     store_out(y, off, v, f32, f16);
     for (uint32_t i = 0; i < e.n_peer; ++i) store_out(e.peer[i], off, v, f32, f16);
 }

@@ -448,7 +448,9 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
                 const PairTile T = pair_tile(p, u / p.ksplit);
                 uint32_t panel = 2 * T.pp + rank;
                 if (panel >= p.panels) panel = p.panels - 1;
-                return T.w + ((uint64_t)panel * p.kb + (u % p.ksplit) * p.kbu + c % p.kbu) * kChunk;
+                uint64_t at = (uint64_t)panel * p.kb + (u % p.ksplit) * p.kbu + c % p.kbu;
+                if (!tc_in_bounds(at < (uint64_t)p.panels * p.kb, p.status)) at = 0;
+                return T.w + at * kChunk;
             };
             for (uint32_t c = 0; c < kWStages && c < n_chunks; ++c) l2_prefetch(chunk_src(c), kChunk);
             for (uint32_t c = 0; ok && c < n_chunks; ++c) {
@@ -581,8 +583,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
 #pragma unroll
                             for (uint32_t c = 0; c < 32; ++c)
                                 if (t0 + c < T.m_end)
-                                    static_cast<float *>(p.y)[yoff + (uint64_t)(t0 + c) * p.ldy + n] =
-                                        __uint_as_float(v[c]);
+                                    store_out_all(p.epi, p.y, yoff + (uint64_t)(t0 + c) * p.ldy + n,
+                                                  __uint_as_float(v[c]), true, false);
                         }
                     }
                     if (half) {   // every TMEM load of the tile is done: hand D back
@@ -903,6 +905,8 @@ cudaError_t launch_pair_split(const CUtensorMap &xm, const YMaps &ym, PairParams
     p.y = sk.ws;
     p.ldy = p.n;
     p.epi = EpiView{};
+    p.epi.y_limit = (uint64_t)sk.ksplit * p.split_stride;
+    p.epi.status = p.status;
     YMaps pm;
     memset(&pm, 0, sizeof(pm));
     p.y_tma = encode_f32_map(encode_fn(), &pm.m[0], sk.ws, p.n, m_total, p.n, sk.ksplit, p.split_stride) ? 1u : 0u;

@@ -153,7 +153,8 @@ __global__ void __launch_bounds__(kThreads, 1)
             bool ok = true;
             for (uint32_t t = blockIdx.x; ok && t < p.n_tiles; t += gridDim.x) {
                 const Tile T = tile_of<BN>(p, t);
-                const uint8_t *panel = T.w + (uint64_t)T.panel * p.kb * kChunk;
+                const uint8_t *panel = T.w + (uint64_t)(tc_in_bounds(T.panel < p.panels, p.status) ? T.panel : 0) *
+                                                 p.kb * kChunk;
                 for (uint32_t kb = 0; ok && kb < p.kb; ++kb) {
                     if (!(ok = bar_wait(w_empty(ws), wph ^ 1, abort_flag, p.status))) break;
                     bar_expect_tx(w_full(ws), kChunk);

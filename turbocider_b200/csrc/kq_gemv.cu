@@ -416,7 +416,8 @@ __global__ void __launch_bounds__(kWarps * 32, 4) gemv_kernel(const __grid_const
     const uint32_t row0 = (blockIdx.x - w.tile_begin) * 16, panel = row0 / kPanelRows, r0 = row0 % kPanelRows;
     const uint32_t n_slices = gridDim.y, kb_begin = blockIdx.y * kb_per_slice;
     const uint32_t kb_end = min(b.kb, kb_begin + kb_per_slice);
-    const uint8_t *pbase = w.chunks + (uint64_t)panel * b.kb * chunk;
+    const uint8_t *pbase =
+        w.chunks + (uint64_t)(tc_in_bounds(row0 < w.n && kb_end <= b.kb, status) ? panel : 0) * b.kb * chunk;
     constexpr bool kStageX = TP == 1;
     constexpr uint32_t stage_bytes = (SG::w_bytes + (kStageX ? 512u : 0u) + 127) / 128 * 128;
     constexpr uint32_t kGemvStages = gemv_stages<NT>();

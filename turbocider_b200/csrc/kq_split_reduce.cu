@@ -44,6 +44,7 @@ __global__ void __launch_bounds__(256) split_reduce_kernel(const float *__restri
     // SwiGLU weights interleave 8 gate rows and the same 8 up rows; V = 4
     // columns starting at a multiple of 4 stay inside one group of 8.
     const uint32_t row0 = glu ? (c0 >> 3) * 16 + (c0 & 7) : c0;
+    if (!tc_in_bounds(m * n_w + row0 + (glu ? 8 : 0) + V <= stride, e.status)) return;
     const float *src = part + m * n_w + row0;
     Vec pa[S], pu[S];
 #pragma unroll

@@ -421,7 +421,8 @@ int tc_cuda_decode(tc_cuda_ctx *ctx, uint32_t type, const void *source, uint64_t
     DeviceGuard guard(ctx->device);
     cudaError_t e = tc::launch_decode_raw(type, static_cast<const uint8_t *>(source), row_bytes, row_begin, rows,
                                           column_begin, columns, dtype, static_cast<uint8_t *>(target), row_stride,
-                                          column_stride, ctx->status, static_cast<cudaStream_t>(stream));
+                                          column_stride, ctx->status, static_cast<cudaStream_t>(stream), nullptr, 0,
+                                          target_bytes);
     if (e != cudaSuccess) return cuda_fail("decode launch", e);
     return ok();
 }
@@ -451,7 +452,7 @@ int tc_cuda_decode_gather(tc_cuda_ctx *ctx, uint32_t type, const void *source, u
     cudaError_t e = tc::launch_decode_raw(type, static_cast<const uint8_t *>(source), row_bytes, 0, n_indices,
                                           column_begin, columns, dtype, static_cast<uint8_t *>(target), row_stride,
                                           column_stride, ctx->status, static_cast<cudaStream_t>(stream), row_indices,
-                                          source_rows);
+                                          source_rows, target_bytes);
     if (e != cudaSuccess) return cuda_fail("gather launch", e);
     return ok();
 }
@@ -620,6 +621,8 @@ int tc_cuda_qlinear_gather(tc_cuda_ctx *ctx, const tc_cuda_weight *const *weight
     if (reinterpret_cast<uintptr_t>(x) % 16) return fail("X must be 16-byte aligned");
     const uint64_t m_total = (uint64_t)seg_offsets[n_seg];
     if (!m_total) return ok();
+    epi.y_limit = (m_total - 1) * ldy + n_out;   // checked by bounds-checked builds
+    epi.status = ctx->status;
     DeviceGuard guard(ctx->device);
     cudaStream_t s = static_cast<cudaStream_t>(stream);
     const uint64_t k = w0->k;

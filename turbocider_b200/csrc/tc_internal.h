@@ -120,7 +120,27 @@ struct EpiView {
     // mapped into this process), so the all-gather happens in the epilogue.
     uint32_t n_peer = 0;
     void *peer[kMaxPeers - 1] = {};
+    // Bounds-checked builds (TC_BOUNDS_CHECK): elements addressable from Y's
+    // base (0: not checked) and the status word that records a violation.
+    uint64_t y_limit = 0;
+    uint32_t *status = nullptr;
 };
+
+// Bounds checks of the -DTC_BOUNDS_CHECK build (libturbocider_cuda_checked.so,
+// the substitute for compute-sanitizer, which this GPU pool does not offer):
+// tc_in_bounds(cond, status) records TC_STATUS_BOUNDS when cond is false and
+// returns cond, so the caller skips (stores) or clamps (reads) the access
+// instead of faulting; in the normal build it is `true` and costs nothing.
+#ifdef TC_BOUNDS_CHECK
+#ifdef __CUDACC__
+__device__ __forceinline__ bool tc_in_bounds(bool cond, uint32_t *status) {
+    if (!cond && status) atomicOr(status, 1u << 5);
+    return cond;
+}
+#endif
+#else
+#define tc_in_bounds(cond, status) true
+#endif
 
 // glu_c > 0: the source holds glu_c gate rows then glu_c up rows, and panel
 // row 16 g + i takes gate row 8 g + i (i < 8) or up row 8 g + i - 8.
@@ -131,11 +151,12 @@ cudaError_t launch_dequant_panel(const WeightView &w, int dtype, void *dst, uint
                                  uint32_t *status, cudaStream_t s);
 // gather != nullptr: target row r decodes source row gather[r] (device array,
 // checked against source_rows; TC_STATUS_GEOMETRY for an index past it).
+// dst_bytes: the target's size (0: not checked by bounds-checked builds).
 cudaError_t launch_decode_raw(uint32_t type, const uint8_t *src, uint64_t row_bytes,
                               uint64_t row_begin, uint64_t rows, uint64_t column_begin,
                               uint64_t columns, int dtype, uint8_t *dst, uint64_t row_stride,
                               uint64_t column_stride, uint32_t *status, cudaStream_t s,
-                              const uint64_t *gather = nullptr, uint64_t source_rows = 0);
+                              const uint64_t *gather = nullptr, uint64_t source_rows = 0, uint64_t dst_bytes = 0);
 // Small-M GEMV K split: n_slices CTAs per 16-row tile.  With n_slices > 1
 // the kernel needs `partials` (gemv_workspace_floats floats) and one zeroed
 // uint32 counter per 16-row tile; both are left as found (counters back to 0).

@@ -119,7 +119,10 @@ extern "C" int tc_cuda_qlinear_small_static(const tc_cuda_weight *weight, const 
     cudaError_t e = cudaMemsetAsync(bytes + kStatusBytes, 0, counter_bytes, s);
     if (e == cudaSuccess) {
         const tc::SegmentView seg{0u, m, view};
-        e = tc::launch_gemv(seg, static_cast<const uint16_t *>(x), weight->k, y, ldy, out_dtype, sp, s);
+        tc::EpiView plain;   // no epilogue; Y's extent for bounds-checked builds
+        plain.y_limit = (uint64_t)(m - 1) * ldy + weight->n;
+        plain.status = sp.status;
+        e = tc::launch_gemv(seg, static_cast<const uint16_t *>(x), weight->k, y, ldy, out_dtype, sp, s, &plain);
     }
     if (previous != weight->device) cudaSetDevice(previous);
     if (e != cudaSuccess) return fail(std::string("static-scratch GEMV launch: ") + cudaGetErrorString(e));

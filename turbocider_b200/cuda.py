@@ -14,12 +14,17 @@ from pathlib import Path
 
 import numpy as np
 
-LIB_PATH = Path(__file__).resolve().parent / "libturbocider_cuda.so"
+# TURBOCIDER_CHECKED=1 loads the bounds-checked build (-DTC_BOUNDS_CHECK:
+# out-of-range indices set STATUS_BOUNDS instead of faulting).
+LIB_PATH = Path(__file__).resolve().parent / ("libturbocider_cuda_checked.so"
+                                             if os.environ.get("TURBOCIDER_CHECKED") == "1"
+                                             else "libturbocider_cuda.so")
 
 Q4_K, Q5_K, Q6_K = 12, 13, 14
 F32, F16, BF16 = 0, 1, 2
 STAGE_BF16, STAGE_F16, STAGE_F16_X16 = 0, 1, 2
 STATUS_NONFINITE_SCALE, STATUS_F16_OVERFLOW, STATUS_TIMEOUT, STATUS_GEOMETRY, STATUS_BF16_OVERFLOW = 1, 2, 4, 8, 16
+STATUS_BOUNDS = 32
 EPI_BIAS, EPI_GELU_TANH, EPI_GELU_ERF, EPI_SWIGLU, EPI_GATE_RESIDUAL = 1, 2, 4, 8, 16
 BLOCK_BYTES = {Q4_K: 144, Q5_K: 176, Q6_K: 210}
 
