@@ -765,6 +765,35 @@ def parity_check(raw_cache, names, layers, y_loc, y_all, x_h, x_f, world, rank, 
             "gathered_y_consistent_on_all_ranks": consistent}
 
 
+def run_leg(args):
+    """One measurement leg alone on GPU 0 (the unit a profiler captures)."""
+    import torch
+    from turbocider_b200 import cuda as tcc
+    torch.cuda.set_device(0)
+    device = torch.device("cuda", 0)
+    hbm_peak, tc_burst, tc_sustained, _ = peaks()
+    ctx = tcc.Context(0)
+    if args.leg == "gemv":
+        out = gemv_measure(ctx, device, hbm_peak)
+    elif args.leg == "config1":
+        out = config1_measure(ctx, device, tc_burst)
+    elif args.leg == "config3":
+        out = config3_measure(ctx, device, tc_sustained)
+    elif args.leg == "config4":
+        out = config4_stream(ctx, device)
+    elif args.leg == "epilogues":
+        out = epilogue_measure(ctx, device)
+    else:
+        weights, raw_cache = build_weights(ctx, 0, 1, 1, device, args.ffn)
+        out = loader_measure(ctx, raw_cache)
+        for lw in weights:
+            for wt in lw.values():
+                wt.free()
+    ctx.close()
+    print(json.dumps({"leg": args.leg, **out}), flush=True)
+    return 0
+
+
 def run_ours(args):
     import torch
     import torch.distributed as dist
@@ -1088,6 +1117,8 @@ def main():
                          "engines beside the next GEMM, or NCCL after each GEMM")
     ap.add_argument("--ffn", choices=["swiglu", "separate"], default="swiglu",
                     help="FFN input projections: one SwiGLU-fused weight (silu(w1 x) * w3 x) or two plain linears")
+    ap.add_argument("--leg", choices=["gemv", "config1", "config3", "config4", "epilogues", "loader"],
+                    default=None, help="run only this measurement leg on GPU 0 and print its JSON (profiling)")
     ap.add_argument("--push-streams", type=int, default=0,
                     help="--gather copy: spread each output's peer copies over this many side streams "
                          "(0 / 1: back to back, the default)")
@@ -1096,6 +1127,8 @@ def main():
     args = ap.parse_args()
     if args.warmup < 3 and args.impl == "ours":
         args.warmup = 3
+    if args.leg:
+        return run_leg(args)
     return run_reference(args) if args.impl == "reference" else run_ours(args)
 
 
