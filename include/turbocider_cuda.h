@@ -348,13 +348,13 @@ int tc_cuda_set_sm_limit(tc_cuda_ctx *ctx, int sms);
  * cannot take cudaMalloc's implicit synchronisation): computes
  * Y[m, N] = X[m, K] * W^T for 1 <= m <= 16 with the split-K GEMV of
  * tc_cuda_qlinear, whose scratch (K-slice partials, per-tile counters, status
- * word) here lives in a 4 MiB file-scope device array instead of a cudaMalloc'd
+ * word) here lives in an 8 MiB file-scope device array instead of a cudaMalloc'd
  * context workspace.  No context argument; X bf16 [m, K] (16-byte aligned), Y
  * f32, f16 or bf16 with row stride ldy (0 = N), all device memory, enqueued on
  * `stream`.  The first call on a device looks up the array's address and
  * clears its status word, synchronously (make it before any stream capture);
- * the K-split rule keeps every shape's scratch under about 0.9 MiB, and a
- * size check rejects anything over 4 MiB; every call shares the array, so
+ * a call needs 4.6 MiB of it plus 4 bytes per 16 weight rows, and a
+ * size check rejects anything over 8 MiB; every call shares the array, so
  * calls that may overlap on the GPU must be serialised by the caller.
  * Device-side errors (TC_STATUS_* bits) accumulate in the array's status word
  * until read with tc_cuda_small_static_status.  Allocates nothing. */

@@ -49,11 +49,11 @@ def test_static_scratch_matches_qlinear_twice(ctx, typ, n, k, m):
 
 
 def test_static_scratch_covers_large_shapes_and_rejects_bad_rows(ctx):
-    """The GEMV splits K only while there are fewer than 444 row tiles, so its
-    scratch stays below ~0.9 MiB for every shape (slices x tiles < 888 tiles
-    of 1 KiB partials); the 4 MiB array's size check remains as a guard.  A
-    large weight (1376 row tiles, one K slice) runs and matches the context
-    path; row counts outside 1..16 are rejected."""
+    """The GEMV's scratch is at most 4.6 MiB of partials (K slices x row
+    tiles < 1184, 4 KiB each) plus one counter per 16 weight rows, inside the 8
+    MiB array, whose size check remains as a guard.  Large weights (22016
+    and 37824 rows, with and without a K split) run and match the context
+    path and the oracle; row counts outside 1..16 are rejected."""
     import torch
     from turbocider_b200 import cuda as tcc
     n, k = 22016, 8448
@@ -67,7 +67,7 @@ def test_static_scratch_covers_large_shapes_and_rejects_bad_rows(ctx):
     rows = np.arange(0, n, 7)   # every 7th output column against the fp32-decode oracle
     sub = raw.reshape(n, -1)[rows]
     assert oracle.rel_l2(got[:, rows], oracle.qlinear_ref(xb, sub, 12, len(rows), k, "f32")) <= 1e-5
-    for n2, k2 in ((3072, 12288), (128, 256), (9000, 1024)):
+    for n2, k2 in ((3072, 12288), (128, 256), (9000, 1024), (591 * 64, 1024)):
         w2 = tcc.Weight.upload(ctx, 14, n2, k2, tcc.quantize(14, kq_cases.synthetic_weight(n2, k2, seed=n2)))
         x2 = torch.randn(16, k2, device="cuda").to(torch.bfloat16)
         ref2 = tcc.qlinear(ctx, w2, x2, out_dtype=tcc.F32).cpu().numpy()

@@ -20,20 +20,21 @@
 // Result: fp32 accumulation of exactly-represented products; equal to the
 // fp32-decode + fp32 matmul oracle up to summation order.
 //
-// Work split: CTA (x, y) = (16 weight rows, one K slice of 4 super-blocks),
-// 4 warps each taking one super-block, so that thousands of short CTAs keep
-// every SM's loads in flight (the CTA count is independent of the SM count).
-// Each warp streams its super-blocks' packed fields through a ring of 3 (2
-// with more than 8 tokens) stages of per-lane cp.async copies.  With one token (TP = 1) the stage also carries
-// that token's 256 columns of X (512 B); with more tokens X is read straight
-// from global memory instead (at most 16 rows x K, the same for every row
-// tile, so it stays in L1 / L2), all of a super-block's X fragments at once:
-// staging M rows per stage would shrink the number of resident CTAs as M
-// grows (one CTA of 4 warps per SM at M = 16).  A CTA
-// sums its warps through shared memory; with several K slices it stores the
-// 16 x M partial in the context workspace, and the last CTA of the row tile to
-// finish (per-tile arrival counter) adds the slices in slice order -- a fixed
-// order, so results are deterministic -- writes Y and resets the counter.
+// Work split: CTA (x, y) = (64 weight rows, one K slice), warp w owning rows
+// 16 w .. 16 w + 15.  The four warps walk the same super-blocks of the slice
+// in step through one ring of stages (3; 2 with more than 8 tokens) filled by
+// per-lane cp.async copies: a stage holds the four warps' packed fields and
+// the super-block's 256 columns of X for every token, copied once per CTA
+// and read by the MMA steps from shared memory.  (With 16 rows per CTA and X
+// fragments loaded from global memory, X -- 16 tokens x the K slice -- came
+// from L2 for every 16 weight rows, 75 MB per config-2 call against 31 MB of
+// weights, and the kernel stalled on those loads.)  One __syncthreads per
+// super-block publishes the stage and frees the slot computed before it.
+// Hundreds of short CTAs keep every SM's loads in flight (the K split sizes
+// the grid, not the SM count).  With several K slices each warp stores its
+// 16 x M partial in the workspace, and the last CTA of the tile to finish
+// (per-tile arrival counter) adds the slices in slice order -- a fixed order,
+// so results are deterministic -- writes Y and resets the counter.
 // The N8 side of the MMA carries the tokens: NT = 1 or 2 tiles of 8.
 // Launches use programmatic dependent launch: weight prefetch overlaps the
 // tail of the previous kernel in the stream; X, the workspace and Y are
@@ -64,8 +65,8 @@ __device__ __forceinline__ void mma16816(float (&d)[4], uint32_t a0, uint32_t a1
 }
 
 // ---------------------------------------------------------------- staging
-// Per-warp stage in shared memory: the packed fields of 16 weight rows for one
-// super-block (contiguous pieces of the panel chunk, one bulk copy each).
+// A warp's piece of a stage: the packed fields of its 16 weight rows for one
+// super-block (contiguous pieces of the panel chunk).
 //   Q4_K: qs [4][16 rows][32] | sc [16][12] | dm [16][4]              = 2304 B
 //   Q6_K: ql [4 = h*2+part][16][32] | qh [2][16][32] | sc [16][16] | d [16][2] = 3360 B
 // Row r of a piece is at row_slot(r0 + r) - r0.
@@ -126,13 +127,6 @@ __device__ __forceinline__ void issue_w(uint8_t *st, const uint8_t *chunk, uint3
         cpa_piece(d + SG::sc, chunk + kQ6Sc + r0 * 16, 256, lane);
         cpa_piece(d + SG::d, chunk + kQ6D + r0 * 2, 32, lane);
     }
-}
-// All lanes: the single token's 256 columns of X for super-block kb (TP = 1).
-template <int TYPE>
-__device__ __forceinline__ void issue_x1(uint8_t *st, const uint16_t *x, uint64_t k, uint32_t m, uint32_t kb,
-                                         uint32_t lane) {
-    cpa_piece(s_u32(st) + StageGeo<TYPE>::w_bytes,
-              reinterpret_cast<const uint8_t *>(x + (uint64_t)m * k + (uint64_t)kb * 256), 512, lane);
 }
 // Programmatic dependent launch: let the next kernel in the stream start its
 // prologue, and wait for the previous one before touching its outputs.
@@ -208,37 +202,30 @@ __device__ __forceinline__ uint32_t own_col(uint32_t c, uint32_t my_j, uint32_t 
         return 32 * (my_j + S * (c >> 1)) + 8 * t + 4 * (c & 1);
     }
 }
-// N own steps' fragments (N = 2 TP: a whole super-block; 8: half of one).
-template <int N, int NT> struct XFrags { uint2 v[N][NT]; };
-template <int TYPE, int TP, int NT, int N>
-__device__ __forceinline__ void load_x(XFrags<N, NT> &xs, const uint16_t *__restrict__ x, uint64_t k,
-                                       uint32_t m_begin, uint32_t kb, uint32_t m_count, uint32_t g, uint32_t t,
-                                       uint32_t c_begin) {
-#pragma unroll
-    for (int nt = 0; nt < NT; ++nt) {
-        const uint16_t *xr = x + (uint64_t)(m_begin + min(8 * nt + g % TP, m_count - 1)) * k + (uint64_t)kb * 256;
-#pragma unroll
-        for (uint32_t c = 0; c < (uint32_t)N; ++c)
-            xs.v[c][nt] = __ldg(reinterpret_cast<const uint2 *>(xr + own_col<TYPE, TP>(c_begin + c, g / TP, t)));
-    }
-}
-
-// Halves [H0, H1) of one super-block (weights 128 H0 .. 128 H1 - 1 of its
-// rows); the scale table is built with half 0.  The own-step fragments in
-// xs_global start at own step C0 (0, or 8 for a second-half call; halves are
-// only computed separately with 8 tokens per tile, where every chain is
-// within a half).
-template <int TYPE, int TP, int NT, int N, uint32_t H0 = 0, uint32_t H1 = 2, uint32_t C0 = 0>
-__device__ __forceinline__ void compute_stage(const uint8_t *st, const XFrags<N, NT> &xs_global, uint32_t g,
-                                              uint32_t t, uint32_t lane, const uint32_t (&bmask)[8 / TP],
-                                              float *wt, float (&acc)[NT][4]) {
+// X in the stage: TP * NT token rows of one super-block's 256 columns (one
+// row for TP = 1), rows clamped to the last real token.  With several rows the
+// row pitch is 544 bytes: the lanes of a quad group (g = 0..7) read rows
+// 8 g apart in banks, so the 16 lanes of one 64-bit phase hit 32 distinct
+// banks.
+template <int TP, int NT> struct XGeo {
+    static constexpr uint32_t rows = TP == 1 ? 1u : (uint32_t)(TP * NT);
+    static constexpr uint32_t pitch = TP == 1 ? 512u : 544u;
+    static constexpr uint32_t bytes = rows * pitch;
+};
+__device__ __forceinline__ uint2 lds64(const uint8_t *p) { return *reinterpret_cast<const uint2 *>(p); }
+// One super-block of the warp's 16 rows (packed fields at st) against the
+// stage's X rows (xs): the scale table first, then the K16 steps.
+template <int TYPE, int TP, int NT>
+__device__ __forceinline__ void compute_stage(const uint8_t *st, const uint8_t *xs, uint32_t g, uint32_t t,
+                                              uint32_t lane, const uint32_t (&bmask)[8 / TP], float *wt,
+                                              float (&acc)[NT][4]) {
     using SG = StageGeo<TYPE>;
     constexpr uint32_t S = 8 / TP;
     const uint32_t rg = row_slot(g), rg8 = row_slot(g + 8);   // slots inside the 16-row piece
     const uint32_t half = lane & 1, rr = lane >> 1;
     // Scale table, written by all lanes: row rr, half `half` of its groups.
     //   Q4_K: float2 (d*sc_g, dmin*m_g) [16][8];  Q6_K: float d*sc_i [16][16].
-    if constexpr (H0 == 0) {
+    {
     __syncwarp();
     if constexpr (TYPE != 14) {
         const uint32_t dm = lds32(st + SG::dm + rr * 4);
@@ -268,15 +255,10 @@ __device__ __forceinline__ void compute_stage(const uint8_t *st, const XFrags<N,
     __syncwarp();
     }
     const uint32_t my_j = g / TP;
-    // one token: its 256 columns of X are part of the stage; read the own steps'
-    XFrags<N, NT> xs_stage;
-    if constexpr (TP == 1) {
-        const uint16_t *x1 = reinterpret_cast<const uint16_t *>(st + SG::w_bytes);
+    // the X rows of this thread's tokens (8 nt + g % TP) in the stage
+    const uint8_t *xrow[NT];
 #pragma unroll
-        for (uint32_t c = 0; c < 2; ++c)
-            xs_stage.v[c][0] = *reinterpret_cast<const uint2 *>(x1 + own_col<TYPE, TP>(c, my_j, t));
-    }
-    const XFrags<N, NT> &xs = TP == 1 ? xs_stage : xs_global;
+    for (int nt = 0; nt < NT; ++nt) xrow[nt] = xs + (8 * nt + g % TP) * XGeo<TP, NT>::pitch;
     const uint32_t ones = 0x3F803F80u;
     constexpr float off = 128.f;   // Q4_K: the code-space offset of code_pair
     float cq[NT][4], c1[NT][4];
@@ -301,7 +283,7 @@ __device__ __forceinline__ void compute_stage(const uint8_t *st, const XFrags<N,
         }
 #pragma unroll
         for (int nt = 0; nt < NT; ++nt) {
-            const uint2 xv = xs.v[c - C0][nt];
+            const uint2 xv = lds64(xrow[nt] + 2 * own_col<TYPE, TP>(c, my_j, t));
             const uint32_t b0 = xv.x * bmask[j], b1 = xv.y * bmask[j];
             mma16816(cq[nt], a0, a1, a2, a3, b0, b1, cq[nt]);
             if constexpr (TYPE != 14) mma16816(c1[nt], ones, ones, ones, ones, b0, b1, c1[nt]);
@@ -340,7 +322,7 @@ __device__ __forceinline__ void compute_stage(const uint8_t *st, const XFrags<N,
             hq8 = *reinterpret_cast<const uint2 *>(st + StageGeo<13>::qh + rg8 * 32 + 8 * t);
         }
 #pragma unroll
-        for (uint32_t q = 2 * H0; q < 2 * H1; ++q) {
+        for (uint32_t q = 0; q < 4; ++q) {
             const uint2 wg = *reinterpret_cast<const uint2 *>(st + SG::qs + q * 512 + rg * 32 + 8 * t);
             const uint2 wg8 = *reinterpret_cast<const uint2 *>(st + SG::qs + q * 512 + rg8 * 32 + 8 * t);
 #pragma unroll
@@ -361,7 +343,7 @@ __device__ __forceinline__ void compute_stage(const uint8_t *st, const XFrags<N,
         }
     } else {
 #pragma unroll
-        for (uint32_t h = H0; h < H1; ++h) {
+        for (uint32_t h = 0; h < 2; ++h) {
 #pragma unroll
             for (uint32_t jj = 0; jj < 2; ++jj) {
                 const uint32_t o0 = SG::ql + (h * 2) * 512 + 16 * jj + 4 * t;
@@ -387,15 +369,34 @@ __device__ __forceinline__ void compute_stage(const uint8_t *st, const XFrags<N,
     }
 }
 
-// Depth of each warp's stage ring: 3 stages, except with two token tiles
-// (M > 8), where 2 stages leave room for more resident CTAs (measured: per
-// call at M = 16, 19.0 -> 18.0 us; at M = 1 a 2-stage ring is slower).
+// Row warps of a CTA (RW; the other 4 / RW split K inside the CTA):
+//   1 (one token): 16 rows; warp w takes super-blocks kb_begin + w + 4 i of
+//     the slice through its own stage ring (its W piece and the token's 512
+//     bytes of X), and the four sums meet in shared memory.  X is small next
+//     to W, and independent warps hide each other's load latency; the K
+//     split inside the CTA spares three quarters of the global fix-up.
+//   4 (several tokens): 64 rows, warp w owning rows 16 w .. 16 w + 15; one
+//     stage ring for the CTA holds the four W pieces and the super-block's X
+//     for every token, copied once and read by all four warps.
+template <int TP> constexpr uint32_t gemv_row_warps() { return TP == 1 ? 1u : 4u; }
+// Depth of the stage rings: 3 stages, except with two token tiles (M > 8),
+// where 2 stages leave room for four resident CTAs.
 template <int NT>
 constexpr uint32_t gemv_stages() { return NT == 2 ? 2u : 3u; }
+// Bytes of one stage: per warp (RW = 1) or per CTA (RW = 4).
+template <int TYPE, int TP, int NT>
+constexpr uint32_t gemv_stage_bytes() {
+    return (gemv_row_warps<TP>() * StageGeo<TYPE>::w_bytes + XGeo<TP, NT>::bytes + 127) / 128 * 128;
+}
+template <int TYPE, int TP, int NT>
+constexpr uint32_t gemv_smem_bytes() {
+    return gemv_stage_bytes<TYPE, TP, NT>() * gemv_stages<NT>() * (kWarps / gemv_row_warps<TP>());
+}
 
-// Weights of one launch: blockIdx.x runs over the 16-row tiles of all of
-// them (entry e owns tiles [tile_begin, next entry's tile_begin)); they share
-// K, type and X, each has its own Y.
+// Weights of one launch: blockIdx.x runs over the 16 RW-row tiles of all of
+// them (entry e owns tiles [tile_begin, next entry's tile_begin)), blockIdx.y
+// over the K slices of kb_per_slice super-blocks; they share K, type and X,
+// each has its own Y.
 template <int TYPE, int TP, int NT, int DT>
 __global__ void __launch_bounds__(kWarps * 32, 4) gemv_kernel(const __grid_constant__ GemvBatch b,
                                                            const uint16_t *__restrict__ x, uint32_t m_begin,
@@ -403,44 +404,65 @@ __global__ void __launch_bounds__(kWarps * 32, 4) gemv_kernel(const __grid_const
                                                            float *__restrict__ partials,
                                                            uint32_t *__restrict__ counters, uint32_t *status) {
     using SG = StageGeo<TYPE>;
+    using XG = XGeo<TP, NT>;
     constexpr uint32_t chunk = chunk_bytes(TYPE);
+    constexpr uint32_t RW = gemv_row_warps<TP>(), KW = kWarps / RW;
+    constexpr uint32_t kStages = gemv_stages<NT>(), stage_bytes = gemv_stage_bytes<TYPE, TP, NT>();
+    constexpr uint32_t w_all = RW * SG::w_bytes;   // X follows the stage's W pieces
     extern __shared__ __align__(128) uint8_t dyn[];
-    __shared__ float red[kWarps][32][4 * NT];
     __shared__ __align__(16) float tab[kWarps][16 * 16];
-    uint32_t ei = 0;
-    while (ei + 1 < b.n_entries && blockIdx.x >= b.e[ei + 1].tile_begin) ++ei;
-    const GemvEntry &w = b.e[ei];
-    void *const y = w.y;
-    const uint64_t ldy = w.ldy;
+    __shared__ uint32_t last;
     const uint32_t warp = threadIdx.x >> 5, lane = threadIdx.x & 31, g = lane >> 2, t = lane & 3;
-    const uint32_t row0 = (blockIdx.x - w.tile_begin) * 16, panel = row0 / kPanelRows, r0 = row0 % kPanelRows;
-    const uint32_t n_slices = gridDim.y, kb_begin = blockIdx.y * kb_per_slice;
-    const uint32_t kb_end = min(b.kb, kb_begin + kb_per_slice);
-    const uint8_t *pbase =
-        w.chunks + (uint64_t)(tc_in_bounds(row0 < w.n && kb_end <= b.kb, status) ? panel : 0) * b.kb * chunk;
-    constexpr bool kStageX = TP == 1;
-    constexpr uint32_t stage_bytes = (SG::w_bytes + (kStageX ? 512u : 0u) + 127) / 128 * 128;
-    constexpr uint32_t kGemvStages = gemv_stages<NT>();
-    uint8_t *mine = dyn + (size_t)warp * kGemvStages * stage_bytes;
+    const uint32_t rw = warp % RW, kw = warp / RW;
+    const uint32_t kb = b.kb, tile = blockIdx.x, n_slices = gridDim.y;
+    const uint32_t kb_begin = blockIdx.y * kb_per_slice, kb_end = min(kb, kb_begin + kb_per_slice);
+    uint32_t ei = 0;
+    while (ei + 1 < b.n_entries && tile >= b.e[ei + 1].tile_begin) ++ei;
+    const GemvEntry &w = b.e[ei];
+    const uint32_t row0 = (tile - w.tile_begin) * (16 * RW) + rw * 16;
+    // rows past n up to the panel end are zero blocks (read, never stored)
+    const uint32_t panel =
+        tc_in_bounds(row0 / kPanelRows < (w.n + kPanelRows - 1) / kPanelRows, status) ? row0 / kPanelRows : 0;
+    const uint8_t *pbase = w.chunks + (uint64_t)panel * kb * chunk;
+    const uint32_t r0 = row0 % kPanelRows;
     float *wt = tab[warp];
 
-    // This warp's super-blocks: kb_begin + warp + kWarps * i.  Stage i is
-    // commit group i; the weights of the first S-1 stages are issued before
-    // the wait on the previous kernel (they do not depend on it), their X
-    // after it, each as a group of its own, so that before computing stage i
-    // exactly the S-1 most recent groups may still be in flight.
-    const uint32_t first = kb_begin + warp;
-    const uint32_t count = first < kb_end ? (kb_end - first + kWarps - 1) / kWarps : 0;
+    // This warp's super-blocks: kb_begin + kw + KW i (RW = 1: its own; RW = 4:
+    // every warp the same).  Stage i of the warp's ring (RW = 1) or the CTA's
+    // (RW = 4) is slot i % kStages: the W pieces, then the X rows.
+    const uint32_t first = kb_begin + kw;
+    const uint32_t count = first < kb_end ? (kb_end - first + KW - 1) / KW : 0;
+    uint8_t *const ring = dyn + (size_t)kw * kStages * stage_bytes;
+    auto slot = [&](uint32_t i) { return ring + (i % kStages) * stage_bytes; };
+    auto issue_w_stage = [&](uint32_t i) {
+        issue_w<TYPE>(slot(i) + rw * SG::w_bytes, pbase + (uint64_t)(first + KW * i) * chunk, r0, lane);
+    };
+    // X rows of stage i: by the warp itself (RW = 1) or shared by the CTA.
+    auto issue_x = [&](uint32_t i) {
+        const uint32_t d = s_u32(slot(i) + w_all), kbx = first + KW * i;
+        const uint32_t me = RW == 1 ? lane : threadIdx.x, step = RW == 1 ? 32u : kWarps * 32u;
+        for (uint32_t q = me; q < XG::rows * 32; q += step) {
+            const uint32_t r = q / 32, c16 = q % 32;
+            const uint64_t tok = m_begin + min(r, m_count - 1);
+            cpa16(d + r * XG::pitch + c16 * 16, x + tok * k + (uint64_t)kbx * 256 + c16 * 8);
+        }
+    };
+    // Each thread commits its copies of a stage as one group; the W of the
+    // first kStages - 1 stages is issued before the wait on the previous
+    // kernel (it does not depend on it), their X after it, as groups of their
+    // own, so that before computing stage i at most kStages - 2 of this
+    // thread's groups -- once stage i + kStages - 1 is committed, kStages - 1
+    // -- may still be in flight.
 #pragma unroll
-    for (uint32_t i = 0; i < kGemvStages - 1; ++i) {
-        if (i < count) issue_w<TYPE>(mine + i * stage_bytes, pbase + (uint64_t)(first + kWarps * i) * chunk, r0, lane);
+    for (uint32_t i = 0; i < kStages - 1; ++i) {
+        if (i < count) issue_w_stage(i);
         cpa_commit();
     }
     if (threadIdx.x == 0) pdl_launch_dependents();
     pdl_wait();
 #pragma unroll
-    for (uint32_t i = 0; i < kGemvStages - 1; ++i) {
-        if (kStageX && i < count) issue_x1<TYPE>(mine + i * stage_bytes, x, k, m_begin, first + kWarps * i, lane);
+    for (uint32_t i = 0; i < kStages - 1; ++i) {
+        if (i < count) issue_x(i);
         cpa_commit();
     }
     float acc[NT][4];
@@ -448,138 +470,113 @@ __global__ void __launch_bounds__(kWarps * 32, 4) gemv_kernel(const __grid_const
     for (int nt = 0; nt < NT; ++nt)
 #pragma unroll
         for (int i = 0; i < 4; ++i) acc[nt][i] = 0.f;
-    // One super-block: refill the slot computed in the previous iteration
-    // (every lane is past it: __syncwarp at the end of the iteration), wait
-    // for this one's stage, load the next super-block's X fragments, compute.
-    // With two token tiles (NT = 2) a second fragment set would halve the
-    // resident CTAs (registers): there X is loaded at the start of its own
-    // super-block instead.
-    constexpr bool kAhead = NT == 1;
     uint32_t bmask[8 / TP];
 #pragma unroll
     for (uint32_t j = 0; j < 8 / TP; ++j) bmask[j] = g / TP == j ? 1u : 0u;
-    auto refill_and_wait = [&](uint32_t i) {
-        if (i + kGemvStages - 1 < count) {
-            const uint32_t j = i + kGemvStages - 1, kb = first + kWarps * j;
-            uint8_t *sj = mine + (j % kGemvStages) * stage_bytes;
-            issue_w<TYPE>(sj, pbase + (uint64_t)kb * chunk, r0, lane);
-            if (kStageX) issue_x1<TYPE>(sj, x, k, m_begin, kb, lane);
-        }
-        cpa_commit();
-        cpa_wait<kGemvStages - 1>();
-        __syncwarp();
-    };
-    if constexpr (kAhead) {
-        // One super-block per iteration: refill the slot computed in the
-        // previous iteration (every lane is past it: __syncwarp at the end of
-        // the iteration), wait for this one's stage, load the next
-        // super-block's X fragments (several tokens), compute.
-        using XF = XFrags<2 * TP, NT>;
-        auto iteration = [&](uint32_t i, XF &xs_cur, XF &xs_next) {
-            refill_and_wait(i);
-            if constexpr (TP > 1)
-                if (i + 1 < count)
-                    load_x<TYPE, TP, NT>(xs_next, x, k, m_begin, first + kWarps * (i + 1), m_count, g, t, 0);
-            compute_stage<TYPE, TP, NT>(mine + (i % kGemvStages) * stage_bytes, xs_cur, g, t, lane, bmask, wt, acc);
+    for (uint32_t i = 0; i < count; ++i) {
+        if constexpr (RW == 1) {
+            // The warp's own ring: refill the slot computed in the previous
+            // iteration (every lane is past it: __syncwarp below), then wait
+            // for stage i.
+            if (i + kStages - 1 < count) {
+                issue_w_stage(i + kStages - 1);
+                issue_x(i + kStages - 1);
+            }
+            cpa_commit();
+            cpa_wait<kStages - 1>();
             __syncwarp();
-        };
-        XF xa, xb;
-        if (TP > 1 && count) load_x<TYPE, TP, NT>(xa, x, k, m_begin, first, m_count, g, t, 0);
-        for (uint32_t i = 0; i < count; i += 2) {
-            iteration(i, xa, xb);
-            if (i + 1 < count) iteration(i + 1, xb, xa);
+        } else {
+            // The CTA's ring: stage i has landed for every thread, and every
+            // warp is past stage i - 1, whose slot is refilled.
+            cpa_wait<kStages - 2>();
+            __syncthreads();
+            if (i + kStages - 1 < count) {
+                issue_w_stage(i + kStages - 1);
+                issue_x(i + kStages - 1);
+            }
+            cpa_commit();
         }
-    } else {
-        // Two token tiles (8 tokens each): a second whole-super-block fragment
-        // set would cost resident CTAs (registers), so X runs half a
-        // super-block ahead instead -- half 1's fragments load while half 0
-        // computes, the next super-block's half 0 while half 1 computes.
-        using XF = XFrags<8, NT>;
-        XF xa, xb;
-        if (count) load_x<TYPE, TP, NT>(xa, x, k, m_begin, first, m_count, g, t, 0);
-        for (uint32_t i = 0; i < count; ++i) {
-            refill_and_wait(i);
-            const uint8_t *st = mine + (i % kGemvStages) * stage_bytes;
-            const uint32_t kb = first + kWarps * i;
-            load_x<TYPE, TP, NT>(xb, x, k, m_begin, kb, m_count, g, t, 8);
-            compute_stage<TYPE, TP, NT, 8, 0, 1, 0>(st, xa, g, t, lane, bmask, wt, acc);
-            if (i + 1 < count) load_x<TYPE, TP, NT>(xa, x, k, m_begin, kb + kWarps, m_count, g, t, 0);
-            compute_stage<TYPE, TP, NT, 8, 1, 2, 8>(st, xb, g, t, lane, bmask, wt, acc);
-            __syncwarp();
-        }
+        compute_stage<TYPE, TP, NT>(slot(i) + rw * SG::w_bytes, slot(i) + w_all, g, t, lane, bmask, wt, acc);
+        if constexpr (RW == 1) __syncwarp();
     }
-    // Columns of one token are spread over the quad (TP < 8): sum them so that
-    // every lane holds the full value of its (row, token) pairs.
-    if constexpr (TP == 1) {   // all 8 columns are token 0: fold the thread's two columns
+
+    // The warp's 16 x M result of the slice (rows g, g + 8 of its piece;
+    // token 8 nt + column, written by the lanes whose column < TP).
+    // Columns of one token are spread over the quad (TP < 8): sum them so
+    // that every lane holds the full value of its (row, token) pairs.
+    auto fold = [&](float (&v)[4 * NT]) {
 #pragma unroll
-        for (int nt = 0; nt < NT; ++nt) {
-            acc[nt][0] += acc[nt][1];
-            acc[nt][2] += acc[nt][3];
-            acc[nt][1] = acc[nt][0];
-            acc[nt][3] = acc[nt][2];
+        for (int nt = 0; nt < NT; ++nt)
+#pragma unroll
+            for (int i = 0; i < 4; ++i) v[4 * nt + i] = acc[nt][i];
+        if constexpr (TP == 1) {   // all 8 columns are token 0: fold the thread's two columns
+#pragma unroll
+            for (int nt = 0; nt < NT; ++nt) {
+                v[4 * nt] += v[4 * nt + 1];
+                v[4 * nt + 2] += v[4 * nt + 3];
+            }
         }
-    }
-    if constexpr (TP <= 2) {
+        if constexpr (TP <= 2) {
+#pragma unroll
+            for (int j = 0; j < 4 * NT; ++j) {
+                v[j] += __shfl_xor_sync(0xffffffffu, v[j], 1);
+                v[j] += __shfl_xor_sync(0xffffffffu, v[j], 2);
+            }
+        } else if constexpr (TP == 4) {
+#pragma unroll
+            for (int j = 0; j < 4 * NT; ++j) v[j] += __shfl_xor_sync(0xffffffffu, v[j], 2);
+        }
+    };
+    // Partial slot of (K slice, tile, row warp): 16 tokens x 16 rows of fp32.
+    auto partial_slot = [&](uint32_t slice) {
+        return partials + (((uint64_t)slice * gridDim.x + tile) * RW + rw) * 256;
+    };
+    auto publish = [&](const float (&v)[4 * NT]) {
+        float *dst = partial_slot(blockIdx.y);
 #pragma unroll
         for (int nt = 0; nt < NT; ++nt)
 #pragma unroll
             for (int i = 0; i < 4; ++i) {
-                acc[nt][i] += __shfl_xor_sync(0xffffffffu, acc[nt][i], 1);
-                acc[nt][i] += __shfl_xor_sync(0xffffffffu, acc[nt][i], 2);
+                const uint32_t col = 2 * t + (i & 1);
+                if (col < TP) __stcg(dst + (8 * nt + col) * 16 + g + 8 * (i >> 1), v[4 * nt + i]);
             }
-    } else if constexpr (TP == 4) {
+    };
+    // Arrival of this CTA at its tile after publishing its partial; true in
+    // the last CTA to arrive, with the tile's sum in v.  The barrier
+    // orders every thread's partial before thread 0's release (acquire-release
+    // arrival at GPU scope, cumulative over the barrier); in the CTA that
+    // arrives last, the acquire and the second barrier order the other
+    // participants' partials before its loads.
+    auto arrive = [&](float (&v)[4 * NT]) -> bool {
+        __syncthreads();
+        if (threadIdx.x == 0) last = (arrive_acq_rel(counters + tile) + 1 == n_slices) ? 1u : 0u;
+        __syncthreads();
+        if (!last) return false;
 #pragma unroll
-        for (int nt = 0; nt < NT; ++nt)
+        for (int j = 0; j < 4 * NT; ++j) v[j] = 0.f;
+        // slices in order (deterministic), four slices' loads in flight
+#pragma unroll 4
+        for (uint32_t q = 0; q < (kw == 0 ? n_slices : 0u); ++q) {
+            const float *src = partial_slot(q);
 #pragma unroll
-            for (int i = 0; i < 4; ++i) acc[nt][i] += __shfl_xor_sync(0xffffffffu, acc[nt][i], 2);
-    }
-
-    // Reduce the warps' fragments; then either store Y directly (one K slice)
-    // or publish the partial and let the tile's last CTA finish.
+            for (int nt = 0; nt < NT; ++nt)
 #pragma unroll
-    for (int nt = 0; nt < NT; ++nt)
-#pragma unroll
-        for (int i = 0; i < 4; ++i) red[warp][lane][4 * nt + i] = acc[nt][i];
-    __syncthreads();
-    __shared__ uint32_t last;
-    if (warp == 0) {
-        float v[4 * NT];
-#pragma unroll
-        for (int j = 0; j < 4 * NT; ++j) {
-            float sum = 0.f;
-#pragma unroll
-            for (int ww2 = 0; ww2 < kWarps; ++ww2) sum += red[ww2][lane][j];
-            v[j] = sum;
-        }
-        bool store = n_slices == 1;
-        if (n_slices > 1) {
-            // partials[slice][tile][lane][4*NT]
-            float *dst = partials + (((uint64_t)blockIdx.y * gridDim.x + blockIdx.x) * 32 + lane) * (4 * NT);
-#pragma unroll
-            for (int j = 0; j < 4 * NT; ++j) __stcg(dst + j, v[j]);
-            // The warp barrier orders every lane's partial stores before lane
-            // 0's arrival; the arrival is one acquire-release atomic: release
-            // publishes this slice's partial, acquire (for the last slice to
-            // arrive) makes the other slices' partials visible -- one round
-            // trip to L2 instead of fence + atomic + fence.
-            __syncwarp();
-            if (lane == 0) last = (arrive_acq_rel(counters + blockIdx.x) + 1 == n_slices) ? 1u : 0u;
-            __syncwarp();
-            if (last) {
-#pragma unroll
-                for (int j = 0; j < 4 * NT; ++j) v[j] = 0.f;
-                for (uint32_t sl = 0; sl < n_slices; ++sl) {
-                    const float *src = partials + (((uint64_t)sl * gridDim.x + blockIdx.x) * 32 + lane) * (4 * NT);
-#pragma unroll
-                    for (int j = 0; j < 4 * NT; ++j) v[j] += __ldcg(src + j);
+                for (int i = 0; i < 4; ++i) {
+                    const uint32_t col = 2 * t + (i & 1);
+                    if (col < TP) v[4 * nt + i] += __ldcg(src + (8 * nt + col) * 16 + g + 8 * (i >> 1));
                 }
-                if (lane == 0) counters[blockIdx.x] = 0u;
-                store = true;
-            }
         }
-        if (store && b.epi.flags) {
-            // Fused epilogue.  A thread holds rows g and g + 8 of the tile for
-            // the same token: for a SwiGLU weight the gate row and its up row.
+        if (threadIdx.x == 0) counters[tile] = 0u;
+        return true;
+    };
+    // Y (with the fused epilogue) of the warp's rows of the finished tile.
+    auto store_tile = [&](const float (&v)[4 * NT]) {
+        void *const y = w.y;
+        const uint64_t ldy = w.ldy;
+        if (b.epi.flags) {
+            // Fused epilogue.  A thread holds rows g and g + 8 of the piece
+            // for the same token: for a SwiGLU weight the gate row and its up
+            // row.
             const EpiView &e = b.epi;
             const bool glu = e.flags & TC_EPI_SWIGLU;
 #pragma unroll
@@ -602,7 +599,7 @@ __global__ void __launch_bounds__(kWarps * 32, 4) gemv_kernel(const __grid_const
                     }
                 }
             }
-        } else if (store) {
+        } else {
 #pragma unroll
             for (int nt = 0; nt < NT; ++nt) {
 #pragma unroll
@@ -619,16 +616,50 @@ __global__ void __launch_bounds__(kWarps * 32, 4) gemv_kernel(const __grid_const
                 }
             }
         }
-        if (store && b.epi.n_peer) __threadfence_system();   // publish peer-replica stores
+    };
+
+    float v[4 * NT];
+    fold(v);
+    if constexpr (KW > 1) {
+        // the K-split warps of the same rows meet in shared memory; warp 0
+        // adds them in warp order
+        __shared__ float red[KW][32][4 * NT];
+#pragma unroll
+        for (int j = 0; j < 4 * NT; ++j) red[kw][lane][j] = v[j];
+        __syncthreads();
+        if (kw == 0) {
+#pragma unroll
+            for (int j = 0; j < 4 * NT; ++j) {
+                float sum = red[0][lane][j];
+#pragma unroll
+                for (uint32_t q = 1; q < KW; ++q) sum += red[q][lane][j];
+                v[j] = sum;
+            }
+        }
     }
+    const bool owner = kw == 0;   // the warps that hold the rows' sums
+    if (n_slices == 1) {
+        if (owner) store_tile(v);
+    } else {
+        if (owner) publish(v);
+        if (arrive(v) && owner) store_tile(v);
+    }
+    if (b.epi.n_peer) __threadfence_system();   // publish peer-replica stores
 }
 
 template <int TYPE, int TP, int NT>
-cudaError_t launch_typed(const GemvBatch &bt, uint32_t tiles, uint32_t m_begin, uint32_t mc, const uint16_t *x,
-                         uint64_t k, int out_dtype, const GemvSplit &sp, cudaStream_t s) {
-    const dim3 grid(tiles, sp.n_slices);
-    const size_t stage = (StageGeo<TYPE>::w_bytes + (TP == 1 ? 512u : 0u) + 127) / 128 * 128;
-    const size_t smem = stage * gemv_stages<NT>() * kWarps;
+cudaError_t launch_typed(const GemvBatch &bt_in, uint32_t m_begin, uint32_t mc, const uint16_t *x, uint64_t k,
+                         int out_dtype, const GemvSplit &sp, cudaStream_t s) {
+    constexpr uint32_t RW = gemv_row_warps<TP>();
+    const size_t smem = gemv_smem_bytes<TYPE, TP, NT>();
+    // tiles of 16 RW rows, numbered across the entries
+    GemvBatch bt = bt_in;
+    uint32_t tiles = 0;
+    for (uint32_t i = 0; i < bt.n_entries; ++i) {
+        bt.e[i].tile_begin = tiles;
+        tiles += (bt.e[i].n + 16 * RW - 1) / (16 * RW);
+    }
+    if (!tiles) return cudaSuccess;
     auto kern = out_dtype == 0 ? gemv_kernel<TYPE, TP, NT, 0>
                 : out_dtype == 1 ? gemv_kernel<TYPE, TP, NT, 1> : gemv_kernel<TYPE, TP, NT, 2>;
     // Opt in once per instantiation and device to its shared-memory size.
@@ -638,8 +669,10 @@ cudaError_t launch_typed(const GemvBatch &bt, uint32_t tiles, uint32_t m_begin, 
         return cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
     });
     if (e != cudaSuccess) return e;
+    const GemvSplit plan = gemv_split_tiles(tiles, bt.kb, RW);
+    if (plan.n_slices > 1 && (!sp.partials || !sp.counters)) return cudaErrorInvalidValue;
     cudaLaunchConfig_t cfg = {};
-    cfg.gridDim = grid;
+    cfg.gridDim = dim3(tiles, plan.n_slices);
     cfg.blockDim = dim3(kWarps * 32);
     cfg.dynamicSmemBytes = smem;
     cfg.stream = s;
@@ -648,59 +681,54 @@ cudaError_t launch_typed(const GemvBatch &bt, uint32_t tiles, uint32_t m_begin, 
     attr[0].val.programmaticStreamSerializationAllowed = 1;
     cfg.attrs = attr;
     cfg.numAttrs = 1;
-    return cudaLaunchKernelEx(&cfg, kern, bt, x, m_begin, mc, k, sp.kb_per_slice, sp.partials, sp.counters,
+    return cudaLaunchKernelEx(&cfg, kern, bt, x, m_begin, mc, k, plan.kb_per_slice, sp.partials, sp.counters,
                               sp.status);
 }
 
 template <int TYPE>
-cudaError_t launch_m(const GemvBatch &bt, uint32_t tiles, uint32_t m_begin, uint32_t m, const uint16_t *x,
-                     uint64_t k, int out_dtype, const GemvSplit &sp, cudaStream_t s) {
-    if (m <= 1) return launch_typed<TYPE, 1, 1>(bt, tiles, m_begin, m, x, k, out_dtype, sp, s);
-    if (m <= 2) return launch_typed<TYPE, 2, 1>(bt, tiles, m_begin, m, x, k, out_dtype, sp, s);
-    if (m <= 4) return launch_typed<TYPE, 4, 1>(bt, tiles, m_begin, m, x, k, out_dtype, sp, s);
-    if (m <= 8) return launch_typed<TYPE, 8, 1>(bt, tiles, m_begin, m, x, k, out_dtype, sp, s);
-    return launch_typed<TYPE, 8, 2>(bt, tiles, m_begin, m, x, k, out_dtype, sp, s);
+cudaError_t launch_m(const GemvBatch &bt, uint32_t m_begin, uint32_t m, const uint16_t *x, uint64_t k,
+                     int out_dtype, const GemvSplit &sp, cudaStream_t s) {
+    if (m <= 1) return launch_typed<TYPE, 1, 1>(bt, m_begin, m, x, k, out_dtype, sp, s);
+    if (m <= 2) return launch_typed<TYPE, 2, 1>(bt, m_begin, m, x, k, out_dtype, sp, s);
+    if (m <= 4) return launch_typed<TYPE, 4, 1>(bt, m_begin, m, x, k, out_dtype, sp, s);
+    if (m <= 8) return launch_typed<TYPE, 8, 1>(bt, m_begin, m, x, k, out_dtype, sp, s);
+    return launch_typed<TYPE, 8, 2>(bt, m_begin, m, x, k, out_dtype, sp, s);
 }
 
 }  // namespace
 
-GemvSplit gemv_split_tiles(uint32_t tiles, uint32_t kb) {
-    // Enough CTAs for about three per SM, with as few K slices as that allows
-    // (each slice costs a partial store and a share of the fixup): a single
-    // weight of a few hundred row tiles splits K three ways, a batch of
-    // thousands of tiles runs whole rows per CTA.  Slices hold a multiple of
-    // the 4 warps' super-blocks.
-    const uint32_t want = 148u * 3u;
+GemvSplit gemv_split_tiles(uint32_t tiles, uint32_t kb, uint32_t row_warps) {
+    // Enough CTAs to fill the resident slots of every SM -- three per SM
+    // with the in-CTA K split of one token, four otherwise -- with as few K
+    // slices as that allows (each slice costs a partial store and a share of
+    // the fixup).  A slice keeps at least two super-blocks per warp, so that
+    // the stage ring has something to overlap; with the in-CTA split its
+    // super-blocks are a multiple of the four warps.  slices x tiles <
+    // 2 kGemvMaxCtas, so the partials fit kGemvPartialFloats.
+    const uint32_t kw = kWarps / row_warps;
+    const uint32_t want = row_warps == 1 ? 148u * 3u : kGemvMaxCtas;
     uint32_t slices = tiles >= want ? 1u : (want + tiles - 1) / tiles;
-    slices = max(1u, min(slices, (kb + kWarps - 1) / kWarps));
+    slices = std::max(1u, std::min(slices, kb / (2 * kw)));
     uint32_t per = (kb + slices - 1) / slices;
-    per = (per + kWarps - 1) / kWarps * kWarps;
+    per = (per + kw - 1) / kw * kw;
     GemvSplit sp;
     sp.kb_per_slice = per;
     sp.n_slices = (kb + per - 1) / per;
     return sp;
 }
-GemvSplit gemv_split(const WeightView &w) { return gemv_split_tiles((w.n + 15) / 16, w.kb); }
 
-size_t gemv_workspace_floats_tiles(uint32_t tiles, uint32_t kb) {
-    const GemvSplit sp = gemv_split_tiles(tiles, kb);
-    return sp.n_slices > 1 ? (size_t)sp.n_slices * tiles * 32 * 8 : 0;
-}
-size_t gemv_workspace_floats(const WeightView &w) { return gemv_workspace_floats_tiles((w.n + 15) / 16, w.kb); }
-
-cudaError_t launch_gemv_batch(const GemvBatch &bt_in, uint32_t type, uint32_t tiles, uint32_t m_begin, uint32_t m,
-                              const uint16_t *x, uint64_t k, int out_dtype, const GemvSplit &sp, cudaStream_t s,
-                              const EpiView *epi, uint32_t gate_row) {
-    if (!m || !tiles) return cudaSuccess;
+cudaError_t launch_gemv_batch(const GemvBatch &bt_in, uint32_t type, uint32_t m_begin, uint32_t m, const uint16_t *x,
+                              uint64_t k, int out_dtype, const GemvSplit &sp, cudaStream_t s, const EpiView *epi,
+                              uint32_t gate_row) {
+    if (!m) return cudaSuccess;
     if (out_dtype < 0 || out_dtype > 2) return cudaErrorInvalidValue;
     GemvBatch bt = bt_in;
     bt.epi = epi ? *epi : EpiView{};
     bt.gate_row = gate_row;
-    if (m > 16 || bt.n_entries == 0 || bt.n_entries > kMaxGemvBatch) return cudaErrorInvalidValue;
-    if (sp.n_slices > 1 && (!sp.partials || !sp.counters)) return cudaErrorInvalidValue;
-    if (type == 12) return launch_m<12>(bt, tiles, m_begin, m, x, k, out_dtype, sp, s);
-    if (type == 13) return launch_m<13>(bt, tiles, m_begin, m, x, k, out_dtype, sp, s);
-    return launch_m<14>(bt, tiles, m_begin, m, x, k, out_dtype, sp, s);
+    if (m > 16 || bt.n_entries == 0 || bt.n_entries > kMaxGemvBatch || !bt.kb) return cudaErrorInvalidValue;
+    if (type == 12) return launch_m<12>(bt, m_begin, m, x, k, out_dtype, sp, s);
+    if (type == 13) return launch_m<13>(bt, m_begin, m, x, k, out_dtype, sp, s);
+    return launch_m<14>(bt, m_begin, m, x, k, out_dtype, sp, s);
 }
 
 cudaError_t launch_gemv(const SegmentView &seg, const uint16_t *x, uint64_t k, void *y, uint64_t ldy,
@@ -710,8 +738,8 @@ cudaError_t launch_gemv(const SegmentView &seg, const uint16_t *x, uint64_t k, v
     bt.n_entries = 1;
     bt.kb = seg.w.kb;
     bt.e[0] = {seg.w.chunks, y, ldy, seg.w.n, 0u};
-    return launch_gemv_batch(bt, seg.w.type, (seg.w.n + 15) / 16, seg.m_begin, seg.m_end - seg.m_begin, x, k,
-                             out_dtype, sp, s, epi, seg.gate_row);
+    return launch_gemv_batch(bt, seg.w.type, seg.m_begin, seg.m_end - seg.m_begin, x, k, out_dtype, sp, s, epi,
+                             seg.gate_row);
 }
 
 }  // namespace tc

@@ -487,25 +487,22 @@ int tc_cuda_qlinear_batched(tc_cuda_ctx *ctx, const tc_cuda_weight *const *weigh
     // One launch per weight type (the kernel is specialised on it).
     for (const uint32_t type : {uint32_t(TC_GGML_Q4_K), uint32_t(TC_GGML_Q5_K), uint32_t(TC_GGML_Q6_K)}) {
         tc::GemvBatch bt{};
-        uint32_t tiles = 0;
+        uint32_t counters = 0;
         for (uint32_t i = 0; i < n_weights; ++i) {
             const tc_cuda_weight *w = weights[i];
             if (w->type != type) continue;
-            bt.e[bt.n_entries++] = {w->chunks, ys[i], ldys && ldys[i] ? ldys[i] : w->n, (uint32_t)w->n, tiles};
-            tiles += (uint32_t)((w->n + 15) / 16);
+            bt.e[bt.n_entries++] = {w->chunks, ys[i], ldys && ldys[i] ? ldys[i] : w->n, (uint32_t)w->n, 0u};
+            counters += tc::gemv_counters(w->n);
         }
         if (!bt.n_entries) continue;
         bt.kb = (uint32_t)(k / 256);
-        tc::GemvSplit sp = tc::gemv_split_tiles(tiles, bt.kb);
+        tc::GemvSplit sp;
         sp.status = ctx->status;
-        if (sp.n_slices > 1) {
-            int rc = ensure_gemv_workspace(ctx, tc::gemv_workspace_floats_tiles(tiles, bt.kb), tiles);
-            if (rc) return rc;
-            sp.partials = ctx->gemv_partials;
-            sp.counters = ctx->gemv_counters;
-        }
-        cudaError_t e = tc::launch_gemv_batch(bt, type, tiles, 0, m, static_cast<const uint16_t *>(x), k, out_dtype,
-                                              sp, s);
+        int rc = ensure_gemv_workspace(ctx, tc::kGemvPartialFloats, counters);
+        if (rc) return rc;
+        sp.partials = ctx->gemv_partials;
+        sp.counters = ctx->gemv_counters;
+        cudaError_t e = tc::launch_gemv_batch(bt, type, 0, m, static_cast<const uint16_t *>(x), k, out_dtype, sp, s);
         if (e != cudaSuccess) return cuda_fail("batched GEMV launch", e);
     }
     return ok();
@@ -695,14 +692,12 @@ int tc_cuda_qlinear_gather(tc_cuda_ctx *ctx, const tc_cuda_weight *const *weight
         }
     }
     for (const auto &sv : gemv) {
-        tc::GemvSplit sp = tc::gemv_split(sv.w);
+        tc::GemvSplit sp;
         sp.status = ctx->status;
-        if (sp.n_slices > 1) {
-            int rc = ensure_gemv_workspace(ctx, tc::gemv_workspace_floats(sv.w), (sv.w.n + 15) / 16);
-            if (rc) return rc;
-            sp.partials = ctx->gemv_partials;
-            sp.counters = ctx->gemv_counters;
-        }
+        int rc = ensure_gemv_workspace(ctx, tc::kGemvPartialFloats, tc::gemv_counters(sv.w.n));
+        if (rc) return rc;
+        sp.partials = ctx->gemv_partials;
+        sp.counters = ctx->gemv_counters;
         cudaError_t e = tc::launch_gemv(sv, static_cast<const uint16_t *>(x), k, y, ldy, out_dtype, sp, s, &epi);
         if (e != cudaSuccess) return cuda_fail("GEMV launch", e);
     }

@@ -157,26 +157,28 @@ cudaError_t launch_decode_raw(uint32_t type, const uint8_t *src, uint64_t row_by
                               uint64_t columns, int dtype, uint8_t *dst, uint64_t row_stride,
                               uint64_t column_stride, uint32_t *status, cudaStream_t s,
                               const uint64_t *gather = nullptr, uint64_t source_rows = 0, uint64_t dst_bytes = 0);
-// Small-M GEMV K split: n_slices CTAs per 16-row tile.  With n_slices > 1
-// the kernel needs `partials` (gemv_workspace_floats floats) and one zeroed
-// uint32 counter per 16-row tile; both are left as found (counters back to 0).
+// Small-M GEMV: a CTA covers a tile of 16 or 64 weight rows (one or four
+// row warps) and one K slice; n_slices CTAs per tile.  With n_slices > 1 the
+// kernel needs `partials` (at most kGemvPartialFloats floats) and one zeroed
+// uint32 counter per tile (at most gemv_counters(n) per weight); both are
+// left as found (counters back to 0).
+constexpr uint32_t kGemvMaxCtas = 148u * 4u;   // a K split aims at four CTAs per SM
+constexpr size_t kGemvPartialFloats = (size_t)kGemvMaxCtas * 2 * 4 * 256;   // slice x tile < 2 kGemvMaxCtas, 4 warps x 16 x 16
+inline uint32_t gemv_counters(uint64_t n) { return (uint32_t)((n + 15) / 16); }
 struct GemvSplit {
     uint32_t kb_per_slice = 0, n_slices = 1;
     float *partials = nullptr;
     uint32_t *counters = nullptr;
     uint32_t *status = nullptr;
 };
-GemvSplit gemv_split(const WeightView &w);
-size_t gemv_workspace_floats(const WeightView &w);
-GemvSplit gemv_split_tiles(uint32_t tiles, uint32_t kb);
-size_t gemv_workspace_floats_tiles(uint32_t tiles, uint32_t kb);
+GemvSplit gemv_split_tiles(uint32_t tiles, uint32_t kb, uint32_t row_warps);
 // Several weights with the same K, type and X in one GEMV launch.
 constexpr uint32_t kMaxGemvBatch = 64;
 struct GemvEntry {
     const uint8_t *chunks;
     void *y;
     uint64_t ldy;
-    uint32_t n, tile_begin;   // rows; first 16-row tile of this weight in the launch
+    uint32_t n, tile_begin;   // rows; first tile of this weight in the launch (set by the launcher)
 };
 struct GemvBatch {
     uint32_t n_entries, kb;
@@ -186,8 +188,8 @@ struct GemvBatch {
 };
 // out_dtype: TC_DTYPE_F32 / F16 / BF16.  epi (optional) applies to every
 // entry, with gate row `gate_row`.
-cudaError_t launch_gemv_batch(const GemvBatch &bt, uint32_t type, uint32_t tiles, uint32_t m_begin, uint32_t m,
-                              const uint16_t *x, uint64_t k, int out_dtype, const GemvSplit &sp, cudaStream_t s,
+cudaError_t launch_gemv_batch(const GemvBatch &bt, uint32_t type, uint32_t m_begin, uint32_t m, const uint16_t *x,
+                              uint64_t k, int out_dtype, const GemvSplit &sp, cudaStream_t s,
                               const EpiView *epi = nullptr, uint32_t gate_row = 0);
 cudaError_t launch_gemv(const SegmentView &seg, const uint16_t *x, uint64_t k, void *y,
                         uint64_t ldy, int out_dtype, const GemvSplit &split, cudaStream_t s,

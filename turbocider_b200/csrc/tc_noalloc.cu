@@ -31,7 +31,8 @@
 //   * calls whose kernels may overlap on the GPU (different streams, or
 //     different host threads) race on the array -- serialise them;
 //   * sizes whose scratch exceeds kScratchBytes are rejected with an error
-//     (a guard: the GEMV's K-split rule keeps every shape under ~0.9 MiB).
+//     (a guard: the GEMV needs 4.6 MiB of partials and 4 bytes per 16 weight
+//     rows, so only weights of over 12 million rows are refused).
 // Nothing here calls cudaMalloc, cudaFree or any allocating library routine.
 #include <mutex>
 #include <string>
@@ -42,7 +43,7 @@
 
 namespace {
 
-constexpr size_t kScratchBytes = size_t(4) << 20;   // 4 MiB per device
+constexpr size_t kScratchBytes = size_t(8) << 20;   // 8 MiB per device
 constexpr size_t kStatusBytes = 256;                // status word, padded
 
 static __device__ __align__(256) unsigned char g_gemv_scratch[kScratchBytes];
@@ -93,10 +94,10 @@ extern "C" int tc_cuda_qlinear_small_static(const tc_cuda_weight *weight, const 
     if (ldy < weight->n) return fail("invalid/overlapping row stride");
 
     const tc::WeightView view{weight->chunks, weight->type, weight->kb, weight->panels, (uint32_t)weight->n};
-    tc::GemvSplit sp = tc::gemv_split(view);
-    const size_t tiles = (weight->n + 15) / 16;
+    tc::GemvSplit sp;
+    const size_t tiles = tc::gemv_counters(weight->n);
     const size_t counter_bytes = (tiles * sizeof(uint32_t) + 255) / 256 * 256;
-    const size_t partial_bytes = tc::gemv_workspace_floats(view) * sizeof(float);
+    const size_t partial_bytes = tc::kGemvPartialFloats * sizeof(float);
     const size_t need = kStatusBytes + counter_bytes + partial_bytes;
     if (need > kScratchBytes)
         return fail("weight needs " + std::to_string(need) + " bytes of GEMV scratch; the static scratch holds " +
