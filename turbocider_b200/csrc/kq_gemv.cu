@@ -6,8 +6,10 @@
 //
 //   * each K16 step of mma.sync.m16n8k16 (bf16 in, fp32 accumulate) takes the
 //     raw 4-/6-bit codes of 16 weight rows as bf16 -- exact: a prmt places
-//     each code byte under the exponent of 128 (0x43cc = 128 + c) and one
-//     bf16x2 subtract removes the 128 (and Q6_K's bias 32);
+//     each code byte under the exponent of 128 (0x43cc = 128 + c); the 128
+//     leaves through sum_k x_k of the group (one more MMA with an all-ones A
+//     on the same B fragment), or, for Q6_K, a bf16x2 subtract makes A =
+//     q - 32 exactly (the per-shape choice is q6_centred below);
 //   * the K16 step never crosses a scale group (Q6_K: 16 weights, Q4_K: 32
 //     weights = two chained steps), so the fp32 fragment holds
 //     sum_k x_k * q_k of one group, scaled afterwards by d*sc in fp32;
@@ -47,6 +49,16 @@ namespace tc {
 namespace {
 
 constexpr int kWarps = 4;
+// Row pitch (floats) of a warp's scale table [16 rows][16]: 20, so that the
+// eight row pairs a warp reads at once (rows g, g + 8) fall in distinct banks
+// (with 16 every second row shares a bank: four-way conflicts).
+constexpr uint32_t kTabPitch = 20;
+// Q6_K codes as q - 32 (an exact bf16 subtract per pair) or as 128 + q with
+// the offset removed per group through an extra all-ones MMA per step.
+// Measured on config 2 (us per call, M = 1 / 8 / 16): centred 9.33 / 12.46 /
+// 13.95, offset 9.68 / 11.02 / 15.12 -- the offset form only for one tile of
+// 8 tokens.
+template <int TP, int NT> constexpr bool q6_centred() { return !(TP == 8 && NT == 1); }
 
 // Two code bytes (selector 0x4140: bytes 0,1; 0x4342: bytes 2,3) as the bf16
 // pair (128 + c0, 128 + c1): each byte lands under the exponent of 128.
@@ -239,7 +251,7 @@ __device__ __forceinline__ void compute_stage(const uint8_t *st, const uint8_t *
         float scf[4], mnf[4];
         bytes_to_float4(scw, scf);
         bytes_to_float4(mnw, mnf);
-        float4 *o = reinterpret_cast<float4 *>(wt + rr * 16 + half * 8);
+        float4 *o = reinterpret_cast<float4 *>(wt + rr * kTabPitch + half * 8);
         o[0] = make_float4(d * scf[0], dmin * mnf[0], d * scf[1], dmin * mnf[1]);
         o[1] = make_float4(d * scf[2], dmin * mnf[2], d * scf[3], dmin * mnf[3]);
     } else {
@@ -248,7 +260,7 @@ __device__ __forceinline__ void compute_stage(const uint8_t *st, const uint8_t *
         float a[4], b[4];
         bytes_to_float4(sw.x ^ 0x80808080u, a);   // int8 + 128 as unsigned bytes
         bytes_to_float4(sw.y ^ 0x80808080u, b);
-        float4 *o = reinterpret_cast<float4 *>(wt + rr * 16 + half * 8);
+        float4 *o = reinterpret_cast<float4 *>(wt + rr * kTabPitch + half * 8);
         o[0] = make_float4(d * (a[0] - 128.f), d * (a[1] - 128.f), d * (a[2] - 128.f), d * (a[3] - 128.f));
         o[1] = make_float4(d * (b[0] - 128.f), d * (b[1] - 128.f), d * (b[2] - 128.f), d * (b[3] - 128.f));
     }
@@ -260,7 +272,13 @@ __device__ __forceinline__ void compute_stage(const uint8_t *st, const uint8_t *
 #pragma unroll
     for (int nt = 0; nt < NT; ++nt) xrow[nt] = xs + (8 * nt + g % TP) * XGeo<TP, NT>::pitch;
     const uint32_t ones = 0x3F803F80u;
-    constexpr float off = 128.f;   // Q4_K: the code-space offset of code_pair
+    constexpr float off = 128.f;    // Q4_K: the code-space offset of code_pair
+    constexpr float off6 = 160.f;   // Q6_K: that offset plus the code bias 32
+    // A = 128 + code (one prmt per pair), the offset removed per group
+    // through sum_k x_k from an all-ones MMA; or, for Q6_K where
+    // q6_centred, A = code - 32 exactly (a bf16x2 subtract per pair, no
+    // second MMA).
+    constexpr bool kOffsetA = TYPE != 14 || !q6_centred<TP, NT>();
     float cq[NT][4], c1[NT][4];
 
     // One K16 step of scale group visit v: A from code words (rows g, g+8).
@@ -274,7 +292,7 @@ __device__ __forceinline__ void compute_stage(const uint8_t *st, const uint8_t *
                 for (int i = 0; i < 4; ++i) cq[nt][i] = c1[nt][i] = 0.f;
         }
         uint32_t a0, a1, a2, a3;
-        if constexpr (TYPE != 14) {
+        if constexpr (kOffsetA) {
             a0 = code_pair(cg, 0x4140u); a1 = code_pair(cg8, 0x4140u);
             a2 = code_pair(cg, 0x4342u); a3 = code_pair(cg8, 0x4342u);
         } else {
@@ -286,7 +304,7 @@ __device__ __forceinline__ void compute_stage(const uint8_t *st, const uint8_t *
             const uint2 xv = lds64(xrow[nt] + 2 * own_col<TYPE, TP>(c, my_j, t));
             const uint32_t b0 = xv.x * bmask[j], b1 = xv.y * bmask[j];
             mma16816(cq[nt], a0, a1, a2, a3, b0, b1, cq[nt]);
-            if constexpr (TYPE != 14) mma16816(c1[nt], ones, ones, ones, ones, b0, b1, c1[nt]);
+            if constexpr (kOffsetA) mma16816(c1[nt], ones, ones, ones, ones, b0, b1, c1[nt]);
         }
     };
     // Scale the finished chain `chain` into the accumulators.
@@ -295,8 +313,8 @@ __device__ __forceinline__ void compute_stage(const uint8_t *st, const uint8_t *
         for (uint32_t ci = 0; ci < 2; ++ci) {
             const uint32_t G = group_of_visit<TYPE>(chain * S + (2 * t + ci) / TP);
             if constexpr (TYPE != 14) {
-                const float2 a = reinterpret_cast<const float2 *>(wt)[g * 8 + G];
-                const float2 b = reinterpret_cast<const float2 *>(wt)[(g + 8) * 8 + G];
+                const float2 a = reinterpret_cast<const float2 *>(wt + g * kTabPitch)[G];
+                const float2 b = reinterpret_cast<const float2 *>(wt + (g + 8) * kTabPitch)[G];
 #pragma unroll
                 for (int nt = 0; nt < NT; ++nt) {
                     acc[nt][ci] = fmaf(a.x, fmaf(-off, c1[nt][ci], cq[nt][ci]), fmaf(-a.y, c1[nt][ci], acc[nt][ci]));
@@ -304,11 +322,16 @@ __device__ __forceinline__ void compute_stage(const uint8_t *st, const uint8_t *
                                            fmaf(-b.y, c1[nt][2 + ci], acc[nt][2 + ci]));
                 }
             } else {
-                const float a = wt[g * 16 + G], b = wt[(g + 8) * 16 + G];
+                const float a = wt[g * kTabPitch + G], b = wt[(g + 8) * kTabPitch + G];
 #pragma unroll
                 for (int nt = 0; nt < NT; ++nt) {
-                    acc[nt][ci] = fmaf(a, cq[nt][ci], acc[nt][ci]);
-                    acc[nt][2 + ci] = fmaf(b, cq[nt][2 + ci], acc[nt][2 + ci]);
+                    if constexpr (kOffsetA) {   // sum x (128 + q) - 160 sum x = sum x (q - 32)
+                        acc[nt][ci] = fmaf(a, fmaf(-off6, c1[nt][ci], cq[nt][ci]), acc[nt][ci]);
+                        acc[nt][2 + ci] = fmaf(b, fmaf(-off6, c1[nt][2 + ci], cq[nt][2 + ci]), acc[nt][2 + ci]);
+                    } else {
+                        acc[nt][ci] = fmaf(a, cq[nt][ci], acc[nt][ci]);
+                        acc[nt][2 + ci] = fmaf(b, cq[nt][2 + ci], acc[nt][2 + ci]);
+                    }
                 }
             }
         }
@@ -379,10 +402,11 @@ __device__ __forceinline__ void compute_stage(const uint8_t *st, const uint8_t *
 //     stage ring for the CTA holds the four W pieces and the super-block's X
 //     for every token, copied once and read by all four warps.
 template <int TP> constexpr uint32_t gemv_row_warps() { return TP == 1 ? 1u : 4u; }
-// Depth of the stage rings: 3 stages, except with two token tiles (M > 8),
-// where 2 stages leave room for four resident CTAs.
-template <int NT>
-constexpr uint32_t gemv_stages() { return NT == 2 ? 2u : 3u; }
+// Depth of the stage rings: 3 stages, except with 8 tokens per tile (M > 4),
+// where the stage's X (8 or 16 rows) leaves room for four resident CTAs only
+// with 2 (measured at M = 8: 3 stages, three CTAs per SM, 15.3 us per call).
+template <int TP>
+constexpr uint32_t gemv_stages() { return TP == 8 ? 2u : 3u; }
 // Bytes of one stage: per warp (RW = 1) or per CTA (RW = 4).
 template <int TYPE, int TP, int NT>
 constexpr uint32_t gemv_stage_bytes() {
@@ -390,7 +414,7 @@ constexpr uint32_t gemv_stage_bytes() {
 }
 template <int TYPE, int TP, int NT>
 constexpr uint32_t gemv_smem_bytes() {
-    return gemv_stage_bytes<TYPE, TP, NT>() * gemv_stages<NT>() * (kWarps / gemv_row_warps<TP>());
+    return gemv_stage_bytes<TYPE, TP, NT>() * gemv_stages<TP>() * (kWarps / gemv_row_warps<TP>());
 }
 
 // Weights of one launch: blockIdx.x runs over the 16 RW-row tiles of all of
@@ -407,10 +431,10 @@ __global__ void __launch_bounds__(kWarps * 32, 4) gemv_kernel(const __grid_const
     using XG = XGeo<TP, NT>;
     constexpr uint32_t chunk = chunk_bytes(TYPE);
     constexpr uint32_t RW = gemv_row_warps<TP>(), KW = kWarps / RW;
-    constexpr uint32_t kStages = gemv_stages<NT>(), stage_bytes = gemv_stage_bytes<TYPE, TP, NT>();
+    constexpr uint32_t kStages = gemv_stages<TP>(), stage_bytes = gemv_stage_bytes<TYPE, TP, NT>();
     constexpr uint32_t w_all = RW * SG::w_bytes;   // X follows the stage's W pieces
     extern __shared__ __align__(128) uint8_t dyn[];
-    __shared__ __align__(16) float tab[kWarps][16 * 16];
+    __shared__ __align__(16) float tab[kWarps][16 * kTabPitch];
     __shared__ uint32_t last;
     const uint32_t warp = threadIdx.x >> 5, lane = threadIdx.x & 31, g = lane >> 2, t = lane & 3;
     const uint32_t rw = warp % RW, kw = warp / RW;
