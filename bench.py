@@ -639,6 +639,15 @@ def config3_measure(ctx, device, tc_sustained):
 
 
 # ---------------------------------------------------------------- multi-GPU
+def push_engine(args) -> str:
+    """How --gather copy moves each output shard to the peers (for the JSON line)."""
+    if args.push_kernel:
+        return f"a peer-push kernel ({args.push_kernel} blocks of SM stores over NVLink, on a side stream"
+    if args.push_streams >= 2:
+        return f"copy-engine peer pushes (over {args.push_streams} side streams"
+    return "copy-engine peer pushes (back to back on a side stream"
+
+
 def gather_measure(ctx, device, world, rank, m, width):
     """The all-gather alone (no GEMM running): one rank's shard of `m` rows x
     `width` fp16 columns goes to every other rank, by copy-engine pushes back
@@ -681,6 +690,12 @@ def gather_measure(ctx, device, world, rank, m, width):
         out["push_serial" if streams == 1 else f"push_{streams}_streams"] = {
             "ms": round(t * 1e3, 3), "gbs_in_per_gpu": round((world - 1) * shard / t / 1e9, 1)}
     ctx.set_push_fanout(0)
+    for ctas in (37, 74, 148, 296):
+        ctx.set_push_kernel(ctas)
+        t = timed(push)
+        out[f"push_kernel_{ctas}_blocks"] = {
+            "ms": round(t * 1e3, 3), "gbs_in_per_gpu": round((world - 1) * shard / t / 1e9, 1)}
+    ctx.set_push_kernel(0)
     src = torch.zeros(m, width, device=device, dtype=torch.float16)
     dst = torch.empty(world * m, width, device=device, dtype=torch.float16)
 
@@ -848,6 +863,7 @@ def run_ours(args):
         from turbocider_b200.peer import PeerGroup
         pg = PeerGroup(ctx, timeout_us=20_000_000)
         ctx.set_push_fanout(args.push_streams)
+        ctx.set_push_kernel(args.push_kernel)
         y_sym = {(name, b): pg.alloc(world * m * nloc[name] * 2) for name in names for b in (0, 1)}
         y_all = {key: buf.tensor((world, m, nloc[key[0]]), f16) for key, buf in y_sym.items()}
         y_loc = {key: y_all[key][rank][:, :weights[0][key[0]].n_out] for key in y_all}
@@ -1017,6 +1033,7 @@ def run_ours(args):
     if world > 1 and not args.no_extras:
         gather = gather_measure(ctx, device, world, rank, m, nloc["w13"])
         ctx.set_push_fanout(args.push_streams)
+        ctx.set_push_kernel(args.push_kernel)
 
     extras = {}
     cpu = None
@@ -1052,9 +1069,7 @@ def run_ours(args):
         parallelism = ("single GPU" if world == 1 else
                        f"N-shard x{world}, all-gather fused into the GEMM epilogue (NVLink peer stores) + device "
                        f"flag barrier per linear" if fused else
-                       f"N-shard x{world}, all-gather by copy-engine peer pushes ("
-                       + ("back to back on a side stream" if args.push_streams < 2 else
-                          f"over {args.push_streams} side streams")
+                       f"N-shard x{world}, all-gather by " + push_engine(args)
                        + ", shard-major Y) beside the next GEMM + device flag barrier per layer" if ce else
                        f"N-shard x{world} + NCCL all-gather" + (f" ({reserve} SMs left to it)" if reserve else ""))
         cfg = workload_config(layers)
@@ -1122,6 +1137,9 @@ def main():
     ap.add_argument("--push-streams", type=int, default=0,
                     help="--gather copy: spread each output's peer copies over this many side streams "
                          "(0 / 1: back to back, the default)")
+    ap.add_argument("--push-kernel", type=int, default=0,
+                    help="--gather copy: push each output with a kernel of this many 128-thread blocks (SM stores "
+                         "over NVLink) instead of the copy engines (0, the default)")
     ap.add_argument("--reserve-sms", type=int, default=None,
                     help="SMs kept free of the GEMM for the all-gather (default 0: measured no gain at N=2)")
     args = ap.parse_args()

@@ -309,6 +309,13 @@ int tc_cuda_peer_push(tc_cuda_ctx *ctx, const void *src, void *const *dst, uint3
  * concurrent copies contend (369 GB/s received per GPU against 535 GB/s back
  * to back). */
 int tc_cuda_set_push_fanout(tc_cuda_ctx *ctx, int streams);
+/* ctas > 0: tc_cuda_peer_push moves the bytes with a kernel of `ctas`
+ * 128-thread blocks on `stream` (each 16-byte vector read once, stored to
+ * every destination by the SMs over NVLink; small blocks that fit beside a
+ * resident GEMM CTA) whenever every address, the width and the pitches are
+ * multiples of 16 bytes; otherwise, and with 0 (the default), by the copy
+ * engines. */
+int tc_cuda_set_push_kernel(tc_cuda_ctx *ctx, int ctas);
 
 /* Batched small-M linear: Y_i[m, N_i] = X[m, K] * W_i^T for n_weights
  * (1..64) weights that share K and X (e.g. every block's AdaLN modulation

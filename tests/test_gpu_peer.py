@@ -113,12 +113,15 @@ def test_dense_weight_replicas(ctx):
     assert torch.equal(ys[0], ys[1]) and not ys[0][:, :n].any()
 
 
-@pytest.mark.parametrize("fanout", [0, 2])
+@pytest.mark.parametrize("engine", [("copy", 0), ("copy", 2), ("kernel", 3), ("kernel", 148)],
+                         ids=["copy", "copy-fanout2", "kernel-3", "kernel-148"])
 @pytest.mark.parametrize("layout", ["shard_major", "strided"])
-def test_copy_engine_push_fills_every_replica(ctx, layout, fanout):
+def test_copy_engine_push_fills_every_replica(ctx, layout, engine):
     """tc_cuda_peer_push: this rank's shard of a GEMM output reaches the same
     place in every replica (linear copies for a shard-major Y[g][M][N/g], 2-D
-    copies for column shards of Y[M, N]); nothing outside the shard is written."""
+    copies for column shards of Y[M, N]) by the copy engines (back to back or
+    fanned out) or by the SMs' push kernel (few or many blocks); nothing
+    outside the shard is written."""
     import torch
     from turbocider_b200 import cuda as tcc
     n, k, m, world, rank = 256, 512, 300, 3, 1
@@ -137,13 +140,18 @@ def test_copy_engine_push_fills_every_replica(ctx, layout, fanout):
         offset = rank * n * 2
     tcc.qlinear(ctx, w, x, out=shard)
     dst = (C.c_void_p * (world - 1))(*[ys[i].data_ptr() + offset for i in range(1, world)])
-    ctx.set_push_fanout(fanout)
+    kind, n_par = engine
+    if kind == "copy":
+        ctx.set_push_fanout(n_par)
+    else:
+        ctx.set_push_kernel(n_par)
     try:
         for _ in range(2):
             tcc._check(tcc.lib().tc_cuda_peer_push(ctx.handle, C.c_void_p(src), dst, world - 1, width, rows, pitch,
                                                    pitch, None))
     finally:
         ctx.set_push_fanout(0)
+        ctx.set_push_kernel(0)
     torch.cuda.synchronize()
     assert ctx.status() == 0
     assert shard.abs().sum() > 0
@@ -201,6 +209,8 @@ def _two_rank_worker(rank, world, port, q, mode="fused"):
         dist.init_process_group("nccl", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=60),
                                 device_id=torch.device("cuda", rank))
         ctx = tcc.Context(rank)
+        if mode == "kernel":
+            ctx.set_push_kernel(64)
         n, k, m = 1024, 1024, 520
         raw = tcc.quantize(12, kq_cases.synthetic_weight(n, k, seed=9))
         per = shard.rows_per_rank(n, world)
@@ -245,18 +255,18 @@ def _two_rank_worker(rank, world, port, q, mode="fused"):
         q.put((rank, -1, repr(e)))
 
 
-@pytest.mark.parametrize("mode", ["fused", "copy"])
+@pytest.mark.parametrize("mode", ["fused", "copy", "kernel"])
 def test_two_rank_gather(mode):
     """Two ranks on two GPUs: each computes its column shard and the full Y on
     each rank matches the oracle, with the all-gather fused into the GEMM
-    epilogue or pushed by the copy engines (fanned out over side streams)."""
+    epilogue, pushed by the copy engines, or pushed by the SMs' kernel."""
     import torch
     if torch.cuda.device_count() < 2:
         pytest.skip("needs two GPUs")
     import torch.multiprocessing as mp
     ctx_mp = mp.get_context("spawn")
     q = ctx_mp.Queue()
-    port = 29500 + os.getpid() % 1000 + (7 if mode == "copy" else 0)
+    port = 29500 + os.getpid() % 1000 + {"fused": 0, "copy": 7, "kernel": 13}[mode]
     procs = [ctx_mp.Process(target=_two_rank_worker, args=(r, 2, port, q, mode)) for r in range(2)]
     for p in procs:
         p.start()

@@ -51,6 +51,48 @@ __global__ void peer_barrier_kernel(FlagPtrs f, uint32_t n, uint32_t rank, uint3
     }
 }
 
+// Push by the SMs: every thread moves 16-byte vectors, each read once from
+// this GPU and stored to every destination over NVLink (destination order
+// rotated by block, so that all links carry stores at once).  128-thread
+// blocks with few registers fit beside a resident GEMM CTA on an SM, so the
+// push overlaps the next linear without taking SMs from it.
+struct PushDst {
+    uint4 *p[kMaxPeers];
+};
+constexpr int kPushUnroll = 4;
+template <bool LINEAR>
+__global__ void __launch_bounds__(128) push_kernel(const uint4 *__restrict__ src, PushDst dst, uint32_t n_dst,
+                                                   uint64_t width16, uint64_t rows, uint64_t src_pitch16,
+                                                   uint64_t dst_pitch16) {
+    const uint64_t total = width16 * rows, per_iter = (uint64_t)blockDim.x * kPushUnroll;
+    for (uint64_t base = (uint64_t)blockIdx.x * per_iter + threadIdx.x; base < total;
+         base += (uint64_t)gridDim.x * per_iter) {
+        uint4 v[kPushUnroll];
+        uint64_t to[kPushUnroll];
+#pragma unroll
+        for (int u = 0; u < kPushUnroll; ++u) {
+            const uint64_t i = base + (uint64_t)u * blockDim.x;
+            to[u] = ~0ull;
+            if (i < total) {
+                uint64_t from = i;
+                to[u] = i;
+                if (!LINEAR) {
+                    const uint64_t r = i / width16, c = i % width16;
+                    from = r * src_pitch16 + c;
+                    to[u] = r * dst_pitch16 + c;
+                }
+                v[u] = __ldg(src + from);
+            }
+        }
+        for (uint32_t d = 0; d < n_dst; ++d) {
+            uint4 *out = dst.p[(d + blockIdx.x) % n_dst];
+#pragma unroll
+            for (int u = 0; u < kPushUnroll; ++u)
+                if (to[u] != ~0ull) out[to[u]] = v[u];
+        }
+    }
+}
+
 int fail(const std::string &reason) {
     set_last_error(reason);
     return TC_CUDA_FAIL;
@@ -135,6 +177,25 @@ int tc_cuda_peer_push(tc_cuda_ctx *ctx, const void *src, void *const *dst, uint3
     const cudaStream_t s = static_cast<cudaStream_t>(stream);
     // Contiguous regions go as one linear copy (the copy engines' fastest form).
     const bool linear = rows == 1 || (src_pitch == width_bytes && dst_pitch == width_bytes);
+    // The SMs' push kernel, when chosen and every address, width and pitch
+    // is a multiple of 16 bytes.
+    bool aligned16 = reinterpret_cast<uintptr_t>(src) % 16 == 0 && width_bytes % 16 == 0 &&
+                     (linear || (src_pitch % 16 == 0 && dst_pitch % 16 == 0));
+    for (uint32_t i = 0; i < n_dst; ++i) aligned16 = aligned16 && reinterpret_cast<uintptr_t>(dst[i]) % 16 == 0;
+    if (ctx->push_ctas > 0 && aligned16 && n_dst) {
+        tc::PushDst d{};
+        for (uint32_t i = 0; i < n_dst; ++i) d.p[i] = static_cast<uint4 *>(dst[i]);
+        const uint64_t w16 = linear ? width_bytes * rows / 16 : width_bytes / 16, r = linear ? 1 : rows;
+        const unsigned ctas = (unsigned)ctx->push_ctas;
+        if (linear)
+            tc::push_kernel<true><<<ctas, 128, 0, s>>>(static_cast<const uint4 *>(src), d, n_dst, w16, r, w16, w16);
+        else
+            tc::push_kernel<false><<<ctas, 128, 0, s>>>(static_cast<const uint4 *>(src), d, n_dst, w16, r,
+                                                        src_pitch / 16, dst_pitch / 16);
+        cudaError_t e = cudaGetLastError();
+        if (e != cudaSuccess) return tc::cuda_fail("peer push kernel", e);
+        return tc::ok();
+    }
     auto copy = [&](uint32_t i, cudaStream_t on) {
         return linear ? cudaMemcpyAsync(dst[i], src, width_bytes * rows, cudaMemcpyDeviceToDevice, on)
                       : cudaMemcpy2DAsync(dst[i], dst_pitch, src, src_pitch, width_bytes, rows,
@@ -172,6 +233,13 @@ int tc_cuda_peer_push(tc_cuda_ctx *ctx, const void *src, void *const *dst, uint3
         if ((e = cudaEventRecord(ctx->push_join[l], ctx->push_stream[l])) != cudaSuccess ||
             (e = cudaStreamWaitEvent(s, ctx->push_join[l], 0)) != cudaSuccess)
             return tc::cuda_fail("peer push", e);
+    return tc::ok();
+}
+
+int tc_cuda_set_push_kernel(tc_cuda_ctx *ctx, int ctas) {
+    if (!ctx) return tc::fail("null context");
+    if (ctas < 0 || ctas > 4096) return tc::fail("push kernel blocks out of range 0..4096");
+    ctx->push_ctas = ctas;
     return tc::ok();
 }
 

@@ -23,8 +23,11 @@ struct tc_cuda_ctx {
     // Copy-engine all-gather (tc_cuda_peer_push): by default the copies to
     // the peers go back to back on the caller's stream; push_fanout = k >= 2
     // spreads them over k side streams (created on first use), forked from
-    // and joined back into the caller's stream.
+    // and joined back into the caller's stream.  push_ctas > 0 runs the
+    // pushes as one kernel of that many 128-thread blocks instead (the SMs
+    // store to the peers over NVLink).
     int push_fanout = 0;
+    int push_ctas = 0;
     cudaStream_t push_stream[8] = {};
     cudaEvent_t push_fork = nullptr, push_join[8] = {};
     float *split_ws = nullptr;       // split-K partial products of the tensor-core GEMM

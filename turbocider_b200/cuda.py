@@ -119,6 +119,7 @@ EXPORTS = {
     "tc_cuda_peer_barrier": (C.c_int, [_vp, C.POINTER(_vp), _u32, _u32, _u32, _u32, _vp]),
     "tc_cuda_peer_push": (C.c_int, [_vp, _vp, C.POINTER(_vp), _u32, _u64, _u64, _u64, _u64, _vp]),
     "tc_cuda_set_push_fanout": (C.c_int, [_vp, C.c_int]),
+    "tc_cuda_set_push_kernel": (C.c_int, [_vp, C.c_int]),
     "tc_cuda_set_path": (C.c_int, [_vp, C.c_int]),
     "tc_cuda_qlinear_batched": (C.c_int, [_vp, C.POINTER(_vp), _u32, _vp, _u32, C.POINTER(_vp), C.POINTER(_u64),
                                           C.c_int, _vp]),
@@ -246,6 +247,12 @@ class Context:
         """Peer pushes spread over `streams` side streams (>= 2) or back to
         back on the caller's stream (0 / 1, the default)."""
         _check(lib().tc_cuda_set_push_fanout(self._h, int(streams)))
+
+    def set_push_kernel(self, ctas: int):
+        """Peer pushes by a kernel of `ctas` 128-thread blocks (the SMs store
+        over NVLink) for 16-byte-aligned regions; 0 (the default): by the
+        copy engines."""
+        _check(lib().tc_cuda_set_push_kernel(self._h, int(ctas)))
 
     def close(self):
         if self._h:

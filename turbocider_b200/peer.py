@@ -101,9 +101,10 @@ class PeerGroup:
         return [p + byte_offset for r, p in enumerate(buf.ptrs) if r != self.rank]
 
     def push(self, buf: SymmetricBuffer, byte_offset: int, nbytes: int, stream=None):
-        """Copy-engine all-gather step: copy bytes [byte_offset, +nbytes) of this
-        rank's `buf` into the same bytes of every other rank's `buf`
-        (tc_cuda_peer_push, enqueued on `stream`).  Rank r sends to r+1, r+2, ...
+        """All-gather step: copy bytes [byte_offset, +nbytes) of this rank's
+        `buf` into the same bytes of every other rank's `buf`
+        (tc_cuda_peer_push, enqueued on `stream`; by the copy engines, or by
+        the SMs' push kernel after Context.set_push_kernel).  Rank r sends to r+1, r+2, ...
         in turn, so at any moment every rank receives from a different sender.
         Completion on every rank: `barrier` on the same stream."""
         order = [(self.rank + i) % self.world for i in range(1, self.world)]
