@@ -134,8 +134,10 @@ def test_gemv_config2_shape(ctx, typ, m):
 @pytest.mark.parametrize("n,k", [(64, 12288), (16, 12288), (1000, 2048), (48, 3072), (16, 4096)])
 def test_gemv_k_split_reductions(ctx, typ, m, n, k):
     """The GEMV's K-slice sums through the workspace and the last-arriving CTA
-    of each row tile: 12 slices (n=64 and n=16 at k=12288), 2 (n=1000), 3
-    (n=48), 4 (n=16 at k=4096).  Each runs twice, so a tile counter not left
+    of each row tile.  One token (16-row tiles, K also split across the
+    CTA's warps): 6 slices at k=12288, 1 at n=1000 / n=48, 2 at n=16, k=4096;
+    several tokens (64-row tiles): 24 slices at k=12288, 4 (n=1000), 6
+    (n=48), 8 (n=16, k=4096).  Each runs twice, so a tile counter not left
     at zero by the first call would break the second."""
     from turbocider_b200 import cuda as tcc
     raw, w, xb, x = _setup(ctx, typ, n, k, m, wseed=n + m)
