@@ -70,7 +70,12 @@ def peaks():
 
 # ---------------------------------------------------------------- clocks
 class ClockSampler:
-    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+    """nvidia-smi clocks and throttle reasons every 50 ms.  Started before the
+    warm-up (so that sampling is running when the timed region begins);
+    stop(window) keeps the samples taken inside the timed region's host-time
+    window -- or, for a region shorter than the sampling period, the first
+    samples after it began."""
+    FIELDS = ("timestamp,index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
               "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
               "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
 
@@ -82,12 +87,20 @@ class ClockSampler:
             fd, self.path = tempfile.mkstemp(suffix=".csv")
             os.close(fd)
             self.proc = subprocess.Popen(["nvidia-smi", "-i", str(self.device), f"--query-gpu={self.FIELDS}",
-                                          "--format=csv,noheader,nounits", "-lms", "200", "-f", self.path],
+                                          "--format=csv,noheader,nounits", "-lms", "50", "-f", self.path],
                                          stdout=subprocess.DEVNULL, stderr=subprocess.DEVNULL)
         except OSError:
             self.proc = None
 
-    def stop(self):
+    @staticmethod
+    def _when(stamp: str):
+        import datetime
+        try:
+            return datetime.datetime.strptime(stamp, "%Y/%m/%d %H:%M:%S.%f").timestamp()
+        except ValueError:
+            return None
+
+    def stop(self, window=None):
         if not self.proc:
             return None
         self.proc.terminate()
@@ -98,16 +111,22 @@ class ClockSampler:
         rows = []
         for line in Path(self.path).read_text().splitlines():
             parts = [p.strip() for p in line.split(",")]
-            if len(parts) >= 9:
+            if len(parts) >= 10:
                 rows.append(parts)
         os.unlink(self.path)
+        if window and rows:
+            t0, t1 = window
+            stamped = [(self._when(r[0]), r) for r in rows]
+            inside = [r for t, r in stamped if t is not None and t0 <= t <= t1]
+            after = [r for t, r in stamped if t is not None and t >= t0]
+            rows = inside or after[:2] or rows[-2:]
         if not rows:
             return None
-        sm = [float(r[1]) for r in rows if r[1].replace(".", "").isdigit()]
+        sm = [float(r[2]) for r in rows if r[2].replace(".", "").isdigit()]
         names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
-        reasons = sorted({names[i] for r in rows for i in range(4) if r[5 + i].lower().startswith("active")})
+        reasons = sorted({names[i] for r in rows for i in range(4) if r[6 + i].lower().startswith("active")})
         return {"sm_mhz": statistics.median(sm) if sm else None,
-                "sm_max_mhz": float(rows[0][2]) if rows[0][2].replace(".", "").isdigit() else None,
+                "sm_max_mhz": float(rows[0][3]) if rows[0][3].replace(".", "").isdigit() else None,
                 "reasons": reasons, "samples": len(rows)}
 
 
@@ -957,6 +976,8 @@ def run_ours(args):
         dist.all_reduce(tt, op=dist.ReduceOp.MAX)
         return float(tt.item())
 
+    clocks = ClockSampler(local)
+    clocks.start()
     with torch.cuda.stream(compute):
         for _ in range(args.warmup):
             one_step()
@@ -964,11 +985,10 @@ def run_ours(args):
     if ctx.status(clear=True):
         raise SystemExit("device status word set during warm-up")
 
-    clocks = ClockSampler(local)
-    clocks.start()
     timing = []
     barrier()
     t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    host_t0 = time.time()
     t0.record(compute)
     for i in range(args.steps):
         # per-launch events only in the last step: events between kernels would
@@ -976,7 +996,7 @@ def run_ours(args):
         one_step(timing if i == args.steps - 1 else None)
     t1.record(compute)
     barrier()
-    clock_info = clocks.stop()
+    clock_info = clocks.stop((host_t0, time.time()))
     elapsed = max_over_ranks(t0.elapsed_time(t1) / 1e3)
     flops = step_flops(layers) * args.steps
     value = flops / elapsed / 1e12
