@@ -22,21 +22,26 @@
 // Result: fp32 accumulation of exactly-represented products; equal to the
 // fp32-decode + fp32 matmul oracle up to summation order.
 //
-// Work split: CTA (x, y) = (64 weight rows, one K slice), warp w owning rows
-// 16 w .. 16 w + 15.  The four warps walk the same super-blocks of the slice
-// in step through one ring of stages (3; 2 with more than 8 tokens) filled by
-// per-lane cp.async copies: a stage holds the four warps' packed fields and
-// the super-block's 256 columns of X for every token, copied once per CTA
-// and read by the MMA steps from shared memory.  (With 16 rows per CTA and X
-// fragments loaded from global memory, X -- 16 tokens x the K slice -- came
-// from L2 for every 16 weight rows, 75 MB per config-2 call against 31 MB of
-// weights, and the kernel stalled on those loads.)  One __syncthreads per
-// super-block publishes the stage and frees the slot computed before it.
+// Work split: CTA (x, y) = (one row tile, one K slice), 4 warps, stages
+// filled by per-lane cp.async copies; two tile shapes (gemv_row_warps):
+//   * several tokens: 64 weight rows, warp w owning rows 16 w .. 16 w + 15.
+//     The four warps walk the same super-blocks of the slice in step through
+//     one ring of stages (3; 2 with 8 tokens per tile): a stage holds the
+//     four warps' packed fields and the super-block's 256 columns of X for
+//     every token, copied once per CTA and read by the MMA steps from shared
+//     memory; one __syncthreads per super-block publishes the stage and frees
+//     the slot computed before it.  (With 16 rows per CTA and X fragments
+//     loaded from global memory, X -- 16 tokens x the K slice -- came from L2
+//     for every 16 weight rows, 75 MB per config-2 call against 31 MB of
+//     weights, and the kernel stalled on those loads.)
+//   * one token: 16 weight rows; the warps take interleaved super-blocks of
+//     the slice, each through its own ring (W piece + the token's 512 B of
+//     X), and their sums meet in shared memory.
 // Hundreds of short CTAs keep every SM's loads in flight (the K split sizes
-// the grid, not the SM count).  With several K slices each warp stores its
-// 16 x M partial in the workspace, and the last CTA of the tile to finish
-// (per-tile arrival counter) adds the slices in slice order -- a fixed order,
-// so results are deterministic -- writes Y and resets the counter.
+// the grid, not the SM count).  With several K slices each row warp stores
+// its 16 x M partial in the workspace, and the last CTA of the tile to
+// finish (per-tile arrival counter) adds the slices in slice order -- a fixed
+// order, so results are deterministic -- writes Y and resets the counter.
 // The N8 side of the MMA carries the tokens: NT = 1 or 2 tiles of 8.
 // Launches use programmatic dependent launch: weight prefetch overlaps the
 // tail of the previous kernel in the stream; X, the workspace and Y are
