@@ -1171,16 +1171,16 @@ def main():
                          "(0 / 1: back to back, the default)")
     ap.add_argument("--push-kernel", type=int, default=None,
                     help="--gather copy: push each output with a kernel of this many 128-thread blocks (SM stores "
-                         "over NVLink) instead of the copy engines (0).  Default: 148 blocks at 8 GPUs, the copy "
+                         "over NVLink) instead of the copy engines (0).  Default: 296 blocks at 8 GPUs, the copy "
                          "engines below (measured stack, TFLOP/s: 2 GPUs 1798 copy / 1617 kernel, 4 GPUs 3248 / "
-                         "2466, 8 GPUs 2745 / 3094)")
+                         "2466, 8 GPUs 2745 / 3078-3094 with 148 blocks, 3156 with 296)")
     ap.add_argument("--reserve-sms", type=int, default=None,
                     help="SMs kept free of the GEMM for the all-gather (default 0: measured no gain at N=2)")
     args = ap.parse_args()
     if args.warmup < 3 and args.impl == "ours":
         args.warmup = 3
     if args.push_kernel is None:
-        args.push_kernel = 148 if args.gpus >= 8 else 0
+        args.push_kernel = 296 if args.gpus >= 8 else 0
     if args.leg:
         return run_leg(args)
     return run_reference(args) if args.impl == "reference" else run_ours(args)
