@@ -288,17 +288,18 @@ int tc_cuda_peer_free(tc_cuda_ctx *ctx, void *ptr);
 int tc_cuda_peer_barrier(tc_cuda_ctx *ctx, uint32_t *const *flags, uint32_t n_ranks, uint32_t rank,
                          uint32_t epoch, uint32_t timeout_us, void *stream);
 
-/* All-gather by the copy engines instead of the GEMM epilogue: after a plain
- * tc_cuda_qlinear has written this rank's shard (e.g. its slot of a
+/* All-gather by a push after the GEMM instead of the GEMM epilogue: after a
+ * plain tc_cuda_qlinear has written this rank's shard (e.g. its slot of a
  * shard-major Y[g][M][N/g], the layout of an NCCL all-gather), push the shard
- * into the same place of every peer's buffer with peer copies enqueued on
- * `stream` (a side stream, so the transfer overlaps the next linear and takes
- * no SMs).  rows x width_bytes region, row pitches src_pitch / dst_pitch
- * (ignored for rows == 1; equal to the width: one linear copy per peer).
- * Completion on every rank: tc_cuda_peer_barrier on the same stream.  Like
- * the fused gather, this replaces the ncclAllGather that follows each
- * N-sharded linear; the reference runs on one device and has no counterpart.
- * The copies go back to back on `stream`. */
+ * into the same place of every peer's buffer, enqueued on `stream` (a side
+ * stream, so the transfer overlaps the next linear).  rows x width_bytes
+ * region, row pitches src_pitch / dst_pitch (ignored for rows == 1; equal to
+ * the width: one linear copy per peer).  Completion on every rank:
+ * tc_cuda_peer_barrier on the same stream.  Like the fused gather, this
+ * replaces the ncclAllGather that follows each N-sharded linear; the
+ * reference runs on one device and has no counterpart.  By default the copy
+ * engines do it, back to back on `stream` (no SMs taken); see
+ * tc_cuda_set_push_fanout and tc_cuda_set_push_kernel for the other forms. */
 int tc_cuda_peer_push(tc_cuda_ctx *ctx, const void *src, void *const *dst, uint32_t n_dst, uint64_t width_bytes,
                       uint64_t rows, uint64_t src_pitch, uint64_t dst_pitch, void *stream);
 /* streams >= 2: tc_cuda_peer_push spreads the destinations' copies over that
@@ -314,7 +315,9 @@ int tc_cuda_set_push_fanout(tc_cuda_ctx *ctx, int streams);
  * every destination by the SMs over NVLink; small blocks that fit beside a
  * resident GEMM CTA) whenever every address, the width and the pitches are
  * multiples of 16 bytes; otherwise, and with 0 (the default), by the copy
- * engines. */
+ * engines.  Measured on B200s beside the N-sharded GEMM stack: faster than
+ * the copy engines at 8 GPUs (296 blocks: 632 against 535 GB/s received per
+ * GPU), slower at 2 and 4, where its stores compete with the GEMM. */
 int tc_cuda_set_push_kernel(tc_cuda_ctx *ctx, int ctas);
 
 /* Batched small-M linear: Y_i[m, N_i] = X[m, K] * W_i^T for n_weights
